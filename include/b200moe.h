@@ -1,0 +1,186 @@
+/*
+ * b200moe — C ABI of the B200 (sm_100a) Qwen3-MoE expert layer.
+ *
+ * Drop-in kernels for the MoE path of spark-gpt's train.py.  Every entry
+ * point takes raw device pointers, plain sizes and a CUDA stream
+ * (cudaStream_t passed as void*), enqueues its kernels on that stream and
+ * returns 0 on success or a positive error code; b200moe_last_error() gives
+ * the message of the calling thread's last failure.  No entry point allocates
+ * device memory: outputs and the scratch areas sized by the *_scratch_bytes
+ * helpers belong to the caller.
+ *
+ * Tensors are row-major and contiguous unless a leading dimension is given.
+ * "bf16" buffers hold IEEE bfloat16 values.  Shapes: T tokens, H hidden, E
+ * experts, k top-k, I moe_intermediate, R = T*k routed slots, Rcap =
+ * b200moe_padded_rows(R, E) padded routed rows (each expert's block of rows is
+ * padded with zero rows to a multiple of 128).
+ *
+ * Shape limits of the GPU path: H % 128 == 0, I % 64 == 0, E <= 256,
+ * k <= 16, 1 <= k <= E.
+ */
+#ifndef B200MOE_H_
+#define B200MOE_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200MOE_OK 0
+#define B200MOE_ERR_INVALID_ARG 1
+#define B200MOE_ERR_CUDA 2
+#define B200MOE_ERR_UNSUPPORTED 3
+
+/* Library version (major*10000 + minor*100 + patch). */
+int b200moe_version(void);
+
+/* Message of this thread's last failed call ("" if none). */
+const char* b200moe_last_error(void);
+
+/* Reads and clears the device fault word of the current device (synchronous).
+ * Bits: 1 = a bounded wait gave up, 2 = an expert id outside [0, E),
+ * 4 = inconsistent sizes.  Kernels never trap; they record and return. */
+int b200moe_fault_read_and_clear(unsigned int* fault);
+
+/* Rows of the padded routed-row buffers: R + E*127 rounded up to 128. */
+long long b200moe_padded_rows(long long routed_rows, int num_experts);
+
+/* Router logits width used on the device: E rounded up to 64, 128 or 256. */
+int b200moe_router_width(int num_experts);
+
+/* fp32 master -> bf16 compute copy (the `.to(bfloat16)` of the expert and
+ * router weights, train.py:2306, :2309 and autocast's F.linear at :2145).
+ * dst has rows_out >= rows_in rows of `cols`; rows >= rows_in are zeroed.
+ * rows_out*cols must be a multiple of 4. */
+int b200moe_cast_f32_to_bf16(const float* src, long long rows_in, long long cols,
+                             long long rows_out, void* dst_bf16, void* stream);
+
+/* ---- router: TopKRouter.forward / backward (train.py:2134-2158) ---------- */
+
+/* logits (T, W) bf16 = x (T,H) bf16 . w_router (W,H) bf16 ^T, W = router width
+ * (rows >= E of w_router are zero).  Replaces F.linear at train.py:2145. */
+int b200moe_router_logits(const void* x, const void* w_router, long long T, int H, int W,
+                          void* logits, void* stream);
+
+/* fp32 softmax over the first E of `ld` logit columns, top-k (probability
+ * desc, lower index first on ties), optional renormalisation.  logits are
+ * bf16 (logits_f32 = 0) or fp32 (1).  selected (T,k) int64, weights (T,k)
+ * bf16.  Replaces train.py:2146-2157. */
+int b200moe_router_topk_fwd(const void* logits, int logits_f32, long long ld, long long T,
+                            int E, int k, int norm_topk_prob, long long* selected,
+                            void* weights, void* stream);
+
+/* d logits (T, ld) bf16 from d(routing weights) (T,k) fp32, plus an optional
+ * extra bf16 logit gradient d_extra (T, ld) (the load-balancing loss); columns
+ * >= E are written as zero.  Backward of train.py:2146-2157. */
+int b200moe_router_topk_bwd(const void* logits, long long ld, const long long* selected,
+                            const float* d_weights, const void* d_extra, long long T, int E,
+                            int k, int norm_topk_prob, void* d_logits, void* stream);
+
+/* dx (T,H) bf16 = d_logits (T,W) bf16 . w_router (W,H) bf16.  Backward of
+ * F.linear at train.py:2145 w.r.t. its input. */
+int b200moe_router_dgrad(const void* d_logits, const void* w_router, long long T, int H, int W,
+                         void* dx, void* stream);
+
+/* dw_router (E,H) fp32 (+)= d_logits[:, :E]^T . x.  Backward of F.linear at
+ * train.py:2145 w.r.t. the router weight. */
+int b200moe_router_wgrad(const void* x, const void* d_logits, long long T, int H, int E, int W,
+                         float* dw_router, int accumulate, void* stream);
+
+/* ---- dispatch: Experts.forward sort / histc / cumsum (train.py:2271-2290) - */
+
+long long b200moe_dispatch_scratch_bytes(long long T, int k, int E);
+
+/* Stable counting sort of the flat expert ids selected (T,k) int64.
+ *   counts (E) int32         rows per expert (histc, train.py:2283)
+ *   offsets (E) int32        inclusive cumulative counts (train.py:2289)
+ *   pad_offsets (E+1) int32  first padded row of each expert; [E] = total
+ *   row_flat (Rcap) int32    padded row -> flat slot t*k+s, -1 for padding
+ *   inv_pad (R) int32        flat slot -> padded row
+ *   tile_expert (Rcap/128)   expert of each 128-row tile
+ * Inside an expert, rows keep flat-slot order (= torch.sort(stable=True)). */
+int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* counts,
+                     int* offsets, int* pad_offsets, int* row_flat, int* inv_pad,
+                     int* tile_expert, void* scratch, long long scratch_bytes, void* stream);
+
+/* ---- gather: _GatherTopK (train.py:2195-2217) ---------------------------- */
+
+/* xs (Rcap,H) bf16: xs[p] = x[row_flat[p]/k], zero rows for padding. */
+int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offsets, int E,
+                        int k, int H, long long rows_cap, void* xs, void* stream);
+
+/* dx (T,H) bf16 = sum_s dxs[inv_pad[t*k+s]] (+ addend (T,H) bf16 if given). */
+int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
+                            int k, int H, void* dx, void* stream);
+
+/* ---- combine: _CombineTopK (train.py:2220-2241) -------------------------- */
+
+/* out (T,H) bf16 = sum_s bf16(y[inv_pad[t*k+s]] * weights[t,s]). */
+int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T,
+                        int k, int H, void* out, void* stream);
+
+/* dy (Rcap,H) bf16 = bf16(d_out[t] * w), zero for padding rows;
+ * d_weights (T*k) fp32 = <d_out[t], y[p]> in flat-slot order. */
+int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat,
+                        const int* pad_offsets, const void* weights, int E, int k, int H,
+                        long long rows_cap, void* dy, float* d_weights, void* stream);
+
+/* ---- expert products: _FusedSwiGLU / _GroupedLinear (train.py:1625-2090) - */
+
+/* gu (Rcap,2I) bf16 = xs . W_gu[e]^T per expert; h (Rcap,I) bf16 =
+ * silu(g)*u from the bf16-rounded g,u.  w_gate_up (E,2I,H) bf16.
+ * Replaces _swiglu_gemm (train.py:1719). */
+int b200moe_expert_gate_up_fwd(const void* xs, const void* w_gate_up, const int* tile_expert,
+                               const int* pad_offsets, long long rows_cap, int E, int H, int I,
+                               void* gu, void* h, void* stream);
+
+/* y (Rcap,H) bf16 = h . W_d[e]^T per expert; w_down (E,H,I) bf16.
+ * Replaces _grouped_gemm (train.py:1803) in _GroupedLinear.forward. */
+int b200moe_expert_down_fwd(const void* h, const void* w_down, const int* tile_expert,
+                            const int* pad_offsets, long long rows_cap, int E, int H, int I,
+                            void* y, void* stream);
+
+/* dh = dy . W_d[e] (rounded to bf16), then the SwiGLU backward in the
+ * epilogue: d_gu (Rcap,2I) bf16 = [dh*u*s*(1+g*(1-s)), dh*g*s], s = sigmoid(g).
+ * Replaces _grouped_gemm(transpose_w) (train.py:1894) + _swiglu_tiles (:1899). */
+int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_down, const void* gu,
+                                     const int* tile_expert, const int* pad_offsets,
+                                     long long rows_cap, int E, int H, int I, void* d_gu,
+                                     void* stream);
+
+/* dxs (Rcap,H) bf16 = d_gu . W_gu[e] per expert.  Replaces _swiglu_dgrad
+ * (train.py:2029). */
+int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gate_up, const int* tile_expert,
+                                 const int* pad_offsets, long long rows_cap, int E, int H, int I,
+                                 void* dxs, void* stream);
+
+/* dw (E,M,N) fp32 (+)= a_e^T . b_e over the padded rows of expert e;
+ * a (Rcap,M) bf16, b (Rcap,N) bf16, M % 128 == 0, N % 64 == 0.  Replaces
+ * _grouped_wgrad (train.py:1863) and _swiglu_wgrad (:2047). */
+int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets,
+                         int E, long long rows_cap, float* dw, int accumulate, void* stream);
+
+/* ---- load-balancing loss: global_load_balancing_loss (train.py:3098-3197) */
+
+long long b200moe_lb_scratch_bytes(long long T, int E);
+
+/* packed (2E+2) fp32 += [hard counts (E), soft sums (E), entropy, valid rows]
+ * of one layer; valid (T) uint8 or NULL (all tokens valid). */
+int b200moe_lb_stats(const void* logits, long long ld, const long long* selected,
+                     const unsigned char* valid, long long T, int E, int k, float* packed,
+                     void* scratch, long long scratch_bytes, void* stream);
+
+/* From the (all-reduced) packed sums: aux (1), stats (5: min_frac, max_frac,
+ * cv, entropy, unused) and coef (E): d(local proxy)/d(soft sums). */
+int b200moe_lb_finalize(const float* packed, int E, int k, int world_size, float* aux,
+                        float* stats, float* coef, void* stream);
+
+/* d_logits (T, ld) bf16 = grad * mask * p * (coef - <p, coef>); grad is a
+ * device fp32 scalar. */
+int b200moe_lb_grad(const void* logits, long long ld, const unsigned char* valid, long long T,
+                    int E, const float* coef, const float* grad, void* d_logits, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200MOE_H_ */

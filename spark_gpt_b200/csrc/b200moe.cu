@@ -1,0 +1,593 @@
+// C-ABI entry points of libb200moe.so (declared in include/b200moe.h):
+// argument checks, TMA tensor-map construction, launch shapes.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "../../include/b200moe.h"
+#include "grouped_gemm.cuh"
+#include "routing.cuh"
+
+namespace b200moe {
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return B200MOE_OK;
+}
+
+#define REQUIRE(cond, ...)                                    \
+  do {                                                        \
+    if (!(cond)) return fail(B200MOE_ERR_INVALID_ARG, __VA_ARGS__); \
+  } while (0)
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major (outer, inner) matrix with row stride
+// `ld` elements; box (box_inner, box_outer) with the 128-byte swizzle.
+int make_tmap(CUtensorMap* m, const void* base, long long inner, long long outer, long long ld,
+              int box_inner, int box_outer, const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: base pointer not 16-byte aligned", what);
+  if ((ld * 2) % 16 != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: row stride not a multiple of 16 bytes", what);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
+template <int BN>
+constexpr int stages_for() {
+  return BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                cudaStream_t st, const char* what) {
+  constexpr int STAGES = stages_for<BN>();
+  auto kern = grouped_gemm_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
+  const int smem = static_cast<int>(GemmSmem<BN, STAGES>::kTotal);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  kern<<<num_sms(), 192, smem, st>>>(ta, tb, p);
+  return check_launch(what);
+}
+
+GemmParams blank_params() {
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  return p;
+}
+
+int grid_for(long long items, int per_block) {
+  long long g = (items + per_block - 1) / per_block;
+  const long long cap = static_cast<long long>(num_sms()) * 32;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+int vpt_for(long long width) { return width <= 64 ? 2 : (width <= 128 ? 4 : 8); }
+
+}  // namespace
+}  // namespace b200moe
+
+using namespace b200moe;
+
+extern "C" {
+
+int b200moe_version(void) { return 100; }
+
+const char* b200moe_last_error(void) { return t_last_error.c_str(); }
+
+int b200moe_fault_read_and_clear(unsigned int* fault) {
+  REQUIRE(fault, "fault: null pointer");
+  unsigned int v = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_fault, sizeof(v));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_fault, &zero, sizeof(zero));
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "fault read: %s", cudaGetErrorString(e));
+  *fault = v;
+  return B200MOE_OK;
+}
+
+long long b200moe_padded_rows(long long routed_rows, int num_experts) {
+  const long long r = routed_rows + static_cast<long long>(num_experts) * (kRowTile - 1);
+  return (r + kRowTile - 1) / kRowTile * kRowTile;
+}
+
+int b200moe_router_width(int num_experts) {
+  if (num_experts <= 64) return 64;
+  if (num_experts <= 128) return 128;
+  return 256;
+}
+
+int b200moe_cast_f32_to_bf16(const float* src, long long rows_in, long long cols,
+                             long long rows_out, void* dst, void* stream) {
+  REQUIRE(src && dst, "cast: null pointer");
+  REQUIRE(rows_in >= 0 && rows_out >= rows_in && cols > 0, "cast: bad shape");
+  REQUIRE((rows_out * cols) % 4 == 0, "cast: rows_out*cols must be a multiple of 4");
+  REQUIRE(reinterpret_cast<uintptr_t>(src) % 16 == 0 && reinterpret_cast<uintptr_t>(dst) % 8 == 0,
+          "cast: misaligned pointer");
+  const long long n4 = rows_out * cols / 4;
+  cast_f32_bf16_kernel<<<grid_for(n4, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      src, rows_in, cols, rows_out, static_cast<__nv_bfloat16*>(dst));
+  return check_launch("cast_f32_to_bf16");
+}
+
+// ---------------------------------------------------------------- router
+int b200moe_router_logits(const void* x, const void* w, long long T, int H, int W, void* logits,
+                          void* stream) {
+  REQUIRE(x && w && logits, "router_logits: null pointer");
+  REQUIRE(T > 0 && H % 64 == 0 && H > 0, "router_logits: H must be a positive multiple of 64");
+  REQUIRE(W == 64 || W == 128 || W == 256, "router_logits: width must be 64, 128 or 256");
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, x, H, T, H, 64, 128, "router_logits x"))) return rc;
+  if ((rc = make_tmap(&tb, w, H, W, H, 64, W, "router_logits w"))) return rc;
+  GemmParams p = blank_params();
+  p.num_groups = 1;
+  p.m_tiles = static_cast<int>((T + 127) / 128);
+  p.n_tiles = 1;
+  p.k_blocks = H / 64;
+  p.m_valid = T;
+  p.n_valid = W;
+  p.out = logits;
+  p.ld_out = W;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (W) {
+    case 64: return launch_gemm<64, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_logits");
+    case 128: return launch_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_logits");
+    default: return launch_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_logits");
+  }
+}
+
+int b200moe_router_topk_fwd(const void* logits, int logits_f32, long long ld, long long T, int E,
+                            int k, int norm, long long* selected, void* weights, void* stream) {
+  REQUIRE(logits && selected && weights, "router_topk_fwd: null pointer");
+  REQUIRE(E >= 1 && E <= 256 && ld >= E && ld <= 256, "router_topk_fwd: need 1 <= E <= ld <= 256");
+  REQUIRE(k >= 1 && k <= kMaxTopK && k <= E, "router_topk_fwd: need 1 <= k <= min(E, 16)");
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(T, 8);
+  auto* w = static_cast<__nv_bfloat16*>(weights);
+#define TOPK_LAUNCH(V)                                                                          \
+  if (logits_f32)                                                                               \
+    router_topk_fwd_kernel<V, float><<<grid, 256, 0, st>>>(static_cast<const float*>(logits), \
+                                                           ld, T, E, k, norm, selected, w);    \
+  else                                                                                          \
+    router_topk_fwd_kernel<V, __nv_bfloat16><<<grid, 256, 0, st>>>(                             \
+        static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, selected, w);
+  switch (vpt_for(E)) {
+    case 2: TOPK_LAUNCH(2) break;
+    case 4: TOPK_LAUNCH(4) break;
+    default: TOPK_LAUNCH(8) break;
+  }
+#undef TOPK_LAUNCH
+  return check_launch("router_topk_fwd");
+}
+
+int b200moe_router_topk_bwd(const void* logits, long long ld, const long long* selected,
+                            const float* d_weights, const void* d_extra, long long T, int E, int k,
+                            int norm, void* d_logits, void* stream) {
+  REQUIRE(logits && selected && d_weights && d_logits, "router_topk_bwd: null pointer");
+  REQUIRE(E >= 1 && E <= 256 && ld >= E && ld <= 256, "router_topk_bwd: need 1 <= E <= ld <= 256");
+  REQUIRE(k >= 1 && k <= kMaxTopK && k <= E, "router_topk_bwd: need 1 <= k <= min(E, 16)");
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(T, 8);
+  auto* lg = static_cast<const __nv_bfloat16*>(logits);
+  auto* ex = static_cast<const __nv_bfloat16*>(d_extra);
+  auto* out = static_cast<__nv_bfloat16*>(d_logits);
+  switch (vpt_for(ld)) {
+    case 2: router_topk_bwd_kernel<2><<<grid, 256, 0, st>>>(lg, ld, selected, d_weights, ex, T, E, k, norm, out); break;
+    case 4: router_topk_bwd_kernel<4><<<grid, 256, 0, st>>>(lg, ld, selected, d_weights, ex, T, E, k, norm, out); break;
+    default: router_topk_bwd_kernel<8><<<grid, 256, 0, st>>>(lg, ld, selected, d_weights, ex, T, E, k, norm, out); break;
+  }
+  return check_launch("router_topk_bwd");
+}
+
+int b200moe_router_dgrad(const void* d_logits, const void* w, long long T, int H, int W, void* dx,
+                         void* stream) {
+  REQUIRE(d_logits && w && dx, "router_dgrad: null pointer");
+  REQUIRE(T > 0 && H % 128 == 0, "router_dgrad: H must be a multiple of 128");
+  REQUIRE(W == 64 || W == 128 || W == 256, "router_dgrad: width must be 64, 128 or 256");
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, d_logits, W, T, W, 64, 128, "router_dgrad d_logits"))) return rc;
+  if ((rc = make_tmap(&tb, w, H, W, H, 64, 64, "router_dgrad w"))) return rc;
+  GemmParams p = blank_params();
+  p.num_groups = 1;
+  p.m_tiles = static_cast<int>((T + 127) / 128);
+  const int BN = (H % 256 == 0) ? 256 : 128;
+  p.n_tiles = H / BN;
+  p.k_blocks = W / 64;
+  p.b_group_rows = 0;
+  p.m_valid = T;
+  p.n_valid = H;
+  p.out = dx;
+  p.ld_out = H;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_dgrad");
+  return launch_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_dgrad");
+}
+
+int b200moe_router_wgrad(const void* x, const void* d_logits, long long T, int H, int E, int W,
+                         float* dw, int accumulate, void* stream) {
+  REQUIRE(x && d_logits && dw, "router_wgrad: null pointer");
+  REQUIRE(T > 0 && H % 128 == 0, "router_wgrad: H must be a multiple of 128");
+  REQUIRE(W == 64 || W == 128 || W == 256, "router_wgrad: width must be 64, 128 or 256");
+  REQUIRE(E >= 1 && E <= W, "router_wgrad: need 1 <= E <= width");
+  REQUIRE(T <= 0x7fffffffLL, "router_wgrad: too many tokens");
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, x, H, T, H, 64, 64, "router_wgrad x"))) return rc;
+  if ((rc = make_tmap(&tb, d_logits, W, T, W, 64, 64, "router_wgrad d_logits"))) return rc;
+  GemmParams p = blank_params();
+  p.num_groups = 1;
+  p.m_tiles = H / 128;
+  p.n_tiles = 1;
+  p.k_blocks = static_cast<int>((T + 63) / 64);
+  p.n_valid = E;
+  p.out = dw;
+  p.ld_out = H;
+  p.accumulate = accumulate;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (W) {
+    case 64: return launch_gemm<64, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad");
+    case 128: return launch_gemm<128, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad");
+    default: return launch_gemm<256, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad");
+  }
+}
+
+// ---------------------------------------------------------------- dispatch
+long long b200moe_dispatch_scratch_bytes(long long T, int k, int E) {
+  const long long R = T * k;
+  const long long nblk = (R + kDispatchChunk - 1) / kDispatchChunk;
+  return (nblk > 0 ? nblk : 1) * E * static_cast<long long>(sizeof(int));
+}
+
+int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* counts,
+                     int* offsets, int* pad_offsets, int* row_flat, int* inv_pad, int* tile_expert,
+                     void* scratch, long long scratch_bytes, void* stream) {
+  REQUIRE(selected && counts && offsets && pad_offsets && row_flat && inv_pad && tile_expert &&
+              scratch,
+          "dispatch: null pointer");
+  REQUIRE(E >= 1 && E <= 4096 && k >= 1 && k <= E, "dispatch: need 1 <= k <= E <= 4096");
+  const long long R = T * k;
+  REQUIRE(R >= 0 && b200moe_padded_rows(R, E) < 0x7fffffffLL, "dispatch: too many rows");
+  REQUIRE(scratch_bytes >= b200moe_dispatch_scratch_bytes(T, k, E), "dispatch: scratch too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nblk = static_cast<int>(R > 0 ? (R + kDispatchChunk - 1) / kDispatchChunk : 1);
+  int* base = static_cast<int*>(scratch);
+  dispatch_count_kernel<<<nblk, kDispatchThreads, E * sizeof(int), st>>>(selected, R, E, nblk, base);
+  int rc = check_launch("dispatch_count");
+  if (rc) return rc;
+  dispatch_scan_kernel<<<1, 1024, (2 * E + 1) * sizeof(int), st>>>(base, nblk, E, counts, offsets,
+                                                                   pad_offsets, row_flat, tile_expert);
+  if ((rc = check_launch("dispatch_scan"))) return rc;
+  const size_t shm = (kDispatchThreads / 32) * E * sizeof(int);
+  if (shm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(dispatch_scatter_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
+    if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "dispatch_scatter: %s", cudaGetErrorString(e));
+  }
+  dispatch_scatter_kernel<<<nblk, kDispatchThreads, shm, st>>>(selected, R, E, nblk, base, row_flat,
+                                                               inv_pad);
+  return check_launch("dispatch_scatter");
+}
+
+// ---------------------------------------------------------------- gather / combine
+int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offsets, int E, int k,
+                        int H, long long rows_cap, void* xs, void* stream) {
+  REQUIRE(x && row_flat && pad_offsets && xs, "gather_rows: null pointer");
+  REQUIRE(H % 8 == 0 && H > 0 && k >= 1, "gather_rows: H must be a multiple of 8");
+  gather_rows_kernel<<<grid_for(rows_cap, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), row_flat, pad_offsets + E, k, H,
+      static_cast<__nv_bfloat16*>(xs));
+  return check_launch("gather_rows");
+}
+
+int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
+                            int k, int H, void* dx, void* stream) {
+  REQUIRE(dxs && inv_pad && dx, "gather_rows_bwd: null pointer");
+  REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "gather_rows_bwd: bad shape");
+  if (T == 0) return B200MOE_OK;
+  gather_rows_bwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(dxs), inv_pad, static_cast<const __nv_bfloat16*>(addend), T,
+      k, H, static_cast<__nv_bfloat16*>(dx));
+  return check_launch("gather_rows_bwd");
+}
+
+int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T, int k,
+                        int H, void* out, void* stream) {
+  REQUIRE(y && inv_pad && weights && out, "combine_fwd: null pointer");
+  REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "combine_fwd: bad shape");
+  if (T == 0) return B200MOE_OK;
+  combine_fwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(y), inv_pad, static_cast<const __nv_bfloat16*>(weights), T,
+      k, H, static_cast<__nv_bfloat16*>(out));
+  return check_launch("combine_fwd");
+}
+
+int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat,
+                        const int* pad_offsets, const void* weights, int E, int k, int H,
+                        long long rows_cap, void* dy, float* d_weights, void* stream) {
+  REQUIRE(d_out && y && row_flat && pad_offsets && weights && dy && d_weights,
+          "combine_bwd: null pointer");
+  REQUIRE(H % 8 == 0 && H > 0 && k >= 1, "combine_bwd: bad shape");
+  combine_bwd_kernel<<<grid_for(rows_cap, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(d_out), static_cast<const __nv_bfloat16*>(y), row_flat,
+      pad_offsets + E, static_cast<const __nv_bfloat16*>(weights), k, H,
+      static_cast<__nv_bfloat16*>(dy), d_weights);
+  return check_launch("combine_bwd");
+}
+
+// ---------------------------------------------------------------- expert GEMMs
+static int check_expert_shape(const char* what, long long rows_cap, int E, int H, int I) {
+  REQUIRE(E >= 1 && E <= 4096, "%s: bad E", what);
+  REQUIRE(H > 0 && H % 128 == 0, "%s: H must be a multiple of 128", what);
+  REQUIRE(I > 0 && I % 64 == 0, "%s: I must be a multiple of 64", what);
+  REQUIRE(rows_cap > 0 && rows_cap % 128 == 0 && rows_cap < 0x7fffffffLL,
+          "%s: rows_cap must be a positive multiple of 128", what);
+  REQUIRE(static_cast<long long>(E) * 2 * I < 0x7fffffffLL && static_cast<long long>(E) * H < 0x7fffffffLL,
+          "%s: weights too large", what);
+  return B200MOE_OK;
+}
+
+int b200moe_expert_gate_up_fwd(const void* xs, const void* w_gu, const int* tile_expert,
+                               const int* pad_offsets, long long rows_cap, int E, int H, int I,
+                               void* gu, void* h, void* stream) {
+  REQUIRE(xs && w_gu && tile_expert && pad_offsets && gu && h, "gate_up_fwd: null pointer");
+  int rc = check_expert_shape("gate_up_fwd", rows_cap, E, H, I);
+  if (rc) return rc;
+  const int half = (I % 128 == 0) ? 128 : 64;  // BN = 2*half: gate and up halves
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, xs, H, rows_cap, H, 64, 128, "gate_up_fwd xs"))) return rc;
+  if ((rc = make_tmap(&tb, w_gu, H, static_cast<long long>(E) * 2 * I, H, 64, half,
+                      "gate_up_fwd w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = I / half;
+  p.k_blocks = H / 64;
+  p.b_group_rows = 2 * I;
+  p.b_half_offset = I;
+  p.m_valid = rows_cap;
+  p.n_valid = I;
+  p.out = gu;
+  p.ld_out = 2 * I;
+  p.out2 = h;
+  p.ld_out2 = I;
+  p.inter = I;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (half == 128) return launch_gemm<256, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
+  return launch_gemm<128, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
+}
+
+int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expert,
+                            const int* pad_offsets, long long rows_cap, int E, int H, int I, void* y,
+                            void* stream) {
+  REQUIRE(h && w_d && tile_expert && pad_offsets && y, "down_fwd: null pointer");
+  int rc = check_expert_shape("down_fwd", rows_cap, E, H, I);
+  if (rc) return rc;
+  const int BN = (H % 256 == 0) ? 256 : 128;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, h, I, rows_cap, I, 64, 128, "down_fwd h"))) return rc;
+  if ((rc = make_tmap(&tb, w_d, I, static_cast<long long>(E) * H, I, 64, BN, "down_fwd w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = H / BN;
+  p.k_blocks = I / 64;
+  p.b_group_rows = H;
+  p.m_valid = rows_cap;
+  p.n_valid = H;
+  p.out = y;
+  p.ld_out = H;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
+  return launch_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
+}
+
+int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void* gu,
+                                     const int* tile_expert, const int* pad_offsets,
+                                     long long rows_cap, int E, int H, int I, void* d_gu,
+                                     void* stream) {
+  REQUIRE(dy && w_d && gu && tile_expert && pad_offsets && d_gu, "down_dgrad: null pointer");
+  int rc = check_expert_shape("down_dgrad", rows_cap, E, H, I);
+  if (rc) return rc;
+  const int BN = (I % 256 == 0) ? 256 : (I % 128 == 0 ? 128 : 64);
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, dy, H, rows_cap, H, 64, 128, "down_dgrad dy"))) return rc;
+  // B[n=i][k=h] = W_d[e][h][i]: MN-major, rows (e*H + h), columns i
+  if ((rc = make_tmap(&tb, w_d, I, static_cast<long long>(E) * H, I, 64, 64, "down_dgrad w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = I / BN;
+  p.k_blocks = H / 64;
+  p.b_group_rows = H;
+  p.m_valid = rows_cap;
+  p.n_valid = I;
+  p.out = d_gu;
+  p.ld_out = 2 * I;
+  p.aux = gu;
+  p.ld_aux = 2 * I;
+  p.inter = I;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+  if (BN == 128) return launch_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+  return launch_gemm<64, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+}
+
+int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* tile_expert,
+                                 const int* pad_offsets, long long rows_cap, int E, int H, int I,
+                                 void* dxs, void* stream) {
+  REQUIRE(d_gu && w_gu && tile_expert && pad_offsets && dxs, "gate_up_dgrad: null pointer");
+  int rc = check_expert_shape("gate_up_dgrad", rows_cap, E, H, I);
+  if (rc) return rc;
+  const int BN = (H % 256 == 0) ? 256 : 128;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, d_gu, 2 * I, rows_cap, 2 * I, 64, 128, "gate_up_dgrad d_gu"))) return rc;
+  // B[n=h][k=j] = W_gu[e][j][h]: MN-major, rows (e*2I + j), columns h
+  if ((rc = make_tmap(&tb, w_gu, H, static_cast<long long>(E) * 2 * I, H, 64, 64,
+                      "gate_up_dgrad w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = H / BN;
+  p.k_blocks = 2 * I / 64;
+  p.b_group_rows = 2 * I;
+  p.m_valid = rows_cap;
+  p.n_valid = H;
+  p.out = dxs;
+  p.ld_out = H;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
+  return launch_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
+}
+
+int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets, int E,
+                         long long rows_cap, float* dw, int accumulate, void* stream) {
+  REQUIRE(a && b && pad_offsets && dw, "expert_wgrad: null pointer");
+  REQUIRE(M > 0 && M % 128 == 0, "expert_wgrad: M must be a multiple of 128");
+  REQUIRE(N > 0 && N % 64 == 0, "expert_wgrad: N must be a multiple of 64");
+  REQUIRE(E >= 1 && rows_cap > 0 && rows_cap % 128 == 0, "expert_wgrad: bad rows/E");
+  const int BN = (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, a, M, rows_cap, M, 64, 64, "expert_wgrad a"))) return rc;
+  if ((rc = make_tmap(&tb, b, N, rows_cap, N, 64, 64, "expert_wgrad b"))) return rc;
+  GemmParams p = blank_params();
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.m_tiles = M / 128;
+  p.n_tiles = N / BN;
+  p.n_valid = N;
+  p.out = dw;
+  p.ld_out = N;
+  p.accumulate = accumulate;
+  p.out_group_stride = static_cast<long long>(M) * N;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+  if (BN == 128) return launch_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+  return launch_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+}
+
+// ---------------------------------------------------------------- load balancing
+long long b200moe_lb_scratch_bytes(long long T, int E) {
+  const long long nblk = (T + kLbTokensPerBlock - 1) / kLbTokensPerBlock;
+  return (nblk > 0 ? nblk : 1) * (2LL * E + 2) * static_cast<long long>(sizeof(float));
+}
+
+int b200moe_lb_stats(const void* logits, long long ld, const long long* selected,
+                     const unsigned char* valid, long long T, int E, int k, float* packed,
+                     void* scratch, long long scratch_bytes, void* stream) {
+  REQUIRE(logits && selected && packed && scratch, "lb_stats: null pointer");
+  REQUIRE(E >= 1 && E <= 256 && ld >= E && ld <= 256 && k >= 1 && k <= E && k <= 32,
+          "lb_stats: bad E/k");
+  REQUIRE(scratch_bytes >= b200moe_lb_scratch_bytes(T, E), "lb_stats: scratch too small");
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nblk = static_cast<int>((T + kLbTokensPerBlock - 1) / kLbTokensPerBlock);
+  const size_t shm = (kLbThreads / 32) * (2 * E + 2) * sizeof(float);
+  float* part = static_cast<float*>(scratch);
+  auto* lg = static_cast<const __nv_bfloat16*>(logits);
+  switch (vpt_for(E)) {
+    case 2: lb_partials_kernel<2><<<nblk, kLbThreads, shm, st>>>(lg, ld, selected, valid, T, E, k, part); break;
+    case 4: lb_partials_kernel<4><<<nblk, kLbThreads, shm, st>>>(lg, ld, selected, valid, T, E, k, part); break;
+    default: lb_partials_kernel<8><<<nblk, kLbThreads, shm, st>>>(lg, ld, selected, valid, T, E, k, part); break;
+  }
+  int rc = check_launch("lb_partials");
+  if (rc) return rc;
+  lb_accumulate_kernel<<<1, 512, 0, st>>>(part, nblk, 2 * E + 2, packed);
+  return check_launch("lb_accumulate");
+}
+
+int b200moe_lb_finalize(const float* packed, int E, int k, int world, float* aux, float* stats,
+                        float* coef, void* stream) {
+  REQUIRE(packed && aux && stats && coef, "lb_finalize: null pointer");
+  REQUIRE(E >= 1 && k >= 1 && world >= 1, "lb_finalize: bad E/k/world");
+  lb_finalize_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(packed, E, k, world, aux,
+                                                                       stats, coef);
+  return check_launch("lb_finalize");
+}
+
+int b200moe_lb_grad(const void* logits, long long ld, const unsigned char* valid, long long T,
+                    int E, const float* coef, const float* grad, void* d_logits, void* stream) {
+  REQUIRE(logits && coef && grad && d_logits, "lb_grad: null pointer");
+  REQUIRE(E >= 1 && E <= 256 && ld >= E && ld <= 256, "lb_grad: bad E");
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(T, 8);
+  auto* lg = static_cast<const __nv_bfloat16*>(logits);
+  auto* out = static_cast<__nv_bfloat16*>(d_logits);
+  switch (vpt_for(ld)) {
+    case 2: lb_grad_kernel<2><<<grid, 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out); break;
+    case 4: lb_grad_kernel<4><<<grid, 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out); break;
+    default: lb_grad_kernel<8><<<grid, 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out); break;
+  }
+  return check_launch("lb_grad");
+}
+
+}  // extern "C"

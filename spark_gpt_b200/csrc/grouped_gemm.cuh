@@ -1,0 +1,457 @@
+// Ragged per-expert grouped GEMM on the 5th-generation tensor cores
+// (tcgen05.mma, accumulators in TMEM, operands staged by TMA).
+//
+// One persistent, warp-specialised kernel template covers every contraction
+// of the MoE layer (spark-gpt train.py:1625-2063 does the same work with six
+// Triton kernels):
+//
+//   gate_up fwd   xs (R,H) . W_gu[e]^T  -> gu (R,2I), h = silu(g)*u  [kEpiSwigluFwd]
+//   down fwd      h  (R,I) . W_d[e]^T   -> y (R,H)                   [kEpiStoreBf16]
+//   down dgrad    dy (R,H) . W_d[e]     -> dh, then the SwiGLU backward
+//                 in the epilogue       -> d_gu (R,2I)               [kEpiSwigluBwd]
+//   gate_up dgrad d_gu (R,2I) . W_gu[e] -> dxs (R,H)                 [kEpiStoreBf16]
+//   wgrads        A_e^T . B_e over the rows of expert e -> fp32 (E,M,N) [kEpiStoreF32]
+//   router        logits / d_x / d_W_r^T (single group)             [kEpiStoreBf16 / F32T]
+//
+// Row layout: routed rows are grouped by expert and every expert's block is
+// padded to a multiple of 128 rows (zero rows), so a 128-row M tile never
+// straddles two experts and a 64-row K block of a weight gradient never mixes
+// experts.  `tile_expert[m]` maps an M tile to its expert; `pad_offsets[e]`
+// is the first padded row of expert e and pad_offsets[E] the padded total.
+//
+// Roles (192 threads, one CTA per SM, persistent over tiles):
+//   warp 0      TMA producer (one lane): A and B tiles into a STAGES-deep ring
+//   warp 1      MMA issuer (one lane): 4 x tcgen05.mma (K=16) per 64-wide K block,
+//               into one of two TMEM accumulators (2 x BN fp32 columns)
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> fused math -> global
+//
+// Shared-memory tiles use the 128-byte swizzle.  K-major tiles are
+// [rows][64] (128 B per row); MN-major tiles (the transposed operands of
+// dgrad/wgrad) are [MN/64 chunks][64 k rows][64] with an 8 KB chunk stride.
+#pragma once
+
+#include "common.cuh"
+
+namespace b200moe {
+
+enum Epilogue : int {
+  kEpiStoreBf16 = 0,
+  kEpiSwigluFwd = 1,
+  kEpiSwigluBwd = 2,
+  kEpiStoreF32 = 3,
+  kEpiStoreF32T = 4,
+};
+
+enum Schedule : int {
+  kRowsRagged = 0,  // M = routed rows (one expert per 128-row tile), K static
+  kKRagged = 1,     // K = the routed rows of one expert (weight gradients)
+};
+
+struct GemmParams {
+  const int* tile_expert;  // kRowsRagged: expert of each M tile (nullptr: one group)
+  const int* pad_offsets;  // E+1 padded row starts (nullptr: one group of k_blocks)
+  int num_groups;
+  int m_tiles;        // kRowsRagged single group / kKRagged: M / 128
+  int n_tiles;        // N / BN
+  int k_blocks;       // kRowsRagged: K / 64; kKRagged single group: ceil(rows / 64)
+  int b_group_rows;   // rows of one group in B's tensor map (outer dimension)
+  int b_half_offset;  // kEpiSwigluFwd: rows from the gate half to the up half (I)
+  long long m_valid;  // rows that may be written (kRowsRagged)
+  int n_valid;        // columns that may be written
+  void* out;
+  long long ld_out;
+  void* out2;
+  long long ld_out2;
+  const void* aux;
+  long long ld_aux;
+  int inter;          // I: column offset of the up half inside gu / d_gu
+  int accumulate;     // fp32 outputs: add into the existing values
+  long long out_group_stride;
+};
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr uint32_t kABytes = 128 * 64 * 2;
+  static constexpr uint32_t kBBytes = BN * 64 * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarrierBytes = 256;
+  static constexpr uint32_t kTotal = STAGES * kStageBytes + kBarrierBytes + 1024;
+};
+
+template <int BN>
+struct TmemCols {
+  static constexpr uint32_t value = (2 * BN < 32) ? 32 : 2 * BN;
+};
+
+struct TileInfo {
+  int m, n, g, krow0, kblocks;
+};
+
+template <int SCHED>
+__device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
+  TileInfo T;
+  if (SCHED == kRowsRagged) {
+    T.m = t / p.n_tiles;
+    T.n = t - T.m * p.n_tiles;
+    T.g = p.tile_expert ? __ldg(p.tile_expert + T.m) : 0;
+    T.krow0 = 0;
+    T.kblocks = p.k_blocks;
+  } else {
+    const int per = p.m_tiles * p.n_tiles;
+    T.g = t / per;
+    const int r = t - T.g * per;
+    T.m = r / p.n_tiles;
+    T.n = r - T.m * p.n_tiles;
+    if (p.pad_offsets) {
+      const int s = __ldg(p.pad_offsets + T.g);
+      const int e = __ldg(p.pad_offsets + T.g + 1);
+      T.krow0 = s;
+      T.kblocks = (e - s) / 64;
+    } else {
+      T.krow0 = 0;
+      T.kblocks = p.k_blocks;
+    }
+  }
+  return T;
+}
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * q + 0], v[8 * q + 1]);
+    w.y = pack_bf16x2(v[8 * q + 2], v[8 * q + 3]);
+    w.z = pack_bf16x2(v[8 * q + 4], v[8 * q + 5]);
+    w.w = pack_bf16x2(v[8 * q + 6], v[8 * q + 7]);
+    d[q] = w;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint4 w = s[q];
+    v[8 * q + 0] = bf16_lo(w.x);
+    v[8 * q + 1] = bf16_hi(w.x);
+    v[8 * q + 2] = bf16_lo(w.y);
+    v[8 * q + 3] = bf16_hi(w.y);
+    v[8 * q + 4] = bf16_lo(w.z);
+    v[8 * q + 5] = bf16_hi(w.z);
+    v[8 * q + 6] = bf16_lo(w.w);
+    v[8 * q + 7] = bf16_hi(w.w);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
+  static_assert(SCHED == kRowsRagged ? !A_MN : (A_MN && B_MN), "operand majors vs schedule");
+  constexpr int BM = 128;
+  constexpr int BK = 64;
+  using S = GemmSmem<BN, STAGES>;
+  constexpr uint32_t kTmemCols = TmemCols<BN>::value;
+  constexpr uint32_t kIdesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int num_tiles;
+  if (SCHED == kRowsRagged) {
+    const int mt = p.tile_expert ? (__ldg(p.pad_offsets + p.num_groups) / BM) : p.m_tiles;
+    num_tiles = mt * p.n_tiles;
+  } else {
+    num_tiles = p.num_groups * p.m_tiles * p.n_tiles;
+  }
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+        const TileInfo T = decode_tile<SCHED>(p, t);
+        for (int kb = 0; kb < T.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], S::kStageBytes);
+          uint8_t* a = sA + stage * S::kABytes;
+          uint8_t* b = sB + stage * S::kBBytes;
+          if (!A_MN) {
+            tma_load_2d(a, &tmA, &full[stage], kb * BK, T.m * BM);
+          } else {
+            const int krow = T.krow0 + kb * BK;
+            tma_load_2d(a, &tmA, &full[stage], T.m * BM, krow);
+            tma_load_2d(a + 8192, &tmA, &full[stage], T.m * BM + 64, krow);
+          }
+          if (!B_MN) {
+            if (EPI == kEpiSwigluFwd) {
+              const int row = T.g * p.b_group_rows + T.n * (BN / 2);
+              tma_load_2d(b, &tmB, &full[stage], kb * BK, row);
+              tma_load_2d(b + S::kBBytes / 2, &tmB, &full[stage], kb * BK, row + p.b_half_offset);
+            } else {
+              tma_load_2d(b, &tmB, &full[stage], kb * BK, T.g * p.b_group_rows + T.n * BN);
+            }
+          } else {
+            const int krow =
+                (SCHED == kKRagged) ? (T.krow0 + kb * BK) : (T.g * p.b_group_rows + kb * BK);
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b + j * 8192, &tmB, &full[stage], T.n * BN + 64 * j, krow);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+        const TileInfo T = decode_tile<SCHED>(p, t);
+        if (T.kblocks == 0) continue;
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < T.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * S::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad =
+                A_MN ? make_sdesc(a0 + kk * 2048, 8192, 1024) : make_sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd =
+                B_MN ? make_sdesc(b0 + kk * 2048, 8192, 1024) : make_sdesc(b0 + kk * 32, 16, 1024);
+            umma_bf16(d_tmem, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int row_in = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      const TileInfo T = decode_tile<SCHED>(p, t);
+      if (T.kblocks == 0) {
+        // a weight-gradient tile of an expert that received no rows
+        if ((EPI == kEpiStoreF32 || EPI == kEpiStoreF32T) && !p.accumulate) {
+          if (EPI == kEpiStoreF32) {
+            float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
+                       static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
+            float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int c = 0; c < BN; c += 4) *reinterpret_cast<float4*>(o + c) = z;
+          } else {
+            for (int c = 0; c < BN; ++c) {
+              const int col = T.n * BN + c;
+              if (col < p.n_valid)
+                static_cast<float*>(p.out)[static_cast<long long>(col) * p.ld_out + T.m * BM +
+                                           row_in] = 0.f;
+            }
+          }
+        }
+        continue;
+      }
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+
+      if (EPI == kEpiStoreBf16) {
+        const long long row = static_cast<long long>(T.m) * BM + row_in;
+        const bool row_ok = row < p.m_valid;
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          const int col0 = T.n * BN + c * 32;
+          if (row_ok) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if (col0 + 32 <= p.n_valid) {
+              store_bf16x32(o + col0, v);
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < p.n_valid) o[col0 + j] = __float2bfloat16_rn(v[j]);
+            }
+          }
+        }
+      } else if (EPI == kEpiSwigluFwd) {
+        constexpr int HALF = BN / 2;
+        const long long row = static_cast<long long>(T.m) * BM + row_in;
+        const bool row_ok = row < p.m_valid;
+        __nv_bfloat16* gu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+        __nv_bfloat16* hh = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
+#pragma unroll 1
+        for (int c = 0; c < HALF / 32; ++c) {
+          uint32_t rg[32], ru[32];
+          tmem_ld32(taddr + c * 32, rg);
+          tmem_ld32(taddr + HALF + c * 32, ru);
+          tmem_wait_ld();
+          if (row_ok) {
+            const int col = T.n * HALF + c * 32;
+            float g[32], u[32], h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              g[j] = bf16_round(__uint_as_float(rg[j]));
+              u[j] = bf16_round(__uint_as_float(ru[j]));
+              h[j] = g[j] * sigmoidf_(g[j]) * u[j];
+            }
+            store_bf16x32(gu + col, g);
+            store_bf16x32(gu + p.inter + col, u);
+            store_bf16x32(hh + col, h);
+          }
+        }
+      } else if (EPI == kEpiSwigluBwd) {
+        const long long row = static_cast<long long>(T.m) * BM + row_in;
+        const bool row_ok = row < p.m_valid;
+        const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
+        __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          if (row_ok) {
+            const int col = T.n * BN + c * 32;
+            float g[32], u[32], dg[32], du[32];
+            load_bf16x32(gu + col, g);
+            load_bf16x32(gu + p.inter + col, u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float dh = bf16_round(__uint_as_float(r[j]));
+              const float sig = sigmoidf_(g[j]);
+              dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+              du[j] = dh * g[j] * sig;
+            }
+            store_bf16x32(dgu + col, dg);
+            store_bf16x32(dgu + p.inter + col, du);
+          }
+        }
+      } else if (EPI == kEpiStoreF32) {
+        float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
+                   static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          float4* d = reinterpret_cast<float4*>(o + c * 32);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+            if (p.accumulate) {
+              const float4 old = d[j];
+              v.x += old.x;
+              v.y += old.y;
+              v.z += old.z;
+              v.w += old.w;
+            }
+            d[j] = v;
+          }
+        }
+      } else {  // kEpiStoreF32T
+        float* o = static_cast<float*>(p.out) + T.m * BM + row_in;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = T.n * BN + c * 32 + j;
+            if (col < p.n_valid) {
+              float* dst = o + static_cast<long long>(col) * p.ld_out;
+              const float v = __uint_as_float(r[j]);
+              *dst = p.accumulate ? (*dst + v) : v;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b200moe

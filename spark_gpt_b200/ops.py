@@ -1,0 +1,312 @@
+"""Tensor-level wrappers over the C ABI (include/b200moe.h).
+
+Each function allocates its outputs through torch's caching allocator, passes
+raw pointers plus torch's current CUDA stream to libb200moe.so, and returns
+the outputs.  Shapes follow spark-gpt's MoE path (train.py:2134-2334).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+# --------------------------------------------------------------------------- #
+# launch accounting and optional per-op CUDA-event timing (used by bench.py)
+# --------------------------------------------------------------------------- #
+LAUNCHES = {"count": 0}
+_timing: dict[str, list] | None = None
+
+
+def set_timing(names):
+    """Record CUDA events around the named ops (None disables)."""
+    global _timing
+    _timing = None if names is None else {n: [] for n in names}
+    return _timing
+
+
+def _launch(name: str, kernels: int, fn, *args):
+    LAUNCHES["count"] += kernels
+    if _timing is not None and name in _timing:
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        _lib.call(fn, *args)
+        e.record()
+        _timing[name].append((s, e))
+    else:
+        _lib.call(fn, *args)
+
+
+def _p(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _s(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)
+
+
+def _check(t: torch.Tensor, dtype, name):
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: the B200 MoE kernels need CUDA tensors (no CPU path)")
+    if t.dtype != dtype:
+        raise RuntimeError(f"{name}: expected {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name}: expected a contiguous tensor")
+
+
+BF16 = torch.bfloat16
+
+
+def padded_rows(routed_rows: int, num_experts: int) -> int:
+    return int(_lib.value("b200moe_padded_rows", routed_rows, num_experts))
+
+
+def router_width(num_experts: int) -> int:
+    return int(_lib.value("b200moe_router_width", num_experts))
+
+
+# --------------------------------------------------------------------------- #
+# weights
+# --------------------------------------------------------------------------- #
+def cast_bf16(w: torch.Tensor, rows_out: int | None = None) -> torch.Tensor:
+    """bf16 compute copy of an fp32 master (rows beyond w.shape[0] zero)."""
+    if w.dtype == BF16 and rows_out in (None, w.shape[0]):
+        return w.contiguous()
+    w = w.detach().float().contiguous()
+    rows = w.shape[0]
+    cols = w[0].numel() if rows else 0
+    rows_out = rows if rows_out is None else rows_out
+    out = torch.empty((rows_out, *w.shape[1:]), device=w.device, dtype=BF16)
+    _launch("cast", 1, "b200moe_cast_f32_to_bf16", _p(w), rows, cols, rows_out, _p(out), _s(w))
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# router (train.py:2144-2158)
+# --------------------------------------------------------------------------- #
+def router_logits(x: torch.Tensor, w_router: torch.Tensor) -> torch.Tensor:
+    _check(x, BF16, "router_logits x")
+    _check(w_router, BF16, "router_logits w")
+    T, H = x.shape
+    W = w_router.shape[0]
+    out = torch.empty(T, W, device=x.device, dtype=BF16)
+    if T:
+        _launch("router_logits", 1, "b200moe_router_logits", _p(x), _p(w_router), T, H, W,
+                _p(out), _s(x))
+    return out
+
+
+def router_topk(logits: torch.Tensor, num_experts: int, top_k: int, norm: bool):
+    """logits (T, ld) bf16 or fp32 (first num_experts columns used)."""
+    if logits.dtype not in (BF16, torch.float32):
+        raise RuntimeError("router_topk: logits must be bf16 or fp32")
+    if logits.stride(1) != 1:
+        raise RuntimeError("router_topk: logits rows must be contiguous")
+    T = logits.shape[0]
+    sel = torch.empty(T, top_k, device=logits.device, dtype=torch.int64)
+    w = torch.empty(T, top_k, device=logits.device, dtype=BF16)
+    if T:
+        _launch("router_topk", 1, "b200moe_router_topk_fwd", _p(logits),
+                int(logits.dtype == torch.float32), logits.stride(0), T, num_experts, top_k,
+                int(norm), _p(sel), _p(w), _s(logits))
+    return sel, w
+
+
+def router_topk_bwd(logits, selected, d_weights, d_extra, num_experts, top_k, norm):
+    T, ld = logits.shape[0], logits.stride(0)
+    out = torch.empty(T, ld, device=logits.device, dtype=BF16)
+    if T:
+        _launch("router_topk_bwd", 1, "b200moe_router_topk_bwd", _p(logits), ld, _p(selected),
+                _p(d_weights), _p(d_extra), T, num_experts, top_k, int(norm), _p(out),
+                _s(logits))
+    return out
+
+
+def router_dgrad(d_logits: torch.Tensor, w_router: torch.Tensor) -> torch.Tensor:
+    T, W = d_logits.shape
+    H = w_router.shape[1]
+    out = torch.empty(T, H, device=d_logits.device, dtype=BF16)
+    if T:
+        _launch("router_dgrad", 1, "b200moe_router_dgrad", _p(d_logits), _p(w_router), T, H, W,
+                _p(out), _s(d_logits))
+    return out
+
+
+def router_wgrad(x, d_logits, num_experts, out=None, accumulate=False):
+    T, H = x.shape
+    W = d_logits.shape[1]
+    if out is None:
+        out = torch.empty(num_experts, H, device=x.device, dtype=torch.float32)
+        accumulate = False
+    if T:
+        _launch("router_wgrad", 1, "b200moe_router_wgrad", _p(x), _p(d_logits), T, H,
+                num_experts, W, _p(out), int(accumulate), _s(x))
+    elif not accumulate:
+        out.zero_()
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# dispatch (train.py:2271-2290)
+# --------------------------------------------------------------------------- #
+@dataclass
+class Dispatch:
+    counts: torch.Tensor       # (E,) int32
+    offsets: torch.Tensor      # (E,) int32 inclusive cumsum
+    pad_offsets: torch.Tensor  # (E+1,) int32 padded starts; [E] = padded total
+    row_flat: torch.Tensor     # (Rcap,) int32 padded row -> flat slot, -1 padding
+    inv_pad: torch.Tensor      # (R,) int32 flat slot -> padded row
+    tile_expert: torch.Tensor  # (Rcap/128,) int32
+    rows_cap: int
+    num_tokens: int
+    top_k: int
+    num_experts: int
+
+
+def dispatch(selected: torch.Tensor, num_experts: int) -> Dispatch:
+    _check(selected, torch.int64, "dispatch selected")
+    T, k = selected.shape
+    R = T * k
+    dev = selected.device
+    cap = padded_rows(R, num_experts)
+    i32 = dict(device=dev, dtype=torch.int32)
+    counts = torch.empty(num_experts, **i32)
+    offsets = torch.empty(num_experts, **i32)
+    pad = torch.empty(num_experts + 1, **i32)
+    row_flat = torch.empty(cap, **i32)
+    inv = torch.empty(max(R, 1), **i32)
+    tiles = torch.empty(cap // 128, **i32)
+    nbytes = int(_lib.value("b200moe_dispatch_scratch_bytes", T, k, num_experts))
+    scratch = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+    _launch("dispatch", 3, "b200moe_dispatch", _p(selected), T, k, num_experts, _p(counts),
+            _p(offsets), _p(pad), _p(row_flat), _p(inv), _p(tiles), _p(scratch), nbytes,
+            _s(selected))
+    return Dispatch(counts, offsets, pad, row_flat, inv[:R], tiles, cap, T, k, num_experts)
+
+
+# --------------------------------------------------------------------------- #
+# gather / combine (train.py:2195-2241)
+# --------------------------------------------------------------------------- #
+def gather_rows(x: torch.Tensor, d: Dispatch) -> torch.Tensor:
+    _check(x, BF16, "gather_rows x")
+    H = x.shape[1]
+    xs = torch.empty(d.rows_cap, H, device=x.device, dtype=BF16)
+    _launch("gather", 1, "b200moe_gather_rows", _p(x), _p(d.row_flat), _p(d.pad_offsets),
+            d.num_experts, d.top_k, H, d.rows_cap, _p(xs), _s(x))
+    return xs
+
+
+def gather_rows_bwd(dxs, d: Dispatch, addend=None) -> torch.Tensor:
+    H = dxs.shape[1]
+    dx = torch.empty(d.num_tokens, H, device=dxs.device, dtype=BF16)
+    if d.num_tokens:
+        _launch("gather_bwd", 1, "b200moe_gather_rows_bwd", _p(dxs), _p(d.inv_pad), _p(addend),
+                d.num_tokens, d.top_k, H, _p(dx), _s(dxs))
+    return dx
+
+
+def combine(y, d: Dispatch, weights) -> torch.Tensor:
+    _check(weights, BF16, "combine weights")
+    H = y.shape[1]
+    out = torch.empty(d.num_tokens, H, device=y.device, dtype=BF16)
+    if d.num_tokens:
+        _launch("combine", 1, "b200moe_combine_fwd", _p(y), _p(d.inv_pad), _p(weights),
+                d.num_tokens, d.top_k, H, _p(out), _s(y))
+    return out
+
+
+def combine_bwd(d_out, y, d: Dispatch, weights):
+    _check(d_out, BF16, "combine_bwd d_out")
+    H = y.shape[1]
+    dy = torch.empty(d.rows_cap, H, device=y.device, dtype=BF16)
+    dw = torch.empty(d.num_tokens, d.top_k, device=y.device, dtype=torch.float32)
+    _launch("combine_bwd", 1, "b200moe_combine_bwd", _p(d_out), _p(y), _p(d.row_flat),
+            _p(d.pad_offsets), _p(weights), d.num_experts, d.top_k, H, d.rows_cap, _p(dy),
+            _p(dw), _s(y))
+    return dy, dw
+
+
+# --------------------------------------------------------------------------- #
+# expert products (train.py:1625-2090)
+# --------------------------------------------------------------------------- #
+def gate_up_fwd(xs, w_gu, d: Dispatch):
+    E, two_i, H = w_gu.shape
+    I = two_i // 2
+    gu = torch.empty(d.rows_cap, two_i, device=xs.device, dtype=BF16)
+    h = torch.empty(d.rows_cap, I, device=xs.device, dtype=BF16)
+    _launch("gate_up_fwd", 1, "b200moe_expert_gate_up_fwd", _p(xs), _p(w_gu), _p(d.tile_expert),
+            _p(d.pad_offsets), d.rows_cap, E, H, I, _p(gu), _p(h), _s(xs))
+    return gu, h
+
+
+def down_fwd(h, w_d, d: Dispatch):
+    E, H, I = w_d.shape
+    y = torch.empty(d.rows_cap, H, device=h.device, dtype=BF16)
+    _launch("down_fwd", 1, "b200moe_expert_down_fwd", _p(h), _p(w_d), _p(d.tile_expert),
+            _p(d.pad_offsets), d.rows_cap, E, H, I, _p(y), _s(h))
+    return y
+
+
+def down_dgrad_swiglu(dy, w_d, gu, d: Dispatch):
+    E, H, I = w_d.shape
+    d_gu = torch.empty(d.rows_cap, 2 * I, device=dy.device, dtype=BF16)
+    _launch("down_dgrad", 1, "b200moe_expert_down_dgrad_swiglu", _p(dy), _p(w_d), _p(gu),
+            _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, I, _p(d_gu), _s(dy))
+    return d_gu
+
+
+def gate_up_dgrad(d_gu, w_gu, d: Dispatch):
+    E, two_i, H = w_gu.shape
+    dxs = torch.empty(d.rows_cap, H, device=d_gu.device, dtype=BF16)
+    _launch("gate_up_dgrad", 1, "b200moe_expert_gate_up_dgrad", _p(d_gu), _p(w_gu),
+            _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, two_i // 2, _p(dxs),
+            _s(d_gu))
+    return dxs
+
+
+def wgrad(a, b, d: Dispatch, name="wgrad", out=None, accumulate=False):
+    """(E, M, N) fp32: a_e^T b_e over the padded rows of each expert."""
+    M, N = a.shape[1], b.shape[1]
+    if out is None:
+        out = torch.empty(d.num_experts, M, N, device=a.device, dtype=torch.float32)
+        accumulate = False
+    _launch(name, 1, "b200moe_expert_wgrad", _p(a), M, _p(b), N, _p(d.pad_offsets),
+            d.num_experts, d.rows_cap, _p(out), int(accumulate), _s(a))
+    return out
+
+
+# --------------------------------------------------------------------------- #
+# load-balancing loss (train.py:3098-3197)
+# --------------------------------------------------------------------------- #
+def lb_stats(logits, selected, valid_u8, num_experts, top_k, packed):
+    T = logits.shape[0]
+    nbytes = int(_lib.value("b200moe_lb_scratch_bytes", T, num_experts))
+    scratch = torch.empty(nbytes, device=logits.device, dtype=torch.uint8)
+    if T:
+        _launch("lb_stats", 2, "b200moe_lb_stats", _p(logits), logits.stride(0), _p(selected),
+                _p(valid_u8), T, num_experts, top_k, _p(packed), _p(scratch), nbytes,
+                _s(logits))
+    return packed
+
+
+def lb_finalize(packed, num_experts, top_k, world):
+    dev = packed.device
+    aux = torch.empty((), device=dev, dtype=torch.float32)
+    stats = torch.empty(5, device=dev, dtype=torch.float32)
+    coef = torch.empty(num_experts, device=dev, dtype=torch.float32)
+    _launch("lb_finalize", 1, "b200moe_lb_finalize", _p(packed), num_experts, top_k, world,
+            _p(aux), _p(stats), _p(coef), _s(packed))
+    return aux, stats, coef
+
+
+def lb_grad(logits, valid_u8, coef, grad, num_experts):
+    T, ld = logits.shape[0], logits.stride(0)
+    out = torch.empty(T, ld, device=logits.device, dtype=BF16)
+    if T:
+        _launch("lb_grad", 1, "b200moe_lb_grad", _p(logits), ld, _p(valid_u8), T, num_experts,
+                _p(coef), _p(grad), _p(out), _s(logits))
+    return out

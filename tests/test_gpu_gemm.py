@@ -1,0 +1,157 @@
+"""GPU parity of the tcgen05 grouped GEMMs (every contraction of the layer)
+against fp32 per-expert products of the same bf16 operands."""
+
+import pytest
+import torch
+
+from tests.helpers import assert_bf16_close, bf16_round
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from spark_gpt_b200 import ops as _ops
+    return _ops
+
+
+def _skewed_routing(T, k, E, seed, empty=(1,)):
+    """Routing with some empty experts and one heavy expert."""
+    g = torch.Generator().manual_seed(seed)
+    p = torch.ones(E)
+    for e in empty:
+        p[e] = 0.0
+    p[-1] = 8.0
+    return torch.stack([torch.multinomial(p, k, replacement=False, generator=g) for _ in range(T)])
+
+
+def _setup(ops, T, k, E, H, I, seed):
+    torch.manual_seed(seed)
+    sel = _skewed_routing(T, k, E, seed)
+    d = ops.dispatch(sel.to(DEV), E)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    xs = ops.gather_rows(x, d)
+    wgu = (torch.randn(E, 2 * I, H, device=DEV) * H ** -0.5).to(torch.bfloat16)
+    wd = (torch.randn(E, H, I, device=DEV) * I ** -0.5).to(torch.bfloat16)
+    return d, x, xs, wgu, wd
+
+
+def _segments(d):
+    pad = d.pad_offsets.cpu().tolist()
+    for e in range(d.num_experts):
+        yield e, pad[e], pad[e + 1]
+
+
+SHAPES = [(1000, 2, 8, 256, 128), (600, 4, 6, 256, 192), (4096, 8, 64, 1024, 256),
+          (512, 8, 16, 2048, 768)]
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_gate_up_forward(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 1)
+    gu, h = ops.gate_up_fwd(xs, wgu, d)
+    ref = torch.zeros(d.rows_cap, 2 * I, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            ref[s:t] = xs[s:t].float() @ wgu[e].float().t()
+    n = int(d.pad_offsets[-1])
+    assert_bf16_close(gu[:n], ref[:n], "gu", max_rel=1e-2, mean_rel=5e-4)
+    g, u = gu[:n, :I].float(), gu[:n, I:].float()
+    h_ref = bf16_round(g * torch.sigmoid(g) * u)
+    assert_bf16_close(h[:n], h_ref, "h", max_rel=1e-2, mean_rel=2e-4)
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_down_forward_and_dgrad_swiglu(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 2)
+    gu, h = ops.gate_up_fwd(xs, wgu, d)
+    y = ops.down_fwd(h, wd, d)
+    n = int(d.pad_offsets[-1])
+    y_ref = torch.zeros(n, H, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            y_ref[s:t] = h[s:t].float() @ wd[e].float().t()
+    assert_bf16_close(y[:n], y_ref, "y", max_rel=1e-2, mean_rel=5e-4)
+    dy = torch.randn(d.rows_cap, H, device=DEV).to(torch.bfloat16)
+    dy[n:] = 0
+    d_gu = ops.down_dgrad_swiglu(dy, wd, gu, d)
+    dh = torch.zeros(n, I, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            dh[s:t] = dy[s:t].float() @ wd[e].float()
+    dh = bf16_round(dh)
+    g, u = gu[:n, :I].float(), gu[:n, I:].float()
+    sig = torch.sigmoid(g)
+    ref = torch.cat([dh * u * (sig * (1 + g * (1 - sig))), dh * g * sig], 1)
+    assert_bf16_close(d_gu[:n], ref, "d_gu", max_rel=2e-2, mean_rel=1e-3)
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_gate_up_dgrad(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 3)
+    n = int(d.pad_offsets[-1])
+    d_gu = torch.randn(d.rows_cap, 2 * I, device=DEV).to(torch.bfloat16)
+    dxs = ops.gate_up_dgrad(d_gu, wgu, d)
+    ref = torch.zeros(n, H, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            ref[s:t] = d_gu[s:t].float() @ wgu[e].float()
+    assert_bf16_close(dxs[:n], ref, "dxs", max_rel=1e-2, mean_rel=5e-4)
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_wgrads(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 4)
+    n = int(d.pad_offsets[-1])
+    d_gu = torch.randn(d.rows_cap, 2 * I, device=DEV).to(torch.bfloat16)
+    d_gu[n:] = 0
+    rows = d.row_flat[: d.rows_cap].clone()
+    rows[n:] = -1
+    d_gu[rows < 0] = 0  # padding rows carry zero gradients in the layer
+    dw = ops.wgrad(d_gu, xs, d)
+    ref = torch.zeros(E, 2 * I, H, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            ref[e] = d_gu[s:t].float().t() @ xs[s:t].float()
+    torch.testing.assert_close(dw, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
+    # accumulate into an existing gradient
+    dw2 = ops.wgrad(d_gu, xs, d, out=dw.clone(), accumulate=True)
+    torch.testing.assert_close(dw2, 2 * ref, rtol=1e-3, atol=2e-3 * ref.abs().max().item())
+    # empty experts get exact zeros
+    counts = d.counts.cpu()
+    for e in range(E):
+        if counts[e] == 0:
+            assert torch.all(dw[e] == 0)
+    dy = torch.randn(d.rows_cap, H, device=DEV).to(torch.bfloat16)
+    dy[rows < 0] = 0
+    h = torch.randn(d.rows_cap, I, device=DEV).to(torch.bfloat16)
+    dwd = ops.wgrad(dy, h, d)
+    ref = torch.zeros(E, H, I, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            ref[e] = dy[s:t].float().t() @ h[s:t].float()
+    torch.testing.assert_close(dwd, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
+
+
+@pytest.mark.parametrize("T,H,E", [(1000, 256, 8), (65536 // 16, 1024, 64), (3000, 2048, 128),
+                                   (777, 768, 256)])
+def test_router_gemms(ops, T, H, E):
+    torch.manual_seed(5)
+    W = ops.router_width(E)
+    x = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    w = torch.randn(E, H, device=DEV) * 0.02
+    wb = ops.cast_bf16(w, W)
+    assert torch.all(wb[E:] == 0)
+    assert torch.equal(wb[:E], w.to(torch.bfloat16))
+    logits = ops.router_logits(x, wb)
+    ref = x.float() @ wb.float().t()
+    assert_bf16_close(logits, ref, "logits", max_rel=1e-2, mean_rel=5e-4)
+    dl = torch.randn(T, W, device=DEV).to(torch.bfloat16)
+    dl[:, E:] = 0
+    dx = ops.router_dgrad(dl, wb)
+    assert_bf16_close(dx, dl.float() @ wb.float(), "router dx", max_rel=1e-2, mean_rel=5e-4)
+    dw = ops.router_wgrad(x, dl, E)
+    ref = dl[:, :E].float().t() @ x.float()
+    torch.testing.assert_close(dw, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())

@@ -1,0 +1,146 @@
+"""Pin the CPU oracle against golden vectors made by the reference itself.
+
+The fixtures come from tests/golden/make_golden.py, which runs spark-gpt's own
+SparseMoE / global_load_balancing_loss (train.py:2325-2334, 3098-3197).
+"""
+
+import numpy as np
+import torch
+
+from oracle import moe_oracle as O
+
+
+def close(a, b, rtol=1e-5, atol=1e-6):
+    torch.testing.assert_close(a.float(), b.float(), rtol=rtol, atol=atol)
+
+
+def test_router_known_case(golden):
+    c = golden["router_known"]
+    logits, probs, w, sel = O.router_forward(c["x"], c["w_router"], c["top_k"], c["norm"])
+    close(logits, c["logits"])
+    assert torch.equal(sel, c["selected"])
+    close(w, c["weights"])
+
+
+def test_experts_with_given_routing(golden):
+    c = golden["experts_given_routing"]
+    k = c["selected"].shape[1]
+    d = O.dispatch(c["selected"], c["w_gate_up"].shape[0])
+    sw = c["weights"].reshape(-1)[torch.from_numpy(d.permutation)]
+    xs = O.gather_forward(c["x"], d)
+    gu, h = O.swiglu_forward(xs, c["w_gate_up"], d.offsets)
+    y = O.grouped_linear_forward(h, c["w_down"], d.offsets)
+    out = O.combine_forward(y, sw, d)
+    close(out, c["out"])
+    dy, _ = O.combine_backward(y, sw, d, c["probe"])
+    dh, dwd = O.grouped_linear_backward(h, c["w_down"], dy, d.offsets)
+    dxs, dwgu, _ = O.swiglu_backward(xs, c["w_gate_up"], gu, dh, d.offsets)
+    close(O.gather_backward(dxs, d), c["dx"])
+    close(dwgu, c["dW_gate_up"])
+    close(dwd, c["dW_down"])
+    assert k == 2
+
+
+def test_aux_loss_masked_and_filler(golden):
+    c = golden["aux_masked"]
+    aux, stats, grads = O.load_balancing_loss((c["logits"],), (c["selected"],), c["valid"],
+                                              num_experts=4, top_k=2)
+    close(aux, c["aux"])
+    close(grads[0], c["d_logits"])
+    for k, v in stats.items():
+        close(v, c["stat_" + k])
+    assert torch.all(grads[0][-1] == 0)
+    c = golden["aux_all_filler"]
+    aux, _, grads = O.load_balancing_loss((c["logits"],), (c["selected"],), c["valid"],
+                                          num_experts=4, top_k=2)
+    assert float(aux) == 0.0 and float(c["aux"]) == 0.0
+    assert torch.all(grads[0] == 0)
+
+
+def assert_same_dispatch(d, ref_perm, selected):
+    """The reference sorts with torch.sort(stable=False) (train.py:2275): the
+    order of rows inside one expert's segment is implementation-defined (torch
+    CPU's small-size sort is not stable).  Pin what is defined: the segments
+    hold the same flat indices, and our order inside them is the stable one
+    (expert, flat index) that torch.sort(stable=True) gives."""
+    flat = selected.reshape(-1)
+    stable = torch.sort(flat, stable=True).indices.numpy()
+    assert np.array_equal(d.permutation, stable)
+    for e, s, t in O.expert_ranges(d.offsets):
+        assert np.array_equal(np.sort(d.permutation[s:t]), np.sort(ref_perm[s:t])), e
+    inv = np.empty_like(d.permutation)
+    inv[d.permutation] = np.arange(d.permutation.size)
+    assert np.array_equal(inv, d.inverse)
+
+
+def _layer(c):
+    T = c["x"].shape[0]
+    aux, stats, g_aux = O.load_balancing_loss(
+        None or (c["x"].float() @ c["w_router"].t(),), None or (c["selected"],), c["valid"],
+        num_experts=c["w_gate_up"].shape[0], top_k=c["top_k"])
+    res = O.layer_forward_backward(c["x"], c["w_router"], c["w_gate_up"], c["w_down"],
+                                   c["top_k"], c["probe"], norm_topk_prob=c["norm"],
+                                   d_logits_extra=1e-3 * g_aux[0])
+    return res, aux, stats, T
+
+
+def test_small_layers_match_reference(golden):
+    for name in ("layer_small", "layer_nonorm_filler", "layer_wide_k8"):
+        c = golden[name]
+        res, aux, stats, _ = _layer(c)
+        assert torch.equal(res["selected"], c["selected"]), name
+        d = res["dispatch"]
+        assert_same_dispatch(d, c["permutation"].numpy(), c["selected"]), name
+        assert np.array_equal(d.offsets, c["offsets"].numpy()), name
+        close(res["logits"], c["logits"])
+        close(res["weights"], c["routing_weights"])
+        close(res["out"], c["out"], rtol=1e-4, atol=1e-5)
+        close(aux, c["aux"])
+        for k, v in stats.items():
+            close(v, c["stat_" + k])
+        close(res["dx"], c["dx"], rtol=1e-4, atol=1e-5)
+        close(res["dW_router"], c["dW_router"], rtol=1e-4, atol=1e-5)
+        close(res["dW_gate_up"], c["dW_gate_up"], rtol=1e-4, atol=1e-5)
+        close(res["dW_down"], c["dW_down"], rtol=1e-4, atol=1e-5)
+
+
+def test_config1_matches_reference(golden):
+    c = golden["config1"]
+    T, H, E, k, I = c["shape"].tolist()
+    from tests.golden.make_golden import seeded_inputs
+    x, w_r, w_gu, w_d, probe = seeded_inputs(T, H, E, I, int(c["seed"]))
+    sums = torch.stack([t.double().sum() for t in (x, w_r, w_gu, w_d, probe)])
+    assert torch.allclose(sums, c["input_sums"], rtol=1e-12, atol=1e-9), "RNG drifted"
+    valid = torch.ones(T, dtype=torch.bool)
+    logits = x @ w_r.t()
+    _, sel0 = O.topk_lowest_index(O.softmax_fp32(logits), k)
+    aux, stats, g_aux = O.load_balancing_loss((logits,), (sel0,), valid, num_experts=E, top_k=k)
+    res = O.layer_forward_backward(x, w_r, w_gu, w_d, k, probe, d_logits_extra=1e-3 * g_aux[0])
+    assert torch.equal(res["selected"].to(torch.int8), c["selected"])
+    assert_same_dispatch(res["dispatch"], c["permutation"].numpy().astype(np.int64), res["selected"])
+    assert np.array_equal(res["dispatch"].offsets, c["offsets"].numpy())
+    close(aux, c["aux"])
+    for key in ("out", "logits", "dx"):
+        close(res[key][:64], c[key + "_head"], rtol=1e-4, atol=1e-5)
+        assert abs(float(res[key].double().norm()) / float(c[key + "_norm"]) - 1) < 1e-5
+    close(res["weights"][:64], c["routing_weights_head"])
+    for key in ("dW_router", "dW_gate_up", "dW_down"):
+        close(res[key].reshape(-1)[:4096], c[key + "_head"], rtol=1e-4, atol=1e-6)
+        assert abs(float(res[key].double().norm()) / float(c[key + "_norm"]) - 1) < 1e-5
+
+
+def test_topk_tie_rule_lowest_index():
+    p = torch.tensor([[0.5, 1.0, 1.0, 1.0, 0.2]])
+    v, i = O.topk_lowest_index(p, 2)
+    assert i.tolist() == [[1, 2]]
+    v, i = O.topk_lowest_index(torch.tensor([[0.1, 0.3, 0.3, 0.2]]), 3)
+    assert i.tolist() == [[1, 2, 3]]
+
+
+def test_dispatch_empty_and_all_one_expert():
+    sel = torch.tensor([[2, 0], [2, 0], [0, 2]])
+    d = O.dispatch(sel, 4)
+    assert d.counts.tolist() == [3, 0, 3, 0]
+    assert d.offsets.tolist() == [3, 3, 6, 6]
+    # rows ordered by (expert, token): expert 0 <- tokens 0,1,2 ; expert 2 <- tokens 0,1,2
+    assert d.token_index.tolist() == [0, 1, 2, 0, 1, 2]
