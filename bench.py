@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""MoE-layer forward+backward throughput on B200 (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config cfg2|cfg3]
+                    [--impl b200|reference]
+
+One step = forward of spark_gpt_b200.SparseMoE on T tokens, the global
+load-balancing loss (its 2E+2 all-reduce when N > 1), and the backward of
+(out . d_out + 1e-3 * aux) into x and all three fp32 master parameters, with
+the fp32 -> bf16 weight casts inside the step as in the reference
+(train.py:2306-2309).  N > 1 runs data-parallel replicas (the reference's own
+DP layout: experts replicated, tokens sharded, counts all-reduced), one rank
+per GPU under torchrun, so T tokens per GPU: weak scaling.
+
+Default workload: BASELINE config 2 (hidden 1024, 64 experts, top-8,
+moe_intermediate 256, 65,536 tokens per GPU, near-uniform routing).
+
+--impl reference times the reference's CPU path (the oracle port of
+train.py's torch MoE path, fp32) on the host cores on a bounded token sample
+of the same shapes; rank 0 alone runs it.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+from types import SimpleNamespace
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer fwd+bwd tokens/s/GPU and % BF16 tensor peak at 1/2/4/8 B200"
+CONFIGS = {
+    "cfg2": dict(T=65536, H=1024, E=64, k=8, I=256, routing="near-uniform"),
+    "cfg3": dict(T=16384, H=2048, E=128, k=8, I=768, routing="zipf1.1"),
+}
+# Zipf(s=1.1) router bias scale for cfg3: max expert count ~8x the mean
+# (calibrated once with the CPU oracle on seeded inputs).
+ZIPF_ALPHA = 0.7
+AUX_COEF = 1e-3
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
+    ap.add_argument("--tokens", type=int, default=None,
+                    help="override tokens per GPU (small cases for profiling only)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16": d["bf16_tflops"],
+                "bf16_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16": 1590.0, "bf16_sustained": 1400.0, "source": "fallback"}
+
+
+def gemm_flops(c, T):
+    R = T * c["k"]
+    H, I, E = c["H"], c["I"], c["E"]
+    return {
+        "gate_up_fwd": 4 * R * H * I, "down_fwd": 2 * R * H * I, "down_dgrad": 2 * R * H * I,
+        "down_wgrad": 2 * R * H * I, "gate_up_dgrad": 4 * R * H * I,
+        "gate_up_wgrad": 4 * R * H * I, "router_logits": 2 * T * H * E,
+        "router_dgrad": 2 * T * H * E, "router_wgrad": 2 * T * H * E,
+    }
+
+
+def layer_flops(c, T):
+    return 18 * c["H"] * c["I"] * c["k"] * T
+
+
+# --------------------------------------------------------------------------- #
+# inputs
+# --------------------------------------------------------------------------- #
+def zipf_bias(E, seed):
+    g = torch.Generator().manual_seed(seed + 7)
+    perm = torch.randperm(E, generator=g).float()
+    return ZIPF_ALPHA * torch.log((perm + 1.0) ** -1.1)
+
+
+def make_weights(c, seed):
+    """muP init at base width 256 (train.py:2727-2739), 12-layer writer scale."""
+    g = torch.Generator().manual_seed(seed)
+    std_in = 0.02 / math.sqrt(c["H"] / 256)
+    std_w = std_in / math.sqrt(2 * 12)
+    w_r = torch.randn(c["E"], c["H"], generator=g) * 0.02
+    w_gu = torch.randn(c["E"], 2 * c["I"], c["H"], generator=g) * std_in
+    w_d = torch.randn(c["E"], c["H"], c["I"], generator=g) * std_w
+    if c["routing"].startswith("zipf"):
+        w_r[:, 0] = zipf_bias(c["E"], seed)
+    return w_r, w_gu, w_d
+
+
+def make_tokens(c, T, seed):
+    g = torch.Generator().manual_seed(seed + 1)
+    x = torch.randn(T, c["H"], generator=g)
+    if c["routing"].startswith("zipf"):
+        x[:, 0] = 1.0
+    d_out = torch.randn(T, c["H"], generator=g) * 1e-2
+    return x, d_out
+
+
+# --------------------------------------------------------------------------- #
+# clocks
+# --------------------------------------------------------------------------- #
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=5)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- #
+# CPU arm: the reference's torch MoE path restated in oracle/ (fp32, host cores)
+# --------------------------------------------------------------------------- #
+def cpu_layer_step(c, T, w, x, d_out):
+    from oracle import moe_oracle as O
+    w_r, w_gu, w_d = w
+    logits = x @ w_r.t()
+    _, sel = O.topk_lowest_index(O.softmax_fp32(logits), c["k"])
+    valid = torch.ones(T, dtype=torch.bool)
+    aux, _, g_aux = O.load_balancing_loss((logits,), (sel,), valid, num_experts=c["E"],
+                                          top_k=c["k"])
+    res = O.layer_forward_backward(x, w_r, w_gu, w_d, c["k"], d_out, logits=logits,
+                                   d_logits_extra=AUX_COEF * g_aux[0])
+    return float(aux) + float(res["out"][0, 0])
+
+
+def cpu_throughput(c, T, steps, warmup):
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    w = make_weights(c, 0)
+    x, d_out = make_tokens(c, T, 0)
+    for _ in range(warmup):
+        cpu_layer_step(c, T, w, x, d_out)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        cpu_layer_step(c, T, w, x, d_out)
+    dt = time.perf_counter() - t0
+    return T * steps / dt, cores
+
+
+def run_reference(args, c):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    T = args.cpu_sample_tokens
+    steps = max(1, args.steps)
+    warm = min(args.warmup, 1)
+    v, cores = cpu_throughput(c, T, steps, warm)
+    sample = (f"{T} tokens of {args.config} shapes per step (fp32 torch-CPU port of "
+              f"train.py's torch MoE path, forward+aux+backward)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm, "ms_per_step": 1e3 * T / v,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_block(args, c, args.gpus),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_block(args, c, n):
+    return {"workload": f"{args.config}: single Qwen3-MoE layer fwd+bwd (BASELINE configs"
+                        f"[{1 if args.config == 'cfg2' else 2}])",
+            "tokens_per_gpu": c["T"], "global_batch": c["T"] * n, "hidden": c["H"],
+            "experts": c["E"], "top_k": c["k"], "moe_intermediate": c["I"],
+            "routing": c["routing"], "parallelism": f"dp{n} (replicated experts)",
+            "l2": "inputs larger than L2: each step streams ~10 GiB of activations"}
+
+
+# --------------------------------------------------------------------------- #
+# GPU arm
+# --------------------------------------------------------------------------- #
+def main():
+    args = parse_args()
+    c = dict(CONFIGS[args.config])
+    if args.tokens:
+        c["T"] = args.tokens
+    if args.impl == "reference":
+        run_reference(args, c)
+        return
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import torch.distributed as dist
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+
+    from spark_gpt_b200 import SparseMoE, global_load_balancing_loss, ops
+
+    T = c["T"]
+    cfg = SimpleNamespace(hidden_size=c["H"], num_experts=c["E"], num_experts_per_tok=c["k"],
+                          moe_intermediate_size=c["I"], norm_topk_prob=True)
+    layer = SparseMoE(cfg).to(dev)
+    w_r, w_gu, w_d = make_weights(c, 0)
+    with torch.no_grad():
+        layer.gate.weight.copy_(w_r)
+        layer.experts.gate_up_proj.copy_(w_gu)
+        layer.experts.down_proj.copy_(w_d)
+    x_h, d_out_h = make_tokens(c, T, rank)
+    x_pin = x_h.to(torch.bfloat16).pin_memory()
+    d_pin = d_out_h.to(torch.bfloat16).pin_memory()
+    x = x_pin.to(dev)
+    d_out = d_pin.to(dev)
+    valid = torch.ones(T, dtype=torch.bool, device=dev)
+    coef = torch.tensor(AUX_COEF, device=dev)
+
+    def step(xb, db):
+        for p in layer.parameters():
+            p.grad = None
+        xin = xb.detach().requires_grad_(True)
+        out, logits, sel = layer(xin)
+        aux, _ = global_load_balancing_loss((logits,), (sel,), valid, num_experts=c["E"],
+                                            top_k=c["k"])
+        torch.autograd.backward([out, aux], [db, coef])
+        return aux
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if world == 1:
+            return v
+        t = torch.tensor([v], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+
+    for _ in range(args.warmup):
+        step(x, d_out)
+    torch.cuda.synchronize()
+
+    # ---------------- timed region: inputs resident in HBM
+    names = list(gemm_flops(c, T)) + ["gather", "combine", "combine_bwd", "gather_bwd",
+                                      "dispatch", "router_topk", "router_topk_bwd", "cast",
+                                      "lb_stats", "lb_grad", "lb_finalize"]
+    timing = ops.set_timing(names)
+    launches0 = ops.LAUNCHES["count"]
+    barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        ev0.record()
+        for _ in range(args.steps):
+            step(x, d_out)
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = ops.LAUNCHES["count"] - launches0
+    ops.set_timing(None)
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    value = world * T / (ms / 1e3)
+
+    per_op = {}
+    for n, evs in timing.items():
+        if evs:
+            per_op[n] = sum(s.elapsed_time(e) for s, e in evs) / len(evs)
+    flops = gemm_flops(c, T)
+    pk = peaks()
+    dominant = max((n for n in per_op if n in flops), key=lambda n: per_op[n] * (
+        len(timing[n]) / args.steps))
+    ach = flops[dominant] / (per_op[dominant] / 1e3) / 1e12
+    traffic = None
+    tfile = ROOT / "profiles" / "traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get(args.config, {}).get(dominant)
+    layer_tflops = layer_flops(c, T) / (ms / 1e3) / 1e12
+    gemm_ms = sum(per_op.get(n, 0.0) * len(timing.get(n, [])) / args.steps for n in flops)
+
+    # ---------------- end to end: host buffers, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        aux_h = torch.empty((), dtype=torch.float32).pin_memory()
+        torch.cuda.synchronize()
+        barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            xb = x_pin.to(dev, non_blocking=True)
+            db = d_pin.to(dev, non_blocking=True)
+            aux = step(xb, db)
+            aux_h.copy_(aux.detach(), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+        e2e = {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": x_pin.numel() * 2 + d_pin.numel() * 2,
+               "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        Ts = args.cpu_sample_tokens
+        v, cores = cpu_throughput(c, Ts, 3, 1)
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{Ts} tokens of {args.config} shapes, fp32 torch-CPU port of the "
+                         f"reference's torch MoE path, 3 timed steps after 1 warm-up"}
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, muP-init weights)",
+        "config": config_block(args, c, world),
+        "per_gpu_tokens_per_s": value / world,
+        "layer_gemm_tflops": layer_tflops,
+        "tensor_peak_frac": layer_tflops / pk["bf16_sustained"],
+        "gemm_kernels_ms_per_step": gemm_ms,
+        "roofline": {"bound": "tensor", "kernel": dominant, "achieved": ach,
+                     "peak": pk["bf16_sustained"], "unit": "TFLOP/s",
+                     "frac": ach / pk["bf16_sustained"], "traffic": traffic,
+                     "peak_source": f"{pk['source']} bf16 sustained (MEASURED_PEAKS.json)"},
+        "kernels_ms": {n: round(v, 5) for n, v in sorted(per_op.items())},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": launches,
+        "gpu_launches_per_step": launches / max(args.steps, 1),
+        "clocks": clocks.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
