@@ -58,7 +58,7 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
-    ap.add_argument("--cpu-sample-tokens", type=int, default=2048)
+    ap.add_argument("--cpu-sample-tokens", type=int, default=8192)
     ap.add_argument("--tokens", type=int, default=None,
                     help="override tokens per GPU (small cases for profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
