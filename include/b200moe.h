@@ -102,6 +102,23 @@ int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* 
                      int* offsets, int* pad_offsets, int* row_flat, int* inv_pad,
                      int* tile_expert, void* scratch, long long scratch_bytes, void* stream);
 
+/* b200moe_dispatch without caller scratch; it has no counterpart in the reference.
+ * For callers that hold only the input and output buffers and cannot allocate device
+ * memory: a host runtime bound through FFI that owns a fixed device arena and has no
+ * caching allocator, or code that must not call cudaMalloc/cudaFree because those can
+ * synchronize the device or fail under memory pressure in the middle of a step.  Outputs
+ * are identical to b200moe_dispatch's.  The per-chunk counts go to a 1 MiB array built into
+ * the library (held on every GPU that loads it until exit), so ceil(T*k/4096) * E must be
+ * <= 262144 (e.g. T*k <= 16.7M slots at E = 64, <= 4.19M at E = 256); larger sizes are
+ * rejected with B200MOE_ERR_INVALID_ARG.  The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * All calls share the array: calls that overlap on the GPU (different streams, or different
+ * host threads, without ordering between them) race and give wrong results.  No call
+ * allocates or frees device memory. */
+int b200moe_dispatch_noalloc(const long long* selected, long long T, int k, int E, int* counts,
+                             int* offsets, int* pad_offsets, int* row_flat, int* inv_pad,
+                             int* tile_expert, void* stream);
+
 /* ---- gather: _GatherTopK (train.py:2195-2217) ---------------------------- */
 
 /* xs (Rcap,H) bf16: xs[p] = x[row_flat[p]/k], zero rows for padding. */

@@ -328,6 +328,80 @@ int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* 
   return check_launch("dispatch_scatter");
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------- allocation-free dispatch
+// Per-(expert, 4096-slot chunk) row counts of b200moe_dispatch_noalloc live in this fixed
+// device array instead of caller-provided scratch.  1 MiB; every GPU that loads the library
+// keeps it until the process exits.  Host code must not pass the array's name to a kernel
+// (on the host it is only a stand-in, not a device address): its device address is looked
+// up once per device with cudaGetSymbolAddress and cached.
+namespace {
+constexpr long long kNoAllocDispatchInts = 262144;
+static __device__ __align__(256) int g_noalloc_dispatch_counts[kNoAllocDispatchInts];
+
+std::mutex g_noalloc_mu;
+int* g_noalloc_ptr[64] = {nullptr};
+
+int noalloc_dispatch_scratch(int** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "dispatch_noalloc: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(B200MOE_ERR_UNSUPPORTED, "dispatch_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_dispatch_counts);
+    if (e != cudaSuccess)
+      return fail(B200MOE_ERR_CUDA, "dispatch_noalloc: cudaGetSymbolAddress: %s",
+                  cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<int*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return B200MOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int b200moe_dispatch_noalloc(const long long* selected, long long T, int k, int E, int* counts,
+                             int* offsets, int* pad_offsets, int* row_flat, int* inv_pad,
+                             int* tile_expert, void* stream) {
+  REQUIRE(selected && counts && offsets && pad_offsets && row_flat && inv_pad && tile_expert,
+          "dispatch_noalloc: null pointer");
+  REQUIRE(E >= 1 && E <= 4096 && k >= 1 && k <= E, "dispatch_noalloc: need 1 <= k <= E <= 4096");
+  const long long R = T * k;
+  REQUIRE(R >= 0 && b200moe_padded_rows(R, E) < 0x7fffffffLL, "dispatch_noalloc: too many rows");
+  const long long nblk_ll = R > 0 ? (R + kDispatchChunk - 1) / kDispatchChunk : 1;
+  REQUIRE(nblk_ll * E <= kNoAllocDispatchInts,
+          "dispatch_noalloc: T*k = %lld slots with E = %d experts needs %lld scratch counts "
+          "(ceil(T*k/4096) * E); the built-in scratch holds %lld. Use b200moe_dispatch with "
+          "caller-provided scratch for this size",
+          R, E, nblk_ll * E, kNoAllocDispatchInts);
+  int* base = nullptr;
+  int rc = noalloc_dispatch_scratch(&base);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nblk = static_cast<int>(nblk_ll);
+  // the count kernel writes every one of the nblk*E entries before the scan reads them, so
+  // whatever an earlier call left in the array needs no clearing
+  dispatch_count_kernel<<<nblk, kDispatchThreads, E * sizeof(int), st>>>(selected, R, E, nblk, base);
+  if ((rc = check_launch("dispatch_noalloc count"))) return rc;
+  dispatch_scan_kernel<<<1, 1024, (2 * E + 1) * sizeof(int), st>>>(base, nblk, E, counts, offsets,
+                                                                   pad_offsets, row_flat, tile_expert);
+  if ((rc = check_launch("dispatch_noalloc scan"))) return rc;
+  const size_t shm = (kDispatchThreads / 32) * E * sizeof(int);
+  if (shm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(dispatch_scatter_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
+    if (e != cudaSuccess)
+      return fail(B200MOE_ERR_CUDA, "dispatch_noalloc scatter: %s", cudaGetErrorString(e));
+  }
+  dispatch_scatter_kernel<<<nblk, kDispatchThreads, shm, st>>>(selected, R, E, nblk, base, row_flat,
+                                                               inv_pad);
+  return check_launch("dispatch_noalloc scatter");
+}
+
 // ---------------------------------------------------------------- gather / combine
 int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offsets, int E, int k,
                         int H, long long rows_cap, void* xs, void* stream) {
