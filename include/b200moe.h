@@ -81,10 +81,15 @@ int b200moe_router_topk_bwd(const void* logits, long long ld, const long long* s
 int b200moe_router_dgrad(const void* d_logits, const void* w_router, long long T, int H, int W,
                          void* dx, void* stream);
 
-/* dw_router (E,H) fp32 (+)= d_logits[:, :E]^T . x.  Backward of F.linear at
- * train.py:2145 w.r.t. the router weight. */
+/* Bytes of scratch b200moe_router_wgrad needs (per-split fp32 partials). */
+long long b200moe_router_wgrad_scratch_bytes(long long T, int H, int E);
+
+/* dw_router (E,H) fp32 (+)= d_logits[:, :E]^T . x, split over the T rows into
+ * per-split partials in `scratch` and summed in a fixed order (deterministic).
+ * Backward of F.linear at train.py:2145 w.r.t. the router weight. */
 int b200moe_router_wgrad(const void* x, const void* d_logits, long long T, int H, int E, int W,
-                         float* dw_router, int accumulate, void* stream);
+                         float* dw_router, int accumulate, void* scratch,
+                         long long scratch_bytes, void* stream);
 
 /* ---- dispatch: Experts.forward sort / histc / cumsum (train.py:2271-2290) - */
 

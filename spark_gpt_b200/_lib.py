@@ -31,7 +31,8 @@ PROTOTYPES = {
     "b200moe_router_topk_fwd": (I, [P, I, L, L, I, I, I, P, P, P]),
     "b200moe_router_topk_bwd": (I, [P, L, P, P, P, L, I, I, I, P, P]),
     "b200moe_router_dgrad": (I, [P, P, L, I, I, P, P]),
-    "b200moe_router_wgrad": (I, [P, P, L, I, I, I, P, I, P]),
+    "b200moe_router_wgrad_scratch_bytes": (L, [L, I, I]),
+    "b200moe_router_wgrad": (I, [P, P, L, I, I, I, P, I, P, L, P]),
     "b200moe_dispatch_scratch_bytes": (L, [L, I, I]),
     "b200moe_dispatch": (I, [P, L, I, I, P, P, P, P, P, P, P, L, P]),
     "b200moe_dispatch_noalloc": (I, [P, L, I, I, P, P, P, P, P, P, P]),

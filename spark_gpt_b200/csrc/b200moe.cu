@@ -101,7 +101,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   const int smem = static_cast<int>(GemmSmem<BN, STAGES>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-  kern<<<num_sms(), 192, smem, st>>>(ta, tb, p);
+  kern<<<num_sms(), kGemmThreads, smem, st>>>(ta, tb, p);
   return check_launch(what);
 }
 
@@ -119,7 +119,21 @@ int grid_for(long long items, int per_block) {
   return static_cast<int>(g);
 }
 
-int vpt_for(long long width) { return width <= 64 ? 2 : (width <= 128 ? 4 : 8); }
+// lanes per token of the router kernels: 8 logits per lane, so 8*L >= width
+int lanes_for(long long width) {
+  int l = 2;
+  while (l < 32 && 8 * l < width) l *= 2;
+  return l;
+}
+
+#define B200_SWITCH_LANES(width, ...)          \
+  switch (lanes_for(width)) {                  \
+    case 2: { constexpr int L = 2; __VA_ARGS__ } break;   \
+    case 4: { constexpr int L = 4; __VA_ARGS__ } break;   \
+    case 8: { constexpr int L = 8; __VA_ARGS__ } break;   \
+    case 16: { constexpr int L = 16; __VA_ARGS__ } break; \
+    default: { constexpr int L = 32; __VA_ARGS__ } break; \
+  }
 
 }  // namespace
 }  // namespace b200moe
@@ -200,21 +214,16 @@ int b200moe_router_topk_fwd(const void* logits, int logits_f32, long long ld, lo
   REQUIRE(k >= 1 && k <= kMaxTopK && k <= E, "router_topk_fwd: need 1 <= k <= min(E, 16)");
   if (T == 0) return B200MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = grid_for(T, 8);
   auto* w = static_cast<__nv_bfloat16*>(weights);
-#define TOPK_LAUNCH(V)                                                                          \
-  if (logits_f32)                                                                               \
-    router_topk_fwd_kernel<V, float><<<grid, 256, 0, st>>>(static_cast<const float*>(logits), \
-                                                           ld, T, E, k, norm, selected, w);    \
-  else                                                                                          \
-    router_topk_fwd_kernel<V, __nv_bfloat16><<<grid, 256, 0, st>>>(                             \
-        static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, selected, w);
-  switch (vpt_for(E)) {
-    case 2: TOPK_LAUNCH(2) break;
-    case 4: TOPK_LAUNCH(4) break;
-    default: TOPK_LAUNCH(8) break;
-  }
-#undef TOPK_LAUNCH
+  B200_SWITCH_LANES(E, {
+    const int grid = grid_for(T, 256 / L);
+    if (logits_f32)
+      router_topk_fwd_kernel<L, float><<<grid, 256, 0, st>>>(
+          static_cast<const float*>(logits), ld, T, E, k, norm, selected, w);
+    else
+      router_topk_fwd_kernel<L, __nv_bfloat16><<<grid, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, selected, w);
+  })
   return check_launch("router_topk_fwd");
 }
 
@@ -226,15 +235,13 @@ int b200moe_router_topk_bwd(const void* logits, long long ld, const long long* s
   REQUIRE(k >= 1 && k <= kMaxTopK && k <= E, "router_topk_bwd: need 1 <= k <= min(E, 16)");
   if (T == 0) return B200MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = grid_for(T, 8);
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
   auto* ex = static_cast<const __nv_bfloat16*>(d_extra);
   auto* out = static_cast<__nv_bfloat16*>(d_logits);
-  switch (vpt_for(ld)) {
-    case 2: router_topk_bwd_kernel<2><<<grid, 256, 0, st>>>(lg, ld, selected, d_weights, ex, T, E, k, norm, out); break;
-    case 4: router_topk_bwd_kernel<4><<<grid, 256, 0, st>>>(lg, ld, selected, d_weights, ex, T, E, k, norm, out); break;
-    default: router_topk_bwd_kernel<8><<<grid, 256, 0, st>>>(lg, ld, selected, d_weights, ex, T, E, k, norm, out); break;
-  }
+  B200_SWITCH_LANES(ld, {
+    router_topk_bwd_kernel<L><<<grid_for(T, 256 / L), 256, 0, st>>>(lg, ld, selected, d_weights,
+                                                                    ex, T, E, k, norm, out);
+  })
   return check_launch("router_topk_bwd");
 }
 
@@ -263,32 +270,64 @@ int b200moe_router_dgrad(const void* d_logits, const void* w, long long T, int H
   return launch_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_dgrad");
 }
 
+namespace {
+// K splits of the router weight gradient: enough (split, 128-row M tile) work items for
+// about two per SM.
+void router_wgrad_splits(long long T, int H, int* splits, int* blocks_per_split) {
+  const int kb = static_cast<int>((T + 63) / 64);
+  const int m_tiles = H / 128;
+  int s = (2 * num_sms() + m_tiles - 1) / m_tiles;
+  s = s < 1 ? 1 : (s > kb ? kb : s);
+  const int per = (kb + s - 1) / s;
+  *blocks_per_split = per;
+  *splits = (kb + per - 1) / per;
+}
+}  // namespace
+
+long long b200moe_router_wgrad_scratch_bytes(long long T, int H, int E) {
+  int s = 1, per = 1;
+  if (T <= 0 || H < 128) return 0;
+  router_wgrad_splits(T, H, &s, &per);
+  return static_cast<long long>(s) * E * H * static_cast<long long>(sizeof(float));
+}
+
 int b200moe_router_wgrad(const void* x, const void* d_logits, long long T, int H, int E, int W,
-                         float* dw, int accumulate, void* stream) {
-  REQUIRE(x && d_logits && dw, "router_wgrad: null pointer");
+                         float* dw, int accumulate, void* scratch, long long scratch_bytes,
+                         void* stream) {
+  REQUIRE(x && d_logits && dw && scratch, "router_wgrad: null pointer");
   REQUIRE(T > 0 && H % 128 == 0, "router_wgrad: H must be a multiple of 128");
   REQUIRE(W == 64 || W == 128 || W == 256, "router_wgrad: width must be 64, 128 or 256");
   REQUIRE(E >= 1 && E <= W, "router_wgrad: need 1 <= E <= width");
   REQUIRE(T <= 0x7fffffffLL, "router_wgrad: too many tokens");
+  REQUIRE(scratch_bytes >= b200moe_router_wgrad_scratch_bytes(T, H, E),
+          "router_wgrad: scratch too small");
+  int splits = 1, per = 1;
+  router_wgrad_splits(T, H, &splits, &per);
   CUtensorMap ta, tb;
   int rc;
   if ((rc = make_tmap(&ta, x, H, T, H, 64, 64, "router_wgrad x"))) return rc;
   if ((rc = make_tmap(&tb, d_logits, W, T, W, 64, 64, "router_wgrad d_logits"))) return rc;
   GemmParams p = blank_params();
-  p.num_groups = 1;
+  p.num_groups = splits;
   p.m_tiles = H / 128;
   p.n_tiles = 1;
   p.k_blocks = static_cast<int>((T + 63) / 64);
+  p.k_split_blocks = per;
   p.n_valid = E;
-  p.out = dw;
+  p.out = scratch;
   p.ld_out = H;
-  p.accumulate = accumulate;
+  p.out_group_stride = static_cast<long long>(E) * H;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   switch (W) {
-    case 64: return launch_gemm<64, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad");
-    case 128: return launch_gemm<128, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad");
-    default: return launch_gemm<256, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad");
+    case 64: rc = launch_gemm<64, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad"); break;
+    case 128: rc = launch_gemm<128, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad"); break;
+    default: rc = launch_gemm<256, true, true, kEpiStoreF32T, kKRagged>(ta, tb, p, st, "router_wgrad"); break;
   }
+  if (rc) return rc;
+  const long long n = static_cast<long long>(E) * H;
+  reduce_splits_kernel<<<grid_for(n / 4, 256), 256, 0, st>>>(static_cast<const float*>(scratch),
+                                                             splits, n, dw, accumulate);
+  return check_launch("router_wgrad reduce");
 }
 
 // ---------------------------------------------------------------- dispatch
@@ -624,14 +663,12 @@ int b200moe_lb_stats(const void* logits, long long ld, const long long* selected
   if (T == 0) return B200MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nblk = static_cast<int>((T + kLbTokensPerBlock - 1) / kLbTokensPerBlock);
-  const size_t shm = (kLbThreads / 32) * (2 * E + 2) * sizeof(float);
   float* part = static_cast<float*>(scratch);
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
-  switch (vpt_for(E)) {
-    case 2: lb_partials_kernel<2><<<nblk, kLbThreads, shm, st>>>(lg, ld, selected, valid, T, E, k, part); break;
-    case 4: lb_partials_kernel<4><<<nblk, kLbThreads, shm, st>>>(lg, ld, selected, valid, T, E, k, part); break;
-    default: lb_partials_kernel<8><<<nblk, kLbThreads, shm, st>>>(lg, ld, selected, valid, T, E, k, part); break;
-  }
+  B200_SWITCH_LANES(E, {
+    lb_partials_kernel<L><<<nblk, kLbThreads, lb_partials_smem<L>(E), st>>>(
+        lg, ld, selected, valid, T, E, k, part);
+  })
   int rc = check_launch("lb_partials");
   if (rc) return rc;
   lb_accumulate_kernel<<<1, 512, 0, st>>>(part, nblk, 2 * E + 2, packed);
@@ -642,8 +679,8 @@ int b200moe_lb_finalize(const float* packed, int E, int k, int world, float* aux
                         float* coef, void* stream) {
   REQUIRE(packed && aux && stats && coef, "lb_finalize: null pointer");
   REQUIRE(E >= 1 && k >= 1 && world >= 1, "lb_finalize: bad E/k/world");
-  lb_finalize_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(packed, E, k, world, aux,
-                                                                       stats, coef);
+  lb_finalize_kernel<<<1, 256, (2 * E + 2) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+      packed, E, k, world, aux, stats, coef);
   return check_launch("lb_finalize");
 }
 
@@ -653,14 +690,11 @@ int b200moe_lb_grad(const void* logits, long long ld, const unsigned char* valid
   REQUIRE(E >= 1 && E <= 256 && ld >= E && ld <= 256, "lb_grad: bad E");
   if (T == 0) return B200MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int grid = grid_for(T, 8);
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
   auto* out = static_cast<__nv_bfloat16*>(d_logits);
-  switch (vpt_for(ld)) {
-    case 2: lb_grad_kernel<2><<<grid, 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out); break;
-    case 4: lb_grad_kernel<4><<<grid, 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out); break;
-    default: lb_grad_kernel<8><<<grid, 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out); break;
-  }
+  B200_SWITCH_LANES(ld, {
+    lb_grad_kernel<L><<<grid_for(T, 256 / L), 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out);
+  })
   return check_launch("lb_grad");
 }
 

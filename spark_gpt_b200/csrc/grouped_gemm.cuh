@@ -19,11 +19,13 @@
 // experts.  `tile_expert[m]` maps an M tile to its expert; `pad_offsets[e]`
 // is the first padded row of expert e and pad_offsets[E] the padded total.
 //
-// Roles (192 threads, one CTA per SM, persistent over tiles):
+// Roles (320 threads, one CTA per SM, persistent over tiles):
 //   warp 0      TMA producer (one lane): A and B tiles into a STAGES-deep ring
 //   warp 1      MMA issuer (one lane): 4 x tcgen05.mma (K=16) per 64-wide K block,
 //               into one of two TMEM accumulators (2 x BN fp32 columns)
-//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> fused math -> global
+//   warps 2..9  epilogue: tcgen05.ld TMEM -> registers -> fused math -> global.
+//               Warp w reads TMEM lanes 32*(w%4).. (its hardware lane quarter); the two
+//               warps of a quarter split the tile's 32-column chunks between them.
 //
 // Shared-memory tiles use the 128-byte swizzle.  K-major tiles are
 // [rows][64] (128 B per row); MN-major tiles (the transposed operands of
@@ -67,6 +69,7 @@ struct GemmParams {
   int inter;          // I: column offset of the up half inside gu / d_gu
   int accumulate;     // fp32 outputs: add into the existing values
   long long out_group_stride;
+  int k_split_blocks; // kKRagged single group split over K: 64-row blocks per split (0: none)
 };
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
@@ -109,6 +112,12 @@ __device__ __forceinline__ TileInfo decode_tile(const GemmParams& p, int t) {
       const int e = __ldg(p.pad_offsets + T.g + 1);
       T.krow0 = s;
       T.kblocks = (e - s) / 64;
+    } else if (p.k_split_blocks > 0) {
+      // group index = K split: blocks [g*ks, min((g+1)*ks, k_blocks))
+      const int b0 = T.g * p.k_split_blocks;
+      const int b1 = min(b0 + p.k_split_blocks, p.k_blocks);
+      T.krow0 = b0 * 64;
+      T.kblocks = max(b1 - b0, 0);
     } else {
       T.krow0 = 0;
       T.kblocks = p.k_blocks;
@@ -146,8 +155,11 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
   }
 }
 
+constexpr int kEpilogueWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
+
 template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
@@ -181,7 +193,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpilogueWarps);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -296,6 +308,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;  // which half of the tile's column chunks
     const int row_in = q * 32 + lane;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
@@ -307,12 +320,14 @@ __global__ void __launch_bounds__(192, 1)
             float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
                        static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
             float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int c = 0; c < BN; c += 4) *reinterpret_cast<float4*>(o + c) = z;
+            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 4)
+              *reinterpret_cast<float4*>(o + c) = z;
           } else {
-            for (int c = 0; c < BN; ++c) {
+            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); ++c) {
               const int col = T.n * BN + c;
               if (col < p.n_valid)
-                static_cast<float*>(p.out)[static_cast<long long>(col) * p.ld_out + T.m * BM +
+                static_cast<float*>(p.out)[T.g * p.out_group_stride +
+                                           static_cast<long long>(col) * p.ld_out + T.m * BM +
                                            row_in] = 0.f;
             }
           }
@@ -331,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
         const bool row_ok = row < p.m_valid;
         __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
@@ -355,7 +370,7 @@ __global__ void __launch_bounds__(192, 1)
         __nv_bfloat16* gu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
         __nv_bfloat16* hh = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
 #pragma unroll 1
-        for (int c = 0; c < HALF / 32; ++c) {
+        for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
           uint32_t rg[32], ru[32];
           tmem_ld32(taddr + c * 32, rg);
           tmem_ld32(taddr + HALF + c * 32, ru);
@@ -380,7 +395,7 @@ __global__ void __launch_bounds__(192, 1)
         const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
         __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
@@ -404,7 +419,7 @@ __global__ void __launch_bounds__(192, 1)
         float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
                    static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();
@@ -424,9 +439,9 @@ __global__ void __launch_bounds__(192, 1)
           }
         }
       } else {  // kEpiStoreF32T
-        float* o = static_cast<float*>(p.out) + T.m * BM + row_in;
+        float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride + T.m * BM + row_in;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           uint32_t r[32];
           tmem_ld32(taddr + c * 32, r);
           tmem_wait_ld();

@@ -1,0 +1,404 @@
+// Router softmax / top-k / renormalisation and the load-balancing statistics
+// (spark-gpt train.py:2144-2158, 3098-3197).
+//
+// A token is handled by a group of L lanes (L = 2..32, a power of two) that
+// hold 8 logits each: expert e lives in lane e % L of the group, register
+// slot e / L.  E = 64 uses 8 lanes, so one warp works on 4 tokens at once and
+// every reduction is log2(L) shuffles.  Loops run in whole-warp rounds so
+// every lane of a warp executes every shuffle.
+#pragma once
+
+#include "common.cuh"
+
+namespace b200moe {
+
+constexpr int kMaxTopK = 16;
+constexpr int kVpt = 8;  // logits per lane
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T v);
+template <>
+__device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+  return __bfloat162float(v);
+}
+
+template <int L>
+__device__ __forceinline__ float group_max(float v) {
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <int L>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// p = softmax(row[0:E]) in fp32 (max-subtract, expf, sum, divide); entries of
+// this lane beyond E are 0.  `valid` false: row is not read, p is garbage but
+// every shuffle still runs.
+template <int L, typename LT>
+__device__ __forceinline__ void softmax_group(const LT* __restrict__ row, int E, int sub,
+                                              bool valid, float (&p)[kVpt]) {
+  float z[kVpt];
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) {
+    const int e = sub + L * j;
+    z[j] = (valid && e < E) ? to_f32(row[e]) : -INFINITY;
+    m = fmaxf(m, z[j]);
+  }
+  m = group_max<L>(m);
+  if (!valid) m = 0.f;
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) {
+    const int e = sub + L * j;
+    p[j] = (valid && e < E) ? expf(z[j] - m) : 0.f;
+    s += p[j];
+  }
+  s = group_sum<L>(s);
+  if (!valid) s = 1.f;
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) p[j] = p[j] / s;
+}
+
+// Grid-stride over tokens in whole-grid rounds: every thread runs the same
+// number of rounds (t may be past T: `valid` false), so no lane of a warp
+// leaves a shuffle early.
+struct GroupTokens {
+  long long first, stride, rounds;
+  template <int L>
+  __device__ __forceinline__ static GroupTokens make(long long T) {
+    GroupTokens g;
+    const long long per_block = blockDim.x / L;
+    g.stride = per_block * gridDim.x;
+    g.first = blockIdx.x * per_block + threadIdx.x / L;
+    g.rounds = (T + g.stride - 1) / g.stride;
+    return g;
+  }
+};
+
+template <int L, typename LT>
+__global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long ld, long long T,
+                                       int E, int k, int norm, long long* __restrict__ selected,
+                                       __nv_bfloat16* __restrict__ weights) {
+  const int sub = threadIdx.x & (L - 1);
+  const GroupTokens gt = GroupTokens::make<L>(T);
+  for (long long rnd = 0; rnd < gt.rounds; ++rnd) {
+    const long long t = gt.first + rnd * gt.stride;
+    const bool valid = t < T;
+    float p[kVpt];
+    softmax_group<L>(logits + (valid ? t : 0) * ld, E, sub, valid, p);
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j)
+      if (sub + L * j >= E) p[j] = -1.f;
+    float sv[kMaxTopK];
+    int si[kMaxTopK];
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) {
+      sv[r] = 0.f;
+      si[r] = 0;
+      if (r < k) {
+        float bv = -2.f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j) {
+          const int e = sub + L * j;
+          if (p[j] > bv || (p[j] == bv && e < bi)) {
+            bv = p[j];
+            bi = e;
+          }
+        }
+#pragma unroll
+        for (int o = L / 2; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j)
+          if (sub + L * j == bi) p[j] = -3.f;
+        sv[r] = bv;
+        si[r] = bi;
+      }
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r)
+      if (r < k) sum += sv[r];
+    if (valid) {
+#pragma unroll
+      for (int r = 0; r < kMaxTopK; ++r) {
+        if (r < k && (r & (L - 1)) == sub) {
+          selected[t * k + r] = si[r];
+          weights[t * k + r] = __float2bfloat16_rn(norm ? sv[r] / sum : sv[r]);
+        }
+      }
+    }
+  }
+}
+
+// d logits (T, ld) of the router from d(routing weights) (T,k) fp32 in slot
+// order, plus an optional extra bf16 logit gradient (the load-balancing loss);
+// columns in [E, ld) are written as zero.  8L >= ld.
+template <int L>
+__global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
+                                       const long long* __restrict__ selected,
+                                       const float* __restrict__ d_weights,
+                                       const __nv_bfloat16* __restrict__ d_extra, long long T,
+                                       int E, int k, int norm,
+                                       __nv_bfloat16* __restrict__ d_logits) {
+  const int sub = threadIdx.x & (L - 1);
+  const GroupTokens gt = GroupTokens::make<L>(T);
+  for (long long rnd = 0; rnd < gt.rounds; ++rnd) {
+    const long long t = gt.first + rnd * gt.stride;
+    const bool valid = t < T;
+    const long long tt = valid ? t : 0;
+    float p[kVpt];
+    softmax_group<L>(logits + tt * ld, E, sub, valid, p);
+    int si[kMaxTopK];
+    float ps[kMaxTopK];
+    float s = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) {
+      si[r] = -1;
+      ps[r] = 0.f;
+      if (r < k) {
+        const int e = valid ? static_cast<int>(selected[tt * k + r]) : -1;
+        float v = 0.f;
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j)
+          if (sub + L * j == e) v = p[j];
+        si[r] = e;
+        ps[r] = group_sum<L>(v);
+        s += ps[r];
+      }
+    }
+    if (!valid) s = 1.f;
+    float dot = 0.f;
+    float dw[kMaxTopK];
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) {
+      dw[r] = (r < k && valid) ? d_weights[tt * k + r] : 0.f;
+      if (r < k) dot += dw[r] * (ps[r] / s);
+    }
+    float g[kVpt];
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) g[j] = 0.f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r) {
+      if (r < k) {
+        const float dp = norm ? (dw[r] - dot) / s : dw[r];
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j)
+          if (sub + L * j == si[r]) g[j] = dp;
+      }
+    }
+    float pg = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) pg += p[j] * g[j];
+    pg = group_sum<L>(pg);
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < kVpt; ++j) {
+        const int e = sub + L * j;
+        if (e < ld) {
+          float v = 0.f;
+          if (e < E) {
+            v = p[j] * (g[j] - pg);
+            if (d_extra) v += __bfloat162float(d_extra[tt * ld + e]);
+          }
+          d_logits[tt * ld + e] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// load-balancing statistics (train.py:3141-3153), deterministic two-pass:
+//   partials[b][0:E]   hard counts (masked top-k bincount)
+//   partials[b][E:2E]  soft sums   (masked softmax sums)
+//   partials[b][2E]    entropy sum, partials[b][2E+1] valid rows
+// ---------------------------------------------------------------------------
+constexpr int kLbThreads = 256;
+constexpr int kLbTokensPerBlock = 256;
+
+template <int L>
+__global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
+                                   const long long* __restrict__ selected,
+                                   const unsigned char* __restrict__ valid_mask, long long T,
+                                   int E, int k, float* __restrict__ partials) {
+  constexpr int kGroups = kLbThreads / L;
+  // [groups][8L] soft sums, then [E] hard counts, then [groups] entropy, [groups] rows
+  extern __shared__ float lsh[];
+  float* soft_sh = lsh;
+  float* hard_sh = lsh + kGroups * kVpt * L;
+  float* ent_sh = hard_sh + E;
+  float* rows_sh = ent_sh + kGroups;
+  const int sub = threadIdx.x & (L - 1);
+  const int grp = threadIdx.x / L;
+  for (int i = threadIdx.x; i < E; i += blockDim.x) hard_sh[i] = 0.f;
+  __syncthreads();
+  float soft[kVpt];
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) soft[j] = 0.f;
+  float ent = 0.f, rows = 0.f;
+  const float tiny = 1.17549435e-38f;
+  const long long t0 = static_cast<long long>(blockIdx.x) * kLbTokensPerBlock;
+  for (int i = grp; i < kLbTokensPerBlock; i += kGroups) {  // uniform trip count per warp
+    const long long t = t0 + i;
+    const bool valid = t < T && (valid_mask == nullptr || valid_mask[t] != 0);
+    float p[kVpt];
+    softmax_group<L>(logits + (valid ? t : 0) * ld, E, sub, valid, p);
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < kVpt; ++j) {
+        if (sub + L * j < E) {
+          soft[j] += p[j];
+          ent -= p[j] * logf(fmaxf(p[j], tiny));
+        }
+      }
+      rows += 1.f;
+      for (int r = sub; r < k; r += L) {
+        const long long e = selected[t * k + r];
+        if (e >= 0 && e < E) atomicAdd(&hard_sh[e], 1.f);  // integer-valued: exact
+      }
+    }
+  }
+  ent = group_sum<L>(ent);
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) soft_sh[grp * kVpt * L + sub + L * j] = soft[j];
+  if (sub == 0) {
+    ent_sh[grp] = ent;
+    rows_sh[grp] = rows;
+  }
+  __syncthreads();
+  const int W = 2 * E + 2;
+  float* out = partials + static_cast<long long>(blockIdx.x) * W;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    float acc = 0.f;
+    for (int g = 0; g < kGroups; ++g) acc += soft_sh[g * kVpt * L + e];
+    out[E + e] = acc;
+    out[e] = hard_sh[e];
+  }
+  if (threadIdx.x == 0) {
+    float a = 0.f, b = 0.f;
+    for (int g = 0; g < kGroups; ++g) {
+      a += ent_sh[g];
+      b += rows_sh[g];
+    }
+    out[2 * E] = a;
+    out[2 * E + 1] = b;
+  }
+}
+
+template <int L>
+constexpr size_t lb_partials_smem(int E) {
+  return (static_cast<size_t>(kLbThreads / L) * kVpt * L + E + 2 * (kLbThreads / L)) *
+         sizeof(float);
+}
+
+// packed[i] += sum over blocks of partials[b][i], fixed block order.
+__global__ void lb_accumulate_kernel(const float* __restrict__ partials, int nblk, int W,
+                                     float* __restrict__ packed) {
+  for (int i = threadIdx.x; i < W; i += blockDim.x) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    int b = 0;
+    for (; b + 3 < nblk; b += 4) {
+      a0 += partials[static_cast<long long>(b) * W + i];
+      a1 += partials[static_cast<long long>(b + 1) * W + i];
+      a2 += partials[static_cast<long long>(b + 2) * W + i];
+      a3 += partials[static_cast<long long>(b + 3) * W + i];
+    }
+    for (; b < nblk; ++b) a0 += partials[static_cast<long long>(b) * W + i];
+    packed[i] += (a0 + a1) + (a2 + a3);
+  }
+}
+
+// aux value, stats and the per-expert gradient coefficient from the
+// all-reduced packed sums (train.py:3163-3196).
+// stats: [min_frac, max_frac, cv, entropy, unused]
+__global__ void lb_finalize_kernel(const float* __restrict__ packed, int E, int k, int world,
+                                   float* __restrict__ aux, float* __restrict__ stats,
+                                   float* __restrict__ coef) {
+  extern __shared__ float fsh[];  // [2E+2]
+  for (int i = threadIdx.x; i < 2 * E + 2; i += blockDim.x) fsh[i] = packed[i];
+  __syncthreads();
+  const float rows = fsh[2 * E + 1];
+  const float safe = fmaxf(rows, 1.f);
+  const float has = rows > 0.f ? 1.f : 0.f;
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    coef[e] = has * static_cast<float>(world) * static_cast<float>(E) / safe * (fsh[e] / safe);
+  if (threadIdx.x != 0) return;
+  float dot = 0.f, mn = INFINITY, mx = -INFINITY, sum = 0.f, unused = 0.f;
+  for (int e = 0; e < E; ++e) {
+    const float a = fsh[e] / safe;
+    dot += a * (fsh[E + e] / safe);
+    const float fr = fsh[e] / (safe * k);
+    mn = fminf(mn, fr);
+    mx = fmaxf(mx, fr);
+    sum += fr;
+    unused += fsh[e] == 0.f ? 1.f : 0.f;
+  }
+  const float mean = sum / E;
+  float var = 0.f;
+  for (int e = 0; e < E; ++e) {
+    const float d = fsh[e] / (safe * k) - mean;
+    var += d * d;
+  }
+  var /= E;
+  *aux = has * static_cast<float>(E) * dot;
+  stats[0] = mn;
+  stats[1] = mx;
+  stats[2] = sqrtf(var) / fmaxf(mean, 1e-12f);
+  stats[3] = fsh[2 * E] / safe;
+  stats[4] = unused;
+}
+
+// d aux / d logits[t,e] = g * mask_t * p_e (coef_e - <p, coef>), g = *grad;
+// columns in [E, ld) are zero.  8L >= ld.
+template <int L>
+__global__ void lb_grad_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
+                               const unsigned char* __restrict__ valid_mask, long long T, int E,
+                               const float* __restrict__ coef, const float* __restrict__ grad,
+                               __nv_bfloat16* __restrict__ d_logits) {
+  const float g = *grad;
+  const int sub = threadIdx.x & (L - 1);
+  float c[kVpt];
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j) c[j] = (sub + L * j < E) ? coef[sub + L * j] : 0.f;
+  const GroupTokens gt = GroupTokens::make<L>(T);
+  for (long long rnd = 0; rnd < gt.rounds; ++rnd) {
+    const long long t = gt.first + rnd * gt.stride;
+    const bool valid = t < T;
+    const long long tt = valid ? t : 0;
+    const bool on = valid && (valid_mask == nullptr || valid_mask[tt] != 0);
+    float p[kVpt];
+    softmax_group<L>(logits + tt * ld, E, sub, valid, p);
+    float pc = 0.f;
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) pc += p[j] * c[j];
+    pc = group_sum<L>(pc);
+    if (valid) {
+#pragma unroll
+      for (int j = 0; j < kVpt; ++j) {
+        const int e = sub + L * j;
+        if (e < ld) {
+          const float v = (on && e < E) ? g * p[j] * (c[j] - pc) : 0.f;
+          d_logits[tt * ld + e] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace b200moe

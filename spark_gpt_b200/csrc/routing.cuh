@@ -1,30 +1,21 @@
-// HBM-bound kernels of the MoE layer: router softmax/top-k (+ backward),
-// dispatch (histogram, scan, stable permutation into 128-row-padded expert
-// blocks), row gather / its top-k sum backward, weighted combine (+ backward)
-// and the load-balancing statistics.
+// HBM-bound kernels of the MoE layer: weight cast, dispatch (histogram, scan,
+// stable permutation into 128-row-padded expert blocks), row gather and its
+// top-k sum backward, weighted combine and its backward.  (Router and
+// load-balancing kernels: router.cuh.)
 //
-// All of them are one-warp-per-row or one-warp-per-token kernels with 16-byte
-// vector accesses; they never allocate and never use atomics on global
-// memory, so every result is deterministic.
+// Row kernels are one warp per row or per token with 16-byte vector accesses;
+// nothing allocates and nothing uses atomics on global memory, so every
+// result is deterministic.
 #pragma once
 
 #include "common.cuh"
+#include "router.cuh"
 
 namespace b200moe {
 
 constexpr int kRowTile = 128;       // padding granule of an expert's row block
 constexpr int kDispatchChunk = 4096;  // flat routed slots per dispatch block
 constexpr int kDispatchThreads = 256;
-constexpr int kMaxTopK = 16;
-
-template <typename T>
-__device__ __forceinline__ float to_f32(T v);
-template <>
-__device__ __forceinline__ float to_f32<float>(float v) { return v; }
-template <>
-__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
-  return __bfloat162float(v);
-}
 
 // ---------------------------------------------------------------------------
 // fp32 master -> bf16 compute copy, rows >= rows_in zero-filled
@@ -53,165 +44,21 @@ __global__ void cast_f32_bf16_kernel(const float* __restrict__ src, long long ro
   }
 }
 
-// ---------------------------------------------------------------------------
-// router: fp32 softmax over E logits, top-k, renormalisation
-// (spark-gpt train.py:2144-2158).  One warp per token, expert e in lane e%32,
-// register slot e/32.  Selection order: probability desc, lower index first
-// on ties (torch CUDA's top-k takes the lowest indices among values equal to
-// the k-th).
-// ---------------------------------------------------------------------------
-template <int VPT, typename LT>
-__device__ __forceinline__ void softmax_row(const LT* __restrict__ row, int E, int lane,
-                                            float (&p)[VPT]) {
-  float z[VPT];
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int e = lane + 32 * j;
-    z[j] = e < E ? to_f32(row[e]) : -INFINITY;
-    m = fmaxf(m, z[j]);
-  }
-  m = warp_max(m);
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) {
-    const int e = lane + 32 * j;
-    p[j] = e < E ? expf(z[j] - m) : 0.f;
-    s += p[j];
-  }
-  s = warp_sum(s);
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) p[j] = p[j] / s;
-}
-
-template <int VPT, typename LT>
-__global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long ld, long long T,
-                                       int E, int k, int norm, long long* __restrict__ selected,
-                                       __nv_bfloat16* __restrict__ weights) {
-  const int lane = threadIdx.x & 31;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
-       t < T; t += warps) {
-    float p[VPT];
-    softmax_row<VPT>(logits + t * ld, E, lane, p);
-#pragma unroll
-    for (int j = 0; j < VPT; ++j)
-      if (lane + 32 * j >= E) p[j] = -1.f;
-    float sv[kMaxTopK];
-    int si[kMaxTopK];
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      sv[r] = 0.f;
-      si[r] = 0;
-      if (r < k) {
-        float bv = -2.f;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < VPT; ++j) {
-          const int e = lane + 32 * j;
-          if (p[j] > bv || (p[j] == bv && e < bi)) {
-            bv = p[j];
-            bi = e;
-          }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < VPT; ++j)
-          if (lane + 32 * j == bi) p[j] = -3.f;
-        sv[r] = bv;
-        si[r] = bi;
-      }
+// out[i] (+)= sum_s partial[s*n + i], fixed order over s (n % 4 == 0)
+__global__ void reduce_splits_kernel(const float* __restrict__ partial, int splits, long long n,
+                                     float* __restrict__ out, int accumulate) {
+  const long long n4 = n / 4;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float4 acc = accumulate ? reinterpret_cast<const float4*>(out)[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < splits; ++s) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(partial + s * n) + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
     }
-    float sum = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r)
-      if (r < k) sum += sv[r];
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      if (r < k && lane == r) {
-        selected[t * k + r] = si[r];
-        weights[t * k + r] = __float2bfloat16_rn(norm ? sv[r] / sum : sv[r]);
-      }
-    }
-  }
-}
-
-// d logits of the router given d(routing weights) (T,k) fp32 in slot order,
-// plus an optional extra bf16 logit gradient (the load-balancing loss).
-template <int VPT>
-__global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
-                                       const long long* __restrict__ selected,
-                                       const float* __restrict__ d_weights,
-                                       const __nv_bfloat16* __restrict__ d_extra, long long T,
-                                       int E, int k, int norm,
-                                       __nv_bfloat16* __restrict__ d_logits) {
-  const int lane = threadIdx.x & 31;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
-       t < T; t += warps) {
-    float p[VPT];
-    softmax_row<VPT>(logits + t * ld, E, lane, p);
-    int si[kMaxTopK];
-    float ps[kMaxTopK];
-    float s = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      si[r] = -1;
-      ps[r] = 0.f;
-      if (r < k) {
-        const int e = static_cast<int>(selected[t * k + r]);
-        float v = 0.f;
-#pragma unroll
-        for (int j = 0; j < VPT; ++j)
-          if (lane + 32 * j == e) v = p[j];
-        si[r] = e;
-        ps[r] = warp_sum(v);
-        s += ps[r];
-      }
-    }
-    float dot = 0.f;
-    float dw[kMaxTopK];
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      dw[r] = r < k ? d_weights[t * k + r] : 0.f;
-      if (r < k) dot += dw[r] * (ps[r] / s);
-    }
-    float g[VPT];
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) g[j] = 0.f;
-#pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      if (r < k) {
-        const float dp = norm ? (dw[r] - dot) / s : dw[r];
-#pragma unroll
-        for (int j = 0; j < VPT; ++j)
-          if (lane + 32 * j == si[r]) g[j] = dp;
-      }
-    }
-    float pg = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) pg += p[j] * g[j];
-    pg = warp_sum(pg);
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int e = lane + 32 * j;
-      if (e < ld) {
-        float v = 0.f;
-        if (e < E) {
-          v = p[j] * (g[j] - pg);
-          if (d_extra) v += __bfloat162float(d_extra[t * ld + e]);
-        }
-        d_logits[t * ld + e] = __float2bfloat16_rn(v);
-      }
-    }
+    reinterpret_cast<float4*>(out)[i] = acc;
   }
 }
 
@@ -250,6 +97,7 @@ __global__ void dispatch_scan_kernel(int* __restrict__ block_base, int nblk, int
   int* pst = sh + E;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int c = 0;
+#pragma unroll 8
     for (int b = 0; b < nblk; ++b) c += block_base[e * nblk + b];
     cnt[e] = c;
   }
@@ -270,6 +118,7 @@ __global__ void dispatch_scan_kernel(int* __restrict__ block_base, int nblk, int
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int run = pst[e];
+#pragma unroll 8
     for (int b = 0; b < nblk; ++b) {
       const int c = block_base[e * nblk + b];
       block_base[e * nblk + b] = run;
@@ -485,148 +334,6 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ d_out,
     }
     dot = warp_sum(dot);
     if (lane == 0) d_weights[f] = dot;
-  }
-}
-
-// ---------------------------------------------------------------------------
-// load-balancing statistics (train.py:3141-3153), deterministic two-pass:
-//   partials[b][0:E]   hard counts (masked top-k bincount)
-//   partials[b][E:2E]  soft sums   (masked softmax sums)
-//   partials[b][2E]    entropy sum, partials[b][2E+1] valid rows
-// ---------------------------------------------------------------------------
-constexpr int kLbThreads = 256;
-constexpr int kLbTokensPerBlock = 256;
-
-template <int VPT>
-__global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
-                                   const long long* __restrict__ selected,
-                                   const unsigned char* __restrict__ valid, long long T, int E,
-                                   int k, float* __restrict__ partials) {
-  extern __shared__ float lsh[];  // [warps][2E+2]
-  constexpr int kWarps = kLbThreads / 32;
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int W = 2 * E + 2;
-  float* mine = lsh + warp * W;
-  for (int i = lane; i < W; i += 32) mine[i] = 0.f;
-  __syncwarp();
-  float soft[VPT];
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) soft[j] = 0.f;
-  float ent = 0.f;
-  float rows = 0.f;
-  const long long t0 = static_cast<long long>(blockIdx.x) * kLbTokensPerBlock;
-  const float tiny = 1.17549435e-38f;
-  for (int i = warp; i < kLbTokensPerBlock; i += kWarps) {
-    const long long t = t0 + i;
-    if (t >= T) break;
-    if (valid && !valid[t]) continue;
-    float p[VPT];
-    softmax_row<VPT>(logits + t * ld, E, lane, p);
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      if (lane + 32 * j < E) {
-        soft[j] += p[j];
-        ent -= p[j] * logf(fmaxf(p[j], tiny));
-      }
-    }
-    rows += 1.f;
-    if (lane < k) {
-      const long long e = selected[t * k + lane];
-      if (e >= 0 && e < E) atomicAdd(&mine[e], 1.f);
-    }
-    __syncwarp();
-  }
-#pragma unroll
-  for (int j = 0; j < VPT; ++j)
-    if (lane + 32 * j < E) mine[E + lane + 32 * j] = soft[j];
-  ent = warp_sum(ent);
-  if (lane == 0) {
-    mine[2 * E] = ent;
-    mine[2 * E + 1] = rows;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < W; i += blockDim.x) {
-    float acc = 0.f;
-    for (int w = 0; w < kWarps; ++w) acc += lsh[w * W + i];
-    partials[static_cast<long long>(blockIdx.x) * W + i] = acc;
-  }
-}
-
-__global__ void lb_accumulate_kernel(const float* __restrict__ partials, int nblk, int W,
-                                     float* __restrict__ packed) {
-  for (int i = threadIdx.x; i < W; i += blockDim.x) {
-    float acc = 0.f;
-    for (int b = 0; b < nblk; ++b) acc += partials[static_cast<long long>(b) * W + i];
-    packed[i] += acc;
-  }
-}
-
-// aux value, stats and the per-expert gradient coefficient from the
-// all-reduced packed sums (train.py:3163-3196).
-// stats: [min_frac, max_frac, cv, entropy, unused]
-__global__ void lb_finalize_kernel(const float* __restrict__ packed, int E, int k, int world,
-                                   float* __restrict__ aux, float* __restrict__ stats,
-                                   float* __restrict__ coef) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  const float rows = packed[2 * E + 1];
-  const float safe = fmaxf(rows, 1.f);
-  const float has = rows > 0.f ? 1.f : 0.f;
-  float dot = 0.f, mn = INFINITY, mx = -INFINITY, sum = 0.f, unused = 0.f;
-  for (int e = 0; e < E; ++e) {
-    const float a = packed[e] / safe;
-    dot += a * (packed[E + e] / safe);
-    const float fr = packed[e] / (safe * k);
-    mn = fminf(mn, fr);
-    mx = fmaxf(mx, fr);
-    sum += fr;
-    unused += packed[e] == 0.f ? 1.f : 0.f;
-    coef[e] = has * static_cast<float>(world) * static_cast<float>(E) / safe * a;
-  }
-  const float mean = sum / E;
-  float var = 0.f;
-  for (int e = 0; e < E; ++e) {
-    const float d = packed[e] / (safe * k) - mean;
-    var += d * d;
-  }
-  var /= E;
-  *aux = has * static_cast<float>(E) * dot;
-  stats[0] = mn;
-  stats[1] = mx;
-  stats[2] = sqrtf(var) / fmaxf(mean, 1e-12f);
-  stats[3] = packed[2 * E] / safe;
-  stats[4] = unused;
-}
-
-// d aux / d logits[t,e] = g * mask_t * p_e (coef_e - <p, coef>), g = *grad
-template <int VPT>
-__global__ void lb_grad_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
-                               const unsigned char* __restrict__ valid, long long T, int E,
-                               const float* __restrict__ coef, const float* __restrict__ grad,
-                               __nv_bfloat16* __restrict__ d_logits) {
-  const int lane = threadIdx.x & 31;
-  const float g = *grad;
-  float c[VPT];
-#pragma unroll
-  for (int j = 0; j < VPT; ++j) c[j] = (lane + 32 * j < E) ? coef[lane + 32 * j] : 0.f;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
-       t < T; t += warps) {
-    const bool on = valid ? valid[t] != 0 : true;
-    float p[VPT];
-    softmax_row<VPT>(logits + t * ld, E, lane, p);
-    float pc = 0.f;
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) pc += p[j] * c[j];
-    pc = warp_sum(pc);
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      const int e = lane + 32 * j;
-      if (e < ld) {
-        const float v = (on && e < E) ? g * p[j] * (c[j] - pc) : 0.f;
-        d_logits[t * ld + e] = __float2bfloat16_rn(v);
-      }
-    }
   }
 }
 

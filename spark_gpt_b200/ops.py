@@ -143,8 +143,10 @@ def router_wgrad(x, d_logits, num_experts, out=None, accumulate=False):
         out = torch.empty(num_experts, H, device=x.device, dtype=torch.float32)
         accumulate = False
     if T:
-        _launch("router_wgrad", 1, "b200moe_router_wgrad", _p(x), _p(d_logits), T, H,
-                num_experts, W, _p(out), int(accumulate), _s(x))
+        nbytes = int(_lib.value("b200moe_router_wgrad_scratch_bytes", T, H, num_experts))
+        scratch = torch.empty(max(nbytes, 16), device=x.device, dtype=torch.uint8)
+        _launch("router_wgrad", 2, "b200moe_router_wgrad", _p(x), _p(d_logits), T, H,
+                num_experts, W, _p(out), int(accumulate), _p(scratch), nbytes, _s(x))
     elif not accumulate:
         out.zero_()
     return out
