@@ -181,6 +181,48 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gate_up, const 
 int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets,
                          int E, long long rows_cap, float* dw, int accumulate, void* stream);
 
+/* ---- expert products with the row gather / combine backward fused in ----
+ * These read token-major tensors (x, d_out) row by row with TMA tile::gather4
+ * in the GEMM's load stage, so the gathered (Rcap,H) copies of the reference's
+ * _GatherTopK forward and _CombineTopK backward (train.py:2206, :2237-2239) are
+ * never written.  Padding rows read as zero. */
+
+/* gate_up fwd with xs[p] = x[row_flat[p]/k] gathered on the fly (x (T,H) bf16).
+ * Replaces _GatherTopK.forward + _swiglu_gemm (train.py:2301-2306). */
+int b200moe_expert_gate_up_fwd_gather(const void* x, const int* row_flat, long long T, int k,
+                                      const void* w_gate_up, const int* tile_expert,
+                                      const int* pad_offsets, long long rows_cap, int E, int H,
+                                      int I, void* gu, void* h, void* stream);
+
+long long b200moe_down_dgrad_combine_scratch_bytes(long long rows_cap, int I);
+
+/* Combine backward + down dgrad + SwiGLU backward.  With d_out (T,H) gathered per
+ * row and w = weights[row_flat[p]] (bf16, flat slot order): acc = d_out[t] . W_d[e];
+ * dh = bf16(w*acc); d_gu (Rcap,2I) as in b200moe_expert_down_dgrad_swiglu;
+ * hw (Rcap,I) = bf16(w*h) (the down weight-gradient operand);
+ * d_weights (T*k) fp32 = <acc, h[p]> = <d_out[t], y[p]> (the routing-weight
+ * gradient).  Replaces _CombineTopK.backward (train.py:2235-2241) +
+ * _grouped_gemm(transpose_w) (:1894) + _swiglu_tiles (:1899). */
+int b200moe_expert_down_dgrad_combine(const void* d_out, const int* row_flat, const void* weights,
+                                      long long T, int k, const void* w_down, const void* gu,
+                                      const void* h, const int* tile_expert,
+                                      const int* pad_offsets, long long rows_cap, int E, int H,
+                                      int I, void* d_gu, void* hw, float* d_weights,
+                                      void* scratch, long long scratch_bytes, void* stream);
+
+/* dw (E,M,N) fp32 (+)= a_e^T . x[tokens of expert e]: a (Rcap,M) bf16, x (T,N)
+ * bf16 gathered per row.  Replaces _swiglu_wgrad (train.py:2047) on xs. */
+int b200moe_expert_wgrad_gather_b(const void* a, int M, const void* x, int N, const int* row_flat,
+                                  long long T, int k, const int* pad_offsets, int E,
+                                  long long rows_cap, float* dw, int accumulate, void* stream);
+
+/* dw (E,M,N) fp32 (+)= src[tokens of expert e]^T . b_e: src (T,M) bf16 gathered
+ * per row, b (Rcap,N) bf16.  With src = d_out and b = hw this is the down
+ * weight gradient dy^T h of _grouped_wgrad (train.py:1863). */
+int b200moe_expert_wgrad_gather_a(const void* src, int M, const int* row_flat, long long T, int k,
+                                  const void* b, int N, const int* pad_offsets, int E,
+                                  long long rows_cap, float* dw, int accumulate, void* stream);
+
 /* ---- load-balancing loss: global_load_balancing_loss (train.py:3098-3197) */
 
 long long b200moe_lb_scratch_bytes(long long T, int E);

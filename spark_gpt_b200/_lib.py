@@ -45,6 +45,12 @@ PROTOTYPES = {
     "b200moe_expert_down_dgrad_swiglu": (I, [P, P, P, P, P, L, I, I, I, P, P]),
     "b200moe_expert_gate_up_dgrad": (I, [P, P, P, P, L, I, I, I, P, P]),
     "b200moe_expert_wgrad": (I, [P, I, P, I, P, I, L, P, I, P]),
+    "b200moe_expert_gate_up_fwd_gather": (I, [P, P, L, I, P, P, P, L, I, I, I, P, P, P]),
+    "b200moe_down_dgrad_combine_scratch_bytes": (L, [L, I]),
+    "b200moe_expert_down_dgrad_combine": (I, [P, P, P, L, I, P, P, P, P, P, L, I, I, I, P, P, P,
+                                              P, L, P]),
+    "b200moe_expert_wgrad_gather_b": (I, [P, I, P, I, P, L, I, P, I, L, P, I, P]),
+    "b200moe_expert_wgrad_gather_a": (I, [P, I, P, L, I, P, I, P, I, L, P, I, P]),
     "b200moe_lb_scratch_bytes": (L, [L, I]),
     "b200moe_lb_stats": (I, [P, L, P, P, L, I, I, P, P, L, P]),
     "b200moe_lb_finalize": (I, [P, I, I, I, P, P, P, P]),

@@ -88,16 +88,23 @@ int make_tmap(CUtensorMap* m, const void* base, long long inner, long long outer
   return B200MOE_OK;
 }
 
+// Tensor map for row gathers (tile::gather4) from a token-major (rows, cols)
+// bf16 matrix: box of one row by 64 columns.
+int make_gather_tmap(CUtensorMap* m, const void* base, long long cols, long long rows,
+                     const char* what) {
+  return make_tmap(m, base, cols, rows, cols, 64, 1, what);
+}
+
 template <int BN>
 constexpr int stages_for() {
   return BN == 256 ? 4 : (BN == 128 ? 6 : 8);
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int GATHER = kGatherNone>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                 cudaStream_t st, const char* what) {
   constexpr int STAGES = stages_for<BN>();
-  auto kern = grouped_gemm_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
+  auto kern = grouped_gemm_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES, GATHER>;
   const int smem = static_cast<int>(GemmSmem<BN, STAGES>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -645,6 +652,179 @@ int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* 
   if (BN == 256) return launch_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   if (BN == 128) return launch_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   return launch_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+}
+
+// ---------------------------------------------------------------- gathered-operand GEMMs
+int b200moe_expert_gate_up_fwd_gather(const void* x, const int* row_flat, long long T, int k,
+                                      const void* w_gu, const int* tile_expert,
+                                      const int* pad_offsets, long long rows_cap, int E, int H,
+                                      int I, void* gu, void* h, void* stream) {
+  REQUIRE(x && row_flat && w_gu && tile_expert && pad_offsets && gu && h,
+          "gate_up_fwd_gather: null pointer");
+  int rc = check_expert_shape("gate_up_fwd_gather", rows_cap, E, H, I);
+  if (rc) return rc;
+  REQUIRE(T > 0 && T < 0x7fffffffLL && k >= 1, "gate_up_fwd_gather: bad T/k");
+  const int half = (I % 128 == 0) ? 128 : 64;
+  CUtensorMap ta, tb;
+  if ((rc = make_gather_tmap(&ta, x, H, T, "gate_up_fwd_gather x"))) return rc;
+  if ((rc = make_tmap(&tb, w_gu, H, static_cast<long long>(E) * 2 * I, H, 64, half,
+                      "gate_up_fwd_gather w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = I / half;
+  p.k_blocks = H / 64;
+  p.b_group_rows = 2 * I;
+  p.b_half_offset = I;
+  p.m_valid = rows_cap;
+  p.n_valid = I;
+  p.out = gu;
+  p.ld_out = 2 * I;
+  p.out2 = h;
+  p.ld_out2 = I;
+  p.inter = I;
+  p.gather_rows = row_flat;
+  p.gather_k = k;
+  p.gather_oob = static_cast<int>(T);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (half == 128)
+    return launch_gemm<256, false, false, kEpiSwigluFwd, kRowsRagged, kGatherA>(ta, tb, p, st,
+                                                                              "gate_up_fwd_gather");
+  return launch_gemm<128, false, false, kEpiSwigluFwd, kRowsRagged, kGatherA>(ta, tb, p, st,
+                                                                            "gate_up_fwd_gather");
+}
+
+static int down_dgrad_bn(int I) { return (I % 256 == 0) ? 256 : (I % 128 == 0 ? 128 : 64); }
+
+long long b200moe_down_dgrad_combine_scratch_bytes(long long rows_cap, int I) {
+  if (I <= 0 || I % 64) return 0;
+  return 2LL * (I / down_dgrad_bn(I)) * rows_cap * static_cast<long long>(sizeof(float));
+}
+
+int b200moe_expert_down_dgrad_combine(const void* d_out, const int* row_flat, const void* weights,
+                                      long long T, int k, const void* w_d, const void* gu,
+                                      const void* h, const int* tile_expert,
+                                      const int* pad_offsets, long long rows_cap, int E, int H,
+                                      int I, void* d_gu, void* hw, float* d_weights,
+                                      void* scratch, long long scratch_bytes, void* stream) {
+  REQUIRE(d_out && row_flat && weights && w_d && gu && h && tile_expert && pad_offsets && d_gu &&
+              hw && d_weights && scratch,
+          "down_dgrad_combine: null pointer");
+  int rc = check_expert_shape("down_dgrad_combine", rows_cap, E, H, I);
+  if (rc) return rc;
+  REQUIRE(T > 0 && T < 0x7fffffffLL && k >= 1, "down_dgrad_combine: bad T/k");
+  REQUIRE(scratch_bytes >= b200moe_down_dgrad_combine_scratch_bytes(rows_cap, I),
+          "down_dgrad_combine: scratch too small");
+  const int BN = down_dgrad_bn(I);
+  CUtensorMap ta, tb;
+  if ((rc = make_gather_tmap(&ta, d_out, H, T, "down_dgrad_combine d_out"))) return rc;
+  if ((rc = make_tmap(&tb, w_d, I, static_cast<long long>(E) * H, I, 64, 64,
+                      "down_dgrad_combine w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = I / BN;
+  p.k_blocks = H / 64;
+  p.b_group_rows = H;
+  p.m_valid = rows_cap;
+  p.n_valid = I;
+  p.out = d_gu;
+  p.ld_out = 2 * I;
+  p.out2 = hw;
+  p.ld_out2 = I;
+  p.aux = gu;
+  p.ld_aux = 2 * I;
+  p.aux2 = h;
+  p.ld_aux2 = I;
+  p.inter = I;
+  p.gather_rows = row_flat;
+  p.gather_k = k;
+  p.gather_oob = static_cast<int>(T);
+  p.route_w = static_cast<const __nv_bfloat16*>(weights);
+  p.dw_part = static_cast<float*>(scratch);
+  p.part_stride = rows_cap;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256)
+    rc = launch_gemm<256, false, true, kEpiSwigluBwdCombine, kRowsRagged, kGatherA>(ta, tb, p, st, "down_dgrad_combine");
+  else if (BN == 128)
+    rc = launch_gemm<128, false, true, kEpiSwigluBwdCombine, kRowsRagged, kGatherA>(ta, tb, p, st, "down_dgrad_combine");
+  else
+    rc = launch_gemm<64, false, true, kEpiSwigluBwdCombine, kRowsRagged, kGatherA>(ta, tb, p, st, "down_dgrad_combine");
+  if (rc) return rc;
+  combine_weight_grad_kernel<<<grid_for(rows_cap, 256), 256, 0, st>>>(
+      static_cast<const float*>(scratch), 2 * (I / BN), rows_cap, row_flat, pad_offsets + E,
+      d_weights);
+  return check_launch("combine_weight_grad");
+}
+
+static int wgrad_bn(int N) { return (N % 256 == 0) ? 256 : (N % 128 == 0 ? 128 : 64); }
+
+int b200moe_expert_wgrad_gather_b(const void* a, int M, const void* x, int N, const int* row_flat,
+                                  long long T, int k, const int* pad_offsets, int E,
+                                  long long rows_cap, float* dw, int accumulate, void* stream) {
+  REQUIRE(a && x && row_flat && pad_offsets && dw, "wgrad_gather_b: null pointer");
+  REQUIRE(M > 0 && M % 128 == 0, "wgrad_gather_b: M must be a multiple of 128");
+  REQUIRE(N > 0 && N % 64 == 0, "wgrad_gather_b: N must be a multiple of 64");
+  REQUIRE(E >= 1 && rows_cap > 0 && rows_cap % 128 == 0, "wgrad_gather_b: bad rows/E");
+  REQUIRE(T > 0 && T < 0x7fffffffLL && k >= 1, "wgrad_gather_b: bad T/k");
+  const int BN = wgrad_bn(N);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_tmap(&ta, a, M, rows_cap, M, 64, 64, "wgrad_gather_b a"))) return rc;
+  if ((rc = make_gather_tmap(&tb, x, N, T, "wgrad_gather_b x"))) return rc;
+  GemmParams p = blank_params();
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.m_tiles = M / 128;
+  p.n_tiles = N / BN;
+  p.n_valid = N;
+  p.out = dw;
+  p.ld_out = N;
+  p.accumulate = accumulate;
+  p.out_group_stride = static_cast<long long>(M) * N;
+  p.gather_rows = row_flat;
+  p.gather_k = k;
+  p.gather_oob = static_cast<int>(T);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, true, true, kEpiStoreF32, kKRagged, kGatherB>(ta, tb, p, st, "wgrad_gather_b");
+  if (BN == 128) return launch_gemm<128, true, true, kEpiStoreF32, kKRagged, kGatherB>(ta, tb, p, st, "wgrad_gather_b");
+  return launch_gemm<64, true, true, kEpiStoreF32, kKRagged, kGatherB>(ta, tb, p, st, "wgrad_gather_b");
+}
+
+int b200moe_expert_wgrad_gather_a(const void* src, int M, const int* row_flat, long long T, int k,
+                                  const void* b, int N, const int* pad_offsets, int E,
+                                  long long rows_cap, float* dw, int accumulate, void* stream) {
+  REQUIRE(src && row_flat && b && pad_offsets && dw, "wgrad_gather_a: null pointer");
+  REQUIRE(M > 0 && M % 128 == 0, "wgrad_gather_a: M must be a multiple of 128");
+  REQUIRE(N > 0 && N % 64 == 0, "wgrad_gather_a: N must be a multiple of 64");
+  REQUIRE(E >= 1 && rows_cap > 0 && rows_cap % 128 == 0, "wgrad_gather_a: bad rows/E");
+  REQUIRE(T > 0 && T < 0x7fffffffLL && k >= 1, "wgrad_gather_a: bad T/k");
+  const int BN = wgrad_bn(N);
+  CUtensorMap ta, tb;
+  int rc;
+  if ((rc = make_gather_tmap(&ta, src, M, T, "wgrad_gather_a src"))) return rc;
+  if ((rc = make_tmap(&tb, b, N, rows_cap, N, 64, 64, "wgrad_gather_a b"))) return rc;
+  GemmParams p = blank_params();
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.m_tiles = M / 128;
+  p.n_tiles = N / BN;
+  p.n_valid = N;
+  p.out = dw;
+  p.ld_out = N;
+  p.accumulate = accumulate;
+  p.out_group_stride = static_cast<long long>(M) * N;
+  p.gather_rows = row_flat;
+  p.gather_k = k;
+  p.gather_oob = static_cast<int>(T);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256) return launch_gemm<256, true, true, kEpiStoreF32, kKRagged, kGatherA>(ta, tb, p, st, "wgrad_gather_a");
+  if (BN == 128) return launch_gemm<128, true, true, kEpiStoreF32, kKRagged, kGatherA>(ta, tb, p, st, "wgrad_gather_a");
+  return launch_gemm<64, true, true, kEpiStoreF32, kKRagged, kGatherA>(ta, tb, p, st, "wgrad_gather_a");
 }
 
 // ---------------------------------------------------------------- load balancing

@@ -135,6 +135,19 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// Four rows (y0..y3) of 64 columns starting at column c0, one 128-byte row
+// each, written to dst as consecutive 128-byte rows (the tensor map's box is
+// {64, 1}).  Rows outside the tensor read as zero.
+__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* tm, uint64_t* bar, int c0,
+                                            int y0, int y1, int y2, int y3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(smem_u32(bar)), "r"(c0), "r"(y0), "r"(y1), "r"(y2),
+      "r"(y3)
+      : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // tcgen05: TMEM allocation, MMA issue, commit, TMEM -> register loads
 // ---------------------------------------------------------------------------

@@ -42,6 +42,16 @@ enum Epilogue : int {
   kEpiSwigluBwd = 2,
   kEpiStoreF32 = 3,
   kEpiStoreF32T = 4,
+  kEpiSwigluBwdCombine = 5,  // down dgrad from gathered d_out: combine backward fused in
+};
+
+// Which operand is gathered row by row from a token-major tensor (x or d_out)
+// with TMA tile::gather4 instead of being read from a materialised
+// routed-row buffer.
+enum Gather : int {
+  kGatherNone = 0,
+  kGatherA = 1,
+  kGatherB = 2,
 };
 
 enum Schedule : int {
@@ -70,7 +80,24 @@ struct GemmParams {
   int accumulate;     // fp32 outputs: add into the existing values
   long long out_group_stride;
   int k_split_blocks; // kKRagged single group split over K: 64-row blocks per split (0: none)
+  // gathered operand: padded row p reads token row_flat[p] / gather_k of the
+  // token-major tensor; padding rows (row_flat < 0) read token gather_oob
+  // (one past the end: zero fill)
+  const int* gather_rows;
+  int gather_k;
+  int gather_oob;
+  // kEpiSwigluBwdCombine
+  const void* aux2;            // h (Rcap, I)
+  long long ld_aux2;
+  const __nv_bfloat16* route_w;  // routing weights, flat slot order (T*k)
+  float* dw_part;              // per-(N tile, half) partial d_weights, [parts][Rcap]
+  long long part_stride;
 };
+
+__device__ __forceinline__ int gather_token(const GemmParams& p, int row) {
+  const int f = __ldg(p.gather_rows + row);
+  return f >= 0 ? f / p.gather_k : p.gather_oob;
+}
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
@@ -158,12 +185,13 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
 constexpr int kEpilogueWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES>
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES, int GATHER = kGatherNone>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN");
   static_assert(SCHED == kRowsRagged ? !A_MN : (A_MN && B_MN), "operand majors vs schedule");
+  static_assert(GATHER != kGatherB || (SCHED == kKRagged && B_MN), "B gathers only in wgrads");
   constexpr int BM = 128;
   constexpr int BK = 64;
   using S = GemmSmem<BN, STAGES>;
@@ -221,46 +249,111 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      int stage = 0;
-      uint32_t phase = 0;
-      bool ok = true;
-      for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
-        const TileInfo T = decode_tile<SCHED>(p, t);
-        for (int kb = 0; kb < T.kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
-            ok = false;
-            break;
-          }
-          mbar_expect_tx(&full[stage], S::kStageBytes);
-          uint8_t* a = sA + stage * S::kABytes;
-          uint8_t* b = sB + stage * S::kBBytes;
-          if (!A_MN) {
-            tma_load_2d(a, &tmA, &full[stage], kb * BK, T.m * BM);
-          } else {
-            const int krow = T.krow0 + kb * BK;
-            tma_load_2d(a, &tmA, &full[stage], T.m * BM, krow);
-            tma_load_2d(a + 8192, &tmA, &full[stage], T.m * BM + 64, krow);
-          }
-          if (!B_MN) {
-            if (EPI == kEpiSwigluFwd) {
-              const int row = T.g * p.b_group_rows + T.n * (BN / 2);
-              tma_load_2d(b, &tmB, &full[stage], kb * BK, row);
-              tma_load_2d(b + S::kBBytes / 2, &tmB, &full[stage], kb * BK, row + p.b_half_offset);
-            } else {
-              tma_load_2d(b, &tmB, &full[stage], kb * BK, T.g * p.b_group_rows + T.n * BN);
+    // Lane 0 waits for a free stage, arms the barrier and issues the plain
+    // tile loads; with a gathered operand every lane then issues gather4 loads
+    // of 4 rows each.
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    // Gathered rows are looked up ahead of use so the index loads never sit on
+    // the producer's critical path: the next tile's 4 rows per lane (row-ragged
+    // A), or the rows of K blocks kb+1..kb+4 (K-ragged gathers), in registers.
+    int4 tok_next = make_int4(0, 0, 0, 0);
+    if (GATHER == kGatherA && SCHED == kRowsRagged && blockIdx.x < num_tiles) {
+      const int r = (blockIdx.x / p.n_tiles) * BM + 4 * lane;
+      tok_next = make_int4(gather_token(p, r), gather_token(p, r + 1), gather_token(p, r + 2),
+                           gather_token(p, r + 3));
+    }
+    for (int t = blockIdx.x; ok && t < num_tiles; t += gridDim.x) {
+      const TileInfo T = decode_tile<SCHED>(p, t);
+      const int4 tok = tok_next;
+      if (GATHER == kGatherA && SCHED == kRowsRagged && t + gridDim.x < num_tiles) {
+        const int r = ((t + gridDim.x) / p.n_tiles) * BM + 4 * lane;
+        tok_next = make_int4(gather_token(p, r), gather_token(p, r + 1), gather_token(p, r + 2),
+                             gather_token(p, r + 3));
+      }
+      // K-ragged gathers: rows 4*(lane%16).. of K block kb live in q0 (kb), q1 (kb+1), ...
+      int4 q0 = make_int4(0, 0, 0, 0), q1 = q0, q2 = q0, q3 = q0;
+      auto k_rows = [&](int kb) -> int4 {
+        if (kb >= T.kblocks) return make_int4(0, 0, 0, 0);
+        const int r = T.krow0 + kb * BK + 4 * (lane & 15);
+        return make_int4(gather_token(p, r), gather_token(p, r + 1), gather_token(p, r + 2),
+                         gather_token(p, r + 3));
+      };
+      if (GATHER != kGatherNone && SCHED == kKRagged) {
+        q0 = k_rows(0);
+        q1 = k_rows(1);
+        q2 = k_rows(2);
+        q3 = k_rows(3);
+      }
+      for (int kb = 0; kb < T.kblocks; ++kb) {
+        int good = 1;
+        uint8_t* a = sA + stage * S::kABytes;
+        uint8_t* b = sB + stage * S::kBBytes;
+        int4 cur = q0;
+        if (GATHER != kGatherNone && SCHED == kKRagged) {
+          q0 = q1;
+          q1 = q2;
+          q2 = q3;
+          q3 = k_rows(kb + 4);
+        }
+        if (lane == 0) {
+          good = mbar_wait(&empty[stage], phase ^ 1u, abort_flag) ? 1 : 0;
+          if (good) {
+            mbar_expect_tx(&full[stage], S::kStageBytes);
+            if (GATHER != kGatherA) {
+              if (!A_MN) {
+                tma_load_2d(a, &tmA, &full[stage], kb * BK, T.m * BM);
+              } else {
+                const int krow = T.krow0 + kb * BK;
+                tma_load_2d(a, &tmA, &full[stage], T.m * BM, krow);
+                tma_load_2d(a + 8192, &tmA, &full[stage], T.m * BM + 64, krow);
+              }
             }
-          } else {
-            const int krow =
-                (SCHED == kKRagged) ? (T.krow0 + kb * BK) : (T.g * p.b_group_rows + kb * BK);
+            if (GATHER != kGatherB) {
+              if (!B_MN) {
+                if (EPI == kEpiSwigluFwd) {
+                  const int row = T.g * p.b_group_rows + T.n * (BN / 2);
+                  tma_load_2d(b, &tmB, &full[stage], kb * BK, row);
+                  tma_load_2d(b + S::kBBytes / 2, &tmB, &full[stage], kb * BK,
+                              row + p.b_half_offset);
+                } else {
+                  tma_load_2d(b, &tmB, &full[stage], kb * BK, T.g * p.b_group_rows + T.n * BN);
+                }
+              } else {
+                const int krow =
+                    (SCHED == kKRagged) ? (T.krow0 + kb * BK) : (T.g * p.b_group_rows + kb * BK);
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_2d(b + j * 8192, &tmB, &full[stage], T.n * BN + 64 * j, krow);
+                for (int j = 0; j < BN / 64; ++j)
+                  tma_load_2d(b + j * 8192, &tmB, &full[stage], T.n * BN + 64 * j, krow);
+              }
+            }
           }
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) {
+          ok = false;
+          break;
+        }
+        if (GATHER == kGatherA) {
+          if (SCHED == kRowsRagged) {
+            tma_gather4(a + lane * 512, &tmA, &full[stage], kb * BK, tok.x, tok.y, tok.z, tok.w);
+          } else {
+            // MN-major A: 2 chunks of [64 k rows][64 m]; lane l: rows 4(l%16).., chunk l/16
+            const int c = lane >> 4;
+            tma_gather4(a + c * 8192 + (lane & 15) * 512, &tmA, &full[stage], T.m * BM + 64 * c,
+                        cur.x, cur.y, cur.z, cur.w);
           }
+        }
+        if (GATHER == kGatherB) {
+          // MN-major B: BN/64 chunks of [64 k rows][64 n]
+          for (int j = lane >> 4; j < BN / 64; j += 2)
+            tma_gather4(b + j * 8192 + (lane & 15) * 512, &tmB, &full[stage], T.n * BN + 64 * j,
+                        cur.x, cur.y, cur.z, cur.w);
+        }
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
         }
       }
     }
@@ -415,6 +508,43 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             store_bf16x32(dgu + p.inter + col, du);
           }
         }
+      } else if (EPI == kEpiSwigluBwdCombine) {
+        // acc = d_out[token] . W_d[e] (unscaled).  dh = bf16(w * acc); the routing
+        // weight's gradient <d_out[token], y[row]> = <acc, h[row]> is summed here;
+        // w * h is written for the down-projection weight gradient.
+        const long long row = static_cast<long long>(T.m) * BM + row_in;
+        const int f = __ldg(p.gather_rows + row);
+        const float w = f >= 0 ? __bfloat162float(p.route_w[f]) : 0.f;
+        const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
+        const __nv_bfloat16* hh = static_cast<const __nv_bfloat16*>(p.aux2) + row * p.ld_aux2;
+        __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+        __nv_bfloat16* hw = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
+        float dwp = 0.f;
+#pragma unroll 1
+        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+          uint32_t r[32];
+          tmem_ld32(taddr + c * 32, r);
+          tmem_wait_ld();
+          const int col = T.n * BN + c * 32;
+          float g[32], u[32], hv[32], dg[32], du[32];
+          load_bf16x32(gu + col, g);
+          load_bf16x32(gu + p.inter + col, u);
+          load_bf16x32(hh + col, hv);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float a = __uint_as_float(r[j]);
+            dwp += a * hv[j];
+            const float dh = bf16_round(w * a);
+            const float sig = sigmoidf_(g[j]);
+            dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+            du[j] = dh * g[j] * sig;
+            hv[j] *= w;
+          }
+          store_bf16x32(dgu + col, dg);
+          store_bf16x32(dgu + p.inter + col, du);
+          store_bf16x32(hw + col, hv);
+        }
+        p.dw_part[(T.n * 2 + half) * p.part_stride + row] = dwp;
       } else if (EPI == kEpiStoreF32) {
         float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
                    static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;

@@ -337,4 +337,22 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ d_out,
   }
 }
 
+// d_weights[row_flat[p]] = sum over parts of dw_part[part][p] (fixed order);
+// the parts are the per-(N tile, column half) partial sums of the fused
+// down-dgrad epilogue.
+__global__ void combine_weight_grad_kernel(const float* __restrict__ dw_part, int parts,
+                                           long long stride, const int* __restrict__ row_flat,
+                                           const int* __restrict__ total_rows,
+                                           float* __restrict__ d_weights) {
+  const long long total = *total_rows;
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; r < total;
+       r += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int f = row_flat[r];
+    if (f < 0) continue;
+    float acc = 0.f;
+    for (int q = 0; q < parts; ++q) acc += dw_part[q * stride + r];
+    d_weights[f] = acc;
+  }
+}
+
 }  // namespace b200moe

@@ -58,9 +58,12 @@ def _extra_logit_grad(d_logits, T, W):
 class _SparseMoEFn(torch.autograd.Function):
     """Router + experts + combine as one autograd node (train.py:2331-2334).
 
-    Forward: router GEMM -> softmax/top-k -> dispatch -> gather -> gate_up
+    Forward: router GEMM -> softmax/top-k -> dispatch -> row gather -> gate_up
     GEMM (+SwiGLU) -> down GEMM -> weighted combine.  Backward mirrors it and
-    folds the router's input gradient into the gather backward."""
+    folds the router's input gradient into the gather backward.  (The
+    tile::gather4 variants in ops.py read x / d_out rows inside the GEMMs
+    instead of materialising xs / dy; on B200 their per-row TMA requests ran
+    slower than the streaming gather kernels, so this path materialises.)"""
 
     @staticmethod
     def forward(ctx, x, w_router, w_gate_up, w_down, top_k, norm):

@@ -282,6 +282,64 @@ def wgrad(a, b, d: Dispatch, name="wgrad", out=None, accumulate=False):
 
 
 # --------------------------------------------------------------------------- #
+# expert products with the row gather / combine backward fused in
+# --------------------------------------------------------------------------- #
+def gate_up_fwd_gather(x, w_gu, d: Dispatch):
+    """gate_up fwd reading xs[p] = x[row_flat[p]/k] in the GEMM's loads."""
+    _check(x, BF16, "gate_up_fwd_gather x")
+    E, two_i, H = w_gu.shape
+    I = two_i // 2
+    gu = torch.empty(d.rows_cap, two_i, device=x.device, dtype=BF16)
+    h = torch.empty(d.rows_cap, I, device=x.device, dtype=BF16)
+    _launch("gate_up_fwd", 1, "b200moe_expert_gate_up_fwd_gather", _p(x), _p(d.row_flat),
+            d.num_tokens, d.top_k, _p(w_gu), _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap,
+            E, H, I, _p(gu), _p(h), _s(x))
+    return gu, h
+
+
+def down_dgrad_combine(d_out, weights, w_d, gu, h, d: Dispatch):
+    """Combine backward + down dgrad + SwiGLU backward -> (d_gu, w*h, d_weights (T,k))."""
+    _check(d_out, BF16, "down_dgrad_combine d_out")
+    _check(weights, BF16, "down_dgrad_combine weights")
+    E, H, I = w_d.shape
+    dev = d_out.device
+    d_gu = torch.empty(d.rows_cap, 2 * I, device=dev, dtype=BF16)
+    hw = torch.empty(d.rows_cap, I, device=dev, dtype=BF16)
+    d_w = torch.empty(d.num_tokens, d.top_k, device=dev, dtype=torch.float32)
+    nbytes = int(_lib.value("b200moe_down_dgrad_combine_scratch_bytes", d.rows_cap, I))
+    scratch = torch.empty(nbytes, device=dev, dtype=torch.uint8)
+    _launch("down_dgrad", 2, "b200moe_expert_down_dgrad_combine", _p(d_out), _p(d.row_flat),
+            _p(weights), d.num_tokens, d.top_k, _p(w_d), _p(gu), _p(h), _p(d.tile_expert),
+            _p(d.pad_offsets), d.rows_cap, E, H, I, _p(d_gu), _p(hw), _p(d_w), _p(scratch),
+            nbytes, _s(d_out))
+    return d_gu, hw, d_w
+
+
+def wgrad_gather_b(a, x, d: Dispatch, name="wgrad", out=None, accumulate=False):
+    """(E, M, N) fp32: a_e^T x[tokens of expert e]."""
+    M, N = a.shape[1], x.shape[1]
+    if out is None:
+        out = torch.empty(d.num_experts, M, N, device=a.device, dtype=torch.float32)
+        accumulate = False
+    _launch(name, 1, "b200moe_expert_wgrad_gather_b", _p(a), M, _p(x), N, _p(d.row_flat),
+            d.num_tokens, d.top_k, _p(d.pad_offsets), d.num_experts, d.rows_cap, _p(out),
+            int(accumulate), _s(a))
+    return out
+
+
+def wgrad_gather_a(src, b, d: Dispatch, name="wgrad", out=None, accumulate=False):
+    """(E, M, N) fp32: src[tokens of expert e]^T b_e."""
+    M, N = src.shape[1], b.shape[1]
+    if out is None:
+        out = torch.empty(d.num_experts, M, N, device=b.device, dtype=torch.float32)
+        accumulate = False
+    _launch(name, 1, "b200moe_expert_wgrad_gather_a", _p(src), M, _p(d.row_flat), d.num_tokens,
+            d.top_k, _p(b), N, _p(d.pad_offsets), d.num_experts, d.rows_cap, _p(out),
+            int(accumulate), _s(b))
+    return out
+
+
+# --------------------------------------------------------------------------- #
 # load-balancing loss (train.py:3098-3197)
 # --------------------------------------------------------------------------- #
 def lb_stats(logits, selected, valid_u8, num_experts, top_k, packed):

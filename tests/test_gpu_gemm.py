@@ -155,3 +155,61 @@ def test_router_gemms(ops, T, H, E):
     dw = ops.router_wgrad(x, dl, E)
     ref = dl[:, :E].float().t() @ x.float()
     torch.testing.assert_close(dw, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
+
+
+# --------------------------------------------------------------------------- #
+# gathered-operand variants: identical operands to the materialised path, so
+# results must match it bit for bit
+# --------------------------------------------------------------------------- #
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_gate_up_forward_gather_equals_materialised(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 6)
+    n = int(d.pad_offsets[-1])
+    gu0, h0 = ops.gate_up_fwd(xs, wgu, d)
+    gu1, h1 = ops.gate_up_fwd_gather(x, wgu, d)
+    assert torch.equal(gu0[:n], gu1[:n])
+    assert torch.equal(h0[:n], h1[:n])
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_wgrad_gathers_equal_materialised(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 7)
+    n = int(d.pad_offsets[-1])
+    rows = d.row_flat.clone()
+    rows[n:] = -1
+    d_gu = torch.randn(d.rows_cap, 2 * I, device=DEV).to(torch.bfloat16)
+    d_gu[rows < 0] = 0
+    assert torch.equal(ops.wgrad(d_gu, xs, d), ops.wgrad_gather_b(d_gu, x, d))
+    d_out = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    douts = ops.gather_rows(d_out, d)
+    hw = torch.randn(d.rows_cap, I, device=DEV).to(torch.bfloat16)
+    hw[rows < 0] = 0
+    assert torch.equal(ops.wgrad(douts, hw, d), ops.wgrad_gather_a(d_out, hw, d))
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_down_dgrad_with_combine_backward(ops, T, k, E, H, I):
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 8)
+    n = int(d.pad_offsets[-1])
+    gu, h = ops.gate_up_fwd(xs, wgu, d)
+    w = torch.rand(T, k, device=DEV).to(torch.bfloat16)
+    d_out = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    d_gu, hw, d_w = ops.down_dgrad_combine(d_out, w, wd, gu, h, d)
+    rows = d.row_flat[:n].long()
+    valid = rows >= 0
+    tok = torch.where(valid, rows // k, torch.zeros_like(rows))
+    wr = torch.where(valid, w.view(-1)[rows.clamp_min(0)].float(), torch.zeros_like(rows, dtype=torch.float32))
+    acc = torch.zeros(n, I, device=DEV)
+    for e, s, t in _segments(d):
+        if t > s:
+            acc[s:t] = d_out[tok[s:t]].float() @ wd[e].float()
+    acc[~valid] = 0
+    dh = bf16_round(wr[:, None] * acc)
+    g, u = gu[:n, :I].float(), gu[:n, I:].float()
+    sig = torch.sigmoid(g)
+    ref = torch.cat([dh * u * (sig * (1 + g * (1 - sig))), dh * g * sig], 1)
+    assert_bf16_close(d_gu[:n], ref, "d_gu", max_rel=2e-2, mean_rel=1e-3)
+    assert torch.equal(hw[:n], (wr[:, None] * h[:n].float()).to(torch.bfloat16))
+    ref_dw = (acc * h[:n].float()).sum(1)
+    got = d_w.view(-1)[rows[valid]]
+    torch.testing.assert_close(got, ref_dw[valid], rtol=1e-3, atol=1e-3 * ref_dw.abs().max().item())
