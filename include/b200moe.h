@@ -130,21 +130,26 @@ int b200moe_dispatch_noalloc(const long long* selected, long long T, int k, int 
 int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offsets, int E,
                         int k, int H, long long rows_cap, void* xs, void* stream);
 
-/* dx (T,H) bf16 = sum_s dxs[inv_pad[t*k+s]] (+ addend (T,H) bf16 if given). */
+/* dx (T,H) bf16 = sum_s dxs[inv_pad[t*k+s]] (+ addend (T,H) bf16 if given).
+ * With inv_pad == NULL, dxs is token-major: slot t*k+s in row t*k+s. */
 int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
                             int k, int H, void* dx, void* stream);
 
 /* ---- combine: _CombineTopK (train.py:2220-2241) -------------------------- */
 
-/* out (T,H) bf16 = sum_s bf16(y[inv_pad[t*k+s]] * weights[t,s]). */
+/* out (T,H) bf16 = sum_s bf16(y[inv_pad[t*k+s]] * weights[t,s]).  With
+ * inv_pad == NULL, y is token-major: slot t*k+s in row t*k+s. */
 int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T,
                         int k, int H, void* out, void* stream);
 
 /* dy (Rcap,H) bf16 = bf16(d_out[t] * w), zero for padding rows;
- * d_weights (T*k) fp32 = <d_out[t], y[p]> in flat-slot order. */
+ * d_weights (T*k) fp32 = <d_out[t], y[row of slot]> in flat-slot order.
+ * y is in padded-row order (y_token_major = 0: row p holds slot row_flat[p])
+ * or token-major (1: row t*k+s holds slot t*k+s; inv_pad required). */
 int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat,
-                        const int* pad_offsets, const void* weights, int E, int k, int H,
-                        long long rows_cap, void* dy, float* d_weights, void* stream);
+                        const int* inv_pad, const int* pad_offsets, const void* weights, int E,
+                        long long T, int k, int H, long long rows_cap, int y_token_major,
+                        void* dy, float* d_weights, void* stream);
 
 /* ---- expert products: _FusedSwiGLU / _GroupedLinear (train.py:1625-2090) - */
 
@@ -155,11 +160,13 @@ int b200moe_expert_gate_up_fwd(const void* xs, const void* w_gate_up, const int*
                                const int* pad_offsets, long long rows_cap, int E, int H, int I,
                                void* gu, void* h, void* stream);
 
-/* y (Rcap,H) bf16 = h . W_d[e]^T per expert; w_down (E,H,I) bf16.
+/* y = h . W_d[e]^T per expert; w_down (E,H,I) bf16.  row_flat_out NULL: y is
+ * (Rcap,H) in padded-row order; else padded row p is written to row
+ * row_flat_out[p] of a token-major (T*k,H) y and padding rows are skipped.
  * Replaces _grouped_gemm (train.py:1803) in _GroupedLinear.forward. */
 int b200moe_expert_down_fwd(const void* h, const void* w_down, const int* tile_expert,
-                            const int* pad_offsets, long long rows_cap, int E, int H, int I,
-                            void* y, void* stream);
+                            const int* pad_offsets, const int* row_flat_out, long long rows_cap,
+                            int E, int H, int I, void* y, void* stream);
 
 /* dh = dy . W_d[e] (rounded to bf16), then the SwiGLU backward in the
  * epilogue: d_gu (Rcap,2I) bf16 = [dh*u*s*(1+g*(1-s)), dh*g*s], s = sigmoid(g).
@@ -169,11 +176,13 @@ int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_down, const v
                                      long long rows_cap, int E, int H, int I, void* d_gu,
                                      void* stream);
 
-/* dxs (Rcap,H) bf16 = d_gu . W_gu[e] per expert.  Replaces _swiglu_dgrad
- * (train.py:2029). */
+/* dxs = d_gu . W_gu[e] per expert, (Rcap,H) padded order, or token-major
+ * (T*k,H) when row_flat_out is given (as b200moe_expert_down_fwd).  Replaces
+ * _swiglu_dgrad (train.py:2029). */
 int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gate_up, const int* tile_expert,
-                                 const int* pad_offsets, long long rows_cap, int E, int H, int I,
-                                 void* dxs, void* stream);
+                                 const int* pad_offsets, const int* row_flat_out,
+                                 long long rows_cap, int E, int H, int I, void* dxs,
+                                 void* stream);
 
 /* dw (E,M,N) fp32 (+)= a_e^T . b_e over the padded rows of expert e;
  * a (Rcap,M) bf16, b (Rcap,N) bf16, M % 128 == 0, N % 64 == 0.  Replaces

@@ -39,11 +39,11 @@ PROTOTYPES = {
     "b200moe_gather_rows": (I, [P, P, P, I, I, I, L, P, P]),
     "b200moe_gather_rows_bwd": (I, [P, P, P, L, I, I, P, P]),
     "b200moe_combine_fwd": (I, [P, P, P, L, I, I, P, P]),
-    "b200moe_combine_bwd": (I, [P, P, P, P, P, I, I, I, L, P, P, P]),
+    "b200moe_combine_bwd": (I, [P, P, P, P, P, P, I, L, I, I, L, I, P, P, P]),
     "b200moe_expert_gate_up_fwd": (I, [P, P, P, P, L, I, I, I, P, P, P]),
-    "b200moe_expert_down_fwd": (I, [P, P, P, P, L, I, I, I, P, P]),
+    "b200moe_expert_down_fwd": (I, [P, P, P, P, P, L, I, I, I, P, P]),
     "b200moe_expert_down_dgrad_swiglu": (I, [P, P, P, P, P, L, I, I, I, P, P]),
-    "b200moe_expert_gate_up_dgrad": (I, [P, P, P, P, L, I, I, I, P, P]),
+    "b200moe_expert_gate_up_dgrad": (I, [P, P, P, P, P, L, I, I, I, P, P]),
     "b200moe_expert_wgrad": (I, [P, I, P, I, P, I, L, P, I, P]),
     "b200moe_expert_gate_up_fwd_gather": (I, [P, P, L, I, P, P, P, L, I, I, I, P, P, P]),
     "b200moe_down_dgrad_combine_scratch_bytes": (L, [L, I]),

@@ -2,6 +2,7 @@
 // argument checks, TMA tensor-map construction, launch shapes.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -141,6 +142,31 @@ int lanes_for(long long width) {
     case 16: { constexpr int L = 16; __VA_ARGS__ } break; \
     default: { constexpr int L = 32; __VA_ARGS__ } break; \
   }
+
+// Launch the shared-memory row reduction (combine forward / gather backward).
+// Returns -1 when one token's k rows do not fit a ring slot (caller falls back).
+constexpr int kReduceSmemPerBlock = 72 * 1024;  // three blocks per SM
+
+int launch_row_reduce(const __nv_bfloat16* rows, const int* inv_pad,
+                      const __nv_bfloat16* weights, const __nv_bfloat16* addend, long long T,
+                      int k, int H, __nv_bfloat16* out, cudaStream_t st, const char* what) {
+  const long long slot_bytes = 2LL * H * k;
+  // slots: a multiple of the consumer-group count, at least one per group
+  const int min_slots = kReduceGroups;
+  if (slot_bytes * min_slots > kReduceSmemPerBlock || H % (8 * kReduceWarpsPerToken) != 0 ||
+      k > kMaxTopK)
+    return -1;
+  int slots = 4 * kReduceGroups;
+  while (slots > min_slots && slots * slot_bytes > kReduceSmemPerBlock) slots -= kReduceGroups;
+  const size_t smem = static_cast<size_t>(slots) * slot_bytes + 2 * slots * sizeof(uint64_t);
+  cudaError_t e = cudaFuncSetAttribute(row_reduce_kernel,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  const long long grid = std::min<long long>(3LL * num_sms(), std::max<long long>(T, 1));
+  row_reduce_kernel<<<static_cast<int>(grid), kReduceThreads, smem, st>>>(
+      rows, inv_pad, weights, addend, T, k, H, slots, out);
+  return check_launch(what);
+}
 
 }  // namespace
 }  // namespace b200moe
@@ -461,9 +487,16 @@ int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offse
 
 int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
                             int k, int H, void* dx, void* stream) {
-  REQUIRE(dxs && inv_pad && dx, "gather_rows_bwd: null pointer");
+  REQUIRE(dxs && dx, "gather_rows_bwd: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "gather_rows_bwd: bad shape");
   if (T == 0) return B200MOE_OK;
+  {
+    const int rc = launch_row_reduce(static_cast<const __nv_bfloat16*>(dxs), inv_pad, nullptr,
+                                     static_cast<const __nv_bfloat16*>(addend), T, k, H,
+                                     static_cast<__nv_bfloat16*>(dx),
+                                     static_cast<cudaStream_t>(stream), "gather_rows_bwd");
+    if (rc >= 0) return rc;
+  }
   gather_rows_bwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(dxs), inv_pad, static_cast<const __nv_bfloat16*>(addend), T,
       k, H, static_cast<__nv_bfloat16*>(dx));
@@ -472,25 +505,46 @@ int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* add
 
 int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T, int k,
                         int H, void* out, void* stream) {
-  REQUIRE(y && inv_pad && weights && out, "combine_fwd: null pointer");
+  REQUIRE(y && weights && out, "combine_fwd: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "combine_fwd: bad shape");
   if (T == 0) return B200MOE_OK;
+  {
+    const int rc = launch_row_reduce(static_cast<const __nv_bfloat16*>(y), inv_pad,
+                                     static_cast<const __nv_bfloat16*>(weights), nullptr, T, k, H,
+                                     static_cast<__nv_bfloat16*>(out),
+                                     static_cast<cudaStream_t>(stream), "combine_fwd");
+    if (rc >= 0) return rc;
+  }
   combine_fwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(y), inv_pad, static_cast<const __nv_bfloat16*>(weights), T,
       k, H, static_cast<__nv_bfloat16*>(out));
   return check_launch("combine_fwd");
 }
 
-int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat,
-                        const int* pad_offsets, const void* weights, int E, int k, int H,
-                        long long rows_cap, void* dy, float* d_weights, void* stream) {
+int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat, const int* inv_pad,
+                        const int* pad_offsets, const void* weights, int E, long long T, int k,
+                        int H, long long rows_cap, int y_token_major, void* dy, float* d_weights,
+                        void* stream) {
   REQUIRE(d_out && y && row_flat && pad_offsets && weights && dy && d_weights,
           "combine_bwd: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1, "combine_bwd: bad shape");
-  combine_bwd_kernel<<<grid_for(rows_cap, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* dyp = static_cast<__nv_bfloat16*>(dy);
+  if (y_token_major) {
+    REQUIRE(inv_pad, "combine_bwd: token-major y needs inv_pad");
+    const long long R = T * k;
+    zero_pad_rows_kernel<<<grid_for(rows_cap, 8), 256, 0, st>>>(row_flat, pad_offsets + E, H, dyp);
+    int rc = check_launch("combine_bwd zero pad");
+    if (rc) return rc;
+    if (R == 0) return B200MOE_OK;
+    combine_bwd_token_major_kernel<<<grid_for(R, 8), 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(d_out), static_cast<const __nv_bfloat16*>(y), inv_pad,
+        static_cast<const __nv_bfloat16*>(weights), R, k, H, dyp, d_weights);
+    return check_launch("combine_bwd");
+  }
+  combine_bwd_kernel<<<grid_for(rows_cap, 8), 256, 0, st>>>(
       static_cast<const __nv_bfloat16*>(d_out), static_cast<const __nv_bfloat16*>(y), row_flat,
-      pad_offsets + E, static_cast<const __nv_bfloat16*>(weights), k, H,
-      static_cast<__nv_bfloat16*>(dy), d_weights);
+      pad_offsets + E, static_cast<const __nv_bfloat16*>(weights), k, H, dyp, d_weights);
   return check_launch("combine_bwd");
 }
 
@@ -539,8 +593,8 @@ int b200moe_expert_gate_up_fwd(const void* xs, const void* w_gu, const int* tile
 }
 
 int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expert,
-                            const int* pad_offsets, long long rows_cap, int E, int H, int I, void* y,
-                            void* stream) {
+                            const int* pad_offsets, const int* row_flat_out, long long rows_cap,
+                            int E, int H, int I, void* y, void* stream) {
   REQUIRE(h && w_d && tile_expert && pad_offsets && y, "down_fwd: null pointer");
   int rc = check_expert_shape("down_fwd", rows_cap, E, H, I);
   if (rc) return rc;
@@ -560,6 +614,7 @@ int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expe
   p.n_valid = H;
   p.out = y;
   p.ld_out = H;
+  p.scatter_rows = row_flat_out;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (BN == 256) return launch_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
   return launch_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
@@ -599,8 +654,8 @@ int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void
 }
 
 int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* tile_expert,
-                                 const int* pad_offsets, long long rows_cap, int E, int H, int I,
-                                 void* dxs, void* stream) {
+                                 const int* pad_offsets, const int* row_flat_out,
+                                 long long rows_cap, int E, int H, int I, void* dxs, void* stream) {
   REQUIRE(d_gu && w_gu && tile_expert && pad_offsets && dxs, "gate_up_dgrad: null pointer");
   int rc = check_expert_shape("gate_up_dgrad", rows_cap, E, H, I);
   if (rc) return rc;
@@ -622,6 +677,7 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* 
   p.n_valid = H;
   p.out = dxs;
   p.ld_out = H;
+  p.scatter_rows = row_flat_out;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (BN == 256) return launch_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
   return launch_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");

@@ -135,6 +135,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* tm, ui
       : "memory");
 }
 
+// Contiguous bulk copy global -> shared (bytes % 16 == 0, both 16-byte aligned),
+// completion signalled on `bar` as transaction bytes.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Four rows (y0..y3) of 64 columns starting at column c0, one 128-byte row
 // each, written to dst as consecutive 128-byte rows (the tensor map's box is
 // {64, 1}).  Rows outside the tensor read as zero.

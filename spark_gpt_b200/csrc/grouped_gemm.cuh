@@ -92,6 +92,9 @@ struct GemmParams {
   const __nv_bfloat16* route_w;  // routing weights, flat slot order (T*k)
   float* dw_part;              // per-(N tile, half) partial d_weights, [parts][Rcap]
   long long part_stride;
+  // kEpiStoreBf16: when set, padded row p is written to output row
+  // scatter_rows[p] (token-major layout t*k+s) and padding rows are skipped
+  const int* scatter_rows;
 };
 
 __device__ __forceinline__ int gather_token(const GemmParams& p, int row) {
@@ -430,14 +433,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag)) break;
+      // every lane waits; the warp leaves together if any lane gave up (the TMEM
+      // loads below are warp-collective)
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
       if (EPI == kEpiStoreBf16) {
-        const long long row = static_cast<long long>(T.m) * BM + row_in;
-        const bool row_ok = row < p.m_valid;
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+        long long row = static_cast<long long>(T.m) * BM + row_in;
+        bool row_ok = row < p.m_valid;
+        if (p.scatter_rows != nullptr && row_ok) {
+          row = __ldg(p.scatter_rows + row);
+          row_ok = row >= 0;
+        }
+        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (row_ok ? row : 0) * p.ld_out;
 #pragma unroll 1
         for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
           uint32_t r[32];

@@ -204,7 +204,9 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
-// dx[t] = sum_s dxs[inv_pad[t*k+s]] (+ addend[t]); fp32 accumulation.
+// dx[t] = sum_s dxs[inv_pad[t*k+s]] (+ addend[t]); fp32 accumulation.  With
+// inv_pad == nullptr the rows are token-major (slot t*k+s in row t*k+s).  Used
+// when one token's k rows do not fit the shared-memory ring of row_reduce_kernel.
 __global__ void gather_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
                                        const int* __restrict__ inv_pad,
                                        const __nv_bfloat16* __restrict__ addend, long long T,
@@ -216,7 +218,8 @@ __global__ void gather_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
        t < T; t += warps) {
     int rows[kMaxTopK];
 #pragma unroll
-    for (int s = 0; s < kMaxTopK; ++s) rows[s] = s < k ? inv_pad[t * k + s] : 0;
+    for (int s = 0; s < kMaxTopK; ++s)
+      rows[s] = s < k ? (inv_pad ? inv_pad[t * k + s] : static_cast<int>(t * k + s)) : 0;
     for (int v = lane; v < nvec; v += 32) {
       float acc[8];
 #pragma unroll
@@ -266,7 +269,7 @@ __global__ void combine_fwd_kernel(const __nv_bfloat16* __restrict__ y,
     float w[kMaxTopK];
 #pragma unroll
     for (int s = 0; s < kMaxTopK; ++s) {
-      rows[s] = s < k ? inv_pad[t * k + s] : 0;
+      rows[s] = s < k ? (inv_pad ? inv_pad[t * k + s] : static_cast<int>(t * k + s)) : 0;
       w[s] = s < k ? __bfloat162float(weights[t * k + s]) : 0.f;
     }
     for (int v = lane; v < nvec; v += 32) {
@@ -334,6 +337,200 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ d_out,
     }
     dot = warp_sum(dot);
     if (lane == 0) d_weights[f] = dot;
+  }
+}
+
+// Token-major combine backward: y_tok (T*k, H) holds the down projection of
+// slot f = t*k+s in row f.  Warp per slot, in slot order (sequential reads of
+// y_tok and d_out): dy[inv_pad[f]] = bf16(d_out[t] * w[f]) (scattered 2*H-byte
+// row writes), d_weights[f] = <d_out[t], y_tok[f]>.
+__global__ void combine_bwd_token_major_kernel(const __nv_bfloat16* __restrict__ d_out,
+                                               const __nv_bfloat16* __restrict__ y_tok,
+                                               const int* __restrict__ inv_pad,
+                                               const __nv_bfloat16* __restrict__ weights,
+                                               long long R, int k, int H,
+                                               __nv_bfloat16* __restrict__ dy,
+                                               float* __restrict__ d_weights) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long f = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       f < R; f += warps) {
+    const float w = __bfloat162float(weights[f]);
+    const uint4* g = reinterpret_cast<const uint4*>(d_out + (f / k) * H);
+    const uint4* yy = reinterpret_cast<const uint4*>(y_tok + f * H);
+    uint4* dst = reinterpret_cast<uint4*>(dy + static_cast<long long>(inv_pad[f]) * H);
+    float dot = 0.f;
+    for (int v = lane; v < nvec; v += 32) {
+      const uint4 a = __ldg(g + v);
+      const uint4 b = __ldg(yy + v);
+      float ga[8] = {bf16_lo(a.x), bf16_hi(a.x), bf16_lo(a.y), bf16_hi(a.y),
+                     bf16_lo(a.z), bf16_hi(a.z), bf16_lo(a.w), bf16_hi(a.w)};
+      float yb[8] = {bf16_lo(b.x), bf16_hi(b.x), bf16_lo(b.y), bf16_hi(b.y),
+                     bf16_lo(b.z), bf16_hi(b.z), bf16_lo(b.w), bf16_hi(b.w)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dot += ga[j] * yb[j];
+      uint4 o;
+      o.x = pack_bf16x2(ga[0] * w, ga[1] * w);
+      o.y = pack_bf16x2(ga[2] * w, ga[3] * w);
+      o.z = pack_bf16x2(ga[4] * w, ga[5] * w);
+      o.w = pack_bf16x2(ga[6] * w, ga[7] * w);
+      dst[v] = o;
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) d_weights[f] = dot;
+  }
+}
+
+// Zero the padding rows (row_flat < 0) of a (Rcap, H) bf16 buffer.
+__global__ void zero_pad_rows_kernel(const int* __restrict__ row_flat,
+                                     const int* __restrict__ total_rows, int H,
+                                     __nv_bfloat16* __restrict__ buf) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const long long total = *total_rows;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long r = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       r < total; r += warps) {
+    if (row_flat[r] >= 0) continue;
+    uint4* dst = reinterpret_cast<uint4*>(buf + r * H);
+    for (int v = lane; v < nvec; v += 32) dst[v] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// k-row reductions per token, streamed through shared memory with bulk copies
+// (the combine forward and the gather backward):
+//   out[t] = sum_s c(s) + addend[t],   c(s) = bf16(rows[j] * w[t,s])  (weights)
+//                                       c(s) = rows[j]                 (no weights)
+//   j = inv_pad[t*k+s] (or t*k+s when rows are token-major); fp32 accumulation
+//   in slot order, one rounding to bf16.
+// Warp 0 produces: lane s < k issues the 2*H-byte bulk copy of row s of a
+// token into a ring slot.  Consumers are kReduceGroups groups of
+// kReduceWarpsPerToken warps; the warps of a group split the H columns of one
+// token.  The slot count is a multiple of the group count, so each slot always
+// has the same consumer group and its phases are waited in order.  Each block
+// owns a contiguous range of tokens, so the k indices of several tokens are
+// one coalesced read, issued a group of tokens ahead of use.
+// ---------------------------------------------------------------------------
+constexpr int kReduceWarpsPerToken = 4;
+constexpr int kReduceGroups = 2;
+constexpr int kReduceThreads = 32 * (1 + kReduceGroups * kReduceWarpsPerToken);
+
+__global__ void __launch_bounds__(kReduceThreads)
+    row_reduce_kernel(const __nv_bfloat16* __restrict__ rows, const int* __restrict__ inv_pad,
+                      const __nv_bfloat16* __restrict__ weights,
+                      const __nv_bfloat16* __restrict__ addend, long long T, int k, int H,
+                      int slots, __nv_bfloat16* __restrict__ out) {
+  extern __shared__ __align__(128) uint8_t rsm[];
+  const uint32_t row_bytes = static_cast<uint32_t>(H) * 2;
+  const uint32_t slot_bytes = row_bytes * k;
+  uint64_t* full = reinterpret_cast<uint64_t*>(rsm + static_cast<size_t>(slots) * slot_bytes);
+  uint64_t* empty = full + slots;
+  __shared__ int abort_flag_s;
+  volatile int* abort_flag = &abort_flag_s;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < slots; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kReduceWarpsPerToken);
+    }
+    abort_flag_s = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const long long per_block = (T + gridDim.x - 1) / gridDim.x;
+  const long long t0 = blockIdx.x * per_block;
+  const long long n = max(0LL, min(T, t0 + per_block) - t0);
+  if (warp == 0) {
+    const int tpg = 32 / k;  // tokens whose k indices one warp load covers
+    const bool active_lane = lane < tpg * k;
+    // row of slot s of token t: inv_pad[t*k+s], or t*k+s itself when the rows
+    // are stored token-major (inv_pad == nullptr)
+    auto slot_row = [&](long long f) -> long long { return inv_pad ? inv_pad[f] : f; };
+    long long idx_next = 0;
+    if (active_lane && lane / k < n) idx_next = slot_row((t0 + lane / k) * k + lane % k);
+    for (long long g = 0; g < n; g += tpg) {
+      const long long idx = idx_next;
+      if (active_lane && g + tpg + lane / k < n)
+        idx_next = slot_row((t0 + g + tpg + lane / k) * k + lane % k);
+      for (int tt = 0; tt < tpg && g + tt < n; ++tt) {
+        const long long i = g + tt;
+        const int s = static_cast<int>(i % slots);
+        const uint32_t ph = static_cast<uint32_t>((i / slots) & 1);
+        int good = 1;
+        if (lane == 0) {
+          good = mbar_wait(&empty[s], ph ^ 1u, abort_flag) ? 1 : 0;
+          if (good) mbar_expect_tx(&full[s], slot_bytes);
+        }
+        good = __shfl_sync(0xffffffffu, good, 0);
+        if (!good) break;
+        if (active_lane && lane / k == tt)
+          bulk_load(rsm + static_cast<size_t>(s) * slot_bytes + (lane % k) * row_bytes,
+                    rows + idx * H, row_bytes, &full[s]);
+      }
+      if (*abort_flag) break;
+    }
+  } else {
+    const int cw = warp - 1;
+    const int group = cw / kReduceWarpsPerToken;
+    const int part = cw % kReduceWarpsPerToken;
+    const int nvec = H / 8;
+    const int v0 = part * (nvec / kReduceWarpsPerToken);
+    const int v1 = (part + 1 == kReduceWarpsPerToken) ? nvec : v0 + nvec / kReduceWarpsPerToken;
+    for (long long i = group; i < n; i += kReduceGroups) {
+      const int s = static_cast<int>(i % slots);
+      const uint32_t ph = static_cast<uint32_t>((i / slots) & 1);
+      // every lane waits (acquire); the warp leaves together if any lane gave up
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, abort_flag))) break;
+      const long long t = t0 + i;
+      // routing weights of the token's k slots, broadcast to every lane before
+      // the column loop (lanes past the last column skip it: no shuffle inside)
+      float wv = 1.f;
+      if (weights && lane < k) wv = __bfloat162float(weights[t * k + lane]);
+      __nv_bfloat162 wr[kMaxTopK];
+#pragma unroll
+      for (int r = 0; r < kMaxTopK; ++r)
+        wr[r] = __float2bfloat162_rn(__shfl_sync(0xffffffffu, wv, r));
+      const uint8_t* slot = rsm + static_cast<size_t>(s) * slot_bytes;
+      for (int v = v0 + lane; v < v1; v += 32) {
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+        for (int r = 0; r < kMaxTopK; ++r) {
+          if (r < k) {
+            uint4 q = *reinterpret_cast<const uint4*>(slot + r * row_bytes + v * 16);
+            if (weights) {
+              // bf16 x bf16 product rounded once to bf16 (= bf16(float(a)*float(b)))
+              __nv_bfloat162* q2 = reinterpret_cast<__nv_bfloat162*>(&q);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) q2[j] = __hmul2(q2[j], wr[r]);
+            }
+            acc[0] += bf16_lo(q.x); acc[1] += bf16_hi(q.x);
+            acc[2] += bf16_lo(q.y); acc[3] += bf16_hi(q.y);
+            acc[4] += bf16_lo(q.z); acc[5] += bf16_hi(q.z);
+            acc[6] += bf16_lo(q.w); acc[7] += bf16_hi(q.w);
+          }
+        }
+        if (addend) {
+          const uint4 a = __ldg(reinterpret_cast<const uint4*>(addend + t * H) + v);
+          acc[0] += bf16_lo(a.x); acc[1] += bf16_hi(a.x);
+          acc[2] += bf16_lo(a.y); acc[3] += bf16_hi(a.y);
+          acc[4] += bf16_lo(a.z); acc[5] += bf16_hi(a.z);
+          acc[6] += bf16_lo(a.w); acc[7] += bf16_hi(a.w);
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        reinterpret_cast<uint4*>(out + t * H)[v] = o;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
   }
 }
 

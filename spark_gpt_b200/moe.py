@@ -24,6 +24,15 @@ from . import ops
 
 BF16 = torch.bfloat16
 
+# Layout of the down-projection output y and of the gate_up input gradient
+# dxs: token-major (slot t*k+s in row t*k+s, so the combine and the gather
+# backward read each token's k rows as one contiguous block) or padded-row
+# order (the GEMMs write rows sequentially).  Measured on B200 at config 2:
+# the shared-memory row reduction reads scattered 2 KB rows as fast as
+# contiguous ones, while scattered epilogue writes slow the two GEMMs, so the
+# padded order is the default.
+TOKEN_MAJOR = False
+
 
 def _require_cuda(*ts):
     for t in ts:
@@ -80,8 +89,8 @@ class _SparseMoEFn(torch.autograd.Function):
         d = ops.dispatch(sel, E)
         xs = ops.gather_rows(xb, d)
         gu, h = ops.gate_up_fwd(xs, wgu, d)
-        y = ops.down_fwd(h, wd, d)
-        out = ops.combine(y, d, rw)
+        y = ops.down_fwd(h, wd, d, token_major=TOKEN_MAJOR)
+        out = ops.combine(y, d, rw, token_major=TOKEN_MAJOR)
         ctx.save_for_backward(xb, wr, wgu, wd, logits_buf, sel, rw, xs, gu, h, y)
         ctx.dispatch = d
         ctx.cfg = (E, W, top_k, norm, x.dtype)
@@ -99,19 +108,19 @@ class _SparseMoEFn(torch.autograd.Function):
         if d_out is None:
             d_out = torch.zeros(T, xb.shape[1], device=xb.device, dtype=BF16)
         d_out = _as_bf16(d_out)
-        dy, d_rw = ops.combine_bwd(d_out, y, d, rw)
+        dy, d_rw = ops.combine_bwd(d_out, y, d, rw, token_major=TOKEN_MAJOR)
         del y
         d_gu = ops.down_dgrad_swiglu(dy, wd, gu, d)
         del gu
         g_down = ops.wgrad(dy, h, d, name="down_wgrad") if w_down else None
         del dy, h
-        dxs = ops.gate_up_dgrad(d_gu, wgu, d)
+        dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
         g_gate_up = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad") if w_gate_up else None
         del d_gu, xs
         extra = _extra_logit_grad(d_logits, T, W)
         dl = ops.router_topk_bwd(logits_buf, sel, d_rw, extra, E, top_k, norm)
         dx_router = ops.router_dgrad(dl, wr)
-        dx = ops.gather_rows_bwd(dxs, d, addend=dx_router)
+        dx = ops.gather_rows_bwd(dxs, d, addend=dx_router, token_major=TOKEN_MAJOR)
         g_router = ops.router_wgrad(xb, dl, E) if w_router else None
         return dx.to(xdtype), g_router, g_gate_up, g_down, None, None
 
@@ -164,8 +173,8 @@ class _ExpertsFn(torch.autograd.Function):
         d = ops.dispatch(sel, E)
         xs = ops.gather_rows(xb, d)
         gu, h = ops.gate_up_fwd(xs, wgu, d)
-        y = ops.down_fwd(h, wd, d)
-        out = ops.combine(y, d, rw)
+        y = ops.down_fwd(h, wd, d, token_major=TOKEN_MAJOR)
+        out = ops.combine(y, d, rw, token_major=TOKEN_MAJOR)
         ctx.save_for_backward(rw, wgu, wd, xs, gu, h, y)
         ctx.dispatch = d
         ctx.cfg = (x.dtype, weights.dtype)
@@ -176,12 +185,12 @@ class _ExpertsFn(torch.autograd.Function):
         rw, wgu, wd, xs, gu, h, y = ctx.saved_tensors
         d = ctx.dispatch
         xdtype, wdtype = ctx.cfg
-        dy, d_rw = ops.combine_bwd(_as_bf16(d_out), y, d, rw)
+        dy, d_rw = ops.combine_bwd(_as_bf16(d_out), y, d, rw, token_major=TOKEN_MAJOR)
         d_gu = ops.down_dgrad_swiglu(dy, wd, gu, d)
         g_down = ops.wgrad(dy, h, d, name="down_wgrad") if ctx.needs_input_grad[4] else None
-        dxs = ops.gate_up_dgrad(d_gu, wgu, d)
+        dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
         g_gu = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad") if ctx.needs_input_grad[3] else None
-        dx = ops.gather_rows_bwd(dxs, d)
+        dx = ops.gather_rows_bwd(dxs, d, token_major=TOKEN_MAJOR)
         return dx.to(xdtype), None, d_rw.to(wdtype), g_gu, g_down
 
 

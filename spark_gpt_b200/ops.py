@@ -202,33 +202,36 @@ def gather_rows(x: torch.Tensor, d: Dispatch) -> torch.Tensor:
     return xs
 
 
-def gather_rows_bwd(dxs, d: Dispatch, addend=None) -> torch.Tensor:
+def gather_rows_bwd(dxs, d: Dispatch, addend=None, token_major=False) -> torch.Tensor:
+    """dx[t] = sum_s dxs[row of slot t*k+s] (+ addend); token_major: row t*k+s."""
     H = dxs.shape[1]
     dx = torch.empty(d.num_tokens, H, device=dxs.device, dtype=BF16)
     if d.num_tokens:
-        _launch("gather_bwd", 1, "b200moe_gather_rows_bwd", _p(dxs), _p(d.inv_pad), _p(addend),
-                d.num_tokens, d.top_k, H, _p(dx), _s(dxs))
+        _launch("gather_bwd", 1, "b200moe_gather_rows_bwd", _p(dxs),
+                None if token_major else _p(d.inv_pad), _p(addend), d.num_tokens, d.top_k, H,
+                _p(dx), _s(dxs))
     return dx
 
 
-def combine(y, d: Dispatch, weights) -> torch.Tensor:
+def combine(y, d: Dispatch, weights, token_major=False) -> torch.Tensor:
     _check(weights, BF16, "combine weights")
     H = y.shape[1]
     out = torch.empty(d.num_tokens, H, device=y.device, dtype=BF16)
     if d.num_tokens:
-        _launch("combine", 1, "b200moe_combine_fwd", _p(y), _p(d.inv_pad), _p(weights),
-                d.num_tokens, d.top_k, H, _p(out), _s(y))
+        _launch("combine", 1, "b200moe_combine_fwd", _p(y),
+                None if token_major else _p(d.inv_pad), _p(weights), d.num_tokens, d.top_k, H,
+                _p(out), _s(y))
     return out
 
 
-def combine_bwd(d_out, y, d: Dispatch, weights):
+def combine_bwd(d_out, y, d: Dispatch, weights, token_major=False):
     _check(d_out, BF16, "combine_bwd d_out")
     H = y.shape[1]
     dy = torch.empty(d.rows_cap, H, device=y.device, dtype=BF16)
     dw = torch.empty(d.num_tokens, d.top_k, device=y.device, dtype=torch.float32)
-    _launch("combine_bwd", 1, "b200moe_combine_bwd", _p(d_out), _p(y), _p(d.row_flat),
-            _p(d.pad_offsets), _p(weights), d.num_experts, d.top_k, H, d.rows_cap, _p(dy),
-            _p(dw), _s(y))
+    _launch("combine_bwd", 2 if token_major else 1, "b200moe_combine_bwd", _p(d_out), _p(y),
+            _p(d.row_flat), _p(d.inv_pad), _p(d.pad_offsets), _p(weights), d.num_experts,
+            d.num_tokens, d.top_k, H, d.rows_cap, int(token_major), _p(dy), _p(dw), _s(y))
     return dy, dw
 
 
@@ -245,11 +248,14 @@ def gate_up_fwd(xs, w_gu, d: Dispatch):
     return gu, h
 
 
-def down_fwd(h, w_d, d: Dispatch):
+def down_fwd(h, w_d, d: Dispatch, token_major=False):
+    """y = h W_d[e]^T; token_major: (T*k, H) with slot t*k+s in row t*k+s."""
     E, H, I = w_d.shape
-    y = torch.empty(d.rows_cap, H, device=h.device, dtype=BF16)
+    rows = d.num_tokens * d.top_k if token_major else d.rows_cap
+    y = torch.empty(max(rows, 1), H, device=h.device, dtype=BF16)
     _launch("down_fwd", 1, "b200moe_expert_down_fwd", _p(h), _p(w_d), _p(d.tile_expert),
-            _p(d.pad_offsets), d.rows_cap, E, H, I, _p(y), _s(h))
+            _p(d.pad_offsets), _p(d.row_flat) if token_major else None, d.rows_cap, E, H, I,
+            _p(y), _s(h))
     return y
 
 
@@ -261,12 +267,14 @@ def down_dgrad_swiglu(dy, w_d, gu, d: Dispatch):
     return d_gu
 
 
-def gate_up_dgrad(d_gu, w_gu, d: Dispatch):
+def gate_up_dgrad(d_gu, w_gu, d: Dispatch, token_major=False):
+    """dxs = d_gu W_gu[e]; token_major: (T*k, H) with slot t*k+s in row t*k+s."""
     E, two_i, H = w_gu.shape
-    dxs = torch.empty(d.rows_cap, H, device=d_gu.device, dtype=BF16)
+    rows = d.num_tokens * d.top_k if token_major else d.rows_cap
+    dxs = torch.empty(max(rows, 1), H, device=d_gu.device, dtype=BF16)
     _launch("gate_up_dgrad", 1, "b200moe_expert_gate_up_dgrad", _p(d_gu), _p(w_gu),
-            _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, two_i // 2, _p(dxs),
-            _s(d_gu))
+            _p(d.tile_expert), _p(d.pad_offsets), _p(d.row_flat) if token_major else None,
+            d.rows_cap, E, H, two_i // 2, _p(dxs), _s(d_gu))
     return dxs
 
 

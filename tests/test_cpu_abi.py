@@ -55,7 +55,7 @@ def test_entry_points_reject_bad_arguments_without_touching_the_gpu(lib):
     with pytest.raises(RuntimeError, match="k <="):
         _lib.call("b200moe_router_topk_fwd", 16, 0, 64, 10, 64, 17, 1, 16, 16, None)
     with pytest.raises(RuntimeError, match="multiple of 128"):
-        _lib.call("b200moe_expert_down_fwd", 16, 16, 16, 16, 1024, 8, 200, 64, 16, None)
+        _lib.call("b200moe_expert_down_fwd", 16, 16, 16, 16, None, 1024, 8, 200, 64, 16, None)
     with pytest.raises(RuntimeError, match="I must be"):
         _lib.call("b200moe_expert_gate_up_fwd", 16, 16, 16, 16, 1024, 8, 256, 100, 16, 16, None)
     with pytest.raises(RuntimeError, match="scratch too small"):

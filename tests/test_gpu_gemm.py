@@ -213,3 +213,20 @@ def test_down_dgrad_with_combine_backward(ops, T, k, E, H, I):
     ref_dw = (acc * h[:n].float()).sum(1)
     got = d_w.view(-1)[rows[valid]]
     torch.testing.assert_close(got, ref_dw[valid], rtol=1e-3, atol=1e-3 * ref_dw.abs().max().item())
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES)
+def test_token_major_outputs_equal_padded(ops, T, k, E, H, I):
+    """down fwd / gate_up dgrad writing rows in token order (row t*k+s) give the
+    padded-order rows, permuted."""
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 9)
+    n = int(d.pad_offsets[-1])
+    rf = d.row_flat[:n].long()
+    gu, h = ops.gate_up_fwd(xs, wgu, d)
+    y0 = ops.down_fwd(h, wd, d)
+    y1 = ops.down_fwd(h, wd, d, token_major=True)
+    assert torch.equal(y1[rf[rf >= 0]], y0[:n][rf >= 0])
+    d_gu = torch.randn(d.rows_cap, 2 * I, device=DEV).to(torch.bfloat16)
+    x0 = ops.gate_up_dgrad(d_gu, wgu, d)
+    x1 = ops.gate_up_dgrad(d_gu, wgu, d, token_major=True)
+    assert torch.equal(x1[rf[rf >= 0]], x0[:n][rf >= 0])

@@ -178,3 +178,28 @@ def test_load_balance_stats_and_grad(ops, E, k, filler):
     assert (dl - ref).abs().max() <= 2 ** -7 * ref.abs().max() + 1e-12
     if filler:
         assert torch.all(dl[~valid] == 0)
+
+
+@pytest.mark.parametrize("T,k,E,H", [(2500, 8, 64, 512), (3000, 4, 16, 256), (700, 2, 8, 128),
+                                     (513, 8, 128, 2048)])
+def test_token_major_combine_paths_equal_padded(ops, T, k, E, H):
+    """The token-major layout (slot t*k+s in row t*k+s) gives the same results
+    as the padded-row layout, bit for bit."""
+    sel = _routing(T, k, E, 3)
+    d = ops.dispatch(sel.to(DEV), E)
+    n = int(d.pad_offsets[-1])
+    y = torch.randn(d.rows_cap, H, device=DEV).to(torch.bfloat16)
+    rf = d.row_flat[:n].long()
+    y_tok = torch.empty(T * k, H, device=DEV, dtype=torch.bfloat16)
+    y_tok[rf[rf >= 0]] = y[:n][rf >= 0]
+    w = torch.rand(T, k, device=DEV).to(torch.bfloat16)
+    assert torch.equal(ops.combine(y, d, w), ops.combine(y_tok, d, w, token_major=True))
+    add = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    assert torch.equal(ops.gather_rows_bwd(y, d, addend=add),
+                       ops.gather_rows_bwd(y_tok, d, addend=add, token_major=True))
+    d_out = torch.randn(T, H, device=DEV).to(torch.bfloat16)
+    dy0, dw0 = ops.combine_bwd(d_out, y, d, w)
+    dy1, dw1 = ops.combine_bwd(d_out, y_tok, d, w, token_major=True)
+    assert torch.equal(dy0[:n], dy1[:n])
+    assert torch.all(dy1[:n][rf < 0] == 0)
+    torch.testing.assert_close(dw0, dw1, rtol=1e-6, atol=1e-6)
