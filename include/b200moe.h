@@ -33,6 +33,11 @@ extern "C" {
 /* Library version (major*10000 + minor*100 + patch). */
 int b200moe_version(void);
 
+/* Expert GEMMs run as two-CTA (cta_group::2) 256-row pair tiles when the
+ * shape allows (default 1); 0 selects the single-CTA 128-row kernel.  Both
+ * give identical results.  Returns the previous setting; process-wide. */
+int b200moe_set_pair_gemm(int enable);
+
 /* Message of this thread's last failed call ("" if none). */
 const char* b200moe_last_error(void);
 

@@ -11,6 +11,7 @@
 
 #include "../../include/b200moe.h"
 #include "grouped_gemm.cuh"
+#include "grouped_gemm_2sm.cuh"
 #include "routing.cuh"
 
 namespace b200moe {
@@ -113,6 +114,55 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   return check_launch(what);
 }
 
+// Expert GEMMs run as two-CTA pair tiles when the shape allows (switchable for
+// parity tests of the two kernels against each other).
+int g_pair_gemm = 1;
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
+int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                     cudaStream_t st, const char* what) {
+  constexpr int STAGES = 6;
+  auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
+  const int smem = static_cast<int>(PairSmem<BN, STAGES>::kTotal);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(num_sms() & ~1), 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
+}
+
+// Whether an expert GEMM runs as two-CTA pair tiles: BN of 128/256, E <= 512
+// (the kernel's per-expert pair table) and, for weight gradients, M a
+// multiple of 256.  Tensor maps of K-major B depend on it (box of BN/2 rows
+// per CTA instead of BN).
+bool use_pair(int BN, int sched, int num_groups, int m_tiles) {
+  return g_pair_gemm && BN >= 128 && num_groups <= kMaxPairExperts &&
+         (sched == kRowsRagged || m_tiles % 2 == 0);
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
+int launch_expert_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
+                       cudaStream_t st, const char* what) {
+  if constexpr (BN >= 128) {
+    if (use_pair(BN, SCHED, p.num_groups, p.m_tiles) &&
+        (SCHED == kKRagged || p.pad_offsets != nullptr))
+      return launch_gemm_pair<BN, A_MN, B_MN, EPI, SCHED>(ta, tb, p, st, what);
+  }
+  return launch_gemm<BN, A_MN, B_MN, EPI, SCHED>(ta, tb, p, st, what);
+}
+
 GemmParams blank_params() {
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -176,6 +226,12 @@ using namespace b200moe;
 extern "C" {
 
 int b200moe_version(void) { return 100; }
+
+int b200moe_set_pair_gemm(int enable) {
+  const int prev = g_pair_gemm;
+  g_pair_gemm = enable ? 1 : 0;
+  return prev;
+}
 
 const char* b200moe_last_error(void) { return t_last_error.c_str(); }
 
@@ -588,8 +644,8 @@ int b200moe_expert_gate_up_fwd(const void* xs, const void* w_gu, const int* tile
   p.ld_out2 = I;
   p.inter = I;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (half == 128) return launch_gemm<256, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
-  return launch_gemm<128, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
+  if (half == 128) return launch_expert_gemm<256, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
+  return launch_expert_gemm<128, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
 }
 
 int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expert,
@@ -601,7 +657,8 @@ int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expe
   const int BN = (H % 256 == 0) ? 256 : 128;
   CUtensorMap ta, tb;
   if ((rc = make_tmap(&ta, h, I, rows_cap, I, 64, 128, "down_fwd h"))) return rc;
-  if ((rc = make_tmap(&tb, w_d, I, static_cast<long long>(E) * H, I, 64, BN, "down_fwd w")))
+  const int b_box = use_pair(BN, kRowsRagged, E, 0) ? BN / 2 : BN;
+  if ((rc = make_tmap(&tb, w_d, I, static_cast<long long>(E) * H, I, 64, b_box, "down_fwd w")))
     return rc;
   GemmParams p = blank_params();
   p.tile_expert = tile_expert;
@@ -616,8 +673,8 @@ int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expe
   p.ld_out = H;
   p.scatter_rows = row_flat_out;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
-  return launch_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
+  if (BN == 256) return launch_expert_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
+  return launch_expert_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
 }
 
 int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void* gu,
@@ -648,9 +705,9 @@ int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void
   p.ld_aux = 2 * I;
   p.inter = I;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
-  if (BN == 128) return launch_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
-  return launch_gemm<64, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+  if (BN == 128) return launch_expert_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+  return launch_expert_gemm<64, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
 }
 
 int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* tile_expert,
@@ -679,8 +736,8 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* 
   p.ld_out = H;
   p.scatter_rows = row_flat_out;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
-  return launch_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
+  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
+  return launch_expert_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
 }
 
 int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets, int E,
@@ -705,9 +762,9 @@ int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* 
   p.accumulate = accumulate;
   p.out_group_stride = static_cast<long long>(M) * N;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
-  if (BN == 128) return launch_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
-  return launch_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+  if (BN == 256) return launch_expert_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+  if (BN == 128) return launch_expert_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+  return launch_expert_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
 }
 
 // ---------------------------------------------------------------- gathered-operand GEMMs

@@ -185,6 +185,196 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
   }
 }
 
+// Epilogue of a weight-gradient tile whose expert received no rows: zeros
+// (or nothing when accumulating).  Warps split the columns by `half`.
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_empty_tile(const GemmParams& p, const TileInfo& T,
+                                                    int row_in, int half) {
+  constexpr int BM = 128;
+  // a weight-gradient tile of an expert that received no rows
+  if ((EPI == kEpiStoreF32 || EPI == kEpiStoreF32T) && !p.accumulate) {
+    if (EPI == kEpiStoreF32) {
+      float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
+                 static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
+      float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 4)
+        *reinterpret_cast<float4*>(o + c) = z;
+    } else {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); ++c) {
+        const int col = T.n * BN + c;
+        if (col < p.n_valid)
+          static_cast<float*>(p.out)[T.g * p.out_group_stride +
+                                     static_cast<long long>(col) * p.ld_out + T.m * BM +
+                                     row_in] = 0.f;
+      }
+    }
+  }
+}
+
+// Drain one accumulator tile (this warp's 32 TMEM lanes, its half of the
+// 32-column chunks) through the fused epilogue.  `taddr` is the TMEM address
+// of the warp's lane quarter at the tile's first column.
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInfo& T,
+                                              int row_in, int half, uint32_t taddr) {
+  constexpr int BM = 128;
+  if (EPI == kEpiStoreBf16) {
+    long long row = static_cast<long long>(T.m) * BM + row_in;
+    bool row_ok = row < p.m_valid;
+    if (p.scatter_rows != nullptr && row_ok) {
+      row = __ldg(p.scatter_rows + row);
+      row_ok = row >= 0;
+    }
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (row_ok ? row : 0) * p.ld_out;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col0 = T.n * BN + c * 32;
+      if (row_ok) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+        if (col0 + 32 <= p.n_valid) {
+          store_bf16x32(o + col0, v);
+        } else {
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.n_valid) o[col0 + j] = __float2bfloat16_rn(v[j]);
+        }
+      }
+    }
+  } else if (EPI == kEpiSwigluFwd) {
+    constexpr int HALF = BN / 2;
+    const long long row = static_cast<long long>(T.m) * BM + row_in;
+    const bool row_ok = row < p.m_valid;
+    __nv_bfloat16* gu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+    __nv_bfloat16* hh = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
+#pragma unroll 1
+    for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(taddr + c * 32, rg);
+      tmem_ld32(taddr + HALF + c * 32, ru);
+      tmem_wait_ld();
+      if (row_ok) {
+        const int col = T.n * HALF + c * 32;
+        float g[32], u[32], h[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          g[j] = bf16_round(__uint_as_float(rg[j]));
+          u[j] = bf16_round(__uint_as_float(ru[j]));
+          h[j] = g[j] * sigmoidf_(g[j]) * u[j];
+        }
+        store_bf16x32(gu + col, g);
+        store_bf16x32(gu + p.inter + col, u);
+        store_bf16x32(hh + col, h);
+      }
+    }
+  } else if (EPI == kEpiSwigluBwd) {
+    const long long row = static_cast<long long>(T.m) * BM + row_in;
+    const bool row_ok = row < p.m_valid;
+    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
+    __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      if (row_ok) {
+        const int col = T.n * BN + c * 32;
+        float g[32], u[32], dg[32], du[32];
+        load_bf16x32(gu + col, g);
+        load_bf16x32(gu + p.inter + col, u);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float dh = bf16_round(__uint_as_float(r[j]));
+          const float sig = sigmoidf_(g[j]);
+          dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+          du[j] = dh * g[j] * sig;
+        }
+        store_bf16x32(dgu + col, dg);
+        store_bf16x32(dgu + p.inter + col, du);
+      }
+    }
+  } else if (EPI == kEpiSwigluBwdCombine) {
+    // acc = d_out[token] . W_d[e] (unscaled).  dh = bf16(w * acc); the routing
+    // weight's gradient <d_out[token], y[row]> = <acc, h[row]> is summed here;
+    // w * h is written for the down-projection weight gradient.
+    const long long row = static_cast<long long>(T.m) * BM + row_in;
+    const int f = __ldg(p.gather_rows + row);
+    const float w = f >= 0 ? __bfloat162float(p.route_w[f]) : 0.f;
+    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
+    const __nv_bfloat16* hh = static_cast<const __nv_bfloat16*>(p.aux2) + row * p.ld_aux2;
+    __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
+    __nv_bfloat16* hw = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
+    float dwp = 0.f;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col = T.n * BN + c * 32;
+      float g[32], u[32], hv[32], dg[32], du[32];
+      load_bf16x32(gu + col, g);
+      load_bf16x32(gu + p.inter + col, u);
+      load_bf16x32(hh + col, hv);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float a = __uint_as_float(r[j]);
+        dwp += a * hv[j];
+        const float dh = bf16_round(w * a);
+        const float sig = sigmoidf_(g[j]);
+        dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+        du[j] = dh * g[j] * sig;
+        hv[j] *= w;
+      }
+      store_bf16x32(dgu + col, dg);
+      store_bf16x32(dgu + p.inter + col, du);
+      store_bf16x32(hw + col, hv);
+    }
+    p.dw_part[(T.n * 2 + half) * p.part_stride + row] = dwp;
+  } else if (EPI == kEpiStoreF32) {
+    float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
+               static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      float4* d = reinterpret_cast<float4*>(o + c * 32);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                               __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+        if (p.accumulate) {
+          const float4 old = d[j];
+          v.x += old.x;
+          v.y += old.y;
+          v.z += old.z;
+          v.w += old.w;
+        }
+        d[j] = v;
+      }
+    }
+  } else {  // kEpiStoreF32T
+    float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride + T.m * BM + row_in;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int col = T.n * BN + c * 32 + j;
+        if (col < p.n_valid) {
+          float* dst = o + static_cast<long long>(col) * p.ld_out;
+          const float v = __uint_as_float(r[j]);
+          *dst = p.accumulate ? (*dst + v) : v;
+        }
+      }
+    }
+  }
+}
 constexpr int kEpilogueWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 
@@ -410,24 +600,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const TileInfo T = decode_tile<SCHED>(p, t);
       if (T.kblocks == 0) {
-        // a weight-gradient tile of an expert that received no rows
-        if ((EPI == kEpiStoreF32 || EPI == kEpiStoreF32T) && !p.accumulate) {
-          if (EPI == kEpiStoreF32) {
-            float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
-                       static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
-            float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 4)
-              *reinterpret_cast<float4*>(o + c) = z;
-          } else {
-            for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); ++c) {
-              const int col = T.n * BN + c;
-              if (col < p.n_valid)
-                static_cast<float*>(p.out)[T.g * p.out_group_stride +
-                                           static_cast<long long>(col) * p.ld_out + T.m * BM +
-                                           row_in] = 0.f;
-            }
-          }
-        }
+        epilogue_empty_tile<EPI, BN>(p, T, row_in, half);
         continue;
       }
       const int acc = local & 1;
@@ -439,162 +612,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
 
-      if (EPI == kEpiStoreBf16) {
-        long long row = static_cast<long long>(T.m) * BM + row_in;
-        bool row_ok = row < p.m_valid;
-        if (p.scatter_rows != nullptr && row_ok) {
-          row = __ldg(p.scatter_rows + row);
-          row_ok = row >= 0;
-        }
-        __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + (row_ok ? row : 0) * p.ld_out;
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          const int col0 = T.n * BN + c * 32;
-          if (row_ok) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if (col0 + 32 <= p.n_valid) {
-              store_bf16x32(o + col0, v);
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < p.n_valid) o[col0 + j] = __float2bfloat16_rn(v[j]);
-            }
-          }
-        }
-      } else if (EPI == kEpiSwigluFwd) {
-        constexpr int HALF = BN / 2;
-        const long long row = static_cast<long long>(T.m) * BM + row_in;
-        const bool row_ok = row < p.m_valid;
-        __nv_bfloat16* gu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
-        __nv_bfloat16* hh = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
-#pragma unroll 1
-        for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
-          uint32_t rg[32], ru[32];
-          tmem_ld32(taddr + c * 32, rg);
-          tmem_ld32(taddr + HALF + c * 32, ru);
-          tmem_wait_ld();
-          if (row_ok) {
-            const int col = T.n * HALF + c * 32;
-            float g[32], u[32], h[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              g[j] = bf16_round(__uint_as_float(rg[j]));
-              u[j] = bf16_round(__uint_as_float(ru[j]));
-              h[j] = g[j] * sigmoidf_(g[j]) * u[j];
-            }
-            store_bf16x32(gu + col, g);
-            store_bf16x32(gu + p.inter + col, u);
-            store_bf16x32(hh + col, h);
-          }
-        }
-      } else if (EPI == kEpiSwigluBwd) {
-        const long long row = static_cast<long long>(T.m) * BM + row_in;
-        const bool row_ok = row < p.m_valid;
-        const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
-        __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          if (row_ok) {
-            const int col = T.n * BN + c * 32;
-            float g[32], u[32], dg[32], du[32];
-            load_bf16x32(gu + col, g);
-            load_bf16x32(gu + p.inter + col, u);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float dh = bf16_round(__uint_as_float(r[j]));
-              const float sig = sigmoidf_(g[j]);
-              dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
-              du[j] = dh * g[j] * sig;
-            }
-            store_bf16x32(dgu + col, dg);
-            store_bf16x32(dgu + p.inter + col, du);
-          }
-        }
-      } else if (EPI == kEpiSwigluBwdCombine) {
-        // acc = d_out[token] . W_d[e] (unscaled).  dh = bf16(w * acc); the routing
-        // weight's gradient <d_out[token], y[row]> = <acc, h[row]> is summed here;
-        // w * h is written for the down-projection weight gradient.
-        const long long row = static_cast<long long>(T.m) * BM + row_in;
-        const int f = __ldg(p.gather_rows + row);
-        const float w = f >= 0 ? __bfloat162float(p.route_w[f]) : 0.f;
-        const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
-        const __nv_bfloat16* hh = static_cast<const __nv_bfloat16*>(p.aux2) + row * p.ld_aux2;
-        __nv_bfloat16* dgu = static_cast<__nv_bfloat16*>(p.out) + row * p.ld_out;
-        __nv_bfloat16* hw = static_cast<__nv_bfloat16*>(p.out2) + row * p.ld_out2;
-        float dwp = 0.f;
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          const int col = T.n * BN + c * 32;
-          float g[32], u[32], hv[32], dg[32], du[32];
-          load_bf16x32(gu + col, g);
-          load_bf16x32(gu + p.inter + col, u);
-          load_bf16x32(hh + col, hv);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float a = __uint_as_float(r[j]);
-            dwp += a * hv[j];
-            const float dh = bf16_round(w * a);
-            const float sig = sigmoidf_(g[j]);
-            dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
-            du[j] = dh * g[j] * sig;
-            hv[j] *= w;
-          }
-          store_bf16x32(dgu + col, dg);
-          store_bf16x32(dgu + p.inter + col, du);
-          store_bf16x32(hw + col, hv);
-        }
-        p.dw_part[(T.n * 2 + half) * p.part_stride + row] = dwp;
-      } else if (EPI == kEpiStoreF32) {
-        float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
-                   static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-          float4* d = reinterpret_cast<float4*>(o + c * 32);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-            if (p.accumulate) {
-              const float4 old = d[j];
-              v.x += old.x;
-              v.y += old.y;
-              v.z += old.z;
-              v.w += old.w;
-            }
-            d[j] = v;
-          }
-        }
-      } else {  // kEpiStoreF32T
-        float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride + T.m * BM + row_in;
-#pragma unroll 1
-        for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-          uint32_t r[32];
-          tmem_ld32(taddr + c * 32, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = T.n * BN + c * 32 + j;
-            if (col < p.n_valid) {
-              float* dst = o + static_cast<long long>(col) * p.ld_out;
-              const float v = __uint_as_float(r[j]);
-              *dst = p.accumulate ? (*dst + v) : v;
-            }
-          }
-        }
-      }
+      epilogue_tile<EPI, BN>(p, T, row_in, half, taddr);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);

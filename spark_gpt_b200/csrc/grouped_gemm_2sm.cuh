@@ -1,0 +1,374 @@
+// Two-CTA (cta_group::2) variant of the grouped GEMM: a cluster of two CTAs on
+// paired SMs computes a 256 x BN tile with one tcgen05.mma.cta_group::2 per
+// K=16 step.  Each CTA stages its own 128 rows of A and half of B (BN/2 rows,
+// or BN/2 columns for MN-major B), so per unit of MMA work each SM moves a
+// third less operand data through L2 than the single-CTA 128 x BN tile.  For
+// the SwiGLU gate_up tile the B halves are exactly the gate rows (leader) and
+// the up rows (follower), so the accumulator layout and the epilogue are the
+// single-CTA ones.
+//
+// Barrier protocol (both CTAs have the same shared-memory layout):
+//   full[s]   leader only: armed by the leader with both CTAs' bytes; both CTAs'
+//             TMA loads complete on it (.cta_group::2, leader's address)
+//   empty[s]  one per CTA: the leader's MMA commit arrives on both
+//   tfull[a]  one per CTA: the leader's MMA commit arrives on both
+//   tempty[a] leader only: every epilogue warp of both CTAs arrives on it
+//
+// Row-ragged schedule: a pair tile covers two consecutive 128-row tiles of one
+// expert.  An expert with an odd number of 128-row tiles ends in a pair whose
+// second half lies past the expert: that half is computed (on whatever rows it
+// loads) and not stored.
+#pragma once
+
+#include "grouped_gemm.cuh"
+
+namespace b200moe {
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile(
+      "barrier.cluster.arrive.release.aligned;\n\t"
+      "barrier.cluster.wait.acquire.aligned;" ::
+          : "memory");
+}
+
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx_u32(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// TMA tile load into this CTA's shared memory whose completion is counted on
+// the barrier at shared::cluster address `bar_cluster` (the leader's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* tm,
+                                                 uint32_t bar_cluster, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(tm)), "r"(bar_cluster), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                               uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on the barrier at this shared-memory offset in both CTAs of the pair
+// once the issuing thread's prior tcgen05 operations have completed.
+__device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(smem_u32(bar)),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+constexpr int kMaxPairExperts = 512;
+
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr uint32_t kABytes = 128 * 64 * 2;
+  static constexpr uint32_t kBBytes = (BN / 2) * 64 * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kBarrierBytes = 256;
+  static constexpr uint32_t kPairTableBytes = (kMaxPairExperts + 1) * 4;
+  static constexpr uint32_t kTotal = STAGES * kStageBytes + kBarrierBytes + kPairTableBytes + 1024;
+};
+
+// This CTA's 128-row tile of pair tile t.  `half_ok` is false for the second
+// half of an expert's last pair when the expert has an odd tile count.
+template <int SCHED>
+__device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* pair_start,
+                                                int t, uint32_t rank, bool& half_ok) {
+  TileInfo T;
+  half_ok = true;
+  if (SCHED == kRowsRagged) {
+    const int pt = t / p.n_tiles;
+    T.n = t - pt * p.n_tiles;
+    int lo = 0, hi = p.num_groups;  // largest e with pair_start[e] <= pt
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (pair_start[mid] <= pt) lo = mid; else hi = mid;
+    }
+    T.g = lo;
+    const int first_tile = __ldg(p.pad_offsets + lo) / 128;
+    const int ntiles = __ldg(p.pad_offsets + lo + 1) / 128 - first_tile;
+    const int local = 2 * (pt - pair_start[lo]) + static_cast<int>(rank);
+    half_ok = local < ntiles;
+    T.m = first_tile + local;
+    T.krow0 = 0;
+    T.kblocks = p.k_blocks;
+  } else {
+    const int mp = p.m_tiles / 2;
+    const int per = mp * p.n_tiles;
+    T.g = t / per;
+    const int r = t - T.g * per;
+    const int mpair = r / p.n_tiles;
+    T.n = r - mpair * p.n_tiles;
+    T.m = 2 * mpair + static_cast<int>(rank);
+    const int s = __ldg(p.pad_offsets + T.g);
+    const int e = __ldg(p.pad_offsets + T.g + 1);
+    T.krow0 = s;
+    T.kblocks = (e - s) / 64;
+  }
+  return T;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                             const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  static_assert(BN == 128 || BN == 256, "BN");
+  static_assert(SCHED == kRowsRagged ? !A_MN : (A_MN && B_MN), "operand majors vs schedule");
+  constexpr int BM = 128;
+  constexpr int BK = 64;
+  using S = PairSmem<BN, STAGES>;
+  constexpr uint32_t kTmemCols = TmemCols<BN>::value;
+  constexpr uint32_t kIdesc = make_idesc_bf16(2 * BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * S::kABytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + STAGES;
+  uint64_t* tfull = bars + 2 * STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* pair_start = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + S::kBarrierBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster_id = blockIdx.x >> 1;
+  const int num_clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpilogueWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (SCHED == kRowsRagged && warp == 2) {
+    // pair_start[e] = pairs of the experts before e (a 32-lane scan over E)
+    int carry = 0;
+    for (int e0 = 0; e0 <= p.num_groups; e0 += 32) {
+      const int e = e0 + lane;
+      int v = 0;
+      if (e < p.num_groups) {
+        const int nt = (__ldg(p.pad_offsets + e + 1) - __ldg(p.pad_offsets + e)) / 128;
+        v = (nt + 1) / 2;
+      }
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (e <= p.num_groups) pair_start[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  int num_tiles;
+  if (SCHED == kRowsRagged) {
+    num_tiles = pair_start[p.num_groups] * p.n_tiles;
+  } else {
+    num_tiles = p.num_groups * (p.m_tiles / 2) * p.n_tiles;
+  }
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+        bool half_ok;
+        const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
+        for (int kb = 0; kb < T.kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&full[stage]), 0);
+          if (leader) mbar_expect_tx_u32(smem_u32(&full[stage]), 2 * S::kStageBytes);
+          uint8_t* a = sA + stage * S::kABytes;
+          uint8_t* b = sB + stage * S::kBBytes;
+          if (!A_MN) {
+            tma_load_2d_pair(a, &tmA, full_leader, kb * BK, T.m * BM);
+          } else {
+            const int krow = T.krow0 + kb * BK;
+            tma_load_2d_pair(a, &tmA, full_leader, T.m * BM, krow);
+            tma_load_2d_pair(a + 8192, &tmA, full_leader, T.m * BM + 64, krow);
+          }
+          if (!B_MN) {
+            // this CTA's BN/2 rows of B: the gate (leader) or up (follower) rows for
+            // SwiGLU, else the leader's or follower's half of the BN rows
+            const int row = (EPI == kEpiSwigluFwd)
+                                ? T.g * p.b_group_rows + static_cast<int>(rank) * p.b_half_offset +
+                                      T.n * (BN / 2)
+                                : T.g * p.b_group_rows + T.n * BN + static_cast<int>(rank) * (BN / 2);
+            tma_load_2d_pair(b, &tmB, full_leader, kb * BK, row);
+          } else {
+            const int krow =
+                (SCHED == kKRagged) ? (T.krow0 + kb * BK) : (T.g * p.b_group_rows + kb * BK);
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j)
+              tma_load_2d_pair(b + j * 8192, &tmB, full_leader,
+                               T.n * BN + static_cast<int>(rank) * (BN / 2) + 64 * j, krow);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // tail: wait until the MMA's releases of every stage this CTA filled have
+      // landed, so no commit arrives on this CTA's barriers after it exits
+      for (int i = 0; ok && i < STAGES; ++i) {
+        if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) break;
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
+        bool half_ok;
+        const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
+        if (T.kblocks == 0) continue;
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        ++local;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < T.kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
+          const uint32_t b0 = smem_u32(sB + stage * S::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad =
+                A_MN ? make_sdesc(a0 + kk * 2048, 8192, 1024) : make_sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd =
+                B_MN ? make_sdesc(b0 + kk * 2048, 8192, 1024) : make_sdesc(b0 + kk * 32, 16, 1024);
+            umma_bf16_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair_both(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) umma_commit_pair_both(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row_in = q * 32 + lane;
+    int local = 0;
+    for (int t = cluster_id; t < num_tiles; t += num_clusters) {
+      bool half_ok;
+      const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
+      if (T.kblocks == 0) {
+        epilogue_empty_tile<EPI, BN>(p, T, row_in, half);
+        continue;
+      }
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      ++local;
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
+      if (half_ok) epilogue_tile<EPI, BN>(p, T, row_in, half, taddr);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace b200moe

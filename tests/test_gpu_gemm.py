@@ -230,3 +230,41 @@ def test_token_major_outputs_equal_padded(ops, T, k, E, H, I):
     x0 = ops.gate_up_dgrad(d_gu, wgu, d)
     x1 = ops.gate_up_dgrad(d_gu, wgu, d, token_major=True)
     assert torch.equal(x1[rf[rf >= 0]], x0[:n][rf >= 0])
+
+
+@pytest.mark.parametrize("T,k,E,H,I", SHAPES + [(3000, 8, 64, 1024, 256)])
+def test_pair_tiles_equal_single_cta_tiles(ops, T, k, E, H, I):
+    """The two-CTA (cta_group::2) 256-row pair kernel gives exactly the
+    single-CTA kernel's results on every expert GEMM, including experts with an
+    odd number of 128-row tiles (half-valid last pair) and empty experts."""
+    from spark_gpt_b200 import _lib
+    d, x, xs, wgu, wd = _setup(ops, T, k, E, H, I, 10)
+    n = int(d.pad_offsets[-1])
+    rows = d.row_flat.clone()
+    rows[n:] = -1
+    dy = torch.randn(d.rows_cap, H, device=DEV).to(torch.bfloat16)
+    dy[rows < 0] = 0
+    d_gu = torch.randn(d.rows_cap, 2 * I, device=DEV).to(torch.bfloat16)
+    d_gu[rows < 0] = 0
+
+    def run():
+        gu, h = ops.gate_up_fwd(xs, wgu, d)
+        y = ops.down_fwd(h, wd, d)
+        dg = ops.down_dgrad_swiglu(dy, wd, gu, d)
+        dxs = ops.gate_up_dgrad(d_gu, wgu, d)
+        w1 = ops.wgrad(d_gu, xs, d)
+        w2 = ops.wgrad(dy, h, d)
+        torch.cuda.synchronize()
+        return [t[:n] for t in (gu, h, y, dg, dxs)] + [w1, w2]
+
+    prev = _lib.load().b200moe_set_pair_gemm(0)
+    try:
+        single = run()
+        _lib.load().b200moe_set_pair_gemm(1)
+        pair = run()
+    finally:
+        _lib.load().b200moe_set_pair_gemm(prev)
+    assert _lib.read_fault() == 0
+    names = ["gu", "h", "y", "d_gu", "dxs", "dW_gate_up", "dW_down"]
+    for name, a, b in zip(names, single, pair):
+        assert torch.equal(a, b), name
