@@ -119,11 +119,13 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
 int g_pair_gemm = 1;
 
 template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
-int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                     cudaStream_t st, const char* what) {
-  constexpr int STAGES = 6;
+int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to0,
+                     const CUtensorMap& to1, const GemmParams& p, cudaStream_t st,
+                     const char* what) {
+  constexpr bool kTmaOut = TmaOut<EPI>::value;
+  constexpr int STAGES = kTmaOut ? (BN == 256 ? 4 : 5) : 6;
   auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
-  const int smem = static_cast<int>(PairSmem<BN, STAGES>::kTotal);
+  const int smem = static_cast<int>(PairSmem<BN, STAGES, kTmaOut>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
@@ -138,7 +140,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmPar
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  e = cudaLaunchKernelEx(&cfg, kern, ta, tb, to0, to1, p);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   return check_launch(what);
 }
@@ -152,13 +154,38 @@ bool use_pair(int BN, int sched, int num_groups, int m_tiles) {
          (sched == kRowsRagged || m_tiles % 2 == 0);
 }
 
+// Output tensor maps of the pair kernel's TMA-store epilogue: a {32, 32} box
+// with the 64-byte swizzle over a (rows, cols) bf16 matrix.
+int make_out_tmap(CUtensorMap* m, const void* base, long long cols, long long rows,
+                  const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
 int launch_expert_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-                       cudaStream_t st, const char* what) {
+                       cudaStream_t st, const char* what, const CUtensorMap* to0 = nullptr,
+                       const CUtensorMap* to1 = nullptr) {
   if constexpr (BN >= 128) {
     if (use_pair(BN, SCHED, p.num_groups, p.m_tiles) &&
-        (SCHED == kKRagged || p.pad_offsets != nullptr))
-      return launch_gemm_pair<BN, A_MN, B_MN, EPI, SCHED>(ta, tb, p, st, what);
+        (SCHED == kKRagged || p.pad_offsets != nullptr)) {
+      if (TmaOut<EPI>::value && p.scatter_rows == nullptr && to0 == nullptr)
+        return fail(B200MOE_ERR_INVALID_ARG, "%s: missing output tensor map", what);
+      return launch_gemm_pair<BN, A_MN, B_MN, EPI, SCHED>(ta, tb, to0 ? *to0 : ta,
+                                                         to1 ? *to1 : (to0 ? *to0 : ta), p, st,
+                                                         what);
+    }
   }
   return launch_gemm<BN, A_MN, B_MN, EPI, SCHED>(ta, tb, p, st, what);
 }
@@ -644,8 +671,12 @@ int b200moe_expert_gate_up_fwd(const void* xs, const void* w_gu, const int* tile
   p.ld_out2 = I;
   p.inter = I;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (half == 128) return launch_expert_gemm<256, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
-  return launch_expert_gemm<128, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd");
+  CUtensorMap to0, to1;
+  if ((rc = make_out_tmap(&to0, gu, 2LL * I, rows_cap, "gate_up_fwd gu"))) return rc;
+  if ((rc = make_out_tmap(&to1, h, I, rows_cap, "gate_up_fwd h"))) return rc;
+  if (half == 128)
+    return launch_expert_gemm<256, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd", &to0, &to1);
+  return launch_expert_gemm<128, false, false, kEpiSwigluFwd, kRowsRagged>(ta, tb, p, st, "gate_up_fwd", &to0, &to1);
 }
 
 int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expert,
@@ -673,8 +704,14 @@ int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expe
   p.ld_out = H;
   p.scatter_rows = row_flat_out;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_expert_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
-  return launch_expert_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd");
+  CUtensorMap to0;
+  const CUtensorMap* o0 = nullptr;
+  if (row_flat_out == nullptr) {
+    if ((rc = make_out_tmap(&to0, y, H, rows_cap, "down_fwd y"))) return rc;
+    o0 = &to0;
+  }
+  if (BN == 256) return launch_expert_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd", o0);
+  return launch_expert_gemm<128, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd", o0);
 }
 
 int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void* gu,
@@ -705,8 +742,10 @@ int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void
   p.ld_aux = 2 * I;
   p.inter = I;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
-  if (BN == 128) return launch_expert_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
+  CUtensorMap to0;
+  if ((rc = make_out_tmap(&to0, d_gu, 2LL * I, rows_cap, "down_dgrad d_gu"))) return rc;
+  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad", &to0);
+  if (BN == 128) return launch_expert_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad", &to0);
   return launch_expert_gemm<64, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
 }
 
@@ -736,8 +775,14 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* 
   p.ld_out = H;
   p.scatter_rows = row_flat_out;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
-  return launch_expert_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad");
+  CUtensorMap to0;
+  const CUtensorMap* o0 = nullptr;
+  if (row_flat_out == nullptr) {
+    if ((rc = make_out_tmap(&to0, dxs, H, rows_cap, "gate_up_dgrad dxs"))) return rc;
+    o0 = &to0;
+  }
+  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad", o0);
+  return launch_expert_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad", o0);
 }
 
 int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets, int E,

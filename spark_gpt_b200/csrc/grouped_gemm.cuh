@@ -375,6 +375,109 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
     }
   }
 }
+// ---------------------------------------------------------------------------
+// Epilogue through shared memory + TMA stores: each warp owns a ring of four
+// 2 KB buffers; a 32-row x 32-column bf16 chunk of its rows is written there
+// (64-byte swizzle, conflict-free) and stored with one TMA tensor store, so
+// global writes are full, coalesced rows and asynchronous.  The output tensor
+// maps have a {32, 32} box and the 64-byte swizzle.
+// ---------------------------------------------------------------------------
+struct OutRing {
+  uint8_t* base;  // 4 x 2048 bytes, 512-byte aligned
+  int next;
+};
+
+__device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap* tm,
+                                                const float* v, int lane, int col, int row0) {
+  uint8_t* buf = ring.base + ring.next * 2048;
+  if (lane == 0) bulk_wait_group_read<3>();  // the store issued 4 chunks ago has read buf
+  __syncwarp();
+  uint4* rowp = reinterpret_cast<uint4*>(buf + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16x2(v[8 * j + 0], v[8 * j + 1]);
+    w.y = pack_bf16x2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16x2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
+    rowp[j ^ sw] = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d(tm, buf, col, row0);
+    bulk_commit_group();
+  }
+  ring.next = (ring.next + 1) & 3;
+}
+
+// The bf16-output epilogues (plain store, SwiGLU forward, SwiGLU backward) with
+// TMA stores.  Outputs: O0 = out (or gu / d_gu), O1 = h (SwiGLU forward).
+template <int EPI, int BN>
+__device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const TileInfo& T,
+                                                  int quarter, int lane, int half,
+                                                  uint32_t taddr, const CUtensorMap* tmO0,
+                                                  const CUtensorMap* tmO1, OutRing& ring) {
+  constexpr int BM = 128;
+  const int row0 = T.m * BM + quarter * 32;
+  if (EPI == kEpiStoreBf16) {
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      store_chunk_tma(ring, tmO0, v, lane, T.n * BN + c * 32, row0);
+    }
+  } else if (EPI == kEpiSwigluFwd) {
+    constexpr int HALF = BN / 2;
+#pragma unroll 1
+    for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(taddr + c * 32, rg);
+      tmem_ld32(taddr + HALF + c * 32, ru);
+      tmem_wait_ld();
+      const int col = T.n * HALF + c * 32;
+      float g[32], u[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        g[j] = bf16_round(__uint_as_float(rg[j]));
+        u[j] = bf16_round(__uint_as_float(ru[j]));
+      }
+      store_chunk_tma(ring, tmO0, g, lane, col, row0);
+      store_chunk_tma(ring, tmO0, u, lane, p.inter + col, row0);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) g[j] = g[j] * sigmoidf_(g[j]) * u[j];
+      store_chunk_tma(ring, tmO1, g, lane, col, row0);
+    }
+  } else {  // kEpiSwigluBwd
+    const long long row = static_cast<long long>(row0) + lane;
+    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col = T.n * BN + c * 32;
+      float g[32], u[32], dg[32];
+      load_bf16x32(gu + col, g);
+      load_bf16x32(gu + p.inter + col, u);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float dh = bf16_round(__uint_as_float(r[j]));
+        const float sig = sigmoidf_(g[j]);
+        dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+        u[j] = dh * g[j] * sig;  // d_up, reusing u's registers
+      }
+      store_chunk_tma(ring, tmO0, dg, lane, col, row0);
+      store_chunk_tma(ring, tmO0, u, lane, p.inter + col, row0);
+    }
+  }
+}
+
 constexpr int kEpilogueWarps = 8;
 constexpr int kGemmThreads = 64 + 32 * kEpilogueWarps;
 

@@ -103,14 +103,23 @@ __device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
 
 constexpr int kMaxPairExperts = 512;
 
-template <int BN, int STAGES>
+// Epilogues whose bf16 output goes through shared memory and TMA stores.
+template <int EPI>
+struct TmaOut {
+  static constexpr bool value =
+      EPI == kEpiStoreBf16 || EPI == kEpiSwigluFwd || EPI == kEpiSwigluBwd;
+};
+
+template <int BN, int STAGES, bool TMA_OUT>
 struct PairSmem {
   static constexpr uint32_t kABytes = 128 * 64 * 2;
   static constexpr uint32_t kBBytes = (BN / 2) * 64 * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t kOutBytes = TMA_OUT ? kEpilogueWarps * 4 * 2048 : 0;
   static constexpr uint32_t kBarrierBytes = 256;
   static constexpr uint32_t kPairTableBytes = (kMaxPairExperts + 1) * 4;
-  static constexpr uint32_t kTotal = STAGES * kStageBytes + kBarrierBytes + kPairTableBytes + 1024;
+  static constexpr uint32_t kTotal =
+      STAGES * kStageBytes + kOutBytes + kBarrierBytes + kPairTableBytes + 1024;
 };
 
 // This CTA's 128-row tile of pair tile t.  `half_ok` is false for the second
@@ -155,12 +164,15 @@ __device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* 
 template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
-                             const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                             const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmO0,
+                             const __grid_constant__ CUtensorMap tmO1, const GemmParams p) {
   static_assert(BN == 128 || BN == 256, "BN");
   static_assert(SCHED == kRowsRagged ? !A_MN : (A_MN && B_MN), "operand majors vs schedule");
   constexpr int BM = 128;
   constexpr int BK = 64;
-  using S = PairSmem<BN, STAGES>;
+  constexpr bool kTmaOut = TmaOut<EPI>::value;
+  using S = PairSmem<BN, STAGES, kTmaOut>;
   constexpr uint32_t kTmemCols = TmemCols<BN>::value;
   constexpr uint32_t kIdesc = make_idesc_bf16(2 * BM, BN, A_MN, B_MN);
 
@@ -169,7 +181,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * S::kBBytes);
+  uint8_t* sOut = sB + STAGES * S::kBBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + S::kOutBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
@@ -220,6 +233,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (kTmaOut) {
+      tma_prefetch_desc(&tmO0);
+      tma_prefetch_desc(&tmO1);
+    }
   }
   if (warp == 1) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
@@ -342,6 +359,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in = q * 32 + lane;
+    OutRing ring{sOut + (warp - 2) * 4 * 2048, 0};
+    const bool tma_out = kTmaOut && p.scatter_rows == nullptr;
     int local = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {
       bool half_ok;
@@ -356,11 +375,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
-      if (half_ok) epilogue_tile<EPI, BN>(p, T, row_in, half, taddr);
+      if (half_ok) {
+        if (tma_out)
+          epilogue_tile_tma<EPI, BN>(p, T, q, lane, half, taddr, &tmO0, &tmO1, ring);
+        else
+          epilogue_tile<EPI, BN>(p, T, row_in, half, taddr);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
     }
+    if (kTmaOut && lane == 0) bulk_wait_group_all();  // stores done before exit
   }
 
   __syncthreads();
