@@ -54,7 +54,7 @@ AUX_COEF = 1e-3
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--config", default="cfg2", choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
@@ -125,59 +125,90 @@ def make_tokens(c, T, seed):
 # clocks
 # --------------------------------------------------------------------------- #
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled during the timed region: NVML
+    every 20 ms (read-only queries), nvidia-smi at 200 ms if NVML is missing."""
 
-    def __init__(self, index):
-        self.index = index
-        self.proc = None
-        self.lines = []
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40,
+               "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []  # (sm_mhz, reasons bitmask)
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._proc = None
+
+    def _nvml_loop(self, nvml, h):
+        while not self._stop.is_set():
+            try:
+                sm = nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM)
+                rs = nvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.samples.append((float(sm), int(rs)))
+            except Exception:  # noqa: BLE001 - sampling is best effort
+                pass
+            self._stop.wait(0.02)
+
+    def _smi_loop(self):
+        for line in self._proc.stdout:
+            parts = [x.strip() for x in line.split(",")]
+            try:
+                mask = 0
+                for name, bit in zip(["hw_slowdown", "hw_thermal_slowdown",
+                                      "sw_thermal_slowdown", "sw_power_cap"], parts[2:6]):
+                    if bit.lower() == "active":
+                        mask |= self.REASONS[name]
+                self.samples.append((float(parts[0]), mask))
+                self.max_mhz = float(parts[1])
+            except (ValueError, IndexError):
+                continue
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
-            self.thread.start()
-        except (OSError, ValueError):
-            self.proc = None
+            import pynvml as nvml
+            nvml.nvmlInit()
+            pr = torch.cuda.get_device_properties(self.device)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            h = nvml.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = float(nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM))
+            self._thread = threading.Thread(target=self._nvml_loop, args=(nvml, h), daemon=True)
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            try:
+                self._proc = subprocess.Popen(
+                    ["nvidia-smi", "-i", str(torch.cuda.current_device()),
+                     "--query-gpu=clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+                     "clocks_event_reasons.hw_thermal_slowdown,"
+                     "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
+                     "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                self._thread = threading.Thread(target=self._smi_loop, daemon=True)
+            except (OSError, ValueError):
+                self._thread = None
+        if self._thread is not None:
+            self._thread.start()
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
+        self._stop.set()
+        if self._proc is not None:
+            self._proc.terminate()
             try:
-                self.proc.wait(timeout=5)
+                self._proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.thread.join(timeout=5)
+                self._proc.kill()
+        if self._thread is not None:
+            self._thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mask = 0
+        for _, m in self.samples:
+            mask |= m
+        return {"sm_mhz": statistics.median(s for s, _ in self.samples),
+                "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(n for n, bit in self.REASONS.items() if mask & bit),
+                "samples": len(self.samples)}
 
 
 # --------------------------------------------------------------------------- #
@@ -317,7 +348,7 @@ def main():
     torch.cuda.synchronize()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(dev) as clocks:
         ev0.record()
         for _ in range(args.steps):
             step(x, d_out)

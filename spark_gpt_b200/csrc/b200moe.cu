@@ -123,7 +123,10 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
                      const CUtensorMap& to1, const GemmParams& p, cudaStream_t st,
                      const char* what) {
   constexpr bool kTmaOut = TmaOut<EPI>::value;
-  constexpr int STAGES = kTmaOut ? (BN == 256 ? 4 : 5) : 6;
+#ifndef B200MOE_PAIR_STAGES_TMA
+#define B200MOE_PAIR_STAGES_TMA 4
+#endif
+  constexpr int STAGES = kTmaOut ? (BN == 256 ? B200MOE_PAIR_STAGES_TMA : 5) : 6;
   auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
   const int smem = static_cast<int>(PairSmem<BN, STAGES, kTmaOut>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -562,9 +565,17 @@ int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offse
                         int H, long long rows_cap, void* xs, void* stream) {
   REQUIRE(x && row_flat && pad_offsets && xs, "gather_rows: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1, "gather_rows: H must be a multiple of 8");
-  gather_rows_kernel<<<grid_for(rows_cap, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), row_flat, pad_offsets + E, k, H,
-      static_cast<__nv_bfloat16*>(xs));
+  auto* xp = static_cast<const __nv_bfloat16*>(x);
+  auto* xsp = static_cast<__nv_bfloat16*>(xs);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(rows_cap, 8);
+  switch (H) {
+    case 256: gather_rows_kernel<1><<<grid, 256, 0, st>>>(xp, row_flat, pad_offsets + E, k, H, xsp); break;
+    case 512: gather_rows_kernel<2><<<grid, 256, 0, st>>>(xp, row_flat, pad_offsets + E, k, H, xsp); break;
+    case 1024: gather_rows_kernel<4><<<grid, 256, 0, st>>>(xp, row_flat, pad_offsets + E, k, H, xsp); break;
+    case 2048: gather_rows_kernel<8><<<grid, 256, 0, st>>>(xp, row_flat, pad_offsets + E, k, H, xsp); break;
+    default: gather_rows_kernel<0><<<grid, 256, 0, st>>>(xp, row_flat, pad_offsets + E, k, H, xsp); break;
+  }
   return check_launch("gather_rows");
 }
 
@@ -625,9 +636,17 @@ int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat, c
         static_cast<const __nv_bfloat16*>(weights), R, k, H, dyp, d_weights);
     return check_launch("combine_bwd");
   }
-  combine_bwd_kernel<<<grid_for(rows_cap, 8), 256, 0, st>>>(
-      static_cast<const __nv_bfloat16*>(d_out), static_cast<const __nv_bfloat16*>(y), row_flat,
-      pad_offsets + E, static_cast<const __nv_bfloat16*>(weights), k, H, dyp, d_weights);
+  auto* dop = static_cast<const __nv_bfloat16*>(d_out);
+  auto* yp = static_cast<const __nv_bfloat16*>(y);
+  auto* wp = static_cast<const __nv_bfloat16*>(weights);
+  const int grid = grid_for(rows_cap, 8);
+  switch (H) {
+    case 256: combine_bwd_kernel<1><<<grid, 256, 0, st>>>(dop, yp, row_flat, pad_offsets + E, wp, k, H, dyp, d_weights); break;
+    case 512: combine_bwd_kernel<2><<<grid, 256, 0, st>>>(dop, yp, row_flat, pad_offsets + E, wp, k, H, dyp, d_weights); break;
+    case 1024: combine_bwd_kernel<4><<<grid, 256, 0, st>>>(dop, yp, row_flat, pad_offsets + E, wp, k, H, dyp, d_weights); break;
+    case 2048: combine_bwd_kernel<8><<<grid, 256, 0, st>>>(dop, yp, row_flat, pad_offsets + E, wp, k, H, dyp, d_weights); break;
+    default: combine_bwd_kernel<0><<<grid, 256, 0, st>>>(dop, yp, row_flat, pad_offsets + E, wp, k, H, dyp, d_weights); break;
+  }
   return check_launch("combine_bwd");
 }
 

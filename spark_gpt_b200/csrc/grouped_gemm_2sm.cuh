@@ -115,7 +115,7 @@ struct PairSmem {
   static constexpr uint32_t kABytes = 128 * 64 * 2;
   static constexpr uint32_t kBBytes = (BN / 2) * 64 * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
-  static constexpr uint32_t kOutBytes = TMA_OUT ? kEpilogueWarps * 4 * 2048 : 0;
+  static constexpr uint32_t kOutBytes = TMA_OUT ? kEpilogueWarps * kOutRing * 2048 : 0;
   static constexpr uint32_t kBarrierBytes = 256;
   static constexpr uint32_t kPairTableBytes = (kMaxPairExperts + 1) * 4;
   static constexpr uint32_t kTotal =
@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row_in = q * 32 + lane;
-    OutRing ring{sOut + (warp - 2) * 4 * 2048, 0};
+    OutRing ring{sOut + (warp - 2) * kOutRing * 2048, 0};
     const bool tma_out = kTmaOut && p.scatter_rows == nullptr;
     int local = 0;
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {

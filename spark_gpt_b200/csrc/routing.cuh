@@ -182,6 +182,10 @@ __global__ void dispatch_scatter_kernel(const long long* __restrict__ sel, long 
 // ---------------------------------------------------------------------------
 // gather (train.py:2195-2217): xs[p] = x[row_flat[p] / k], zero for padding
 // ---------------------------------------------------------------------------
+// VPL = 16-byte vectors per lane per row (H = 256 * VPL); every load of a row
+// is issued before the first store, so a warp keeps VPL loads in flight.
+// VPL == 0: any H (multiple of 8), one vector at a time.
+template <int VPL>
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
                                    const int* __restrict__ row_flat,
                                    const int* __restrict__ total_rows, int k, int H,
@@ -194,8 +198,15 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
        r < total; r += warps) {
     const int f = row_flat[r];
     uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
-    if (f >= 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(f / k) * H);
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(f < 0 ? 0 : f / k) * H);
+    if (VPL > 0) {
+      uint4 v[VPL > 0 ? VPL : 1];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j)
+        v[j] = f >= 0 ? __ldg(src + lane + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) dst[lane + 32 * j] = v[j];
+    } else if (f >= 0) {
       for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
     } else {
       const uint4 z = make_uint4(0u, 0u, 0u, 0u);
@@ -296,6 +307,7 @@ __global__ void combine_fwd_kernel(const __nv_bfloat16* __restrict__ y,
   }
 }
 
+template <int VPL>
 __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ d_out,
                                    const __nv_bfloat16* __restrict__ y,
                                    const int* __restrict__ row_flat,
@@ -319,9 +331,7 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ d_out,
     const uint4* g = reinterpret_cast<const uint4*>(d_out + static_cast<long long>(f / k) * H);
     const uint4* yy = reinterpret_cast<const uint4*>(y + r * H);
     float dot = 0.f;
-    for (int v = lane; v < nvec; v += 32) {
-      const uint4 a = __ldg(g + v);
-      const uint4 b = __ldg(yy + v);
+    auto one = [&](const uint4 a, const uint4 b, int v) {
       float ga[8] = {bf16_lo(a.x), bf16_hi(a.x), bf16_lo(a.y), bf16_hi(a.y),
                      bf16_lo(a.z), bf16_hi(a.z), bf16_lo(a.w), bf16_hi(a.w)};
       float yb[8] = {bf16_lo(b.x), bf16_hi(b.x), bf16_lo(b.y), bf16_hi(b.y),
@@ -334,6 +344,18 @@ __global__ void combine_bwd_kernel(const __nv_bfloat16* __restrict__ d_out,
       o.z = pack_bf16x2(ga[4] * w, ga[5] * w);
       o.w = pack_bf16x2(ga[6] * w, ga[7] * w);
       dst[v] = o;
+    };
+    if (VPL > 0) {
+      uint4 a[VPL > 0 ? VPL : 1], b[VPL > 0 ? VPL : 1];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        a[j] = __ldg(g + lane + 32 * j);
+        b[j] = __ldg(yy + lane + 32 * j);
+      }
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) one(a[j], b[j], lane + 32 * j);
+    } else {
+      for (int v = lane; v < nvec; v += 32) one(__ldg(g + v), __ldg(yy + v), v);
     }
     dot = warp_sum(dot);
     if (lane == 0) d_weights[f] = dot;
