@@ -1,0 +1,108 @@
+"""Expert-parallel layer on 2 GPUs over NCCL against the single-GPU layer.
+
+Each rank holds half of the experts; its output, input gradient and router
+gradient must equal spark_gpt_b200.SparseMoE (all experts on one GPU) on the
+same tokens: bit for bit for the output and input gradient (the same bf16
+products in the same order), within fp32 summation-order noise for the
+weight gradients (rows of an expert arrive in a different order).  Runs as two
+spawned processes; skipped where fewer than two GPUs are visible.
+"""
+
+import os
+import socket
+from types import SimpleNamespace
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+T, H, E, K, I = 2048, 1024, 16, 4, 256
+
+
+def _cfg():
+    return SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=K,
+                           moe_intermediate_size=I, norm_topk_prob=True)
+
+
+def _weights():
+    g = torch.Generator().manual_seed(3)
+    return (torch.randn(E, H, generator=g) * 0.05, torch.randn(E, 2 * I, H, generator=g) * 0.01,
+            torch.randn(E, H, I, generator=g) * 0.01)
+
+
+def _inputs(rank):
+    g = torch.Generator().manual_seed(40 + rank)
+    return (torch.randn(T, H, generator=g).to(torch.bfloat16),
+            (torch.randn(T, H, generator=g) * 1e-2).to(torch.bfloat16))
+
+
+def _worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    from datetime import timedelta
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=timedelta(seconds=60))
+    try:
+        from spark_gpt_b200 import SparseMoE
+        from spark_gpt_b200.ep import ExpertParallelMoE
+        w_r, w_gu, w_d = _weights()
+        ep = ExpertParallelMoE(_cfg()).to(dev)
+        lo, hi = ep.expert_offset, ep.expert_offset + ep.local_experts
+        ref = SparseMoE(_cfg()).to(dev)
+        with torch.no_grad():
+            for m in (ep, ref):
+                m.gate.weight.copy_(w_r)
+            ep.experts.gate_up_proj.copy_(w_gu[lo:hi])
+            ep.experts.down_proj.copy_(w_d[lo:hi])
+            ref.experts.gate_up_proj.copy_(w_gu)
+            ref.experts.down_proj.copy_(w_d)
+        x, d_out = _inputs(rank)
+        x, d_out = x.to(dev), d_out.to(dev)
+        outs = {}
+        for name, m in (("ep", ep), ("ref", ref)):
+            xin = x.clone().requires_grad_(True)
+            out, logits, sel = m(xin)
+            out.backward(d_out)
+            outs[name] = (out.detach().cpu(), sel.cpu(), xin.grad.cpu(), m.gate.weight.grad.cpu())
+        gu_sum = ref.experts.gate_up_proj.grad.clone()
+        d_sum = ref.experts.down_proj.grad.clone()
+        dist.all_reduce(gu_sum)
+        dist.all_reduce(d_sum)
+        torch.cuda.synchronize()
+        results[rank] = {"ep": outs["ep"], "ref": outs["ref"],
+                         "ep_gu": ep.experts.gate_up_proj.grad.cpu(),
+                         "ep_d": ep.experts.down_proj.grad.cpu(),
+                         "ref_gu": gu_sum[lo:hi].cpu(), "ref_d": d_sum[lo:hi].cpu()}
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_expert_parallel_two_gpus_matches_single_gpu_layer():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_worker, args=(2, _free_port(), results), nprocs=2, join=True,
+                       start_method="spawn")
+    for rank in range(2):
+        r = results[rank]
+        (o_ep, s_ep, dx_ep, dr_ep), (o_ref, s_ref, dx_ref, dr_ref) = r["ep"], r["ref"]
+        assert torch.equal(s_ep, s_ref)
+        assert torch.equal(o_ep, o_ref)
+        assert torch.equal(dx_ep, dx_ref)
+        torch.testing.assert_close(dr_ep, dr_ref, rtol=1e-4, atol=1e-5)
+        scale = r["ref_gu"].abs().max().item()
+        torch.testing.assert_close(r["ep_gu"], r["ref_gu"], rtol=1e-3, atol=1e-3 * scale)
+        scale = r["ref_d"].abs().max().item()
+        torch.testing.assert_close(r["ep_d"], r["ref_d"], rtol=1e-3, atol=1e-3 * scale)
