@@ -21,17 +21,10 @@ import torch
 import torch.nn as nn
 
 from . import ops
+from .custom_ops import TOKEN_MAJOR, sparse_moe
 
 BF16 = torch.bfloat16
 
-# Layout of the down-projection output y and of the gate_up input gradient
-# dxs: token-major (slot t*k+s in row t*k+s, so the combine and the gather
-# backward read each token's k rows as one contiguous block) or padded-row
-# order (the GEMMs write rows sequentially).  Measured on B200 at config 2:
-# the shared-memory row reduction reads scattered 2 KB rows as fast as
-# contiguous ones, while scattered epilogue writes slow the two GEMMs, so the
-# padded order is the default.
-TOKEN_MAJOR = False
 
 
 def _require_cuda(*ts):
@@ -62,67 +55,6 @@ def _extra_logit_grad(d_logits, T, W):
     buf = torch.zeros(T, W, device=d_logits.device, dtype=BF16)
     buf[:, : d_logits.shape[1]] = d_logits
     return buf
-
-
-class _SparseMoEFn(torch.autograd.Function):
-    """Router + experts + combine as one autograd node (train.py:2331-2334).
-
-    Forward: router GEMM -> softmax/top-k -> dispatch -> row gather -> gate_up
-    GEMM (+SwiGLU) -> down GEMM -> weighted combine.  Backward mirrors it and
-    folds the router's input gradient into the gather backward.  (The
-    tile::gather4 variants in ops.py read x / d_out rows inside the GEMMs
-    instead of materialising xs / dy; on B200 their per-row TMA requests ran
-    slower than the streaming gather kernels, so this path materialises.)"""
-
-    @staticmethod
-    def forward(ctx, x, w_router, w_gate_up, w_down, top_k, norm):
-        _require_cuda(x, w_router, w_gate_up, w_down)
-        T, H = x.shape
-        E = w_gate_up.shape[0]
-        W = ops.router_width(E)
-        xb = _as_bf16(x)
-        wr = ops.cast_bf16(w_router, W)
-        wgu = ops.cast_bf16(w_gate_up)
-        wd = ops.cast_bf16(w_down)
-        logits_buf = ops.router_logits(xb, wr)
-        sel, rw = ops.router_topk(logits_buf, E, top_k, norm)
-        d = ops.dispatch(sel, E)
-        xs = ops.gather_rows(xb, d)
-        gu, h = ops.gate_up_fwd(xs, wgu, d)
-        y = ops.down_fwd(h, wd, d, token_major=TOKEN_MAJOR)
-        out = ops.combine(y, d, rw, token_major=TOKEN_MAJOR)
-        ctx.save_for_backward(xb, wr, wgu, wd, logits_buf, sel, rw, xs, gu, h, y)
-        ctx.dispatch = d
-        ctx.cfg = (E, W, top_k, norm, x.dtype)
-        ctx.mark_non_differentiable(sel)
-        logits = logits_buf if W == E else logits_buf[:, :E]
-        return out.to(x.dtype), logits, sel
-
-    @staticmethod
-    def backward(ctx, d_out, d_logits, _d_sel):
-        xb, wr, wgu, wd, logits_buf, sel, rw, xs, gu, h, y = ctx.saved_tensors
-        d = ctx.dispatch
-        E, W, top_k, norm, xdtype = ctx.cfg
-        T = xb.shape[0]
-        w_router, w_gate_up, w_down = ctx.needs_input_grad[1:4]
-        if d_out is None:
-            d_out = torch.zeros(T, xb.shape[1], device=xb.device, dtype=BF16)
-        d_out = _as_bf16(d_out)
-        dy, d_rw = ops.combine_bwd(d_out, y, d, rw, token_major=TOKEN_MAJOR)
-        del y
-        d_gu = ops.down_dgrad_swiglu(dy, wd, gu, d)
-        del gu
-        g_down = ops.wgrad(dy, h, d, name="down_wgrad") if w_down else None
-        del dy, h
-        dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
-        g_gate_up = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad") if w_gate_up else None
-        del d_gu, xs
-        extra = _extra_logit_grad(d_logits, T, W)
-        dl = ops.router_topk_bwd(logits_buf, sel, d_rw, extra, E, top_k, norm)
-        dx_router = ops.router_dgrad(dl, wr)
-        dx = ops.gather_rows_bwd(dxs, d, addend=dx_router, token_major=TOKEN_MAJOR)
-        g_router = ops.router_wgrad(xb, dl, E) if w_router else None
-        return dx.to(xdtype), g_router, g_gate_up, g_down, None, None
 
 
 class _RouterFn(torch.autograd.Function):
@@ -244,7 +176,8 @@ class SparseMoE(nn.Module):
     def forward(self, hidden_states: torch.Tensor):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
-        out, logits, sel = _SparseMoEFn.apply(
+        _require_cuda(x)
+        out, logits, sel = sparse_moe(
             x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
             self.gate.top_k, self.gate.norm_topk_prob)
         return out.view(shape), logits.view(*shape[:-1], -1), sel.view(*shape[:-1], -1)
