@@ -19,8 +19,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libb200moe.so"
 SOURCES = [CSRC / "b200moe.cu"]
-DEPS = SOURCES + [CSRC / "common.cuh", CSRC / "grouped_gemm.cuh", CSRC / "routing.cuh",
-                  ROOT / "include" / "b200moe.h"]
+DEPS = SOURCES + sorted(CSRC.glob("*.cuh")) + [ROOT / "include" / "b200moe.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

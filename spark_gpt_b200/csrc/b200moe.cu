@@ -114,6 +114,22 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   return check_launch(what);
 }
 
+// Operand ring depth of the pair kernel: as many stages as fit next to the
+// output staging ring in the 227 KB a CTA may hold (deeper rings hide more of
+// the operand load latency), at most B200MOE_PAIR_STAGES_MAX.
+#ifndef B200MOE_PAIR_STAGES_MAX
+#define B200MOE_PAIR_STAGES_MAX 8
+#endif
+constexpr uint32_t kMaxDynSmem = 227 * 1024;
+
+template <int BN, bool TMA_OUT>
+constexpr int pair_stages() {
+  using S1 = PairSmem<BN, 1, TMA_OUT>;
+  constexpr int fit = static_cast<int>((kMaxDynSmem - (S1::kTotal - S1::kStageBytes)) /
+                                       S1::kStageBytes);
+  return fit < B200MOE_PAIR_STAGES_MAX ? fit : B200MOE_PAIR_STAGES_MAX;
+}
+
 // Expert GEMMs run as two-CTA pair tiles when the shape allows (switchable for
 // parity tests of the two kernels against each other).
 int g_pair_gemm = 1;
@@ -123,10 +139,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
                      const CUtensorMap& to1, const GemmParams& p, cudaStream_t st,
                      const char* what) {
   constexpr bool kTmaOut = TmaOut<EPI>::value;
-#ifndef B200MOE_PAIR_STAGES_TMA
-#define B200MOE_PAIR_STAGES_TMA 4
-#endif
-  constexpr int STAGES = kTmaOut ? (BN == 256 ? B200MOE_PAIR_STAGES_TMA : 5) : 6;
+  constexpr int STAGES = pair_stages<BN, kTmaOut>();
   auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
   const int smem = static_cast<int>(PairSmem<BN, STAGES, kTmaOut>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -148,7 +161,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   return check_launch(what);
 }
 
-// Whether an expert GEMM runs as two-CTA pair tiles: BN of 128/256, E <= 512
+// Whether an expert GEMM runs as two-CTA pair tiles: BN of 128/256, E <= 256
 // (the kernel's per-expert pair table) and, for weight gradients, M a
 // multiple of 256.  Tensor maps of K-major B depend on it (box of BN/2 rows
 // per CTA instead of BN).
@@ -1056,3 +1069,15 @@ int b200moe_lb_grad(const void* logits, long long ld, const unsigned char* valid
 }
 
 }  // extern "C"
+
+#ifdef B200MOE_PROF
+// Instrumented builds only (not declared in the public header).
+extern "C" int b200moe_prof_reset() {
+  unsigned long long z[16] = {};
+  return cudaMemcpyToSymbol(b200moe::g_prof, z, sizeof(z)) == cudaSuccess ? 0 : 1;
+}
+extern "C" int b200moe_prof_read(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, b200moe::g_prof, 16 * sizeof(unsigned long long)) ==
+                 cudaSuccess ? 0 : 1;
+}
+#endif

@@ -119,6 +119,16 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Optional wait-time instrumentation (off in the library build): with
+// B200MOE_PROF defined, the GEMM roles sum the SM cycles it spends waiting on its
+// barriers and working into g_prof (read with b200moe_prof_read).
+#ifdef B200MOE_PROF
+__device__ unsigned long long g_prof[16];
+#define B200_PROF(...) __VA_ARGS__
+#else
+#define B200_PROF(...)
+#endif
+
 // ---------------------------------------------------------------------------
 // TMA (no multicast anywhere in this library)
 // ---------------------------------------------------------------------------

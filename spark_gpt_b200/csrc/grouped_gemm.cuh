@@ -394,11 +394,21 @@ struct OutRing {
   int next;
 };
 
-__device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap* tm,
-                                                const float* v, int lane, int col, int row0) {
-  uint8_t* buf = ring.base + ring.next * 2048;
-  if (lane == 0) bulk_wait_group_read<kOutRing - 1>();  // the last store from buf has read it
+// Chunks of one warp are stored in groups of G: G chunks are written to
+// consecutive ring buffers, then one proxy fence and one bulk group of G TMA
+// stores cover them.  Within one kernel every group has the same G, so
+// "at most kOutRing/G - 1 groups still reading" frees the next G buffers.
+template <int G>
+__device__ __forceinline__ void ring_acquire(int lane) {
+  static_assert(kOutRing % G == 0, "ring size must be a multiple of the store group");
+  if (lane == 0) bulk_wait_group_read<kOutRing / G - 1>();
   __syncwarp();
+}
+
+// Chunk `slot` of the group: this lane's row of 32 fp32 values as bf16 in the
+// 64-byte-swizzled 32 x 32 box.
+__device__ __forceinline__ void ring_put(const OutRing& ring, int slot, const float* v, int lane) {
+  uint8_t* buf = ring.base + ((ring.next + slot) % kOutRing) * 2048;
   uint4* rowp = reinterpret_cast<uint4*>(buf + lane * 64);
   const int sw = (lane >> 1) & 3;
 #pragma unroll
@@ -410,14 +420,32 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
     w.w = pack_bf16x2(v[8 * j + 6], v[8 * j + 7]);
     rowp[j ^ sw] = w;
   }
+}
+
+template <int G>
+__device__ __forceinline__ void ring_flush(OutRing& ring, const CUtensorMap* const* tm,
+                                           const int* col, int row0, int lane) {
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    tma_store_2d(tm, buf, col, row0);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      tma_store_2d(tm[g], ring.base + ((ring.next + g) % kOutRing) * 2048, col[g], row0);
     bulk_commit_group();
   }
-  ring.next = (ring.next + 1) % kOutRing;
+  ring.next = (ring.next + G) % kOutRing;
 }
+
+__device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap* tm,
+                                                const float* v, int lane, int col, int row0) {
+  ring_acquire<1>(lane);
+  ring_put(ring, 0, v, lane);
+  ring_flush<1>(ring, &tm, &col, row0, lane);
+}
+
+#ifndef B200MOE_EPI_GROUP
+#define B200MOE_EPI_GROUP 1  // chunks per proxy fence in the plain bf16 epilogue
+#endif
 
 // The bf16-output epilogues (plain store, SwiGLU forward, SwiGLU backward) with
 // TMA stores.  Outputs: O0 = out (or gu / d_gu), O1 = h (SwiGLU forward).
@@ -425,19 +453,35 @@ template <int EPI, int BN>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const TileInfo& T,
                                                   int quarter, int lane, int half,
                                                   uint32_t taddr, const CUtensorMap* tmO0,
-                                                  const CUtensorMap* tmO1, OutRing& ring) {
+                                                  const CUtensorMap* tmO1, OutRing& ring,
+                                                  unsigned long long* prof = nullptr) {
   constexpr int BM = 128;
   const int row0 = T.m * BM + quarter * 32;
   if (EPI == kEpiStoreBf16) {
+    constexpr int G = B200MOE_EPI_GROUP < BN / 64 ? B200MOE_EPI_GROUP : BN / 64;
 #pragma unroll 1
-    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-      uint32_t r[32];
-      tmem_ld32(taddr + c * 32, r);
-      tmem_wait_ld();
-      float v[32];
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c += G) {
+      uint32_t r[G][32];
+      B200_PROF(long long q0 = clock64();)
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-      store_chunk_tma(ring, tmO0, v, lane, T.n * BN + c * 32, row0);
+      for (int g = 0; g < G; ++g) tmem_ld32(taddr + (c + g) * 32, r[g]);
+      tmem_wait_ld();
+      B200_PROF(long long q1 = clock64(); prof[0] += q1 - q0;)
+      ring_acquire<G>(lane);
+      B200_PROF(long long q2 = clock64(); prof[1] += q2 - q1;)
+      const CUtensorMap* tms[G];
+      int cols[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[g][j]);
+        ring_put(ring, g, v, lane);
+        tms[g] = tmO0;
+        cols[g] = T.n * BN + (c + g) * 32;
+      }
+      ring_flush<G>(ring, tms, cols, row0, lane);
+      B200_PROF(prof[2] += clock64() - q2;)
     }
   } else if (EPI == kEpiSwigluFwd) {
     constexpr int HALF = BN / 2;

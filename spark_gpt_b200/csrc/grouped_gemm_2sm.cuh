@@ -44,9 +44,13 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   return r;
 }
 
+// Arrive on a barrier of another CTA of the cluster (default .release at CTA
+// scope).  The epilogue's TMEM-release arrive needs no cluster-scope release:
+// its TMEM reads have completed (tcgen05.wait::ld) before it.  A
+// .release.cluster arrive here waited for the warp's in-flight TMA stores and
+// took half of the plain-store epilogue's time.
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
-               : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
 __device__ __forceinline__ void mbar_expect_tx_u32(uint32_t bar, uint32_t bytes) {
@@ -101,7 +105,7 @@ __device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
       : "memory");
 }
 
-constexpr int kMaxPairExperts = 512;
+constexpr int kMaxPairExperts = 256;  // the library takes E <= 256
 
 // Epilogues whose bf16 output goes through shared memory and TMA stores.
 template <int EPI>
@@ -261,11 +265,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      B200_PROF(unsigned long long pw = 0; const long long pt0 = clock64();)
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         bool half_ok;
         const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
         for (int kb = 0; kb < T.kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag)) {
+          B200_PROF(const long long w0 = clock64();)
+          const bool got = mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
+          B200_PROF(pw += clock64() - w0;)
+          if (!got) {
             ok = false;
             break;
           }
@@ -302,6 +310,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           }
         }
       }
+      B200_PROF(atomicAdd(&g_prof[0], pw); atomicAdd(&g_prof[1], clock64() - pt0);)
       // tail: wait until the MMA's releases of every stage this CTA filled have
       // landed, so no commit arrives on this CTA's barriers after it exits
       for (int i = 0; ok && i < STAGES; ++i) {
@@ -319,6 +328,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
+      B200_PROF(unsigned long long we = 0, wf = 0; const long long mt0 = clock64();)
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         bool half_ok;
         const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
@@ -326,11 +336,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
         ++local;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag)) break;
+        B200_PROF(long long w0 = clock64();)
+        const bool got_acc = mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag);
+        B200_PROF(we += clock64() - w0;)
+        if (!got_acc) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         for (int kb = 0; kb < T.kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], phase, abort_flag)) {
+          B200_PROF(w0 = clock64();)
+          const bool got = mbar_wait(&full[stage], phase, abort_flag);
+          B200_PROF(wf += clock64() - w0;)
+          if (!got) {
             ok = false;
             break;
           }
@@ -353,6 +369,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
         if (ok) umma_commit_pair_both(&tfull[acc]);
       }
+      B200_PROF(atomicAdd(&g_prof[2], we); atomicAdd(&g_prof[3], wf);
+                atomicAdd(&g_prof[4], clock64() - mt0); atomicAdd(&g_prof[8], 1ull);)
     }
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
@@ -362,6 +380,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     OutRing ring{sOut + (warp - 2) * kOutRing * 2048, 0};
     const bool tma_out = kTmaOut && p.scatter_rows == nullptr;
     int local = 0;
+    B200_PROF(unsigned long long ew = 0, eb = 0, ea = 0; const long long et0 = clock64();
+              unsigned long long pacc[3] = {0, 0, 0};)
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {
       bool half_ok;
       const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
@@ -372,20 +392,36 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;
+      B200_PROF(const long long w0 = clock64();)
+      const bool got_acc = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag));
+      B200_PROF(const long long w1 = clock64(); ew += w1 - w0;)
+      if (!got_acc) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       if (half_ok) {
         if (tma_out)
-          epilogue_tile_tma<EPI, BN>(p, T, q, lane, half, taddr, &tmO0, &tmO1, ring);
+          epilogue_tile_tma<EPI, BN>(p, T, q, lane, half, taddr, &tmO0, &tmO1, ring
+                                     B200_PROF(, pacc));
         else
           epilogue_tile<EPI, BN>(p, T, row_in, half, taddr);
       }
+      B200_PROF(const long long w2 = clock64();)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+      B200_PROF(const long long w3 = clock64(); eb += w3 - w1; ea += w3 - w2;)
     }
     if (kTmaOut && lane == 0) bulk_wait_group_all();  // stores done before exit
+    B200_PROF(if (lane == 0) {
+      atomicAdd(&g_prof[5], ew);
+      atomicAdd(&g_prof[6], eb);
+      atomicAdd(&g_prof[7], clock64() - et0);
+      atomicAdd(&g_prof[9], 1ull);
+      atomicAdd(&g_prof[10], pacc[0]);
+      atomicAdd(&g_prof[11], pacc[1]);
+      atomicAdd(&g_prof[12], pacc[2]);
+      atomicAdd(&g_prof[13], ea);
+    })
   }
 
   __syncthreads();
