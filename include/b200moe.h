@@ -131,9 +131,13 @@ int b200moe_dispatch_noalloc(const long long* selected, long long T, int k, int 
 
 /* ---- gather: _GatherTopK (train.py:2195-2217) ---------------------------- */
 
-/* xs (Rcap,H) bf16: xs[p] = x[row_flat[p]/k], zero rows for padding. */
-int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offsets, int E,
-                        int k, int H, long long rows_cap, void* xs, void* stream);
+/* xs (Rcap,H) bf16: xs[p] = x[row_flat[p]/k], zero rows for padding.  With
+ * inv_pad (T*k, from dispatch) the copy runs in token order (each of the T x
+ * rows read once, written to its k rows; k <= 32); with inv_pad == NULL, in
+ * padded-row order (T unused). */
+int b200moe_gather_rows(const void* x, const int* row_flat, const int* inv_pad,
+                        const int* pad_offsets, long long T, int E, int k, int H,
+                        long long rows_cap, void* xs, void* stream);
 
 /* dx (T,H) bf16 = sum_s dxs[inv_pad[t*k+s]] (+ addend (T,H) bf16 if given).
  * With inv_pad == NULL, dxs is token-major: slot t*k+s in row t*k+s. */

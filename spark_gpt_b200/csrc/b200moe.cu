@@ -574,13 +574,31 @@ int b200moe_dispatch_noalloc(const long long* selected, long long T, int k, int 
 }
 
 // ---------------------------------------------------------------- gather / combine
-int b200moe_gather_rows(const void* x, const int* row_flat, const int* pad_offsets, int E, int k,
-                        int H, long long rows_cap, void* xs, void* stream) {
+#ifndef B200MOE_TOKEN_ORDER
+#define B200MOE_TOKEN_ORDER 1  // gather / combine backward traverse tokens (0: padded rows)
+#endif
+
+int b200moe_gather_rows(const void* x, const int* row_flat, const int* inv_pad,
+                        const int* pad_offsets, long long T, int E, int k, int H,
+                        long long rows_cap, void* xs, void* stream) {
   REQUIRE(x && row_flat && pad_offsets && xs, "gather_rows: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1, "gather_rows: H must be a multiple of 8");
   auto* xp = static_cast<const __nv_bfloat16*>(x);
   auto* xsp = static_cast<__nv_bfloat16*>(xs);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (B200MOE_TOKEN_ORDER && inv_pad) {
+    REQUIRE(k <= 32 && T >= 0 && T * k <= rows_cap, "gather_rows: need k <= 32, T*k <= rows_cap");
+    const int grid = grid_for(T > rows_cap / 32 ? T : rows_cap / 32, 8);
+    const int* tot = pad_offsets + E;
+    switch (H) {
+      case 256: scatter_rows_kernel<1><<<grid, 256, 0, st>>>(xp, inv_pad, row_flat, tot, T, k, H, xsp); break;
+      case 512: scatter_rows_kernel<2><<<grid, 256, 0, st>>>(xp, inv_pad, row_flat, tot, T, k, H, xsp); break;
+      case 1024: scatter_rows_kernel<4><<<grid, 256, 0, st>>>(xp, inv_pad, row_flat, tot, T, k, H, xsp); break;
+      case 2048: scatter_rows_kernel<8><<<grid, 256, 0, st>>>(xp, inv_pad, row_flat, tot, T, k, H, xsp); break;
+      default: scatter_rows_kernel<0><<<grid, 256, 0, st>>>(xp, inv_pad, row_flat, tot, T, k, H, xsp); break;
+    }
+    return check_launch("gather_rows");
+  }
   const int grid = grid_for(rows_cap, 8);
   switch (H) {
     case 256: gather_rows_kernel<1><<<grid, 256, 0, st>>>(xp, row_flat, pad_offsets + E, k, H, xsp); break;
@@ -652,6 +670,19 @@ int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat, c
   auto* dop = static_cast<const __nv_bfloat16*>(d_out);
   auto* yp = static_cast<const __nv_bfloat16*>(y);
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
+  if (B200MOE_TOKEN_ORDER && inv_pad && k <= 32 &&
+      (H == 256 || H == 512 || H == 1024 || H == 2048)) {
+    REQUIRE(T >= 0 && T * k <= rows_cap, "combine_bwd: T*k exceeds rows_cap");
+    const int grid = grid_for(T > rows_cap / 32 ? T : rows_cap / 32, 8);
+    const int* tot = pad_offsets + E;
+    switch (H) {
+      case 256: combine_bwd_tokens_kernel<1><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights); break;
+      case 512: combine_bwd_tokens_kernel<2><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights); break;
+      case 1024: combine_bwd_tokens_kernel<4><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights); break;
+      default: combine_bwd_tokens_kernel<8><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights); break;
+    }
+    return check_launch("combine_bwd");
+  }
   const int grid = grid_for(rows_cap, 8);
   switch (H) {
     case 256: combine_bwd_kernel<1><<<grid, 256, 0, st>>>(dop, yp, row_flat, pad_offsets + E, wp, k, H, dyp, d_weights); break;

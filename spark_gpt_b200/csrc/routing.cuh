@@ -215,6 +215,147 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x,
   }
 }
 
+// Zero the padding rows (row_flat < 0) of a padded-row buffer: each warp
+// checks 32 rows at a time and clears the padding rows among them together.
+template <int VPL>
+__device__ __forceinline__ void zero_padding_rows(const int* __restrict__ row_flat,
+                                                  long long total, int H, long long warp_id,
+                                                  long long warps, int lane,
+                                                  __nv_bfloat16* __restrict__ buf) {
+  const int nvec = H / 8;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (long long base = warp_id * 32; base < total; base += warps * 32) {
+    const long long r = base + lane;
+    unsigned m = __ballot_sync(0xffffffffu, r < total && row_flat[r] < 0);
+    while (m) {
+      const int i = __ffs(m) - 1;
+      m &= m - 1;
+      uint4* dst = reinterpret_cast<uint4*>(buf + (base + i) * H);
+      if (VPL > 0) {
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) dst[lane + 32 * j] = z;
+      } else {
+        for (int v = lane; v < nvec; v += 32) dst[v] = z;
+      }
+    }
+  }
+}
+
+// Token-order gather: warp per token; x[t] is read once and written to the
+// padded rows of its k slots (inv_pad), then the padding rows are zeroed.
+// Reads each token row once instead of once per slot.
+template <int VPL>
+__global__ void scatter_rows_kernel(const __nv_bfloat16* __restrict__ x,
+                                    const int* __restrict__ inv_pad,
+                                    const int* __restrict__ row_flat,
+                                    const int* __restrict__ total_rows, long long T, int k, int H,
+                                    __nv_bfloat16* __restrict__ xs) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long warp_id = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (long long t = warp_id; t < T; t += warps) {
+    const int rl = lane < k ? inv_pad[t * k + lane] : 0;
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * H);
+    if (VPL > 0) {
+      uint4 v[VPL > 0 ? VPL : 1];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) v[j] = __ldg(src + lane + 32 * j);
+      for (int s = 0; s < k; ++s) {
+        const long long r = __shfl_sync(0xffffffffu, rl, s);
+        uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) dst[lane + 32 * j] = v[j];
+      }
+    } else {
+      for (int s = 0; s < k; ++s) {
+        const long long r = __shfl_sync(0xffffffffu, rl, s);
+        uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
+        for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
+      }
+    }
+  }
+  zero_padding_rows<VPL>(row_flat, *total_rows, H, warp_id, warps, lane, xs);
+}
+
+// Token-order combine backward over the padded layout: warp per token; d_out[t]
+// is read once and the rows of its k slots are visited through inv_pad (the
+// next slot's y row is loaded while the current one is processed):
+//   dy[r] = bf16(d_out[t] * w[t,s]),  d_weights[t*k+s] = <d_out[t], y[r]>,
+// then the padding rows of dy are zeroed.
+template <int VPL>
+__global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_out,
+                                          const __nv_bfloat16* __restrict__ y,
+                                          const int* __restrict__ inv_pad,
+                                          const int* __restrict__ row_flat,
+                                          const int* __restrict__ total_rows,
+                                          const __nv_bfloat16* __restrict__ weights, long long T,
+                                          int k, int H, __nv_bfloat16* __restrict__ dy,
+                                          float* __restrict__ d_weights) {
+  static_assert(VPL > 0, "token-order combine backward needs H in {256, 512, 1024, 2048}");
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  const long long warp_id = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+  for (long long t = warp_id; t < T; t += warps) {
+    int rl = 0;
+    float wl = 0.f;
+    if (lane < k) {
+      rl = inv_pad[t * k + lane];
+      wl = __bfloat162float(weights[t * k + lane]);
+    }
+    const uint4* g = reinterpret_cast<const uint4*>(d_out + t * H);
+    float ga[VPL][8];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      const uint4 a = __ldg(g + lane + 32 * j);
+      ga[j][0] = bf16_lo(a.x); ga[j][1] = bf16_hi(a.x);
+      ga[j][2] = bf16_lo(a.y); ga[j][3] = bf16_hi(a.y);
+      ga[j][4] = bf16_lo(a.z); ga[j][5] = bf16_hi(a.z);
+      ga[j][6] = bf16_lo(a.w); ga[j][7] = bf16_hi(a.w);
+    }
+    float my_dot = 0.f;
+    uint4 bn[VPL];
+    {
+      const long long r0 = __shfl_sync(0xffffffffu, rl, 0);
+      const uint4* yy = reinterpret_cast<const uint4*>(y + r0 * H);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) bn[j] = __ldg(yy + lane + 32 * j);
+    }
+    for (int s = 0; s < k; ++s) {
+      const long long r = __shfl_sync(0xffffffffu, rl, s);
+      const float w = __shfl_sync(0xffffffffu, wl, s);
+      uint4 b[VPL];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) b[j] = bn[j];
+      const long long rn = __shfl_sync(0xffffffffu, rl, s + 1 < k ? s + 1 : s);
+      if (s + 1 < k) {
+        const uint4* yy = reinterpret_cast<const uint4*>(y + rn * H);
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) bn[j] = __ldg(yy + lane + 32 * j);
+      }
+      uint4* dst = reinterpret_cast<uint4*>(dy + r * H);
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const float yb[8] = {bf16_lo(b[j].x), bf16_hi(b[j].x), bf16_lo(b[j].y), bf16_hi(b[j].y),
+                             bf16_lo(b[j].z), bf16_hi(b[j].z), bf16_lo(b[j].w), bf16_hi(b[j].w)};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) dot += ga[j][e] * yb[e];
+        uint4 o;
+        o.x = pack_bf16x2(ga[j][0] * w, ga[j][1] * w);
+        o.y = pack_bf16x2(ga[j][2] * w, ga[j][3] * w);
+        o.z = pack_bf16x2(ga[j][4] * w, ga[j][5] * w);
+        o.w = pack_bf16x2(ga[j][6] * w, ga[j][7] * w);
+        dst[lane + 32 * j] = o;
+      }
+      dot = warp_sum(dot);
+      if (lane == s) my_dot = dot;
+    }
+    if (lane < k) d_weights[t * k + lane] = my_dot;
+  }
+  zero_padding_rows<VPL>(row_flat, *total_rows, H, warp_id, warps, lane, dy);
+}
+
 // dx[t] = sum_s dxs[inv_pad[t*k+s]] (+ addend[t]); fp32 accumulation.  With
 // inv_pad == nullptr the rows are token-major (slot t*k+s in row t*k+s).  Used
 // when one token's k rows do not fit the shared-memory ring of row_reduce_kernel.

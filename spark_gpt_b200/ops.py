@@ -197,7 +197,8 @@ def gather_rows(x: torch.Tensor, d: Dispatch) -> torch.Tensor:
     _check(x, BF16, "gather_rows x")
     H = x.shape[1]
     xs = torch.empty(d.rows_cap, H, device=x.device, dtype=BF16)
-    _launch("gather", 1, "b200moe_gather_rows", _p(x), _p(d.row_flat), _p(d.pad_offsets),
+    _launch("gather", 1, "b200moe_gather_rows", _p(x), _p(d.row_flat),
+            _p(d.inv_pad) if d.inv_pad.numel() else None, _p(d.pad_offsets), d.num_tokens,
             d.num_experts, d.top_k, H, d.rows_cap, _p(xs), _s(x))
     return xs
 
