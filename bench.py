@@ -391,27 +391,53 @@ def main():
     layer_tflops = layer_flops(c, T) / (ms / 1e3) / 1e12
     gemm_ms = sum(per_op.get(n, 0.0) * len(timing.get(n, [])) / args.steps for n in flops)
 
-    # ---------------- end to end: host buffers, copies inside the timed region
+    # ---------------- end to end: host buffers, copies inside the timed region.
+    # Each step's x and d_out come from pinned host memory; as a training
+    # input pipeline does, the copy of step i+1's inputs runs on a copy stream
+    # while step i computes (two device buffers, ordered by events), and each
+    # step's aux loss is read back to pinned host memory.  Every copy lies
+    # inside the timed region.
     e2e = None
     if not args.no_e2e:
         aux_h = torch.empty((), dtype=torch.float32).pin_memory()
+        comp = torch.cuda.current_stream(dev)
+        copy = torch.cuda.Stream(dev)
+        bufs = [(torch.empty_like(x), torch.empty_like(d_out)) for _ in range(2)]
+        copied = [torch.cuda.Event() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]
+
+        def prefetch(i):
+            xb, db = bufs[i % 2]
+            with torch.cuda.stream(copy):
+                if i >= 2:
+                    copy.wait_event(freed[i % 2])  # step i-2 is done with this buffer
+                xb.copy_(x_pin, non_blocking=True)
+                db.copy_(d_pin, non_blocking=True)
+                copied[i % 2].record(copy)
+
         torch.cuda.synchronize()
         barrier()
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(args.steps):
-            xb = x_pin.to(dev, non_blocking=True)
-            db = d_pin.to(dev, non_blocking=True)
+        e0.record(comp)
+        prefetch(0)
+        for i in range(args.steps):
+            if i + 1 < args.steps:
+                prefetch(i + 1)
+            comp.wait_event(copied[i % 2])
+            xb, db = bufs[i % 2]
             aux = step(xb, db)
+            freed[i % 2].record(comp)
             aux_h.copy_(aux.detach(), non_blocking=True)
-        e1.record()
+        e1.record(comp)
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
         e2e = {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": x_pin.numel() * 2 + d_pin.numel() * 2,
-               "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms}
+               "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms,
+               "pipeline": "next step's H2D overlapped with this step's compute (copy stream, "
+                           "double-buffered inputs)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not c.get("ep"):
