@@ -212,6 +212,8 @@ GemmParams blank_params() {
   return p;
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 int grid_for(long long items, int per_block) {
   long long g = (items + per_block - 1) / per_block;
   const long long cap = static_cast<long long>(num_sms()) * 32;
@@ -347,14 +349,15 @@ int b200moe_router_topk_fwd(const void* logits, int logits_f32, long long ld, lo
   if (T == 0) return B200MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* w = static_cast<__nv_bfloat16*>(weights);
+  const int vec = aligned16(logits) && (ld * (logits_f32 ? 4 : 2)) % 16 == 0;
   B200_SWITCH_LANES(E, {
     const int grid = grid_for(T, 256 / L);
     if (logits_f32)
       router_topk_fwd_kernel<L, float><<<grid, 256, 0, st>>>(
-          static_cast<const float*>(logits), ld, T, E, k, norm, selected, w);
+          static_cast<const float*>(logits), ld, T, E, k, norm, vec, selected, w);
     else
       router_topk_fwd_kernel<L, __nv_bfloat16><<<grid, 256, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, selected, w);
+          static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, vec, selected, w);
   })
   return check_launch("router_topk_fwd");
 }
@@ -370,9 +373,11 @@ int b200moe_router_topk_bwd(const void* logits, long long ld, const long long* s
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
   auto* ex = static_cast<const __nv_bfloat16*>(d_extra);
   auto* out = static_cast<__nv_bfloat16*>(d_logits);
+  const int vec = aligned16(lg) && aligned16(out) && (ex == nullptr || aligned16(ex)) &&
+                  (ld * 2) % 16 == 0;
   B200_SWITCH_LANES(ld, {
     router_topk_bwd_kernel<L><<<grid_for(T, 256 / L), 256, 0, st>>>(lg, ld, selected, d_weights,
-                                                                    ex, T, E, k, norm, out);
+                                                                    ex, T, E, k, norm, vec, out);
   })
   return check_launch("router_topk_bwd");
 }
@@ -1068,11 +1073,12 @@ int b200moe_lb_stats(const void* logits, long long ld, const long long* selected
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
   B200_SWITCH_LANES(E, {
     lb_partials_kernel<L><<<nblk, kLbThreads, lb_partials_smem<L>(E), st>>>(
-        lg, ld, selected, valid, T, E, k, part);
+        lg, ld, selected, valid, T, E, k, aligned16(lg) && (ld * 2) % 16 == 0, part);
   })
   int rc = check_launch("lb_partials");
   if (rc) return rc;
-  lb_accumulate_kernel<<<1, 512, 0, st>>>(part, nblk, 2 * E + 2, packed);
+  lb_accumulate_kernel<<<1, 512, 16 * (2 * E + 2) * sizeof(float), st>>>(part, nblk, 2 * E + 2,
+                                                                          packed);
   return check_launch("lb_accumulate");
 }
 
@@ -1094,7 +1100,9 @@ int b200moe_lb_grad(const void* logits, long long ld, const unsigned char* valid
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
   auto* out = static_cast<__nv_bfloat16*>(d_logits);
   B200_SWITCH_LANES(ld, {
-    lb_grad_kernel<L><<<grid_for(T, 256 / L), 256, 0, st>>>(lg, ld, valid, T, E, coef, grad, out);
+    lb_grad_kernel<L><<<grid_for(T, 256 / L), 256, 0, st>>>(
+        lg, ld, valid, T, E, coef, grad, aligned16(lg) && aligned16(out) && (ld * 2) % 16 == 0,
+        out);
   })
   return check_launch("lb_grad");
 }

@@ -2,10 +2,11 @@
 // (spark-gpt train.py:2144-2158, 3098-3197).
 //
 // A token is handled by a group of L lanes (L = 2..32, a power of two) that
-// hold 8 logits each: expert e lives in lane e % L of the group, register
-// slot e / L.  E = 64 uses 8 lanes, so one warp works on 4 tokens at once and
-// every reduction is log2(L) shuffles.  Loops run in whole-warp rounds so
-// every lane of a warp executes every shuffle.
+// hold 8 logits each: expert e lives in lane e / 8 of the group, register
+// slot e % 8, so a lane's logits are one 16-byte load.  E = 64 uses 8 lanes,
+// so one warp works on 4 tokens at once and every reduction is log2(L)
+// shuffles.  Loops run in whole-warp rounds so every lane of a warp executes
+// every shuffle.
 #pragma once
 
 #include "common.cuh"
@@ -38,33 +39,74 @@ __device__ __forceinline__ float group_sum(float v) {
   return v;
 }
 
-// p = softmax(row[0:E]) in fp32 (max-subtract, expf, sum, divide); entries of
-// this lane beyond E are 0.  `valid` false: row is not read, p is garbage but
-// every shuffle still runs.
-template <int L, typename LT>
+// Logits [e0, e0+8) of a row as fp32, -inf at e >= E or for an invalid row.
+// vec: the row start is 16-byte aligned and ld is a multiple of 16 bytes, so a
+// chunk that lies inside E is one vector load.
+template <typename LT>
+__device__ __forceinline__ void load_chunk(const LT* __restrict__ row, int e0, int E, bool valid,
+                                           bool vec, float (&z)[kVpt]) {
+  if (valid && vec && e0 + kVpt <= E) {
+    if constexpr (sizeof(LT) == 2) {
+      const uint4 v = *reinterpret_cast<const uint4*>(row + e0);
+      z[0] = bf16_lo(v.x); z[1] = bf16_hi(v.x); z[2] = bf16_lo(v.y); z[3] = bf16_hi(v.y);
+      z[4] = bf16_lo(v.z); z[5] = bf16_hi(v.z); z[6] = bf16_lo(v.w); z[7] = bf16_hi(v.w);
+    } else {
+      const float4 a = *reinterpret_cast<const float4*>(row + e0);
+      const float4 b = *reinterpret_cast<const float4*>(row + e0 + 4);
+      z[0] = a.x; z[1] = a.y; z[2] = a.z; z[3] = a.w;
+      z[4] = b.x; z[5] = b.y; z[6] = b.z; z[7] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) {
+      const int e = e0 + j;
+      z[j] = (valid && e < E) ? to_f32(row[e]) : -INFINITY;
+    }
+  }
+}
+
+// p = softmax(row[0:E]) in fp32 (max-subtract, exp, sum, divide) for this
+// lane's experts e = 8*sub + j; entries beyond E are 0.  FAST (gradient and
+// statistics kernels): __expf and one reciprocal; otherwise expf and a
+// division per entry (the forward selection).  `valid` false: row is not
+// read, p is garbage but every shuffle still runs.
+template <int L, bool FAST, typename LT>
 __device__ __forceinline__ void softmax_group(const LT* __restrict__ row, int E, int sub,
-                                              bool valid, float (&p)[kVpt]) {
+                                              bool valid, bool vec, float (&p)[kVpt]) {
   float z[kVpt];
+  load_chunk(row, sub * kVpt, E, valid, vec, z);
   float m = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kVpt; ++j) {
-    const int e = sub + L * j;
-    z[j] = (valid && e < E) ? to_f32(row[e]) : -INFINITY;
-    m = fmaxf(m, z[j]);
-  }
+  for (int j = 0; j < kVpt; ++j) m = fmaxf(m, z[j]);
   m = group_max<L>(m);
   if (!valid) m = 0.f;
   float s = 0.f;
 #pragma unroll
   for (int j = 0; j < kVpt; ++j) {
-    const int e = sub + L * j;
-    p[j] = (valid && e < E) ? expf(z[j] - m) : 0.f;
+    const bool in = valid && sub * kVpt + j < E;
+    p[j] = in ? (FAST ? __expf(z[j] - m) : expf(z[j] - m)) : 0.f;
     s += p[j];
   }
   s = group_sum<L>(s);
   if (!valid) s = 1.f;
+  if (FAST) {
+    const float inv = 1.0f / s;
 #pragma unroll
-  for (int j = 0; j < kVpt; ++j) p[j] = p[j] / s;
+    for (int j = 0; j < kVpt; ++j) p[j] *= inv;
+  } else {
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) p[j] = p[j] / s;
+  }
+}
+
+// Value of register slot e % 8 from lane e / 8 of the group (all lanes call).
+template <int L>
+__device__ __forceinline__ float group_fetch(const float (&v)[kVpt], int e) {
+  float x = 0.f;
+#pragma unroll
+  for (int j = 0; j < kVpt; ++j)
+    if ((e & (kVpt - 1)) == j) x = v[j];
+  return __shfl_sync(0xffffffffu, x, (e >> 3) & (L - 1), L);
 }
 
 // Grid-stride over tokens in whole-grid rounds: every thread runs the same
@@ -85,7 +127,8 @@ struct GroupTokens {
 
 template <int L, typename LT>
 __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long ld, long long T,
-                                       int E, int k, int norm, long long* __restrict__ selected,
+                                       int E, int k, int norm, int vec,
+                                       long long* __restrict__ selected,
                                        __nv_bfloat16* __restrict__ weights) {
   const int sub = threadIdx.x & (L - 1);
   const GroupTokens gt = GroupTokens::make<L>(T);
@@ -93,10 +136,10 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
     const long long t = gt.first + rnd * gt.stride;
     const bool valid = t < T;
     float p[kVpt];
-    softmax_group<L>(logits + (valid ? t : 0) * ld, E, sub, valid, p);
+    softmax_group<L, false>(logits + (valid ? t : 0) * ld, E, sub, valid, vec != 0, p);
 #pragma unroll
     for (int j = 0; j < kVpt; ++j)
-      if (sub + L * j >= E) p[j] = -1.f;
+      if (sub * kVpt + j >= E) p[j] = -1.f;
     float sv[kMaxTopK];
     int si[kMaxTopK];
 #pragma unroll
@@ -104,14 +147,14 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
       sv[r] = 0.f;
       si[r] = 0;
       if (r < k) {
+        // lane-local best (ascending e: the first maximum is the lowest index)
         float bv = -2.f;
         int bi = 0x7fffffff;
 #pragma unroll
         for (int j = 0; j < kVpt; ++j) {
-          const int e = sub + L * j;
-          if (p[j] > bv || (p[j] == bv && e < bi)) {
+          if (p[j] > bv) {
             bv = p[j];
-            bi = e;
+            bi = sub * kVpt + j;
           }
         }
 #pragma unroll
@@ -125,7 +168,7 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
         }
 #pragma unroll
         for (int j = 0; j < kVpt; ++j)
-          if (sub + L * j == bi) p[j] = -3.f;
+          if (sub * kVpt + j == bi) p[j] = -3.f;
         sv[r] = bv;
         si[r] = bi;
       }
@@ -154,52 +197,60 @@ __global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits,
                                        const long long* __restrict__ selected,
                                        const float* __restrict__ d_weights,
                                        const __nv_bfloat16* __restrict__ d_extra, long long T,
-                                       int E, int k, int norm,
+                                       int E, int k, int norm, int vec,
                                        __nv_bfloat16* __restrict__ d_logits) {
+  constexpr int kSlots = (kMaxTopK + L - 1) / L;  // slots r = sub + L*i held by this lane
   const int sub = threadIdx.x & (L - 1);
+  const int e0 = sub * kVpt;
   const GroupTokens gt = GroupTokens::make<L>(T);
   for (long long rnd = 0; rnd < gt.rounds; ++rnd) {
     const long long t = gt.first + rnd * gt.stride;
     const bool valid = t < T;
     const long long tt = valid ? t : 0;
     float p[kVpt];
-    softmax_group<L>(logits + tt * ld, E, sub, valid, p);
+    softmax_group<L, true>(logits + tt * ld, E, sub, valid, vec != 0, p);
+    int sl[kSlots];
+    float dl[kSlots];
+#pragma unroll
+    for (int i = 0; i < kSlots; ++i) {
+      const int r = sub + L * i;
+      const bool on = valid && r < k;
+      sl[i] = on ? static_cast<int>(selected[tt * k + r]) : -1;
+      dl[i] = on ? d_weights[tt * k + r] : 0.f;
+    }
     int si[kMaxTopK];
-    float ps[kMaxTopK];
+    float ps[kMaxTopK], dw[kMaxTopK];
     float s = 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxTopK; ++r) {
       si[r] = -1;
       ps[r] = 0.f;
+      dw[r] = 0.f;
       if (r < k) {
-        const int e = valid ? static_cast<int>(selected[tt * k + r]) : -1;
-        float v = 0.f;
-#pragma unroll
-        for (int j = 0; j < kVpt; ++j)
-          if (sub + L * j == e) v = p[j];
+        const int e = __shfl_sync(0xffffffffu, sl[r / L], r % L, L);
+        dw[r] = __shfl_sync(0xffffffffu, dl[r / L], r % L, L);
         si[r] = e;
-        ps[r] = group_sum<L>(v);
+        const float pe = group_fetch<L>(p, e < 0 ? 0 : e);  // every lane shuffles
+        ps[r] = e >= 0 ? pe : 0.f;
         s += ps[r];
       }
     }
-    if (!valid) s = 1.f;
+    if (!valid || s == 0.f) s = 1.f;
+    const float inv_s = 1.0f / s;
     float dot = 0.f;
-    float dw[kMaxTopK];
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
-      dw[r] = (r < k && valid) ? d_weights[tt * k + r] : 0.f;
-      if (r < k) dot += dw[r] * (ps[r] / s);
-    }
+    for (int r = 0; r < kMaxTopK; ++r)
+      if (r < k) dot += dw[r] * (ps[r] * inv_s);
     float g[kVpt];
 #pragma unroll
     for (int j = 0; j < kVpt; ++j) g[j] = 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxTopK; ++r) {
       if (r < k) {
-        const float dp = norm ? (dw[r] - dot) / s : dw[r];
+        const float dp = norm ? (dw[r] - dot) * inv_s : dw[r];
 #pragma unroll
         for (int j = 0; j < kVpt; ++j)
-          if (sub + L * j == si[r]) g[j] = dp;
+          if (e0 + j == si[r]) g[j] = dp;
       }
     }
     float pg = 0.f;
@@ -207,17 +258,35 @@ __global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits,
     for (int j = 0; j < kVpt; ++j) pg += p[j] * g[j];
     pg = group_sum<L>(pg);
     if (valid) {
+      float ex[kVpt];
 #pragma unroll
-      for (int j = 0; j < kVpt; ++j) {
-        const int e = sub + L * j;
-        if (e < ld) {
-          float v = 0.f;
-          if (e < E) {
-            v = p[j] * (g[j] - pg);
-            if (d_extra) v += __bfloat162float(d_extra[tt * ld + e]);
-          }
-          d_logits[tt * ld + e] = __float2bfloat16_rn(v);
+      for (int j = 0; j < kVpt; ++j) ex[j] = 0.f;
+      const bool vio = vec && e0 + kVpt <= ld;
+      if (d_extra) {
+        if (vio) {
+          const uint4 v = *reinterpret_cast<const uint4*>(d_extra + tt * ld + e0);
+          ex[0] = bf16_lo(v.x); ex[1] = bf16_hi(v.x); ex[2] = bf16_lo(v.y); ex[3] = bf16_hi(v.y);
+          ex[4] = bf16_lo(v.z); ex[5] = bf16_hi(v.z); ex[6] = bf16_lo(v.w); ex[7] = bf16_hi(v.w);
+        } else {
+#pragma unroll
+          for (int j = 0; j < kVpt; ++j)
+            if (e0 + j < ld) ex[j] = __bfloat162float(d_extra[tt * ld + e0 + j]);
         }
+      }
+      float v[kVpt];
+#pragma unroll
+      for (int j = 0; j < kVpt; ++j) v[j] = (e0 + j < E) ? p[j] * (g[j] - pg) + ex[j] : 0.f;
+      if (vio) {
+        uint4 o;
+        o.x = pack_bf16x2(v[0], v[1]);
+        o.y = pack_bf16x2(v[2], v[3]);
+        o.z = pack_bf16x2(v[4], v[5]);
+        o.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(d_logits + tt * ld + e0) = o;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j)
+          if (e0 + j < ld) d_logits[tt * ld + e0 + j] = __float2bfloat16_rn(v[j]);
       }
     }
   }
@@ -236,7 +305,7 @@ template <int L>
 __global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
                                    const long long* __restrict__ selected,
                                    const unsigned char* __restrict__ valid_mask, long long T,
-                                   int E, int k, float* __restrict__ partials) {
+                                   int E, int k, int vec, float* __restrict__ partials) {
   constexpr int kGroups = kLbThreads / L;
   // [groups][8L] soft sums, then [E] hard counts, then [groups] entropy, [groups] rows
   extern __shared__ float lsh[];
@@ -258,11 +327,11 @@ __global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, lon
     const long long t = t0 + i;
     const bool valid = t < T && (valid_mask == nullptr || valid_mask[t] != 0);
     float p[kVpt];
-    softmax_group<L>(logits + (valid ? t : 0) * ld, E, sub, valid, p);
+    softmax_group<L, true>(logits + (valid ? t : 0) * ld, E, sub, valid, vec != 0, p);
     if (valid) {
 #pragma unroll
       for (int j = 0; j < kVpt; ++j) {
-        if (sub + L * j < E) {
+        if (sub * kVpt + j < E) {
           soft[j] += p[j];
           ent -= p[j] * logf(fmaxf(p[j], tiny));
         }
@@ -276,7 +345,7 @@ __global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, lon
   }
   ent = group_sum<L>(ent);
 #pragma unroll
-  for (int j = 0; j < kVpt; ++j) soft_sh[grp * kVpt * L + sub + L * j] = soft[j];
+  for (int j = 0; j < kVpt; ++j) soft_sh[grp * kVpt * L + sub * kVpt + j] = soft[j];
   if (sub == 0) {
     ent_sh[grp] = ent;
     rows_sh[grp] = rows;
@@ -308,19 +377,26 @@ constexpr size_t lb_partials_smem(int E) {
 }
 
 // packed[i] += sum over blocks of partials[b][i], fixed block order.
+// packed[i] += sum over blocks of partials[b][i]: warp w sums the blocks
+// b = w (mod warps) for its lane's columns, then the warps' sums are added in
+// warp order (a fixed order: deterministic).  Shared memory: warps * W floats.
 __global__ void lb_accumulate_kernel(const float* __restrict__ partials, int nblk, int W,
                                      float* __restrict__ packed) {
+  extern __shared__ float acc_sh[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  for (int i = lane; i < W; i += 32) {
+    float a = 0.f;
+#pragma unroll 4
+    for (int b = warp; b < nblk; b += nw) a += partials[static_cast<long long>(b) * W + i];
+    acc_sh[warp * W + i] = a;
+  }
+  __syncthreads();
   for (int i = threadIdx.x; i < W; i += blockDim.x) {
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-    int b = 0;
-    for (; b + 3 < nblk; b += 4) {
-      a0 += partials[static_cast<long long>(b) * W + i];
-      a1 += partials[static_cast<long long>(b + 1) * W + i];
-      a2 += partials[static_cast<long long>(b + 2) * W + i];
-      a3 += partials[static_cast<long long>(b + 3) * W + i];
-    }
-    for (; b < nblk; ++b) a0 += partials[static_cast<long long>(b) * W + i];
-    packed[i] += (a0 + a1) + (a2 + a3);
+    float a = 0.f;
+    for (int w = 0; w < nw; ++w) a += acc_sh[w * W + i];
+    packed[i] += a;
   }
 }
 
@@ -370,12 +446,14 @@ template <int L>
 __global__ void lb_grad_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
                                const unsigned char* __restrict__ valid_mask, long long T, int E,
                                const float* __restrict__ coef, const float* __restrict__ grad,
-                               __nv_bfloat16* __restrict__ d_logits) {
+                               int vec, __nv_bfloat16* __restrict__ d_logits) {
   const float g = *grad;
   const int sub = threadIdx.x & (L - 1);
+  const int e0 = sub * kVpt;
   float c[kVpt];
 #pragma unroll
-  for (int j = 0; j < kVpt; ++j) c[j] = (sub + L * j < E) ? coef[sub + L * j] : 0.f;
+  for (int j = 0; j < kVpt; ++j) c[j] = (e0 + j < E) ? coef[e0 + j] : 0.f;
+  const bool vio = vec && e0 + kVpt <= ld;
   const GroupTokens gt = GroupTokens::make<L>(T);
   for (long long rnd = 0; rnd < gt.rounds; ++rnd) {
     const long long t = gt.first + rnd * gt.stride;
@@ -383,19 +461,26 @@ __global__ void lb_grad_kernel(const __nv_bfloat16* __restrict__ logits, long lo
     const long long tt = valid ? t : 0;
     const bool on = valid && (valid_mask == nullptr || valid_mask[tt] != 0);
     float p[kVpt];
-    softmax_group<L>(logits + tt * ld, E, sub, valid, p);
+    softmax_group<L, true>(logits + tt * ld, E, sub, valid, vec != 0, p);
     float pc = 0.f;
 #pragma unroll
     for (int j = 0; j < kVpt; ++j) pc += p[j] * c[j];
     pc = group_sum<L>(pc);
     if (valid) {
+      float v[kVpt];
 #pragma unroll
-      for (int j = 0; j < kVpt; ++j) {
-        const int e = sub + L * j;
-        if (e < ld) {
-          const float v = (on && e < E) ? g * p[j] * (c[j] - pc) : 0.f;
-          d_logits[tt * ld + e] = __float2bfloat16_rn(v);
-        }
+      for (int j = 0; j < kVpt; ++j) v[j] = (on && e0 + j < E) ? g * p[j] * (c[j] - pc) : 0.f;
+      if (vio) {
+        uint4 o;
+        o.x = pack_bf16x2(v[0], v[1]);
+        o.y = pack_bf16x2(v[2], v[3]);
+        o.z = pack_bf16x2(v[4], v[5]);
+        o.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4*>(d_logits + tt * ld + e0) = o;
+      } else {
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j)
+          if (e0 + j < ld) d_logits[tt * ld + e0 + j] = __float2bfloat16_rn(v[j]);
       }
     }
   }

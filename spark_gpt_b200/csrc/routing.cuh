@@ -88,6 +88,18 @@ __global__ void dispatch_count_kernel(const long long* __restrict__ sel, long lo
   for (int e = threadIdx.x; e < E; e += blockDim.x) block_base[e * nblk + blockIdx.x] = hist[e];
 }
 
+// Lanes per expert in the dispatch scan: a power of two <= 32 with
+// lanes * E <= threads (1 when E >= threads).
+__device__ __forceinline__ int scan_parts(int E, int threads) {
+  int p = 1;
+  while (p < 32 && 2 * p * E <= threads) p *= 2;
+  return p;
+}
+
+// One block.  Each expert's nblk per-block counts are handled by P lanes of
+// one warp (a contiguous chunk of blocks per lane): totals, then the expert
+// scans (warp 0), then each block's starting padded row, the padding rows
+// (row_flat = -1) and the tile -> expert table, all spread over the lanes.
 __global__ void dispatch_scan_kernel(int* __restrict__ block_base, int nblk, int E,
                                      int* __restrict__ counts, int* __restrict__ offsets,
                                      int* __restrict__ pad_offsets, int* __restrict__ row_flat,
@@ -95,16 +107,42 @@ __global__ void dispatch_scan_kernel(int* __restrict__ block_base, int nblk, int
   extern __shared__ int sh[];  // counts[E], pad_start[E+1]
   int* cnt = sh;
   int* pst = sh + E;
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+  const int P = scan_parts(E, blockDim.x);
+  const int groups = blockDim.x / P;
+  const int part = threadIdx.x % P;
+  const int slot = threadIdx.x / P;
+  const int lane = threadIdx.x & 31;
+  const int per = (nblk + P - 1) / P;
+  const int b0 = part * per;
+  const int b1 = min(nblk, b0 + per);
+  for (int e0 = 0; e0 < E; e0 += groups) {  // same trip count for every thread
+    const int e = e0 + slot;
     int c = 0;
-#pragma unroll 8
-    for (int b = 0; b < nblk; ++b) c += block_base[e * nblk + b];
-    cnt[e] = c;
+    if (e < E)
+      for (int b = b0; b < b1; ++b) c += block_base[static_cast<long long>(e) * nblk + b];
+    for (int o = 1; o < P; o <<= 1) c += __shfl_xor_sync(0xffffffffu, c, o, P);
+    if (e < E && part == 0) cnt[e] = c;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, prun = 0;
-    for (int e = 0; e < E; ++e) {
+  if (threadIdx.x < 32) {
+    const int per_l = (E + 31) / 32;
+    const int a = min(E, lane * per_l), z = min(E, a + per_l);
+    int s = 0, ps = 0;
+    for (int e = a; e < z; ++e) {
+      s += cnt[e];
+      ps += (cnt[e] + kRowTile - 1) / kRowTile * kRowTile;
+    }
+    int is = s, ips = ps;
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, is, o);
+      const int w = __shfl_up_sync(0xffffffffu, ips, o);
+      if (lane >= o) {
+        is += v;
+        ips += w;
+      }
+    }
+    int run = is - s, prun = ips - ps;
+    for (int e = a; e < z; ++e) {
       run += cnt[e];
       offsets[e] = run;
       counts[e] = cnt[e];
@@ -112,20 +150,33 @@ __global__ void dispatch_scan_kernel(int* __restrict__ block_base, int nblk, int
       pad_offsets[e] = prun;
       prun += (cnt[e] + kRowTile - 1) / kRowTile * kRowTile;
     }
-    pst[E] = prun;
-    pad_offsets[E] = prun;
+    if (lane == 31) {
+      pst[E] = ips;
+      pad_offsets[E] = ips;
+    }
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int run = pst[e];
-#pragma unroll 8
-    for (int b = 0; b < nblk; ++b) {
-      const int c = block_base[e * nblk + b];
-      block_base[e * nblk + b] = run;
-      run += c;
+  for (int e0 = 0; e0 < E; e0 += groups) {
+    const int e = e0 + slot;
+    int c = 0;
+    if (e < E)
+      for (int b = b0; b < b1; ++b) c += block_base[static_cast<long long>(e) * nblk + b];
+    int inc = c;
+    for (int o = 1; o < P; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, inc, o, P);
+      if (part >= o) inc += v;
     }
-    for (int r = pst[e] + cnt[e]; r < pst[e + 1]; ++r) row_flat[r] = -1;
-    for (int j = pst[e] / kRowTile; j < pst[e + 1] / kRowTile; ++j) tile_expert[j] = e;
+    if (e < E) {
+      int run = pst[e] + inc - c;
+      for (int b = b0; b < b1; ++b) {
+        const long long i = static_cast<long long>(e) * nblk + b;
+        const int v = block_base[i];
+        block_base[i] = run;
+        run += v;
+      }
+      for (int r = pst[e] + cnt[e] + part; r < pst[e + 1]; r += P) row_flat[r] = -1;
+      for (int j = pst[e] / kRowTile + part; j < pst[e + 1] / kRowTile; j += P) tile_expert[j] = e;
+    }
   }
 }
 
