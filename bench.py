@@ -269,8 +269,11 @@ def run_reference(args, c):
 
 
 def config_block(args, c, n):
-    par = (f"ep{n} (experts sharded, NCCL all_to_all)" if c.get("ep")
-           else f"dp{n} (replicated experts)")
+    if c.get("ep"):
+        par = (f"ep{n} (experts sharded, NCCL all_to_all, one row per (token, rank))" if n > 1
+               else "ep1 = the single-GPU layer, all experts local (the scaling baseline)")
+    else:
+        par = f"dp{n} (replicated experts)"
     return {"workload": f"{args.config}: single Qwen3-MoE layer fwd+bwd (BASELINE configs"
                         f"[{CONFIG_INDEX[args.config]}])",
             "tokens_per_gpu": c["T"], "global_batch": c["T"] * n, "hidden": c["H"],
@@ -306,10 +309,7 @@ def main():
     cfg = SimpleNamespace(hidden_size=c["H"], num_experts=c["E"], num_experts_per_tok=c["k"],
                           moe_intermediate_size=c["I"], norm_topk_prob=True)
     w_r, w_gu, w_d = make_weights(c, 0)
-    if c.get("ep"):
-        if world == 1 and not dist.is_initialized():
-            dist.init_process_group("nccl", rank=0, world_size=1, device_id=dev,
-                                    init_method="tcp://127.0.0.1:29517")
+    if c.get("ep") and world > 1:
         from spark_gpt_b200.ep import ExpertParallelMoE
         layer = ExpertParallelMoE(cfg).to(dev)
         lo, hi = layer.expert_offset, layer.expert_offset + layer.local_experts
@@ -357,6 +357,8 @@ def main():
     names = list(gemm_flops(c, T)) + ["gather", "combine", "combine_bwd", "gather_bwd",
                                       "dispatch", "router_topk", "router_topk_bwd", "cast",
                                       "lb_stats", "lb_grad", "lb_finalize"]
+    if c.get("ep"):
+        names += ["ep_route", "ep_pack", "ep_unpack", "ep_weight_grad", "all_to_all"]
     timing = ops.set_timing(names)
     launches0 = ops.LAUNCHES["count"]
     barrier()

@@ -107,7 +107,11 @@ long long b200moe_dispatch_scratch_bytes(long long T, int k, int E);
  *   row_flat (Rcap) int32    padded row -> flat slot t*k+s, -1 for padding
  *   inv_pad (R) int32        flat slot -> padded row
  *   tile_expert (Rcap/128)   expert of each 128-row tile
- * Inside an expert, rows keep flat-slot order (= torch.sort(stable=True)). */
+ * Inside an expert, rows keep flat-slot order (= torch.sort(stable=True)).
+ * A negative id marks a slot that goes to no expert: it gets no row and
+ * inv_pad = -1; the gather, combine and gather-backward entry points skip such
+ * slots (the combine backward gives them d_weights = 0).  Ids >= E set fault
+ * bit 2. */
 int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* counts,
                      int* offsets, int* pad_offsets, int* row_flat, int* inv_pad,
                      int* tile_expert, void* scratch, long long scratch_bytes, void* stream);
@@ -240,6 +244,44 @@ int b200moe_expert_wgrad_gather_b(const void* a, int M, const void* x, int N, co
 int b200moe_expert_wgrad_gather_a(const void* src, int M, const int* row_flat, long long T, int k,
                                   const void* b, int N, const int* pad_offsets, int E,
                                   long long rows_cap, float* dw, int accumulate, void* stream);
+
+/* ---- expert parallel: experts sharded over P ranks -----------------------
+ * The reference trains data-parallel only (experts replicated; Experts.forward,
+ * train.py:2262-2322, runs every expert on every rank).  These entry points
+ * serve the expert-parallel layout of the same layer: rank r owns experts
+ * [r*Er, (r+1)*Er), Er = experts_per_rank; each token travels once to every
+ * rank that owns one of its k experts, as one row with k packed slot words
+ * (uint32: bf16 routing-weight bits << 16 | local expert id, or 0xFFFF in the
+ * low half when the slot's expert lives elsewhere).  The rows cross the fabric
+ * with NCCL all-to-all; the owner runs its experts on the received rows as a
+ * k-slot layer whose foreign slots are skipped. */
+
+/* dest (T,P) int64: dest[t*P+r] = r if token t selected an expert of rank r,
+ * else -1; b200moe_dispatch(dest, T, P, P, ...) then gives the send layout
+ * (rank-major, token order within a rank, 128-row padded blocks).
+ * slot_counts (P) int32 = routed slots per destination rank (set here). */
+int b200moe_ep_route(const long long* selected, long long T, int k, int experts_per_rank,
+                     int ranks, long long* dest, int* slot_counts, void* stream);
+
+/* meta (rows_cap, k) uint32 slot words of the send rows p < pad_offsets[P]
+ * (row_flat/pad_offsets from the dispatch of dest); padding rows get 0xFFFF
+ * words.  weights (T,k) bf16 routing weights. */
+int b200moe_ep_pack(const long long* selected, const void* weights, const int* row_flat,
+                    const int* pad_offsets, long long rows_cap, int k, int experts_per_rank,
+                    int ranks, unsigned int* meta, void* stream);
+
+/* Owner side: meta (rows, k) -> selected_local (rows, k) int64 local expert ids
+ * (-1 for foreign slots) and weights_local (rows, k) bf16 (0 for foreign slots). */
+int b200moe_ep_unpack(const unsigned int* meta, long long rows, int k, long long* selected_local,
+                      void* weights_local, void* stream);
+
+/* Source side: d_weights (T,k) fp32 of the routing weights from the owners'
+ * per-row slot gradients dw_rows (send rows, k) fp32 (returned in the send
+ * layout): d_weights[t*k+s] = dw_rows[inv_send[t*P + sel[t,s]/Er]*k + s];
+ * inv_send (T*P) is the inv_pad of the dispatch of dest. */
+int b200moe_ep_weight_grad(const float* dw_rows, const int* inv_send, const long long* selected,
+                           long long T, int k, int experts_per_rank, int ranks, float* d_weights,
+                           void* stream);
 
 /* ---- load-balancing loss: global_load_balancing_loss (train.py:3098-3197) */
 

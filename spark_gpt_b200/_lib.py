@@ -52,6 +52,10 @@ PROTOTYPES = {
                                               P, L, P]),
     "b200moe_expert_wgrad_gather_b": (I, [P, I, P, I, P, L, I, P, I, L, P, I, P]),
     "b200moe_expert_wgrad_gather_a": (I, [P, I, P, L, I, P, I, P, I, L, P, I, P]),
+    "b200moe_ep_route": (I, [P, L, I, I, I, P, P, P]),
+    "b200moe_ep_pack": (I, [P, P, P, P, L, I, I, I, P, P]),
+    "b200moe_ep_unpack": (I, [P, L, I, P, P, P]),
+    "b200moe_ep_weight_grad": (I, [P, P, P, L, I, I, I, P, P]),
     "b200moe_lb_scratch_bytes": (L, [L, I]),
     "b200moe_lb_stats": (I, [P, L, P, P, L, I, I, P, P, L, P]),
     "b200moe_lb_finalize": (I, [P, I, I, I, P, P, P, P]),

@@ -13,6 +13,7 @@
 #include "grouped_gemm.cuh"
 #include "grouped_gemm_2sm.cuh"
 #include "routing.cuh"
+#include "ep.cuh"
 
 namespace b200moe {
 namespace {
@@ -592,7 +593,7 @@ int b200moe_gather_rows(const void* x, const int* row_flat, const int* inv_pad,
   auto* xsp = static_cast<__nv_bfloat16*>(xs);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (B200MOE_TOKEN_ORDER && inv_pad) {
-    REQUIRE(k <= 32 && T >= 0 && T * k <= rows_cap, "gather_rows: need k <= 32, T*k <= rows_cap");
+    REQUIRE(k <= 32 && T >= 0, "gather_rows: need k <= 32");
     const int grid = grid_for(T > rows_cap / 32 ? T : rows_cap / 32, 8);
     const int* tot = pad_offsets + E;
     switch (H) {
@@ -677,7 +678,7 @@ int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat, c
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
   if (B200MOE_TOKEN_ORDER && inv_pad && k <= 32 &&
       (H == 256 || H == 512 || H == 1024 || H == 2048)) {
-    REQUIRE(T >= 0 && T * k <= rows_cap, "combine_bwd: T*k exceeds rows_cap");
+    REQUIRE(T >= 0, "combine_bwd: negative T");
     const int grid = grid_for(T > rows_cap / 32 ? T : rows_cap / 32, 8);
     const int* tot = pad_offsets + E;
     switch (H) {
@@ -687,6 +688,11 @@ int b200moe_combine_bwd(const void* d_out, const void* y, const int* row_flat, c
       default: combine_bwd_tokens_kernel<8><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights); break;
     }
     return check_launch("combine_bwd");
+  }
+  if (inv_pad && T * k > 0) {  // slots without an expert have no row: their d_weights are 0
+    zero_skipped_slots_kernel<<<grid_for(T * k, 256), 256, 0, st>>>(inv_pad, T * k, d_weights);
+    const int rc = check_launch("combine_bwd zero skipped");
+    if (rc) return rc;
   }
   const int grid = grid_for(rows_cap, 8);
   switch (H) {
@@ -1051,6 +1057,60 @@ int b200moe_expert_wgrad_gather_a(const void* src, int M, const int* row_flat, l
   if (BN == 256) return launch_gemm<256, true, true, kEpiStoreF32, kKRagged, kGatherA>(ta, tb, p, st, "wgrad_gather_a");
   if (BN == 128) return launch_gemm<128, true, true, kEpiStoreF32, kKRagged, kGatherA>(ta, tb, p, st, "wgrad_gather_a");
   return launch_gemm<64, true, true, kEpiStoreF32, kKRagged, kGatherA>(ta, tb, p, st, "wgrad_gather_a");
+}
+
+// ---------------------------------------------------------------- expert parallel
+int b200moe_ep_route(const long long* selected, long long T, int k, int experts_per_rank,
+                     int ranks, long long* dest, int* slot_counts, void* stream) {
+  REQUIRE(selected && dest && slot_counts, "ep_route: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= kEpMaxRanks && experts_per_rank >= 1 && k >= 1 &&
+              k <= kMaxTopK && T >= 0,
+          "ep_route: need 1 <= ranks <= %d, experts_per_rank >= 1, 1 <= k <= %d", kEpMaxRanks,
+          kMaxTopK);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(slot_counts, 0, ranks * sizeof(int), st);
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "ep_route: %s", cudaGetErrorString(e));
+  if (T == 0) return B200MOE_OK;
+  ep_route_kernel<<<grid_for(T, 256), 256, 0, st>>>(selected, T, k, experts_per_rank, ranks, dest,
+                                                    slot_counts);
+  return check_launch("ep_route");
+}
+
+int b200moe_ep_pack(const long long* selected, const void* weights, const int* row_flat,
+                    const int* pad_offsets, long long rows_cap, int k, int experts_per_rank,
+                    int ranks, unsigned int* meta, void* stream) {
+  REQUIRE(selected && weights && row_flat && pad_offsets && meta, "ep_pack: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= kEpMaxRanks && experts_per_rank >= 1 && k >= 1 &&
+              k <= kMaxTopK && rows_cap >= 0,
+          "ep_pack: bad ranks/k");
+  if (rows_cap == 0) return B200MOE_OK;
+  ep_pack_kernel<<<grid_for(rows_cap * k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      selected, static_cast<const unsigned short*>(weights), row_flat, pad_offsets + ranks, k,
+      experts_per_rank, ranks, meta);
+  return check_launch("ep_pack");
+}
+
+int b200moe_ep_unpack(const unsigned int* meta, long long rows, int k, long long* selected_local,
+                      void* weights_local, void* stream) {
+  REQUIRE(meta && selected_local && weights_local, "ep_unpack: null pointer");
+  REQUIRE(rows >= 0 && k >= 1 && k <= kMaxTopK, "ep_unpack: bad rows/k");
+  if (rows == 0) return B200MOE_OK;
+  ep_unpack_kernel<<<grid_for(rows * k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      meta, rows * k, selected_local, static_cast<unsigned short*>(weights_local));
+  return check_launch("ep_unpack");
+}
+
+int b200moe_ep_weight_grad(const float* dw_rows, const int* inv_send, const long long* selected,
+                           long long T, int k, int experts_per_rank, int ranks, float* d_weights,
+                           void* stream) {
+  REQUIRE(dw_rows && inv_send && selected && d_weights, "ep_weight_grad: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= kEpMaxRanks && experts_per_rank >= 1 && k >= 1 &&
+              k <= kMaxTopK && T >= 0,
+          "ep_weight_grad: bad ranks/k");
+  if (T == 0) return B200MOE_OK;
+  ep_weight_grad_kernel<<<grid_for(T * k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      dw_rows, inv_send, selected, T, k, experts_per_rank, ranks, d_weights);
+  return check_launch("ep_weight_grad");
 }
 
 // ---------------------------------------------------------------- load balancing

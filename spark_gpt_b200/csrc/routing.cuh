@@ -64,7 +64,9 @@ __global__ void reduce_splits_kernel(const float* __restrict__ partial, int spli
 
 // ---------------------------------------------------------------------------
 // dispatch (spark-gpt train.py:2271-2290): stable counting sort of the flat
-// expert ids into expert blocks padded to kRowTile rows.
+// expert ids into expert blocks padded to kRowTile rows.  A negative id marks
+// a slot that goes to no expert (the expert-parallel layer's rows carry only
+// the slots of one rank's experts): it gets no row and inv_pad = -1.
 //   block_base[e * nblk + b]: rows of expert e in chunk b (pass 1), then the
 //   padded start of those rows (pass 2).
 // ---------------------------------------------------------------------------
@@ -80,8 +82,8 @@ __global__ void dispatch_count_kernel(const long long* __restrict__ sel, long lo
       const long long e = sel[f];
       if (e >= 0 && e < E)
         atomicAdd(&hist[e], 1);
-      else
-        raise_fault(kFaultBadExpert);
+      else if (e >= E)
+        raise_fault(kFaultBadExpert);  // negative: the slot goes to no expert
     }
   }
   __syncthreads();
@@ -226,6 +228,8 @@ __global__ void dispatch_scatter_kernel(const long long* __restrict__ sel, long 
     if (e >= 0) {
       row_flat[pos] = static_cast<int>(f);
       inv_pad[f] = pos;
+    } else if (f < R) {
+      inv_pad[f] = -1;  // a slot without an expert has no row
     }
   }
 }
@@ -314,6 +318,7 @@ __global__ void scatter_rows_kernel(const __nv_bfloat16* __restrict__ x,
       for (int j = 0; j < VPL; ++j) v[j] = __ldg(src + lane + 32 * j);
       for (int s = 0; s < k; ++s) {
         const long long r = __shfl_sync(0xffffffffu, rl, s);
+        if (r < 0) continue;  // slot without an expert
         uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
 #pragma unroll
         for (int j = 0; j < VPL; ++j) dst[lane + 32 * j] = v[j];
@@ -321,6 +326,7 @@ __global__ void scatter_rows_kernel(const __nv_bfloat16* __restrict__ x,
     } else {
       for (int s = 0; s < k; ++s) {
         const long long r = __shfl_sync(0xffffffffu, rl, s);
+        if (r < 0) continue;
         uint4* dst = reinterpret_cast<uint4*>(xs + r * H);
         for (int v = lane; v < nvec; v += 32) dst[v] = __ldg(src + v);
       }
@@ -368,9 +374,9 @@ __global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_ou
     uint4 bn[VPL];
     {
       const long long r0 = __shfl_sync(0xffffffffu, rl, 0);
-      const uint4* yy = reinterpret_cast<const uint4*>(y + r0 * H);
+      const uint4* yy = reinterpret_cast<const uint4*>(y + (r0 < 0 ? 0 : r0) * H);
 #pragma unroll
-      for (int j = 0; j < VPL; ++j) bn[j] = __ldg(yy + lane + 32 * j);
+      for (int j = 0; j < VPL; ++j) bn[j] = r0 >= 0 ? __ldg(yy + lane + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
     }
     for (int s = 0; s < k; ++s) {
       const long long r = __shfl_sync(0xffffffffu, rl, s);
@@ -379,11 +385,12 @@ __global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_ou
 #pragma unroll
       for (int j = 0; j < VPL; ++j) b[j] = bn[j];
       const long long rn = __shfl_sync(0xffffffffu, rl, s + 1 < k ? s + 1 : s);
-      if (s + 1 < k) {
+      if (s + 1 < k && rn >= 0) {
         const uint4* yy = reinterpret_cast<const uint4*>(y + rn * H);
 #pragma unroll
         for (int j = 0; j < VPL; ++j) bn[j] = __ldg(yy + lane + 32 * j);
       }
+      if (r < 0) continue;  // slot without an expert: d_weights stays 0
       uint4* dst = reinterpret_cast<uint4*>(dy + r * H);
       float dot = 0.f;
 #pragma unroll
@@ -429,7 +436,7 @@ __global__ void gather_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dxs,
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 #pragma unroll
       for (int s = 0; s < kMaxTopK; ++s) {
-        if (s < k) {
+        if (s < k && rows[s] >= 0) {
           const uint4 w = __ldg(reinterpret_cast<const uint4*>(dxs + static_cast<long long>(rows[s]) * H) + v);
           acc[0] += bf16_lo(w.x); acc[1] += bf16_hi(w.x);
           acc[2] += bf16_lo(w.y); acc[3] += bf16_hi(w.y);
@@ -481,7 +488,7 @@ __global__ void combine_fwd_kernel(const __nv_bfloat16* __restrict__ y,
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 #pragma unroll
       for (int s = 0; s < kMaxTopK; ++s) {
-        if (s < k) {
+        if (s < k && rows[s] >= 0) {
           const uint4 q = __ldg(reinterpret_cast<const uint4*>(y + static_cast<long long>(rows[s]) * H) + v);
           acc[0] += bf16_round(bf16_lo(q.x) * w[s]); acc[1] += bf16_round(bf16_hi(q.x) * w[s]);
           acc[2] += bf16_round(bf16_lo(q.y) * w[s]); acc[3] += bf16_round(bf16_hi(q.y) * w[s]);
@@ -570,10 +577,15 @@ __global__ void combine_bwd_token_major_kernel(const __nv_bfloat16* __restrict__
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long f = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
        f < R; f += warps) {
+    const int row = inv_pad[f];
+    if (row < 0) {  // slot without an expert
+      if (lane == 0) d_weights[f] = 0.f;
+      continue;
+    }
     const float w = __bfloat162float(weights[f]);
     const uint4* g = reinterpret_cast<const uint4*>(d_out + (f / k) * H);
     const uint4* yy = reinterpret_cast<const uint4*>(y_tok + f * H);
-    uint4* dst = reinterpret_cast<uint4*>(dy + static_cast<long long>(inv_pad[f]) * H);
+    uint4* dst = reinterpret_cast<uint4*>(dy + static_cast<long long>(row) * H);
     float dot = 0.f;
     for (int v = lane; v < nvec; v += 32) {
       const uint4 a = __ldg(g + v);
@@ -618,7 +630,8 @@ __global__ void zero_pad_rows_kernel(const int* __restrict__ row_flat,
 //   out[t] = sum_s c(s) + addend[t],   c(s) = bf16(rows[j] * w[t,s])  (weights)
 //                                       c(s) = rows[j]                 (no weights)
 //   j = inv_pad[t*k+s] (or t*k+s when rows are token-major); fp32 accumulation
-//   in slot order, one rounding to bf16.
+//   in slot order, one rounding to bf16.  Slots with j = -1 (no expert)
+//   contribute nothing and are not copied.
 // Warp 0 produces: lane s < k issues the 2*H-byte bulk copy of row s of a
 // token into a ring slot.  Consumers are kReduceGroups groups of
 // kReduceWarpsPerToken warps; the warps of a group split the H columns of one
@@ -673,14 +686,18 @@ __global__ void __launch_bounds__(kReduceThreads)
         const long long i = g + tt;
         const int s = static_cast<int>(i % slots);
         const uint32_t ph = static_cast<uint32_t>((i / slots) & 1);
+        // slots without an expert (row -1) are not copied; the barrier expects
+        // the bytes of the token's real rows only (zero bytes complete it at once)
+        const bool mine = active_lane && lane / k == tt && idx >= 0;
+        const uint32_t nrows = __popc(__ballot_sync(0xffffffffu, mine));
         int good = 1;
         if (lane == 0) {
           good = mbar_wait(&empty[s], ph ^ 1u, abort_flag) ? 1 : 0;
-          if (good) mbar_expect_tx(&full[s], slot_bytes);
+          if (good) mbar_expect_tx(&full[s], nrows * row_bytes);
         }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) break;
-        if (active_lane && lane / k == tt)
+        if (mine)
           bulk_load(rsm + static_cast<size_t>(s) * slot_bytes + (lane % k) * row_bytes,
                     rows + idx * H, row_bytes, &full[s]);
       }
@@ -703,6 +720,10 @@ __global__ void __launch_bounds__(kReduceThreads)
       // the column loop (lanes past the last column skip it: no shuffle inside)
       float wv = 1.f;
       if (weights && lane < k) wv = __bfloat162float(weights[t * k + lane]);
+      // slots with a row (inv_pad >= 0); the others were not copied
+      const unsigned have =
+          inv_pad ? __ballot_sync(0xffffffffu, lane < k && inv_pad[t * k + lane] >= 0)
+                  : (k >= 32 ? 0xffffffffu : (1u << k) - 1u);
       __nv_bfloat162 wr[kMaxTopK];
 #pragma unroll
       for (int r = 0; r < kMaxTopK; ++r)
@@ -714,7 +735,7 @@ __global__ void __launch_bounds__(kReduceThreads)
         for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 #pragma unroll
         for (int r = 0; r < kMaxTopK; ++r) {
-          if (r < k) {
+          if (r < k && ((have >> r) & 1u)) {
             uint4 q = *reinterpret_cast<const uint4*>(slot + r * row_bytes + v * 16);
             if (weights) {
               // bf16 x bf16 product rounded once to bf16 (= bf16(float(a)*float(b)))

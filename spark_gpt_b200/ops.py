@@ -8,6 +8,7 @@ the outputs.  Shapes follow spark-gpt's MoE path (train.py:2134-2334).
 from __future__ import annotations
 
 import ctypes
+from contextlib import contextmanager
 from dataclasses import dataclass
 
 import torch
@@ -26,6 +27,20 @@ def set_timing(names):
     global _timing
     _timing = None if names is None else {n: [] for n in names}
     return _timing
+
+
+@contextmanager
+def timed(name: str):
+    """CUDA events on the current stream around a block (e.g. a collective)."""
+    if _timing is not None and name in _timing:
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        yield
+        e.record()
+        _timing[name].append((s, e))
+    else:
+        yield
 
 
 def _launch(name: str, kernels: int, fn, *args):
@@ -169,12 +184,15 @@ class Dispatch:
     num_experts: int
 
 
-def dispatch(selected: torch.Tensor, num_experts: int) -> Dispatch:
+def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None = None) -> Dispatch:
+    """Negative ids mark slots without an expert (no row, inv_pad -1);
+    routed_slots, when given, is the number of non-negative ids and sizes the
+    padded-row buffers."""
     _check(selected, torch.int64, "dispatch selected")
     T, k = selected.shape
     R = T * k
     dev = selected.device
-    cap = padded_rows(R, num_experts)
+    cap = padded_rows(R if routed_slots is None else routed_slots, num_experts)
     i32 = dict(device=dev, dtype=torch.int32)
     counts = torch.empty(num_experts, **i32)
     offsets = torch.empty(num_experts, **i32)
@@ -346,6 +364,52 @@ def wgrad_gather_a(src, b, d: Dispatch, name="wgrad", out=None, accumulate=False
             d.top_k, _p(b), N, _p(d.pad_offsets), d.num_experts, d.rows_cap, _p(out),
             int(accumulate), _s(b))
     return out
+
+
+# --------------------------------------------------------------------------- #
+# expert parallel: send plan, slot words, routing-weight gradient
+# --------------------------------------------------------------------------- #
+def ep_route(selected: torch.Tensor, experts_per_rank: int, ranks: int):
+    """dest (T, P) int64 (r or -1 per destination rank) and the routed slots
+    per destination rank (P,) int32."""
+    _check(selected, torch.int64, "ep_route selected")
+    T, k = selected.shape
+    dest = torch.empty(T, ranks, device=selected.device, dtype=torch.int64)
+    slots = torch.empty(ranks, device=selected.device, dtype=torch.int32)
+    _launch("ep_route", 1, "b200moe_ep_route", _p(selected), T, k, experts_per_rank, ranks,
+            _p(dest), _p(slots), _s(selected))
+    return dest, slots
+
+
+def ep_pack(selected, weights, send: Dispatch, experts_per_rank: int) -> torch.Tensor:
+    """(send.rows_cap, k) int32 slot words of the send rows."""
+    _check(weights, BF16, "ep_pack weights")
+    k = selected.shape[1]
+    meta = torch.empty(send.rows_cap, k, device=selected.device, dtype=torch.int32)
+    _launch("ep_pack", 1, "b200moe_ep_pack", _p(selected), _p(weights), _p(send.row_flat),
+            _p(send.pad_offsets), send.rows_cap, k, experts_per_rank, send.num_experts,
+            _p(meta), _s(selected))
+    return meta
+
+
+def ep_unpack(meta: torch.Tensor):
+    """slot words (n, k) -> local expert ids (n, k) int64 (-1: foreign) and bf16 weights."""
+    _check(meta, torch.int32, "ep_unpack meta")
+    n, k = meta.shape
+    sel = torch.empty(n, k, device=meta.device, dtype=torch.int64)
+    w = torch.empty(n, k, device=meta.device, dtype=BF16)
+    if n:
+        _launch("ep_unpack", 1, "b200moe_ep_unpack", _p(meta), n, k, _p(sel), _p(w), _s(meta))
+    return sel, w
+
+
+def ep_weight_grad(dw_rows, send: Dispatch, selected, experts_per_rank: int) -> torch.Tensor:
+    T, k = selected.shape
+    d_w = torch.empty(T, k, device=selected.device, dtype=torch.float32)
+    if T:
+        _launch("ep_weight_grad", 1, "b200moe_ep_weight_grad", _p(dw_rows), _p(send.inv_pad),
+                _p(selected), T, k, experts_per_rank, send.num_experts, _p(d_w), _s(selected))
+    return d_w
 
 
 # --------------------------------------------------------------------------- #

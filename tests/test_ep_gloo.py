@@ -1,12 +1,12 @@
-"""Expert-parallel orchestration on CPU ranks (gloo, world size 2).
+"""Expert-parallel orchestration on CPU ranks (gloo, world sizes 2 and 4).
 
 spark_gpt_b200.ep.ExpertParallelMoE is driven with an oracle-backed ops
-object in place of the device kernels, so the routing, the send order, the
-all_to_all_single exchanges and the backward's reverse exchanges are checked
-on CPU: every rank's output and input gradient must equal the single-process
-oracle layer on that rank's tokens, and each rank's expert-shard gradients
-must equal the oracle's gradients of those experts summed over both ranks'
-tokens.  Test infrastructure only: the product path runs the CUDA kernels.
+object in place of the device kernels, so the routing, the per-(token, rank)
+send plan, the all_to_all_single exchanges, the owner-side partial combine and
+the backward's reverse exchanges are checked on CPU: every rank's output and
+input gradient must equal the single-process oracle layer on that rank's
+tokens, and each rank's expert-shard gradients must equal the oracle's
+gradients of those experts summed over all ranks' tokens.  Test infrastructure only: the product path runs the CUDA kernels.
 """
 
 import os
@@ -23,7 +23,11 @@ from oracle import moe_oracle as O
 
 
 class OracleOps:
-    """CPU stand-in for spark_gpt_b200.ep.CudaExpertOps (fp32 oracle math)."""
+    """CPU stand-in for spark_gpt_b200.ep.CudaExpertOps (fp32 oracle math).
+
+    Same send plan as the device path: one row per (token, destination rank)
+    in rank-major, token order, with the row's k slots marked by local expert
+    id (or -1) and routing weight; slot words are fp32 pairs here."""
 
     @staticmethod
     def router(x, w_router, num_experts, top_k, norm):
@@ -39,43 +43,76 @@ class OracleOps:
         return dx, dwr
 
     @staticmethod
-    def row_map(order, inv, top_k):
-        return SimpleNamespace(order=order, inv=inv, k=top_k)
+    def send_plan(sel, rw, experts_per_rank, ranks):
+        T, k = sel.shape
+        dest = torch.div(sel, experts_per_rank, rounding_mode="floor")
+        mask = torch.zeros(T, ranks, dtype=torch.bool)
+        mask[torch.arange(T).unsqueeze(1).expand(T, k), dest] = True
+        pairs = mask.t().nonzero()                     # (rank, token), rank-major
+        rank_of, tok = pairs[:, 0], pairs[:, 1]
+        inv = torch.full((T, ranks), -1, dtype=torch.int64)
+        inv[tok, rank_of] = torch.arange(len(tok))
+        mine = dest[tok] == rank_of.unsqueeze(1)       # (rows, k)
+        ids = torch.where(mine, sel[tok] % experts_per_rank, torch.full_like(sel[tok], -1))
+        w = torch.where(mine, rw[tok].float(), torch.zeros(()))
+        meta = torch.cat([ids.float(), w], 1)
+        sizes = torch.stack([mask.sum(0), torch.bincount(dest.reshape(-1), minlength=ranks)], 1)
+        plan = SimpleNamespace(tok=tok, inv=inv, k=k, experts_per_rank=experts_per_rank,
+                               meta=meta)
+        return plan, sizes.to(torch.int64)
 
     @staticmethod
-    def experts_fwd(rows, ids, w_gu, w_d):
-        n = rows.shape[0]
-        d = O.dispatch(ids.view(n, 1).long(), w_gu.shape[0])
-        xs = rows.float()[torch.from_numpy(d.permutation)]
+    def pack_rows(src, plan):
+        return src.float()[plan.tok]
+
+    @staticmethod
+    def unpack(meta):
+        k = meta.shape[1] // 2
+        return meta[:, :k].long(), meta[:, k:]
+
+    @staticmethod
+    def experts_fwd(rows, sel_loc, w_loc, w_gu, w_d, slots):
+        row_of, slot_of = (sel_loc >= 0).nonzero(as_tuple=True)
+        ids = sel_loc[row_of, slot_of]
+        n = len(ids)
+        d = O.dispatch(ids.view(n, 1), w_gu.shape[0])
+        perm = torch.from_numpy(d.permutation)
+        xs = rows.float()[row_of][perm]
         gu, h = O.swiglu_forward(xs, w_gu, d.offsets)
-        y = O.grouped_linear_forward(h, w_d, d.offsets)
-        return y[torch.from_numpy(d.inverse)], (d, xs, gu, h, w_gu, w_d)
+        y = O.grouped_linear_forward(h, w_d, d.offsets)[torch.from_numpy(d.inverse)]
+        w = w_loc[row_of, slot_of].unsqueeze(1)
+        part = torch.zeros(rows.shape[0], rows.shape[1]).index_add_(0, row_of, y * w)
+        return part, (d, row_of, slot_of, w, xs, gu, h, y, w_gu, w_d)
 
     @staticmethod
-    def experts_bwd(ctx, dy_rows, E, H, I, device):
-        d, xs, gu, h, w_gu, w_d = ctx
-        dy = dy_rows.float()[torch.from_numpy(d.permutation)]
+    def experts_bwd(ctx, d_rows, k, E, H, I, device):
+        d, row_of, slot_of, w, xs, gu, h, y, w_gu, w_d = ctx
+        g = d_rows.float()[row_of]
+        dw = torch.zeros(d_rows.shape[0], k)
+        dw[row_of, slot_of] = (g * y).sum(-1)
+        perm = torch.from_numpy(d.permutation)
+        dy = (g * w)[perm]
         dh, dwd = O.grouped_linear_backward(h, w_d, dy, d.offsets)
         dxs, dwgu, _ = O.swiglu_backward(xs, w_gu, gu, dh, d.offsets)
-        return dxs[torch.from_numpy(d.inverse)], dwgu, dwd
+        dxs = dxs[torch.from_numpy(d.inverse)]
+        dx = torch.zeros(d_rows.shape[0], H).index_add_(0, row_of, dxs)
+        return dx, dw, dwgu, dwd
 
     @staticmethod
-    def combine(y_sorted, rm, rw):
-        rows = y_sorted.float()[rm.inv] * rw.reshape(-1, 1).float()
-        return rows.view(-1, rm.k, rows.shape[-1]).sum(1)
+    def reduce_rows(rows_back, plan, addend=None):
+        T, P = plan.inv.shape
+        out = torch.zeros(T, rows_back.shape[1])
+        has = plan.inv >= 0
+        t_idx, r_idx = has.nonzero(as_tuple=True)
+        out.index_add_(0, t_idx, rows_back.float()[plan.inv[t_idx, r_idx]])
+        return out if addend is None else out + addend
 
     @staticmethod
-    def combine_bwd(d_out, y_sorted, rm, rw):
-        g = d_out.float()[torch.div(rm.order, rm.k, rounding_mode="floor")]
-        dy = g * rw.reshape(-1)[rm.order].unsqueeze(-1).float()
-        dw = torch.empty(rm.order.numel())
-        dw[rm.order] = (g * y_sorted.float()).sum(-1)
-        return dy, dw.view(-1, rm.k)
-
-    @staticmethod
-    def gather_bwd(dx_sorted, rm, addend):
-        rows = dx_sorted.float()[rm.inv]
-        return rows.view(-1, rm.k, rows.shape[-1]).sum(1) + addend
+    def weight_grad(dw_back, plan, sel):
+        T, k = sel.shape
+        r = torch.div(sel, plan.experts_per_rank, rounding_mode="floor")
+        rows = plan.inv[torch.arange(T).unsqueeze(1), r]
+        return dw_back[rows, torch.arange(k).unsqueeze(0)]
 
     @staticmethod
     def cast(w):
@@ -129,8 +166,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_expert_parallel_matches_single_process_oracle():
-    world = 2
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_parallel_matches_single_process_oracle(world):
     mgr = mp.get_context("spawn").Manager()
     results = mgr.dict()
     mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world,

@@ -1,11 +1,12 @@
 """Expert-parallel layer on 2 GPUs over NCCL against the single-GPU layer.
 
-Each rank holds half of the experts; its output, input gradient and router
-gradient must equal spark_gpt_b200.SparseMoE (all experts on one GPU) on the
-same tokens: bit for bit for the output and input gradient (the same bf16
-products in the same order), within fp32 summation-order noise for the
-weight gradients (rows of an expert arrive in a different order).  Runs as two
-spawned processes; skipped where fewer than two GPUs are visible.
+Each rank holds half of the experts; its routing must equal
+spark_gpt_b200.SparseMoE's (all experts on one GPU) on the same tokens, and
+its output, input gradient and router gradient, and each expert shard's weight
+gradients summed over both ranks' tokens, must agree with it within the
+layer's bf16 tolerance (the owner rounds its partial sum of a token's local
+slots to bf16 before the source adds the two ranks' partial rows).  Runs as
+two spawned processes; skipped where fewer than two GPUs are visible.
 """
 
 import os
@@ -16,6 +17,8 @@ import pytest
 import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
+
+from tests.helpers import assert_bf16_close
 
 pytestmark = pytest.mark.gpu
 
@@ -99,10 +102,8 @@ def test_expert_parallel_two_gpus_matches_single_gpu_layer():
         r = results[rank]
         (o_ep, s_ep, dx_ep, dr_ep), (o_ref, s_ref, dx_ref, dr_ref) = r["ep"], r["ref"]
         assert torch.equal(s_ep, s_ref)
-        assert torch.equal(o_ep, o_ref)
-        assert torch.equal(dx_ep, dx_ref)
-        torch.testing.assert_close(dr_ep, dr_ref, rtol=1e-4, atol=1e-5)
-        scale = r["ref_gu"].abs().max().item()
-        torch.testing.assert_close(r["ep_gu"], r["ref_gu"], rtol=1e-3, atol=1e-3 * scale)
-        scale = r["ref_d"].abs().max().item()
-        torch.testing.assert_close(r["ep_d"], r["ref_d"], rtol=1e-3, atol=1e-3 * scale)
+        assert_bf16_close(o_ep, o_ref, "out")
+        assert_bf16_close(dx_ep, dx_ref, "dx")
+        assert_bf16_close(dr_ep, dr_ref, "dW_router")
+        assert_bf16_close(r["ep_gu"], r["ref_gu"], "dW_gate_up")
+        assert_bf16_close(r["ep_d"], r["ref_d"], "dW_down")

@@ -1,0 +1,233 @@
+"""Expert-parallel kernels on one GPU.
+
+1. Slots without an expert (negative ids): dispatch gives them no row and
+   inv_pad -1; gather, combine, gather backward and combine backward skip
+   them (d_weights 0).  Checked against torch references.
+2. The send-plan kernels (ep_route, ep_pack, ep_unpack, ep_weight_grad)
+   against a torch restatement of the plan: bit-exact.
+3. The whole expert-parallel data path with P ranks emulated on one GPU (the
+   all-to-all exchanges become slices of the ranks' send buffers): every
+   rank's output and input gradient match the single-GPU layer on its tokens,
+   and every expert shard's weight gradients match the single-GPU layer's
+   summed over all ranks' tokens, within the layer's bf16 tolerance.
+"""
+
+import pytest
+import torch
+from types import SimpleNamespace
+
+from tests.helpers import assert_bf16_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from spark_gpt_b200 import ops as _ops
+    return _ops
+
+
+def _partial_routing(T, k, E, seed, keep=0.4):
+    """top-k ids with a random subset of slots replaced by -1 (no expert)."""
+    g = torch.Generator().manual_seed(seed)
+    sel = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    drop = torch.rand(T, k, generator=g) > keep
+    drop[: T // 10] = True           # some rows with no slot at all
+    drop[T // 10: T // 5] = False    # some rows with every slot
+    return torch.where(drop, torch.full_like(sel, -1), sel)
+
+
+@pytest.mark.parametrize("T,k,E,H", [(3000, 8, 16, 2048), (2500, 4, 8, 1024),
+                                     (1700, 8, 8, 256), (900, 3, 5, 384)])
+def test_slots_without_expert_are_skipped(ops, T, k, E, H):
+    from spark_gpt_b200 import _lib
+    sel = _partial_routing(T, k, E, T + k)
+    valid = sel >= 0
+    S = int(valid.sum())
+    d = ops.dispatch(sel.to(DEV), E, routed_slots=S)
+    assert d.rows_cap == ops.padded_rows(S, E)
+    counts = torch.bincount(sel[valid], minlength=E)
+    assert torch.equal(d.counts.cpu().long(), counts)
+    inv = d.inv_pad.cpu().long().view(T, k)
+    assert torch.all(inv[~valid] == -1) and torch.all(inv[valid] >= 0)
+    rf = d.row_flat.cpu().long()
+    assert torch.equal(rf[inv[valid]], torch.arange(T * k).view(T, k)[valid])
+    # gather (token order) writes each valid slot's row, zero padding rows
+    x = torch.randn(T, H).to(torch.bfloat16)
+    xs = ops.gather_rows(x.to(DEV), d).cpu()
+    t_idx = torch.arange(T).unsqueeze(1).expand(T, k)
+    assert torch.equal(xs[inv[valid]], x[t_idx[valid]])
+    n = int(d.pad_offsets[-1])
+    assert torch.all(xs[:n][rf[:n] < 0] == 0)
+    # combine: skipped slots contribute nothing
+    y = torch.randn(d.rows_cap, H).to(torch.bfloat16)
+    w = torch.rand(T, k).to(torch.bfloat16)
+    out = ops.combine(y.to(DEV), d, w.to(DEV)).cpu().float()
+    inv0 = inv.clamp_min(0)
+    prod = (y.float()[inv0] * w.float().unsqueeze(-1)).to(torch.bfloat16).float()
+    ref = (prod * valid.unsqueeze(-1)).sum(1)
+    assert (out - ref).abs().max() <= 2 ** -7 * ref.abs().max()
+    # gather backward with addend
+    add = torch.randn(T, H).to(torch.bfloat16)
+    dx = ops.gather_rows_bwd(y.to(DEV), d, addend=add.to(DEV)).cpu().float()
+    ref = (y.float()[inv0] * valid.unsqueeze(-1)).sum(1) + add.float()
+    assert (dx - ref).abs().max() <= 2 ** -7 * ref.abs().max()
+    # combine backward: d_weights of skipped slots are 0
+    d_out = torch.randn(T, H).to(torch.bfloat16)
+    dy, dw = ops.combine_bwd(d_out.to(DEV), y.to(DEV), d, w.to(DEV))
+    dy, dw = dy.cpu().float(), dw.cpu()
+    assert torch.all(dw[~valid] == 0)
+    ref_dw = (d_out.float().unsqueeze(1) * y.float()[inv0]).sum(-1)
+    assert (dw[valid] - ref_dw[valid]).abs().max() <= 1e-4 * ref_dw.abs().max()
+    ref_dy = (d_out.float()[t_idx[valid]] * w.float()[valid].unsqueeze(-1)).to(torch.bfloat16)
+    assert torch.equal(dy[inv[valid]], ref_dy.float())
+    assert torch.all(dy[:n][rf[:n] < 0] == 0)
+    assert _lib.read_fault() == 0
+
+
+def _plan_ref(sel, rw, E_loc, P):
+    T, k = sel.shape
+    dest = sel // E_loc
+    mask = torch.zeros(T, P, dtype=torch.bool)
+    mask[torch.arange(T).unsqueeze(1).expand(T, k), dest] = True
+    dest_ids = torch.where(mask, torch.arange(P).expand(T, P), torch.full((T, P), -1))
+    return dest, mask, dest_ids
+
+
+@pytest.mark.parametrize("T,k,E,P", [(4096, 8, 128, 8), (3000, 8, 64, 2), (777, 4, 32, 4),
+                                     (500, 2, 16, 16)])
+def test_send_plan_kernels_bit_exact(ops, T, k, E, P):
+    E_loc = E // P
+    g = torch.Generator().manual_seed(T)
+    sel = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    rw = torch.rand(T, k, generator=g).to(torch.bfloat16)
+    dest, mask, dest_ids = _plan_ref(sel, rw, E_loc, P)
+    d_dest, d_slots = ops.ep_route(sel.to(DEV), E_loc, P)
+    assert torch.equal(d_dest.cpu(), dest_ids)
+    assert torch.equal(d_slots.cpu().long(), torch.bincount(dest.view(-1), minlength=P))
+    send = ops.dispatch(d_dest, P)
+    assert torch.equal(send.counts.cpu().long(), mask.sum(0))
+    meta = ops.ep_pack(sel.to(DEV), rw.to(DEV), send, E_loc).cpu()
+    rf = send.row_flat.cpu().long()
+    n = int(send.pad_offsets[-1])
+    rows = rf[:n]
+    real = rows >= 0
+    t, r = rows[real] // P, rows[real] % P
+    # rank-major, token order within a rank
+    assert torch.equal(r, torch.sort(r, stable=True).values)
+    mine = dest[t] == r.unsqueeze(1)
+    bits = rw.view(torch.int16).long()[t] & 0xFFFF
+    ref_words = torch.where(mine, (bits << 16) | (sel[t] - r.unsqueeze(1) * E_loc),
+                            torch.full_like(sel[t], 0xFFFF))
+    got = meta[:n][real].long() & 0xFFFFFFFF
+    assert torch.equal(got, ref_words)
+    assert torch.all(meta[:n][~real].long() & 0xFFFF == 0xFFFF)
+    sel_loc, w_loc = ops.ep_unpack(meta[:n].to(DEV))
+    sel_loc, w_loc = sel_loc.cpu()[real], w_loc.cpu()[real]
+    assert torch.equal(sel_loc, torch.where(mine, sel[t] - r.unsqueeze(1) * E_loc,
+                                            torch.full_like(sel[t], -1)))
+    assert torch.equal(w_loc.view(torch.int16), torch.where(
+        mine, rw[t].view(torch.int16), torch.zeros_like(rw[t].view(torch.int16))))
+    # routing-weight gradient gathered back from the send rows
+    dw_rows = torch.randn(n, k)
+    d_w = ops.ep_weight_grad(dw_rows.to(DEV), send, sel.to(DEV), E_loc).cpu()
+    inv = send.inv_pad.cpu().long().view(T, P)
+    ref = dw_rows[inv[torch.arange(T).unsqueeze(1), dest], torch.arange(k).unsqueeze(0)]
+    assert torch.equal(d_w, ref)
+
+
+def _emulated_ep(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
+    """Run ExpertParallelMoE's forward and backward for P ranks on one GPU."""
+    from spark_gpt_b200.ep import CudaExpertOps as B
+    E = w_gu.shape[0]
+    E_loc = E // P
+    I, H = w_d.shape[2], w_d.shape[1]
+    st = []
+    for r in range(P):
+        xb = x_list[r]
+        logits_buf, wr, sel, rw = B.router(xb, w_r, E, k, True)
+        plan, sizes = B.send_plan(sel, rw, E_loc, P)
+        st.append(SimpleNamespace(xb=xb, logits_buf=logits_buf, wr=wr, sel=sel, rw=rw, plan=plan,
+                                  sizes=sizes.cpu(), x_send=B.pack_rows(xb, plan)))
+    starts = [torch.cat([torch.zeros(1, dtype=torch.int64), s.sizes[:, 0].cumsum(0)]) for s in st]
+
+    def to_owner(bufs, o):  # rows every source sends to owner o, in source order
+        return torch.cat([bufs[r][starts[r][o]: starts[r][o + 1]] for r in range(P)])
+
+    def to_sources(rows_o_list):  # owner outputs back to each source's send layout
+        out = []
+        for r in range(P):
+            parts = []
+            for o in range(P):
+                off = sum(int(st[q].sizes[o, 0]) for q in range(r))
+                parts.append(rows_o_list[o][off: off + int(st[r].sizes[o, 0])])
+            out.append(torch.cat(parts))
+        return out
+
+    own = []
+    for o in range(P):
+        wgu_b = ops.cast_bf16(w_gu[o * E_loc:(o + 1) * E_loc].contiguous())
+        wd_b = ops.cast_bf16(w_d[o * E_loc:(o + 1) * E_loc].contiguous())
+        x_recv = to_owner([s.x_send for s in st], o)
+        meta = to_owner([s.plan.meta for s in st], o)
+        sel_loc, w_loc = B.unpack(meta)
+        slots = sum(int(s.sizes[o, 1]) for s in st)
+        part, ectx = B.experts_fwd(x_recv, sel_loc, w_loc, wgu_b, wd_b, slots)
+        own.append(SimpleNamespace(part=part, ectx=ectx))
+    back = to_sources([o.part for o in own])
+    outs = [B.reduce_rows(back[r], st[r].plan) for r in range(P)]
+    d_send = [B.pack_rows(d_out_list[r], st[r].plan) for r in range(P)]
+    dxr, dwr, ggu, gd = [], [], [], []
+    for o in range(P):
+        d_recv = to_owner(d_send, o)
+        a, b, c, e = B.experts_bwd(own[o].ectx, d_recv, k, E_loc, H, I, d_recv.device)
+        dxr.append(a)
+        dwr.append(b)
+        ggu.append(c)
+        gd.append(e)
+    dx_back = to_sources(dxr)
+    dw_back = to_sources(dwr)
+    dxs, g_routers = [], []
+    for r in range(P):
+        s = st[r]
+        d_rw = B.weight_grad(dw_back[r], s.plan, s.sel)
+        dx_router, g_router = B.router_bwd(s.xb, s.wr, s.logits_buf, s.sel, d_rw, None, E, k, True)
+        dxs.append(B.reduce_rows(dx_back[r], s.plan, addend=dx_router))
+        g_routers.append(g_router)
+    return outs, [s.sel for s in st], dxs, g_routers, torch.cat(ggu), torch.cat(gd)
+
+
+@pytest.mark.parametrize("T,H,E,k,I,P", [(2048, 1024, 32, 8, 256, 4), (1500, 2048, 16, 4, 128, 2),
+                                         (1024, 512, 64, 8, 192, 8)])
+def test_emulated_expert_parallel_matches_single_gpu_layer(ops, T, H, E, k, I, P):
+    from spark_gpt_b200 import SparseMoE, _lib
+    g = torch.Generator().manual_seed(E + P)
+    w_r = (torch.randn(E, H, generator=g) * 0.05).to(DEV)
+    w_gu = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(DEV)
+    w_d = (torch.randn(E, H, I, generator=g) * 0.02).to(DEV)
+    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV) for _ in range(P)]
+    ds = [(torch.randn(T, H, generator=g) * 1e-2).to(torch.bfloat16).to(DEV) for _ in range(P)]
+    outs, sels, dxs, g_routers, g_gu, g_d = _emulated_ep(ops, xs, ds, w_r, w_gu, w_d, k, P)
+    cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=k,
+                          moe_intermediate_size=I, norm_topk_prob=True)
+    ref = SparseMoE(cfg).to(DEV)
+    with torch.no_grad():
+        ref.gate.weight.copy_(w_r)
+        ref.experts.gate_up_proj.copy_(w_gu)
+        ref.experts.down_proj.copy_(w_d)
+    for r in range(P):
+        xin = xs[r].clone().requires_grad_(True)
+        ref.gate.weight.grad = None
+        out, _, sel = ref(xin)
+        out.backward(ds[r])
+        assert torch.equal(sels[r], sel)
+        assert_bf16_close(outs[r], out, f"out rank {r}")
+        assert_bf16_close(dxs[r], xin.grad, f"dx rank {r}")
+        assert_bf16_close(g_routers[r], ref.gate.weight.grad, f"dW_router rank {r}")
+    # ref's expert grads accumulated over the P ranks' tokens
+    assert_bf16_close(g_gu, ref.experts.gate_up_proj.grad, "dW_gate_up")
+    assert_bf16_close(g_d, ref.experts.down_proj.grad, "dW_down")
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0
