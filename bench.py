@@ -67,6 +67,11 @@ def parse_args():
                     help="override tokens per GPU (small cases for profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--ep-chunks", type=int, default=2,
+                    help="expert parallel: token chunks pipelined against the exchanges")
+    ap.add_argument("--comm-sms", type=int, default=16,
+                    help="expert parallel: SMs the persistent kernels leave to NCCL while an "
+                         "exchange is in flight (0: none)")
     return ap.parse_args()
 
 
@@ -270,8 +275,9 @@ def run_reference(args, c):
 
 def config_block(args, c, n):
     if c.get("ep"):
-        par = (f"ep{n} (experts sharded, NCCL all_to_all, one row per (token, rank))" if n > 1
-               else "ep1 = the single-GPU layer, all experts local (the scaling baseline)")
+        par = (f"ep{n} (experts sharded, NCCL all_to_all, one row per (token, rank), "
+               f"{args.ep_chunks} token chunks overlapped, {args.comm_sms} SMs left to NCCL)"
+               if n > 1 else "ep1 = the single-GPU layer, all experts local (the scaling baseline)")
     else:
         par = f"dp{n} (replicated experts)"
     return {"workload": f"{args.config}: single Qwen3-MoE layer fwd+bwd (BASELINE configs"
@@ -311,7 +317,7 @@ def main():
     w_r, w_gu, w_d = make_weights(c, 0)
     if c.get("ep") and world > 1:
         from spark_gpt_b200.ep import ExpertParallelMoE
-        layer = ExpertParallelMoE(cfg).to(dev)
+        layer = ExpertParallelMoE(cfg, chunks=args.ep_chunks, comm_sms=args.comm_sms).to(dev)
         lo, hi = layer.expert_offset, layer.expert_offset + layer.local_experts
         w_gu, w_d = w_gu[lo:hi], w_d[lo:hi]
     else:
@@ -358,7 +364,7 @@ def main():
                                       "dispatch", "router_topk", "router_topk_bwd", "cast",
                                       "lb_stats", "lb_grad", "lb_finalize"]
     if c.get("ep"):
-        names += ["ep_route", "ep_pack", "ep_unpack", "ep_weight_grad", "all_to_all"]
+        names += ["ep_route", "ep_pack", "ep_unpack", "ep_weight_grad"]
     timing = ops.set_timing(names)
     launches0 = ops.LAUNCHES["count"]
     barrier()

@@ -38,6 +38,15 @@ int b200moe_version(void);
  * give identical results.  Returns the previous setting; process-wide. */
 int b200moe_set_pair_gemm(int enable);
 
+/* Grids of the persistent kernels (expert and router GEMMs, the row
+ * reductions of combine / gather backward) span at most `sms` SMs (0 = all,
+ * the default), leaving the rest to kernels that run beside them on other
+ * streams, such as the NCCL all-to-all of the expert-parallel layer: every
+ * CTA of a persistent grid is then resident at once and no statically
+ * scheduled tile waits for the collective to finish.  Results do not depend
+ * on it.  Returns the previous setting; process-wide. */
+int b200moe_set_persistent_sm_limit(int sms);
+
 /* Message of this thread's last failed call ("" if none). */
 const char* b200moe_last_error(void);
 

@@ -54,6 +54,17 @@ int num_sms() {
   return cache[dev];
 }
 
+// SMs the persistent kernels (expert GEMMs, row reductions) size their grids
+// for: all of them, or fewer while a collective runs beside them on another
+// stream (b200moe_set_persistent_sm_limit), so that every CTA of the grid is
+// resident at once and no statically scheduled tile waits for the collective.
+int g_sm_limit = 0;
+
+int persistent_sms() {
+  const int n = num_sms();
+  return (g_sm_limit > 0 && g_sm_limit < n) ? g_sm_limit : n;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -111,7 +122,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
   const int smem = static_cast<int>(GemmSmem<BN, STAGES>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-  kern<<<num_sms(), kGemmThreads, smem, st>>>(ta, tb, p);
+  kern<<<persistent_sms(), kGemmThreads, smem, st>>>(ta, tb, p);
   return check_launch(what);
 }
 
@@ -146,7 +157,7 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(num_sms() & ~1), 1, 1);
+  cfg.gridDim = dim3(static_cast<unsigned>(persistent_sms() & ~1), 1, 1);
   cfg.blockDim = dim3(kGemmThreads, 1, 1);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = st;
@@ -258,7 +269,7 @@ int launch_row_reduce(const __nv_bfloat16* rows, const int* inv_pad,
   cudaError_t e = cudaFuncSetAttribute(row_reduce_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-  const long long grid = std::min<long long>(3LL * num_sms(), std::max<long long>(T, 1));
+  const long long grid = std::min<long long>(3LL * persistent_sms(), std::max<long long>(T, 1));
   row_reduce_kernel<<<static_cast<int>(grid), kReduceThreads, smem, st>>>(
       rows, inv_pad, weights, addend, T, k, H, slots, out);
   return check_launch(what);
@@ -272,6 +283,12 @@ using namespace b200moe;
 extern "C" {
 
 int b200moe_version(void) { return 100; }
+
+int b200moe_set_persistent_sm_limit(int sms) {
+  const int prev = g_sm_limit;
+  g_sm_limit = sms > 0 ? (sms < 2 ? 2 : sms) : 0;
+  return prev;
+}
 
 int b200moe_set_pair_gemm(int enable) {
   const int prev = g_pair_gemm;

@@ -20,10 +20,14 @@ tokens.  Per forward:
 
 The backward mirrors it: d_out rows go to the owners along the same plan; the
 owner computes the combine backward (slot gradients and routing-weight
-gradients), its experts' backward (expert weight gradients stay local) and
-sums each row's slot input-gradients into one row; rows and routing-weight
-gradients travel back and the source adds them to the router's input
-gradient.  The load-balancing counts are all-reduced by
+gradients), its experts' dgrads, and sums each row's slot input-gradients
+into one row; rows and routing-weight gradients travel back (while the owner
+computes its expert weight gradients, which stay local) and the source adds
+them to the router's input gradient.
+
+Overlap: the tokens may be split into chunks with one send plan each, so that
+one chunk's exchange runs while another chunk's experts compute (see
+_EPMoEFn); the persistent kernels can leave SMs to the collective.  The load-balancing counts are all-reduced by
 global_load_balancing_loss as in the data-parallel layout (train.py:3162).
 
 Each (token, rank) row crosses the fabric once per pass instead of once per
@@ -40,6 +44,7 @@ this rank's shard: gate_up_proj (E/P, 2I, H), down_proj (E/P, H, I).
 
 from __future__ import annotations
 
+from contextlib import nullcontext
 from types import SimpleNamespace
 
 import torch
@@ -102,69 +107,122 @@ class CudaExpertOps:
         return part, (d, w_loc, xs, gu, h, y, w_gu, w_d)
 
     @staticmethod
-    def experts_bwd(ctx, d_rows, k, E, H, I, device):
-        """-> (dx rows, d_weights (rows, k) fp32, dW_gate_up, dW_down)."""
-        n = d_rows.shape[0]
+    def experts_dgrad(ctx, d_rows, k, device):
+        """-> (dx rows, d_weights (rows, k) fp32, state for experts_wgrad)."""
+        n, H = d_rows.shape
         if ctx is None:
-            z = torch.zeros(E, 2 * I, H, device=device), torch.zeros(E, H, I, device=device)
-            return (d_rows.new_zeros(n, H), torch.zeros(n, k, device=device), z[0], z[1])
+            return d_rows.new_zeros(n, H), torch.zeros(n, k, device=device), None
         d, w_loc, xs, gu, h, y, w_gu, w_d = ctx
         dy, dw = ops.combine_bwd(_as_bf16(d_rows), y, d, w_loc)
         d_gu = ops.down_dgrad_swiglu(dy, w_d, gu, d)
-        g_down = ops.wgrad(dy, h, d, name="down_wgrad")
         dxs = ops.gate_up_dgrad(d_gu, w_gu, d)
-        g_gu = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad")
-        return ops.gather_rows_bwd(dxs, d), dw, g_gu, g_down
+        return ops.gather_rows_bwd(dxs, d), dw, (d, dy, h, d_gu, xs)
 
     @staticmethod
-    def reduce_rows(rows_back, plan, addend=None):
+    def experts_wgrad(state, g_gu, g_d, E, H, I, device):
+        """Adds this chunk's expert weight gradients to (g_gu, g_d) (None: start)."""
+        if state is None:
+            if g_gu is None:
+                g_gu = torch.zeros(E, 2 * I, H, device=device)
+                g_d = torch.zeros(E, H, I, device=device)
+            return g_gu, g_d
+        d, dy, h, d_gu, xs = state
+        acc = g_gu is not None
+        g_d = ops.wgrad(dy, h, d, name="down_wgrad", out=g_d, accumulate=acc)
+        g_gu = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad", out=g_gu, accumulate=acc)
+        return g_gu, g_d
+
+    @staticmethod
+    def reduce_rows(rows_back, plan, addend=None, out=None):
         """out[t] = sum over the ranks token t went to of its returned row (+ addend)."""
-        return ops.gather_rows_bwd(rows_back, plan.send, addend=addend)
+        return ops.gather_rows_bwd(rows_back, plan.send, addend=addend, out=out)
 
     @staticmethod
-    def weight_grad(dw_back, plan, sel):
-        return ops.ep_weight_grad(dw_back, plan.send, sel, plan.experts_per_rank)
+    def weight_grad(dw_back, plan, sel, out=None):
+        return ops.ep_weight_grad(dw_back, plan.send, sel, plan.experts_per_rank, out=out)
 
     @staticmethod
     def cast(w):
         return ops.cast_bf16(w)
 
+    @staticmethod
+    def overlap(comm_sms):
+        """Persistent kernels leave `comm_sms` SMs to the all-to-all beside them."""
+        return ops.persistent_sm_limit(max(2, torch.cuda.get_device_properties(
+            torch.cuda.current_device()).multi_processor_count - comm_sms))
 
-def _exchange(buf, send_counts, recv_counts, group):
-    """all_to_all_single of row blocks; counts are host lists of row counts."""
+
+def _start(buf, send_counts, recv_counts, group):
+    """Asynchronous all_to_all_single of row blocks -> (receive buffer, work)."""
     out = buf.new_empty((sum(recv_counts), *buf.shape[1:]))
-    with ops.timed("all_to_all"):
-        dist.all_to_all_single(out, buf[: sum(send_counts)].contiguous(), recv_counts,
-                               send_counts, group=group)
-    return out
+    work = dist.all_to_all_single(out, buf[: sum(send_counts)].contiguous(), recv_counts,
+                                  send_counts, group=group, async_op=True)
+    return out, work
 
 
 class _EPMoEFn(torch.autograd.Function):
+    """Forward and backward of the expert-parallel layer.
+
+    The tokens are split into `chunks` contiguous ranges, each with its own send
+    plan.  Chunk c+1's rows cross the fabric while chunk c's experts compute,
+    and chunk c's results travel back while chunk c+1 computes; in the backward,
+    each chunk's input-gradient rows travel back while the next chunk's dgrads
+    and then all chunks' weight gradients compute.  With comm_sms > 0 the
+    persistent kernels of those windows leave that many SMs to the collective.
+    Collectives are issued in the same order on every rank."""
+
     @staticmethod
-    def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, backend):
+    def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, backend, chunks,
+                comm_sms):
         P = dist.get_world_size(group)
         E_loc = w_gu.shape[0]
         T, H = x.shape
         xb = _as_bf16(x) if x.is_cuda else x
         logits_buf, wr, sel, rw = backend.router(xb, w_router, num_experts, top_k, norm)
-        plan, sizes = backend.send_plan(sel, rw, E_loc, P)
-        x_send = backend.pack_rows(xb, plan)
-        recv_sizes = torch.empty_like(sizes)
-        dist.all_to_all_single(recv_sizes, sizes, group=group)
-        host = torch.cat([sizes, recv_sizes]).cpu()  # the one host read of the step
-        send_rows = host[:P, 0].tolist()
-        recv_rows = host[P:, 0].tolist()
-        recv_slots = int(host[P:, 1].sum())
-        x_recv = _exchange(x_send, send_rows, recv_rows, group)
-        meta_recv = _exchange(plan.meta, send_rows, recv_rows, group)
-        sel_loc, w_loc = backend.unpack(meta_recv)
+        C = max(1, min(int(chunks), T))
+        bounds = [T * c // C for c in range(C + 1)]
+        span = [(bounds[c], bounds[c + 1]) for c in range(C)]
+        plans, sizes = [], []
+        for a, b in span:
+            plan, sz = backend.send_plan(sel[a:b], rw[a:b], E_loc, P)
+            plans.append(plan)
+            sizes.append(sz)
+        x_sends = [backend.pack_rows(xb[a:b], plans[c]) for c, (a, b) in enumerate(span)]
+        sizes_t = torch.stack(sizes).transpose(0, 1).contiguous()     # (P, C, 2)
+        recv_t = torch.empty_like(sizes_t)
+        dist.all_to_all_single(recv_t, sizes_t, group=group)
+        host = torch.stack([sizes_t, recv_t]).cpu()  # the one host read of the step
+        send_rows = [host[0, :, c, 0].tolist() for c in range(C)]
+        recv_rows = [host[1, :, c, 0].tolist() for c in range(C)]
+        recv_slots = [int(host[1, :, c, 1].sum()) for c in range(C)]
         wgu_b, wd_b = backend.cast(w_gu), backend.cast(w_d)
-        part, ectx = backend.experts_fwd(x_recv, sel_loc, w_loc, wgu_b, wd_b, recv_slots)
-        back = _exchange(part, recv_rows, send_rows, group)
-        out = backend.reduce_rows(back, plan)
+
+        def start_rows(c):
+            return (_start(x_sends[c], send_rows[c], recv_rows[c], group),
+                    _start(plans[c].meta, send_rows[c], recv_rows[c], group))
+
+        ectxs, backs = [None] * C, [None] * C
+        overlap = backend.overlap(comm_sms) if (C > 1 and comm_sms) else nullcontext()
+        with overlap:
+            pend = start_rows(0)
+            for c in range(C):
+                (x_recv, wx), (meta_recv, wm) = pend
+                if c + 1 < C:
+                    pend = start_rows(c + 1)
+                wx.wait()
+                wm.wait()
+                sel_loc, w_loc = backend.unpack(meta_recv)
+                part, ectxs[c] = backend.experts_fwd(x_recv, sel_loc, w_loc, wgu_b, wd_b,
+                                                     recv_slots[c])
+                backs[c] = _start(part, recv_rows[c], send_rows[c], group)
+        out = xb.new_empty(T, H)
+        for c, (a, b) in enumerate(span):
+            rows, w = backs[c]
+            w.wait()
+            backend.reduce_rows(rows, plans[c], out=out[a:b])
         ctx.save_for_backward(xb, logits_buf, wr, sel)
-        ctx.meta = (plan, ectx, send_rows, recv_rows, group, backend, top_k, norm, num_experts,
-                    E_loc, H, w_gu.shape[1] // 2, x.dtype)
+        ctx.meta = (plans, ectxs, span, send_rows, recv_rows, group, backend, top_k, norm,
+                    num_experts, E_loc, H, w_gu.shape[1] // 2, x.dtype, comm_sms)
         ctx.mark_non_differentiable(sel)
         E = num_experts
         logits = logits_buf if logits_buf.shape[1] == E else logits_buf[:, :E]
@@ -173,21 +231,42 @@ class _EPMoEFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, d_out, d_logits, _d_sel):
         xb, logits_buf, wr, sel = ctx.saved_tensors
-        (plan, ectx, send_rows, recv_rows, group, backend, top_k, norm, num_experts, E_loc, H, I,
-         xdtype) = ctx.meta
+        (plans, ectxs, span, send_rows, recv_rows, group, backend, top_k, norm, num_experts,
+         E_loc, H, I, xdtype, comm_sms) = ctx.meta
+        C = len(span)
+        T = xb.shape[0]
         if d_out is None:
             d_out = torch.zeros(xb.shape, device=xb.device, dtype=xb.dtype)
-        d_send = backend.pack_rows(d_out, plan)
-        d_recv = _exchange(d_send, send_rows, recv_rows, group)
-        dx_rows, dw_rows, g_gu, g_d = backend.experts_bwd(ectx, d_recv, top_k, E_loc, H, I,
-                                                          xb.device)
-        dx_back = _exchange(dx_rows, recv_rows, send_rows, group)
-        dw_back = _exchange(dw_rows, recv_rows, send_rows, group)
-        d_rw = backend.weight_grad(dw_back, plan, sel)
+        d_sends = [backend.pack_rows(d_out[a:b], plans[c]) for c, (a, b) in enumerate(span)]
+        rets, states = [None] * C, [None] * C
+        g_gu = g_d = None
+        overlap = backend.overlap(comm_sms) if comm_sms else nullcontext()
+        with overlap:
+            pend = _start(d_sends[0], send_rows[0], recv_rows[0], group)
+            for c in range(C):
+                d_recv, wd = pend
+                if c + 1 < C:
+                    pend = _start(d_sends[c + 1], send_rows[c + 1], recv_rows[c + 1], group)
+                wd.wait()
+                dx_rows, dw_rows, states[c] = backend.experts_dgrad(ectxs[c], d_recv, top_k,
+                                                                    xb.device)
+                rets[c] = (_start(dx_rows, recv_rows[c], send_rows[c], group),
+                           _start(dw_rows, recv_rows[c], send_rows[c], group))
+            # the weight gradients run while the last input-gradient rows travel back
+            for c in range(C):
+                g_gu, g_d = backend.experts_wgrad(states[c], g_gu, g_d, E_loc, H, I, xb.device)
+        d_rw = torch.empty(T, top_k, device=xb.device, dtype=torch.float32)
+        for c, (a, b) in enumerate(span):
+            (_, w1), (dw_back, w2) = rets[c]
+            w1.wait()
+            w2.wait()
+            backend.weight_grad(dw_back, plans[c], sel[a:b], out=d_rw[a:b])
         dx_router, g_router = backend.router_bwd(xb, wr, logits_buf, sel, d_rw, d_logits,
                                                  num_experts, top_k, norm)
-        dx = backend.reduce_rows(dx_back, plan, addend=dx_router)
-        return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None)
+        dx = xb.new_empty(T, H)
+        for c, (a, b) in enumerate(span):
+            backend.reduce_rows(rets[c][0][0], plans[c], addend=dx_router[a:b], out=dx[a:b])
+        return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None, None)
 
 
 class ExpertParallelMoE(nn.Module):
@@ -198,8 +277,10 @@ class ExpertParallelMoE(nn.Module):
     data-parallel parameter); ``experts.gate_up_proj`` / ``down_proj`` hold
     this rank's E/P experts."""
 
-    def __init__(self, config, group=None, backend=CudaExpertOps):
+    def __init__(self, config, group=None, backend=CudaExpertOps, chunks=1, comm_sms=0):
         super().__init__()
+        self.chunks = chunks
+        self.comm_sms = comm_sms
         self.group = group
         P = dist.get_world_size(group)
         r = dist.get_rank(group)
@@ -218,6 +299,49 @@ class ExpertParallelMoE(nn.Module):
         self.experts.gate_up_proj = nn.Parameter(torch.empty(self.local_experts, 2 * I, H))
         self.experts.down_proj = nn.Parameter(torch.empty(self.local_experts, H, I))
 
+    # ------------------------------------------------------------------ #
+    # checkpoints and export: shards <-> the reference's full layout
+    # ------------------------------------------------------------------ #
+    def get_extra_state(self):
+        """Layout tag saved with this rank's shard in state_dict()."""
+        return {"expert_parallel_ranks": dist.get_world_size(self.group),
+                "rank": dist.get_rank(self.group), "num_experts": self.num_experts}
+
+    def set_extra_state(self, state):
+        want = self.get_extra_state()
+        if state != want:
+            raise ValueError(f"expert shard saved as {state} cannot load into {want}; "
+                             "load the full state dict with load_full_state_dict instead")
+
+    @torch.no_grad()
+    def full_state_dict(self):
+        """gate.weight and the full (E,2I,H) / (E,H,I) expert tensors, gathered
+        over the group (every rank returns them): the keys, shapes and dtypes of
+        the reference SparseMoE's state dict (train.py:2244-2334), so HF export
+        (export_unfused_state_dict / export_hf, train.py:2540-2691) and strict
+        Qwen3MoeForCausalLM loading work unchanged."""
+        P = dist.get_world_size(self.group)
+        out = {"gate.weight": self.gate.weight.detach().clone()}
+        for name in ("gate_up_proj", "down_proj"):
+            shard = getattr(self.experts, name).detach().contiguous()
+            parts = [torch.empty_like(shard) for _ in range(P)]
+            dist.all_gather(parts, shard, group=self.group)
+            out["experts." + name] = torch.cat(parts)
+        return out
+
+    @torch.no_grad()
+    def load_full_state_dict(self, state):
+        """Load a full (unsharded) SparseMoE state dict: every rank keeps its
+        experts [rank*E/P, (rank+1)*E/P)."""
+        lo, hi = self.expert_offset, self.expert_offset + self.local_experts
+        self.gate.weight.copy_(state["gate.weight"])
+        for name in ("gate_up_proj", "down_proj"):
+            full = state["experts." + name]
+            if full.shape[0] != self.num_experts:
+                raise ValueError(f"experts.{name}: expected {self.num_experts} experts, "
+                                 f"got {full.shape[0]}")
+            getattr(self.experts, name).copy_(full[lo:hi])
+
     def forward(self, hidden_states):
         if self.backend is CudaExpertOps:
             _require_cuda(hidden_states)
@@ -226,5 +350,5 @@ class ExpertParallelMoE(nn.Module):
         out, logits, sel = _EPMoEFn.apply(
             x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
             self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group,
-            self.backend)
+            self.backend, self.chunks, self.comm_sms)
         return out.view(shape), logits.view(*shape[:-1], -1), sel.view(*shape[:-1], -1)

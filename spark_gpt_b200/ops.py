@@ -43,6 +43,17 @@ def timed(name: str):
         yield
 
 
+@contextmanager
+def persistent_sm_limit(sms: int):
+    """Persistent kernels enqueued inside the block use at most `sms` SMs
+    (0 = all), leaving the rest to a collective running beside them."""
+    prev = int(_lib.value("b200moe_set_persistent_sm_limit", int(sms)))
+    try:
+        yield
+    finally:
+        _lib.value("b200moe_set_persistent_sm_limit", prev)
+
+
 def _launch(name: str, kernels: int, fn, *args):
     LAUNCHES["count"] += kernels
     if _timing is not None and name in _timing:
@@ -221,10 +232,15 @@ def gather_rows(x: torch.Tensor, d: Dispatch) -> torch.Tensor:
     return xs
 
 
-def gather_rows_bwd(dxs, d: Dispatch, addend=None, token_major=False) -> torch.Tensor:
-    """dx[t] = sum_s dxs[row of slot t*k+s] (+ addend); token_major: row t*k+s."""
+def gather_rows_bwd(dxs, d: Dispatch, addend=None, token_major=False, out=None) -> torch.Tensor:
+    """dx[t] = sum_s dxs[row of slot t*k+s] (+ addend); token_major: row t*k+s.
+    out: an optional contiguous (T, H) bf16 destination."""
     H = dxs.shape[1]
-    dx = torch.empty(d.num_tokens, H, device=dxs.device, dtype=BF16)
+    if out is None:
+        dx = torch.empty(d.num_tokens, H, device=dxs.device, dtype=BF16)
+    else:
+        _check(out, BF16, "gather_rows_bwd out")
+        dx = out
     if d.num_tokens:
         _launch("gather_bwd", 1, "b200moe_gather_rows_bwd", _p(dxs),
                 None if token_major else _p(d.inv_pad), _p(addend), d.num_tokens, d.top_k, H,
@@ -403,9 +419,10 @@ def ep_unpack(meta: torch.Tensor):
     return sel, w
 
 
-def ep_weight_grad(dw_rows, send: Dispatch, selected, experts_per_rank: int) -> torch.Tensor:
+def ep_weight_grad(dw_rows, send: Dispatch, selected, experts_per_rank: int,
+                   out=None) -> torch.Tensor:
     T, k = selected.shape
-    d_w = torch.empty(T, k, device=selected.device, dtype=torch.float32)
+    d_w = torch.empty(T, k, device=selected.device, dtype=torch.float32) if out is None else out
     if T:
         _launch("ep_weight_grad", 1, "b200moe_ep_weight_grad", _p(dw_rows), _p(send.inv_pad),
                 _p(selected), T, k, experts_per_rank, send.num_experts, _p(d_w), _s(selected))

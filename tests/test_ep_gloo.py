@@ -9,6 +9,7 @@ tokens, and each rank's expert-shard gradients must equal the oracle's
 gradients of those experts summed over all ranks' tokens.  Test infrastructure only: the product path runs the CUDA kernels.
 """
 
+import contextlib
 import os
 import socket
 from types import SimpleNamespace
@@ -85,7 +86,7 @@ class OracleOps:
         return part, (d, row_of, slot_of, w, xs, gu, h, y, w_gu, w_d)
 
     @staticmethod
-    def experts_bwd(ctx, d_rows, k, E, H, I, device):
+    def experts_dgrad(ctx, d_rows, k, device):
         d, row_of, slot_of, w, xs, gu, h, y, w_gu, w_d = ctx
         g = d_rows.float()[row_of]
         dw = torch.zeros(d_rows.shape[0], k)
@@ -95,24 +96,44 @@ class OracleOps:
         dh, dwd = O.grouped_linear_backward(h, w_d, dy, d.offsets)
         dxs, dwgu, _ = O.swiglu_backward(xs, w_gu, gu, dh, d.offsets)
         dxs = dxs[torch.from_numpy(d.inverse)]
-        dx = torch.zeros(d_rows.shape[0], H).index_add_(0, row_of, dxs)
-        return dx, dw, dwgu, dwd
+        dx = torch.zeros(d_rows.shape[0], d_rows.shape[1]).index_add_(0, row_of, dxs)
+        return dx, dw, (dwgu, dwd)
 
     @staticmethod
-    def reduce_rows(rows_back, plan, addend=None):
+    def experts_wgrad(state, g_gu, g_d, E, H, I, device):
+        dwgu, dwd = state
+        if g_gu is None:
+            return dwgu, dwd
+        return g_gu + dwgu, g_d + dwd
+
+    @staticmethod
+    def reduce_rows(rows_back, plan, addend=None, out=None):
         T, P = plan.inv.shape
-        out = torch.zeros(T, rows_back.shape[1])
+        res = torch.zeros(T, rows_back.shape[1])
         has = plan.inv >= 0
         t_idx, r_idx = has.nonzero(as_tuple=True)
-        out.index_add_(0, t_idx, rows_back.float()[plan.inv[t_idx, r_idx]])
-        return out if addend is None else out + addend
+        res.index_add_(0, t_idx, rows_back.float()[plan.inv[t_idx, r_idx]])
+        if addend is not None:
+            res = res + addend
+        if out is None:
+            return res
+        out.copy_(res)
+        return out
 
     @staticmethod
-    def weight_grad(dw_back, plan, sel):
+    def weight_grad(dw_back, plan, sel, out=None):
         T, k = sel.shape
         r = torch.div(sel, plan.experts_per_rank, rounding_mode="floor")
         rows = plan.inv[torch.arange(T).unsqueeze(1), r]
-        return dw_back[rows, torch.arange(k).unsqueeze(0)]
+        res = dw_back[rows, torch.arange(k).unsqueeze(0)]
+        if out is None:
+            return res
+        out.copy_(res)
+        return out
+
+    @staticmethod
+    def overlap(comm_sms):
+        return contextlib.nullcontext()
 
     @staticmethod
     def cast(w):
@@ -133,7 +154,7 @@ def rank_inputs(rank):
     return torch.randn(T, H, generator=g), torch.randn(T, H, generator=g)
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, chunks):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -141,7 +162,7 @@ def _worker(rank, world, port, results):
         from spark_gpt_b200.ep import ExpertParallelMoE
         cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=K,
                               moe_intermediate_size=I, norm_topk_prob=True)
-        m = ExpertParallelMoE(cfg, backend=OracleOps)
+        m = ExpertParallelMoE(cfg, backend=OracleOps, chunks=chunks, comm_sms=8)
         w_r, w_gu, w_d = full_weights()
         lo, hi = m.expert_offset, m.expert_offset + m.local_experts
         with torch.no_grad():
@@ -166,11 +187,11 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_expert_parallel_matches_single_process_oracle(world):
+@pytest.mark.parametrize("world,chunks", [(2, 1), (4, 1), (2, 3)])
+def test_expert_parallel_matches_single_process_oracle(world, chunks):
     mgr = mp.get_context("spawn").Manager()
     results = mgr.dict()
-    mp.start_processes(_worker, args=(world, _free_port(), results), nprocs=world,
+    mp.start_processes(_worker, args=(world, _free_port(), results, chunks), nprocs=world,
                        join=True, start_method="spawn")
     w_r, w_gu, w_d = full_weights()
     sum_gu = torch.zeros_like(w_gu)
@@ -192,3 +213,57 @@ def test_expert_parallel_matches_single_process_oracle(world):
     # every expert received rows from both ranks in this routing
     assert np.all(np.bincount(torch.cat([results[r]["sel"].reshape(-1) for r in range(world)]),
                               minlength=E) > 0)
+
+
+def _ckpt_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from spark_gpt_b200.ep import ExpertParallelMoE
+        cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=K,
+                              moe_intermediate_size=I, norm_topk_prob=True)
+        w_r, w_gu, w_d = full_weights()
+        full = {"gate.weight": w_r, "experts.gate_up_proj": w_gu, "experts.down_proj": w_d}
+        m = ExpertParallelMoE(cfg, backend=OracleOps)
+        m.load_full_state_dict(full)
+        got = m.full_state_dict()
+        sd = m.state_dict()
+        m2 = ExpertParallelMoE(cfg, backend=OracleOps)
+        m2.load_state_dict(sd)                      # same layout: loads
+        mismatch = None
+        try:
+            bad = dict(sd)
+            bad["_extra_state"] = {**sd["_extra_state"], "expert_parallel_ranks": world * 2}
+            m2.load_state_dict(bad)
+        except ValueError as e:
+            mismatch = str(e)
+        results[rank] = {"full": {k: v.clone() for k, v in got.items()},
+                         "shard_gu": sd["experts.gate_up_proj"].clone(),
+                         "m2_gu": m2.experts.gate_up_proj.detach().clone(),
+                         "keys": sorted(sd.keys()), "mismatch": mismatch,
+                         "lo": m.expert_offset, "hi": m.expert_offset + m.local_experts}
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_expert_shards_round_trip_to_the_full_layout(world):
+    """full_state_dict gathers the reference's (E,2I,H)/(E,H,I) tensors from the
+    shards; load_full_state_dict slices them back; a shard's state dict carries
+    its layout and refuses to load into another one."""
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_ckpt_worker, args=(world, _free_port(), results), nprocs=world,
+                       join=True, start_method="spawn")
+    w_r, w_gu, w_d = full_weights()
+    for rank in range(world):
+        r = results[rank]
+        assert torch.equal(r["full"]["gate.weight"], w_r)
+        assert torch.equal(r["full"]["experts.gate_up_proj"], w_gu)
+        assert torch.equal(r["full"]["experts.down_proj"], w_d)
+        assert sorted(r["full"]) == ["experts.down_proj", "experts.gate_up_proj", "gate.weight"]
+        assert torch.equal(r["shard_gu"], w_gu[r["lo"]:r["hi"]])
+        assert torch.equal(r["m2_gu"], w_gu[r["lo"]:r["hi"]])
+        assert "_extra_state" in r["keys"]
+        assert r["mismatch"] is not None and "cannot load" in r["mismatch"]

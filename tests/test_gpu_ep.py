@@ -23,6 +23,9 @@ from tests.helpers import assert_bf16_close
 pytestmark = pytest.mark.gpu
 
 T, H, E, K, I = 2048, 1024, 16, 4, 256
+# one send plan per step, exchanges in sequence; and 3 token chunks with the
+# exchanges overlapped and 16 SMs left to NCCL
+VARIANTS = {"plain": dict(chunks=1, comm_sms=0), "overlap": dict(chunks=3, comm_sms=16)}
 
 
 def _cfg():
@@ -54,20 +57,22 @@ def _worker(rank, world, port, results):
         from spark_gpt_b200 import SparseMoE
         from spark_gpt_b200.ep import ExpertParallelMoE
         w_r, w_gu, w_d = _weights()
-        ep = ExpertParallelMoE(_cfg()).to(dev)
-        lo, hi = ep.expert_offset, ep.expert_offset + ep.local_experts
+        eps = {name: ExpertParallelMoE(_cfg(), **kw).to(dev) for name, kw in VARIANTS.items()}
+        ep0 = next(iter(eps.values()))
+        lo, hi = ep0.expert_offset, ep0.expert_offset + ep0.local_experts
         ref = SparseMoE(_cfg()).to(dev)
         with torch.no_grad():
-            for m in (ep, ref):
+            for m in (*eps.values(), ref):
                 m.gate.weight.copy_(w_r)
-            ep.experts.gate_up_proj.copy_(w_gu[lo:hi])
-            ep.experts.down_proj.copy_(w_d[lo:hi])
+            for ep in eps.values():
+                ep.experts.gate_up_proj.copy_(w_gu[lo:hi])
+                ep.experts.down_proj.copy_(w_d[lo:hi])
             ref.experts.gate_up_proj.copy_(w_gu)
             ref.experts.down_proj.copy_(w_d)
         x, d_out = _inputs(rank)
         x, d_out = x.to(dev), d_out.to(dev)
         outs = {}
-        for name, m in (("ep", ep), ("ref", ref)):
+        for name, m in (*eps.items(), ("ref", ref)):
             xin = x.clone().requires_grad_(True)
             out, logits, sel = m(xin)
             out.backward(d_out)
@@ -77,9 +82,9 @@ def _worker(rank, world, port, results):
         dist.all_reduce(gu_sum)
         dist.all_reduce(d_sum)
         torch.cuda.synchronize()
-        results[rank] = {"ep": outs["ep"], "ref": outs["ref"],
-                         "ep_gu": ep.experts.gate_up_proj.grad.cpu(),
-                         "ep_d": ep.experts.down_proj.grad.cpu(),
+        results[rank] = {"outs": outs,
+                         "ep_gu": {n: ep.experts.gate_up_proj.grad.cpu() for n, ep in eps.items()},
+                         "ep_d": {n: ep.experts.down_proj.grad.cpu() for n, ep in eps.items()},
                          "ref_gu": gu_sum[lo:hi].cpu(), "ref_d": d_sum[lo:hi].cpu()}
     finally:
         dist.destroy_process_group()
@@ -100,10 +105,14 @@ def test_expert_parallel_two_gpus_matches_single_gpu_layer():
                        start_method="spawn")
     for rank in range(2):
         r = results[rank]
-        (o_ep, s_ep, dx_ep, dr_ep), (o_ref, s_ref, dx_ref, dr_ref) = r["ep"], r["ref"]
-        assert torch.equal(s_ep, s_ref)
-        assert_bf16_close(o_ep, o_ref, "out")
-        assert_bf16_close(dx_ep, dx_ref, "dx")
-        assert_bf16_close(dr_ep, dr_ref, "dW_router")
-        assert_bf16_close(r["ep_gu"], r["ref_gu"], "dW_gate_up")
-        assert_bf16_close(r["ep_d"], r["ref_d"], "dW_down")
+        o_ref, s_ref, dx_ref, dr_ref = r["outs"]["ref"]
+        for name in VARIANTS:
+            o_ep, s_ep, dx_ep, dr_ep = r["outs"][name]
+            assert torch.equal(s_ep, s_ref)
+            assert_bf16_close(o_ep, o_ref, f"{name} out")
+            assert_bf16_close(dx_ep, dx_ref, f"{name} dx")
+            assert_bf16_close(dr_ep, dr_ref, f"{name} dW_router")
+            assert_bf16_close(r["ep_gu"][name], r["ref_gu"], f"{name} dW_gate_up")
+            assert_bf16_close(r["ep_d"][name], r["ref_d"], f"{name} dW_down")
+        # the chunked, overlapped schedule computes the same values
+        assert torch.equal(r["outs"]["plain"][0], r["outs"]["overlap"][0])

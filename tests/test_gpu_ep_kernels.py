@@ -182,7 +182,8 @@ def _emulated_ep(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
     dxr, dwr, ggu, gd = [], [], [], []
     for o in range(P):
         d_recv = to_owner(d_send, o)
-        a, b, c, e = B.experts_bwd(own[o].ectx, d_recv, k, E_loc, H, I, d_recv.device)
+        a, b, state = B.experts_dgrad(own[o].ectx, d_recv, k, d_recv.device)
+        c, e = B.experts_wgrad(state, None, None, E_loc, H, I, d_recv.device)
         dxr.append(a)
         dwr.append(b)
         ggu.append(c)
