@@ -67,6 +67,8 @@ def parse_args():
                     help="override tokens per GPU (small cases for profiling only)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-muon", action="store_true",
+                    help="skip the Muon optimizer-step measurement of the expert tensors")
     ap.add_argument("--ep-chunks", type=int, default=2,
                     help="expert parallel: token chunks pipelined against the exchanges")
     ap.add_argument("--comm-sms", type=int, default=16,
@@ -447,6 +449,44 @@ def main():
                "pipeline": "next step's H2D overlapped with this step's compute (copy stream, "
                            "double-buffered inputs)"}
 
+    # ---------------- Muon step of the packed expert tensors (the optimizer that
+    # consumes the fp32 weight gradients written above, train.py:2930-3024)
+    muon_line = None
+    if not args.no_muon and not (c.get("ep") and world > 1):
+        from spark_gpt_b200.muon import PackedExpertMuon
+        step(x, d_out)
+        eparams = [layer.experts.gate_up_proj, layer.experts.down_proj]
+        saved = [p.detach().clone() for p in eparams]
+        opt = PackedExpertMuon(eparams, lr=0.02)
+        for _ in range(3):
+            opt.step()
+        torch.cuda.synchronize()
+        m0 = torch.cuda.Event(enable_timing=True)
+        m1 = torch.cuda.Event(enable_timing=True)
+        n_muon = max(5, args.steps // 2)
+        m0.record()
+        for _ in range(n_muon):
+            opt.step()
+        m1.record()
+        torch.cuda.synchronize()
+        muon_ms = m0.elapsed_time(m1) / n_muon
+        with torch.no_grad():
+            for p, s0 in zip(eparams, saved):
+                p.copy_(s0)
+
+        def ns_flops(Eq, r, cc, steps=5):
+            g, G = min(r, cc), max(r, cc)
+            return Eq * steps * (4 * g * g * G + 2 * g ** 3)
+
+        mflops = (ns_flops(layer.experts.gate_up_proj.shape[0], 2 * c["I"], c["H"]) +
+                  ns_flops(layer.experts.down_proj.shape[0], c["H"], c["I"]))
+        mt = mflops / (muon_ms / 1e3) / 1e12
+        muon_line = {"ms_per_step": muon_ms, "ns_tflop": mflops / 1e12, "tflops": mt,
+                     "frac_of_bf16_burst": mt / pk["bf16"],
+                     "what": "PackedExpertMuon.step on gate_up_proj + down_proj: momentum, "
+                             "5 Newton-Schulz iterations as grouped tcgen05 GEMMs, fused "
+                             "parameter update"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not c.get("ep"):
         Ts = args.cpu_sample_tokens
@@ -477,6 +517,7 @@ def main():
         "kernels_ms": {n: round(v, 5) for n, v in sorted(per_op.items())},
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "muon_step": muon_line,
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / max(args.steps, 1),
         "clocks": clocks.summary(),

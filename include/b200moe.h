@@ -292,6 +292,33 @@ int b200moe_ep_weight_grad(const float* dw_rows, const int* inv_send, const long
                            long long T, int k, int experts_per_rank, int ranks, float* d_weights,
                            void* stream);
 
+/* ---- Muon on the packed expert weights (train.py:2877-3024) --------------
+ * The optimizer step of the 3-D expert tensors (Muon groups, train.py:3066-3070):
+ * momentum, then the batched Newton-Schulz orthogonalisation of each matrix,
+ * then p -= lr * result. */
+
+/* momentum_buf (n) fp32 <- lerp(momentum_buf, grad, 1 - momentum); staged (n)
+ * bf16 <- lerp(grad, momentum_buf, momentum) (nesterov) or momentum_buf, with
+ * fp32 math and one rounding.  n % 4 == 0.  Replaces _momentum_stage
+ * (train.py:2806-2839) / the lerp pair of MuonAdamWHybrid._muon_group (:3001-3005). */
+int b200moe_muon_momentum(const float* grad, float* momentum_buf, void* staged, long long n,
+                          double momentum, int nesterov, void* stream);
+
+long long b200moe_newton_schulz_scratch_bytes(int batch, int rows, int cols);
+
+/* Newton-Schulz orthogonalisation of a stack x (batch, rows, cols) bf16 of
+ * same-shape matrices (_newtonschulz5_batched, train.py:2877-2927): x is
+ * normalised in place by its Frobenius norm (bf16, + 1e-7) and then used as a
+ * work buffer; `steps` iterations of A = X X^T, P = c*A.A + b*A, X = P.X + a*X
+ * (for rows > cols the same on X^T, computed without transposing: A = X^T X,
+ * X = X.P^T + a*X), each product in fp32 with one bf16 rounding.  The result
+ * goes to out (batch, rows, cols) bf16, or, when update (batch, rows, cols)
+ * fp32 is given, is applied as update += neg_lr * bf16(result) instead.
+ * rows and cols are multiples of 128. */
+int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, float a, float b,
+                          float c, void* out, float* update, float neg_lr, void* scratch,
+                          long long scratch_bytes, void* stream);
+
 /* ---- load-balancing loss: global_load_balancing_loss (train.py:3098-3197) */
 
 long long b200moe_lb_scratch_bytes(long long T, int E);

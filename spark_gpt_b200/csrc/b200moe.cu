@@ -14,6 +14,7 @@
 #include "grouped_gemm_2sm.cuh"
 #include "routing.cuh"
 #include "ep.cuh"
+#include "muon.cuh"
 
 namespace b200moe {
 namespace {
@@ -1128,6 +1129,197 @@ int b200moe_ep_weight_grad(const float* dw_rows, const int* inv_send, const long
   ep_weight_grad_kernel<<<grid_for(T * k, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       dw_rows, inv_send, selected, T, k, experts_per_rank, ranks, d_weights);
   return check_launch("ep_weight_grad");
+}
+
+// ---------------------------------------------------------------- Muon (packed experts)
+int b200moe_muon_momentum(const float* grad, float* momentum_buf, void* staged, long long n,
+                          double momentum, int nesterov, void* stream) {
+  REQUIRE(grad && momentum_buf && staged, "muon_momentum: null pointer");
+  REQUIRE(n >= 0 && n % 4 == 0, "muon_momentum: n must be a multiple of 4");
+  if (n == 0) return B200MOE_OK;
+  muon_momentum_kernel<<<grid_for(n / 4, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      grad, momentum_buf, static_cast<__nv_bfloat16*>(staged), n,
+      static_cast<float>(1.0 - momentum), static_cast<float>(momentum), nesterov);
+  return check_launch("muon_momentum");
+}
+
+}  // extern "C"
+
+namespace {
+struct NsScratch {
+  __nv_bfloat16 *gram, *poly, *xb;
+  int *pad_r, *tile_r, *pad_g, *tile_g;
+  float* partial;
+  long long bytes;
+};
+
+long long align256(long long v) { return (v + 255) / 256 * 256; }
+
+NsScratch ns_layout(void* base, int batch, int rows, int cols) {
+  const long long g = std::min(rows, cols);
+  const int chunks = static_cast<int>((static_cast<long long>(rows) * cols + kNsChunk - 1) / kNsChunk);
+  NsScratch s;
+  long long off = 0;
+  auto take = [&](long long bytes) {
+    void* p = base ? static_cast<uint8_t*>(base) + off : nullptr;
+    off += align256(bytes);
+    return p;
+  };
+  s.gram = static_cast<__nv_bfloat16*>(take(2LL * batch * g * g));
+  s.poly = static_cast<__nv_bfloat16*>(take(2LL * batch * g * g));
+  s.xb = static_cast<__nv_bfloat16*>(take(2LL * batch * rows * cols));
+  s.pad_r = static_cast<int*>(take(4LL * (batch + 1)));
+  s.tile_r = static_cast<int*>(take(4LL * batch * (rows / 128)));
+  s.pad_g = static_cast<int*>(take(4LL * (batch + 1)));
+  s.tile_g = static_cast<int*>(take(4LL * batch * (g / 128)));
+  s.partial = static_cast<float*>(take(4LL * batch * chunks));
+  s.bytes = off;
+  return s;
+}
+
+// One product of the Newton-Schulz step: out = alpha * A.B + beta * aux, over
+// `batch` groups.  K-major A rows are the stacked groups of `a_rows` rows.
+template <bool B_MN>
+int ns_rows_product(const CUtensorMap& ta, const CUtensorMap& tb, int n, GemmParams p,
+                    cudaStream_t st, const char* what) {
+  if (n % 256 == 0) return launch_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+  return launch_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+}
+}  // namespace
+
+extern "C" {
+
+long long b200moe_newton_schulz_scratch_bytes(int batch, int rows, int cols) {
+  if (batch < 1 || rows < 1 || cols < 1) return 0;
+  return ns_layout(nullptr, batch, rows, cols).bytes;
+}
+
+int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, float a, float b,
+                          float c, void* out, float* update, float neg_lr, void* scratch,
+                          long long scratch_bytes, void* stream) {
+  REQUIRE(x && scratch && (out || update), "newton_schulz: null pointer");
+  REQUIRE(batch >= 1 && steps >= 1, "newton_schulz: need batch >= 1 and steps >= 1");
+  REQUIRE(rows % 128 == 0 && cols % 128 == 0 && rows > 0 && cols > 0,
+          "newton_schulz: rows and cols must be positive multiples of 128");
+  REQUIRE(static_cast<long long>(batch) * std::max(rows, cols) < 0x7fffffffLL,
+          "newton_schulz: stack too large");
+  REQUIRE(scratch_bytes >= b200moe_newton_schulz_scratch_bytes(batch, rows, cols),
+          "newton_schulz: scratch too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const NsScratch S = ns_layout(scratch, batch, rows, cols);
+  const int g = std::min(rows, cols);
+  const bool tall = rows > cols;
+  const long long per = static_cast<long long>(rows) * cols;
+  const int chunks = static_cast<int>((per + kNsChunk - 1) / kNsChunk);
+  auto* X0 = static_cast<__nv_bfloat16*>(x);
+  int rc;
+
+  ns_tables_kernel<<<grid_for(std::max(batch + 1, batch * (rows / 128)), 256), 256, 0, st>>>(
+      batch, rows, S.pad_r, S.tile_r);
+  if ((rc = check_launch("newton_schulz tables"))) return rc;
+  ns_tables_kernel<<<grid_for(std::max(batch + 1, batch * (g / 128)), 256), 256, 0, st>>>(
+      batch, g, S.pad_g, S.tile_g);
+  if ((rc = check_launch("newton_schulz tables"))) return rc;
+  ns_sumsq_kernel<<<batch * chunks, 256, 0, st>>>(X0, per, chunks, S.partial);
+  if ((rc = check_launch("newton_schulz sumsq"))) return rc;
+  ns_normalize_kernel<<<dim3(static_cast<unsigned>(std::min<long long>((per / 8 + 255) / 256, 64)),
+                             static_cast<unsigned>(batch)), 256, 0, st>>>(X0, per, chunks, S.partial);
+  if ((rc = check_launch("newton_schulz normalize"))) return rc;
+
+  const long long R = static_cast<long long>(batch) * rows;  // stacked rows of X
+  const long long G = static_cast<long long>(batch) * g;     // stacked rows of the Gram stack
+  const int bn_g = g % 256 == 0 ? 256 : 128;
+  const int bn_x = cols % 256 == 0 ? 256 : 128;
+  __nv_bfloat16* cur = X0;
+  for (int it = 0; it < steps; ++it) {
+    const bool last = it + 1 == steps;
+    __nv_bfloat16* nxt = (it % 2 == 0) ? S.xb : X0;
+    CUtensorMap ta, tb;
+    // 1. Gram: A = X X^T (wide) or X^T X (tall), g x g per matrix
+    GemmParams p = blank_params();
+    p.num_groups = batch;
+    p.alpha = 1.f;
+    p.beta = 0.f;
+    p.out = S.gram;
+    p.ld_out = g;
+    p.n_valid = g;
+    p.n_tiles = g / bn_g;
+    if (!tall) {
+      if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns gram a"))) return rc;
+      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, bn_g, "ns gram b"))) return rc;
+      p.tile_expert = S.tile_r;
+      p.pad_offsets = S.pad_r;
+      p.k_blocks = cols / 64;
+      p.b_group_rows = rows;
+      p.m_valid = R;
+      if ((rc = ns_rows_product<false>(ta, tb, g, p, st, "ns gram"))) return rc;
+    } else {
+      if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 64, "ns gram a"))) return rc;
+      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, 64, "ns gram b"))) return rc;
+      p.pad_offsets = S.pad_r;
+      p.m_tiles = g / 128;
+      p.m_valid = g;
+      p.out_group_stride = static_cast<long long>(g) * g;
+      rc = bn_g == 256
+               ? launch_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
+               : launch_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
+      if (rc) return rc;
+    }
+    // 2. P = c * A.A + b * A (A symmetric, so A.A = A.A^T)
+    p = blank_params();
+    if ((rc = make_tmap(&ta, S.gram, g, G, g, 64, 128, "ns poly a"))) return rc;
+    if ((rc = make_tmap(&tb, S.gram, g, G, g, 64, bn_g, "ns poly b"))) return rc;
+    p.tile_expert = S.tile_g;
+    p.pad_offsets = S.pad_g;
+    p.num_groups = batch;
+    p.n_tiles = g / bn_g;
+    p.k_blocks = g / 64;
+    p.b_group_rows = g;
+    p.m_valid = G;
+    p.n_valid = g;
+    p.out = S.poly;
+    p.ld_out = g;
+    p.aux = S.gram;
+    p.ld_aux = g;
+    p.alpha = c;
+    p.beta = b;
+    if ((rc = ns_rows_product<false>(ta, tb, g, p, st, "ns poly"))) return rc;
+    // 3. X' = P.X + a*X (wide) or X.P + a*X (tall), in X's layout
+    p = blank_params();
+    p.tile_expert = S.tile_r;
+    p.pad_offsets = S.pad_r;
+    p.num_groups = batch;
+    p.n_tiles = cols / bn_x;
+    p.m_valid = R;
+    p.n_valid = cols;
+    p.aux = cur;
+    p.ld_aux = cols;
+    p.alpha = 1.f;
+    p.beta = a;
+    if (last && update) {
+      p.update = update;
+      p.ld_update = cols;
+      p.neg_lr = neg_lr;
+    } else {
+      p.out = last ? out : nxt;
+      p.ld_out = cols;
+    }
+    if (!tall) {
+      if ((rc = make_tmap(&ta, S.poly, g, G, g, 64, 128, "ns update a"))) return rc;
+      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, 64, "ns update b"))) return rc;
+      p.k_blocks = rows / 64;
+      p.b_group_rows = rows;
+      if ((rc = ns_rows_product<true>(ta, tb, cols, p, st, "ns update"))) return rc;
+    } else {
+      if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns update a"))) return rc;
+      if ((rc = make_tmap(&tb, S.poly, g, G, g, 64, bn_x, "ns update b"))) return rc;
+      p.k_blocks = cols / 64;
+      p.b_group_rows = g;
+      if ((rc = ns_rows_product<false>(ta, tb, cols, p, st, "ns update"))) return rc;
+    }
+    cur = nxt;
+  }
+  return B200MOE_OK;
 }
 
 // ---------------------------------------------------------------- load balancing

@@ -43,6 +43,7 @@ enum Epilogue : int {
   kEpiStoreF32 = 3,
   kEpiStoreF32T = 4,
   kEpiSwigluBwdCombine = 5,  // down dgrad from gathered d_out: combine backward fused in
+  kEpiAxpby = 6,             // bf16 out = alpha*acc + beta*aux, or fp32 update += neg_lr*bf16(..)
 };
 
 // Which operand is gathered row by row from a token-major tensor (x or d_out)
@@ -95,6 +96,14 @@ struct GemmParams {
   // kEpiStoreBf16: when set, padded row p is written to output row
   // scatter_rows[p] (token-major layout t*k+s) and padding rows are skipped
   const int* scatter_rows;
+  // kEpiAxpby (the batched Newton-Schulz products of Muon): v = alpha*acc +
+  // beta*aux[row, col] (aux bf16, or alpha*acc when aux is null); with `update`
+  // set, update[row, col] += neg_lr * bf16(v) (fp32) instead of storing v.
+  // Row offsets of a group's output: T.g * out_group_stride (K-ragged Gram
+  // products); rows-ragged products index the stacked rows directly.
+  float alpha, beta, neg_lr;
+  float* update;
+  long long ld_update;
 };
 
 __device__ __forceinline__ int gather_token(const GemmParams& p, int row) {
@@ -335,6 +344,41 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
       store_bf16x32(hw + col, hv);
     }
     p.dw_part[(T.n * 2 + half) * p.part_stride + row] = dwp;
+  } else if (EPI == kEpiAxpby) {
+    const long long row = static_cast<long long>(T.m) * BM + row_in;
+    const long long base = T.g * p.out_group_stride;
+    const bool row_ok = row < p.m_valid;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const int col0 = T.n * BN + c * 32;
+      if (!row_ok) continue;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+      if (p.aux != nullptr) {
+        float cv[32];
+        load_bf16x32(static_cast<const __nv_bfloat16*>(p.aux) + base + row * p.ld_aux + col0, cv);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] += p.beta * cv[j];
+      }
+      if (p.update != nullptr) {
+        float4* u = reinterpret_cast<float4*>(p.update + base + row * p.ld_update + col0);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float4 w = u[j];
+          w.x += p.neg_lr * bf16_round(v[4 * j + 0]);
+          w.y += p.neg_lr * bf16_round(v[4 * j + 1]);
+          w.z += p.neg_lr * bf16_round(v[4 * j + 2]);
+          w.w += p.neg_lr * bf16_round(v[4 * j + 3]);
+          u[j] = w;
+        }
+      } else {
+        store_bf16x32(static_cast<__nv_bfloat16*>(p.out) + base + row * p.ld_out + col0, v);
+      }
+    }
   } else if (EPI == kEpiStoreF32) {
     float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
                static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;

@@ -8,7 +8,10 @@ It imports ``train.py`` from the reference checkout (not copied), runs its
 ``SparseMoE`` (train.py:2325-2334) and ``global_load_balancing_loss``
 (train.py:3098-3197) on seeded CPU fp32 inputs, back-propagates
 ``(out * probe).sum() + 1e-3 * aux``, and stores inputs and outputs in
-``tests/golden/moe_golden.pt``.  The large config-1 case stores its inputs as a
+``tests/golden/moe_golden.pt``; it also runs two ``MuonAdamWHybrid`` steps
+(train.py:2930-3024) on seeded packed expert tensors and the batched
+Newton-Schulz iteration (train.py:2877-2927) on its own, stored in
+``tests/golden/muon_golden.pt`` (``--only muon`` writes just that file).  The large config-1 case stores its inputs as a
 seed plus checksums and keeps only slices and norms of the float outputs, so
 the fixture stays small.
 """
@@ -69,15 +72,69 @@ def run_layer(train, x, w_r, w_gu, w_d, probe, top_k, norm, valid):
     }
 
 
+MUON_CASES = {
+    # name: (E, rows, cols, lr, momentum, nesterov, seed): gate_up-like wide and
+    # down-like tall packed expert tensors
+    "muon_wide": (2, 128, 256, 0.02, 0.95, True, 11),
+    "muon_tall": (2, 256, 128, 0.02, 0.95, True, 12),
+    "muon_square_plain": (1, 128, 128, 0.05, 0.9, False, 13),
+}
+NS_CASES = {"ns_wide": ((2, 128, 256), 21), "ns_tall": ((2, 256, 128), 22)}
+
+
+def muon_case_inputs(E, rows, cols, seed):
+    """Initial packed parameter and the two steps' gradients of a Muon case."""
+    g = torch.Generator().manual_seed(seed)
+    p0 = torch.randn(E, rows, cols, generator=g) * 0.02
+    grads = [torch.randn(E, rows, cols, generator=g) * 1e-3 for _ in range(2)]
+    return p0, grads
+
+
+def ns_case_input(shape, seed):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * 0.3).to(torch.bfloat16)
+
+
+def make_muon_golden(train, out_path):
+    """Two MuonAdamWHybrid steps (train.py:2930-3024) on seeded packed expert
+    tensors, run by the reference itself on CPU (its lerp + bmm/baddbmm path).
+    Inputs are regenerated from the seeds (muon_case_inputs); stored: the
+    parameter change after two steps and the momentum buffer."""
+    cases = {}
+    for name, (E, rows, cols, lr, mom, nest, seed) in MUON_CASES.items():
+        p0, grads = muon_case_inputs(E, rows, cols, seed)
+        p = torch.nn.Parameter(p0.clone())
+        opt = train.MuonAdamWHybrid([{"params": [p], "use_muon": True, "lr": lr,
+                                      "momentum": mom, "nesterov": nest, "ns_steps": 5}])
+        for gr in grads:
+            p.grad = gr.clone()
+            opt.step()
+        cases[name] = {"delta2": p.detach() - p0, "v2": opt.state[p]["v"].clone(),
+                       "input_sum": p0.double().sum() + sum(gr.double().sum() for gr in grads)}
+    # the orthogonalisation on its own (train.py:2877-2927)
+    for name, (shape, seed) in NS_CASES.items():
+        x = ns_case_input(shape, seed)
+        cases[name] = {"out": train._newtonschulz5_batched(x.clone(), steps=5)}
+    torch.save(cases, out_path)
+    print(f"wrote {out_path}: {', '.join(cases)}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPARK_GPT_REFERENCE", "/root/reference"))
     ap.add_argument("--out", default=str(HERE / "moe_golden.pt"))
+    ap.add_argument("--muon-out", default=str(HERE / "muon_golden.pt"))
+    ap.add_argument("--only", choices=["moe", "muon"], default=None)
     args = ap.parse_args()
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)
     import train  # the reference module, imported in place
     import torch.nn.functional as F
+
+    if args.only != "moe":
+        make_muon_golden(train, args.muon_out)
+    if args.only == "muon":
+        return
 
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     cases = {}

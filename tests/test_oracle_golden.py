@@ -1,10 +1,12 @@
 """Pin the CPU oracle against golden vectors made by the reference itself.
 
 The fixtures come from tests/golden/make_golden.py, which runs spark-gpt's own
-SparseMoE / global_load_balancing_loss (train.py:2325-2334, 3098-3197).
+SparseMoE / global_load_balancing_loss (train.py:2325-2334, 3098-3197) and its
+MuonAdamWHybrid / _newtonschulz5_batched (train.py:2877-3024).
 """
 
 import numpy as np
+import pytest
 import torch
 
 from oracle import moe_oracle as O
@@ -144,3 +146,39 @@ def test_dispatch_empty_and_all_one_expert():
     assert d.offsets.tolist() == [3, 3, 6, 6]
     # rows ordered by (expert, token): expert 0 <- tokens 0,1,2 ; expert 2 <- tokens 0,1,2
     assert d.token_index.tolist() == [0, 1, 2, 0, 1, 2]
+
+
+# --------------------------------------------------------------------------- #
+# Muon on the packed expert tensors (train.py:2877-3024)
+# --------------------------------------------------------------------------- #
+@pytest.fixture(scope="module")
+def muon_golden():
+    from tests.conftest import ROOT
+    return torch.load(ROOT / "tests" / "golden" / "muon_golden.pt", weights_only=True)
+
+
+@pytest.mark.parametrize("name", ["muon_wide", "muon_tall", "muon_square_plain"])
+def test_muon_oracle_matches_reference_steps(muon_golden, name):
+    from oracle import muon_oracle as M
+    from tests.golden.make_golden import MUON_CASES, muon_case_inputs
+    from tests.helpers import assert_bf16_close
+    E, rows, cols, lr, mom, nest, seed = MUON_CASES[name]
+    p0, grads = muon_case_inputs(E, rows, cols, seed)
+    c = muon_golden[name]
+    assert torch.isclose(c["input_sum"], p0.double().sum() + sum(g.double().sum() for g in grads))
+    p, v = p0.clone(), torch.zeros_like(p0)
+    for g in grads:
+        p, v = M.muon_step(p, g, v, lr, mom, nest)
+    torch.testing.assert_close(v, c["v2"], rtol=1e-6, atol=1e-9)
+    assert_bf16_close(p - p0, c["delta2"], f"{name} update")
+
+
+@pytest.mark.parametrize("name", ["ns_wide", "ns_tall"])
+def test_newton_schulz_oracle_matches_reference(muon_golden, name):
+    from oracle import muon_oracle as M
+    from tests.golden.make_golden import NS_CASES, ns_case_input
+    from tests.helpers import assert_bf16_close
+    shape, seed = NS_CASES[name]
+    out = M.newton_schulz(ns_case_input(shape, seed), steps=5)
+    assert out.dtype == torch.bfloat16 and out.shape == shape
+    assert_bf16_close(out, muon_golden[name]["out"], name)
