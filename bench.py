@@ -69,7 +69,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-muon", action="store_true",
                     help="skip the Muon optimizer-step measurement of the expert tensors")
-    ap.add_argument("--ep-chunks", type=int, default=2,
+    ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallel: token chunks pipelined against the exchanges")
     ap.add_argument("--comm-sms", type=int, default=16,
                     help="expert parallel: SMs the persistent kernels leave to NCCL while an "

@@ -153,16 +153,19 @@ int b200moe_gather_rows(const void* x, const int* row_flat, const int* inv_pad,
                         long long rows_cap, void* xs, void* stream);
 
 /* dx (T,H) bf16 = sum_s dxs[inv_pad[t*k+s]] (+ addend (T,H) bf16 if given).
- * With inv_pad == NULL, dxs is token-major: slot t*k+s in row t*k+s. */
+ * With inv_pad == NULL, dxs is token-major: slot t*k+s in row t*k+s.
+ * partial = 1 when some slots have no row (inv_pad -1, skipped); with
+ * partial = 0 every inv_pad entry must be a row. */
 int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
-                            int k, int H, void* dx, void* stream);
+                            int k, int H, int partial, void* dx, void* stream);
 
 /* ---- combine: _CombineTopK (train.py:2220-2241) -------------------------- */
 
 /* out (T,H) bf16 = sum_s bf16(y[inv_pad[t*k+s]] * weights[t,s]).  With
- * inv_pad == NULL, y is token-major: slot t*k+s in row t*k+s. */
+ * inv_pad == NULL, y is token-major: slot t*k+s in row t*k+s.  partial as in
+ * b200moe_gather_rows_bwd. */
 int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T,
-                        int k, int H, void* out, void* stream);
+                        int k, int H, int partial, void* out, void* stream);
 
 /* dy (Rcap,H) bf16 = bf16(d_out[t] * w), zero for padding rows;
  * d_weights (T*k) fp32 = <d_out[t], y[row of slot]> in flat-slot order.

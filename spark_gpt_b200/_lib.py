@@ -39,8 +39,8 @@ PROTOTYPES = {
     "b200moe_dispatch": (I, [P, L, I, I, P, P, P, P, P, P, P, L, P]),
     "b200moe_dispatch_noalloc": (I, [P, L, I, I, P, P, P, P, P, P, P]),
     "b200moe_gather_rows": (I, [P, P, P, P, L, I, I, I, L, P, P]),
-    "b200moe_gather_rows_bwd": (I, [P, P, P, L, I, I, P, P]),
-    "b200moe_combine_fwd": (I, [P, P, P, L, I, I, P, P]),
+    "b200moe_gather_rows_bwd": (I, [P, P, P, L, I, I, I, P, P]),
+    "b200moe_combine_fwd": (I, [P, P, P, L, I, I, I, P, P]),
     "b200moe_combine_bwd": (I, [P, P, P, P, P, P, I, L, I, I, L, I, P, P, P]),
     "b200moe_expert_gate_up_fwd": (I, [P, P, P, P, L, I, I, I, P, P, P]),
     "b200moe_expert_down_fwd": (I, [P, P, P, P, P, L, I, I, I, P, P]),

@@ -257,22 +257,23 @@ constexpr int kReduceSmemPerBlock = 72 * 1024;  // three blocks per SM
 
 int launch_row_reduce(const __nv_bfloat16* rows, const int* inv_pad,
                       const __nv_bfloat16* weights, const __nv_bfloat16* addend, long long T,
-                      int k, int H, __nv_bfloat16* out, cudaStream_t st, const char* what) {
+                      int k, int H, __nv_bfloat16* out, cudaStream_t st, const char* what,
+                      bool partial) {
   const long long slot_bytes = 2LL * H * k;
   // slots: a multiple of the consumer-group count, at least one per group
   const int min_slots = kReduceGroups;
   if (slot_bytes * min_slots > kReduceSmemPerBlock || H % (8 * kReduceWarpsPerToken) != 0 ||
       k > kMaxTopK)
     return -1;
-  int slots = 4 * kReduceGroups;
+  int slots = kMaxReduceSlots;
   while (slots > min_slots && slots * slot_bytes > kReduceSmemPerBlock) slots -= kReduceGroups;
   const size_t smem = static_cast<size_t>(slots) * slot_bytes + 2 * slots * sizeof(uint64_t);
-  cudaError_t e = cudaFuncSetAttribute(row_reduce_kernel,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  auto kern = partial && inv_pad ? row_reduce_kernel<true> : row_reduce_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   const long long grid = std::min<long long>(3LL * persistent_sms(), std::max<long long>(T, 1));
-  row_reduce_kernel<<<static_cast<int>(grid), kReduceThreads, smem, st>>>(
-      rows, inv_pad, weights, addend, T, k, H, slots, out);
+  kern<<<static_cast<int>(grid), kReduceThreads, smem, st>>>(rows, inv_pad, weights, addend, T, k,
+                                                              H, slots, out);
   return check_launch(what);
 }
 
@@ -635,7 +636,7 @@ int b200moe_gather_rows(const void* x, const int* row_flat, const int* inv_pad,
 }
 
 int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
-                            int k, int H, void* dx, void* stream) {
+                            int k, int H, int partial, void* dx, void* stream) {
   REQUIRE(dxs && dx, "gather_rows_bwd: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "gather_rows_bwd: bad shape");
   if (T == 0) return B200MOE_OK;
@@ -643,7 +644,8 @@ int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* add
     const int rc = launch_row_reduce(static_cast<const __nv_bfloat16*>(dxs), inv_pad, nullptr,
                                      static_cast<const __nv_bfloat16*>(addend), T, k, H,
                                      static_cast<__nv_bfloat16*>(dx),
-                                     static_cast<cudaStream_t>(stream), "gather_rows_bwd");
+                                     static_cast<cudaStream_t>(stream), "gather_rows_bwd",
+                                     partial != 0);
     if (rc >= 0) return rc;
   }
   gather_rows_bwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
@@ -653,7 +655,7 @@ int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* add
 }
 
 int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T, int k,
-                        int H, void* out, void* stream) {
+                        int H, int partial, void* out, void* stream) {
   REQUIRE(y && weights && out, "combine_fwd: null pointer");
   REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "combine_fwd: bad shape");
   if (T == 0) return B200MOE_OK;
@@ -661,7 +663,8 @@ int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, 
     const int rc = launch_row_reduce(static_cast<const __nv_bfloat16*>(y), inv_pad,
                                      static_cast<const __nv_bfloat16*>(weights), nullptr, T, k, H,
                                      static_cast<__nv_bfloat16*>(out),
-                                     static_cast<cudaStream_t>(stream), "combine_fwd");
+                                     static_cast<cudaStream_t>(stream), "combine_fwd",
+                                     partial != 0);
     if (rc >= 0) return rc;
   }
   combine_fwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(

@@ -642,8 +642,12 @@ __global__ void zero_pad_rows_kernel(const int* __restrict__ row_flat,
 // ---------------------------------------------------------------------------
 constexpr int kReduceWarpsPerToken = 4;
 constexpr int kReduceGroups = 2;
+constexpr int kMaxReduceSlots = 4 * kReduceGroups;
 constexpr int kReduceThreads = 32 * (1 + kReduceGroups * kReduceWarpsPerToken);
 
+// SKIP: some slots may have no row (inv_pad -1, the expert-parallel layouts);
+// without it every one of a token's k slots is copied and summed.
+template <bool SKIP>
 __global__ void __launch_bounds__(kReduceThreads)
     row_reduce_kernel(const __nv_bfloat16* __restrict__ rows, const int* __restrict__ inv_pad,
                       const __nv_bfloat16* __restrict__ weights,
@@ -655,6 +659,9 @@ __global__ void __launch_bounds__(kReduceThreads)
   uint64_t* full = reinterpret_cast<uint64_t*>(rsm + static_cast<size_t>(slots) * slot_bytes);
   uint64_t* empty = full + slots;
   __shared__ int abort_flag_s;
+  // per ring slot: which of the token's k rows were copied (bit s = slot s),
+  // written by the producer before it arms the slot's full barrier
+  __shared__ unsigned slot_mask[kMaxReduceSlots];
   volatile int* abort_flag = &abort_flag_s;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -688,12 +695,19 @@ __global__ void __launch_bounds__(kReduceThreads)
         const uint32_t ph = static_cast<uint32_t>((i / slots) & 1);
         // slots without an expert (row -1) are not copied; the barrier expects
         // the bytes of the token's real rows only (zero bytes complete it at once)
-        const bool mine = active_lane && lane / k == tt && idx >= 0;
-        const uint32_t nrows = __popc(__ballot_sync(0xffffffffu, mine));
+        const bool mine = active_lane && lane / k == tt && (!SKIP || idx >= 0);
+        const unsigned have = SKIP ? __ballot_sync(0xffffffffu, mine) : 0u;
         int good = 1;
         if (lane == 0) {
           good = mbar_wait(&empty[s], ph ^ 1u, abort_flag) ? 1 : 0;
-          if (good) mbar_expect_tx(&full[s], nrows * row_bytes);
+          if (good) {
+            if (SKIP) {
+              slot_mask[s] = (have >> (tt * k)) & ((1u << k) - 1u);
+              mbar_expect_tx(&full[s], __popc(have) * row_bytes);  // release: orders the mask
+            } else {
+              mbar_expect_tx(&full[s], slot_bytes);
+            }
+          }
         }
         good = __shfl_sync(0xffffffffu, good, 0);
         if (!good) break;
@@ -721,9 +735,7 @@ __global__ void __launch_bounds__(kReduceThreads)
       float wv = 1.f;
       if (weights && lane < k) wv = __bfloat162float(weights[t * k + lane]);
       // slots with a row (inv_pad >= 0); the others were not copied
-      const unsigned have =
-          inv_pad ? __ballot_sync(0xffffffffu, lane < k && inv_pad[t * k + lane] >= 0)
-                  : (k >= 32 ? 0xffffffffu : (1u << k) - 1u);
+      const unsigned have = SKIP ? slot_mask[s] : 0xffffffffu;
       __nv_bfloat162 wr[kMaxTopK];
 #pragma unroll
       for (int r = 0; r < kMaxTopK; ++r)
@@ -735,7 +747,7 @@ __global__ void __launch_bounds__(kReduceThreads)
         for (int j = 0; j < 8; ++j) acc[j] = 0.f;
 #pragma unroll
         for (int r = 0; r < kMaxTopK; ++r) {
-          if (r < k && ((have >> r) & 1u)) {
+          if (r < k && (!SKIP || ((have >> r) & 1u))) {
             uint4 q = *reinterpret_cast<const uint4*>(slot + r * row_bytes + v * 16);
             if (weights) {
               // bf16 x bf16 product rounded once to bf16 (= bf16(float(a)*float(b)))

@@ -79,7 +79,7 @@ class CudaExpertOps:
     def send_plan(sel, rw, experts_per_rank, ranks):
         """Send layout + slot words; sizes (P, 2) int64 = [rows, slots] per rank."""
         dest, slots = ops.ep_route(sel, experts_per_rank, ranks)
-        send = ops.dispatch(dest, ranks)
+        send = ops.dispatch(dest, ranks, partial=True)
         meta = ops.ep_pack(sel, rw, send, experts_per_rank)
         rows = send.pad_offsets[1:] - send.pad_offsets[:-1]
         sizes = torch.stack([rows.to(torch.int64), slots.to(torch.int64)], 1)

@@ -193,12 +193,14 @@ class Dispatch:
     num_tokens: int
     top_k: int
     num_experts: int
+    partial: bool = False      # some slots carry no expert (id -1: no row, inv_pad -1)
 
 
-def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None = None) -> Dispatch:
-    """Negative ids mark slots without an expert (no row, inv_pad -1);
-    routed_slots, when given, is the number of non-negative ids and sizes the
-    padded-row buffers."""
+def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None = None,
+             partial: bool = False) -> Dispatch:
+    """partial: negative ids may occur and mark slots without an expert (no row,
+    inv_pad -1; the row reductions then skip them).  routed_slots, when given,
+    is the number of non-negative ids and sizes the padded-row buffers."""
     _check(selected, torch.int64, "dispatch selected")
     T, k = selected.shape
     R = T * k
@@ -216,7 +218,8 @@ def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None 
     _launch("dispatch", 3, "b200moe_dispatch", _p(selected), T, k, num_experts, _p(counts),
             _p(offsets), _p(pad), _p(row_flat), _p(inv), _p(tiles), _p(scratch), nbytes,
             _s(selected))
-    return Dispatch(counts, offsets, pad, row_flat, inv[:R], tiles, cap, T, k, num_experts)
+    return Dispatch(counts, offsets, pad, row_flat, inv[:R], tiles, cap, T, k, num_experts,
+                    partial or routed_slots is not None)
 
 
 # --------------------------------------------------------------------------- #
@@ -244,7 +247,7 @@ def gather_rows_bwd(dxs, d: Dispatch, addend=None, token_major=False, out=None) 
     if d.num_tokens:
         _launch("gather_bwd", 1, "b200moe_gather_rows_bwd", _p(dxs),
                 None if token_major else _p(d.inv_pad), _p(addend), d.num_tokens, d.top_k, H,
-                _p(dx), _s(dxs))
+                int(d.partial), _p(dx), _s(dxs))
     return dx
 
 
@@ -255,7 +258,7 @@ def combine(y, d: Dispatch, weights, token_major=False) -> torch.Tensor:
     if d.num_tokens:
         _launch("combine", 1, "b200moe_combine_fwd", _p(y),
                 None if token_major else _p(d.inv_pad), _p(weights), d.num_tokens, d.top_k, H,
-                _p(out), _s(y))
+                int(d.partial), _p(out), _s(y))
     return out
 
 
