@@ -71,6 +71,8 @@ def parse_args():
                     help="skip the Muon optimizer-step measurement of the expert tensors")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallel: token chunks pipelined against the exchanges")
+    ap.add_argument("--transport", default="nccl", choices=["nccl", "p2p"],
+                    help="expert parallel: NCCL all-to-all or peer-memory stores")
     ap.add_argument("--comm-sms", type=int, default=16,
                     help="expert parallel: SMs the persistent kernels leave to NCCL while an "
                          "exchange is in flight (0: none)")
@@ -277,9 +279,14 @@ def run_reference(args, c):
 
 def config_block(args, c, n):
     if c.get("ep"):
-        par = (f"ep{n} (experts sharded, NCCL all_to_all, one row per (token, rank), "
-               f"{args.ep_chunks} token chunks overlapped, {args.comm_sms} SMs left to NCCL)"
-               if n > 1 else "ep1 = the single-GPU layer, all experts local (the scaling baseline)")
+        if n == 1:
+            par = "ep1 = the single-GPU layer, all experts local (the scaling baseline)"
+        elif args.transport == "p2p":
+            par = (f"ep{n} (experts sharded, one row per (token, rank) stored into the owners' "
+                   f"peer memory by the gather / combine kernels, bounded barriers)")
+        else:
+            par = (f"ep{n} (experts sharded, NCCL all_to_all, one row per (token, rank), "
+                   f"{args.ep_chunks} token chunks overlapped, {args.comm_sms} SMs left to NCCL)")
     else:
         par = f"dp{n} (replicated experts)"
     return {"workload": f"{args.config}: single Qwen3-MoE layer fwd+bwd (BASELINE configs"
@@ -319,7 +326,8 @@ def main():
     w_r, w_gu, w_d = make_weights(c, 0)
     if c.get("ep") and world > 1:
         from spark_gpt_b200.ep import ExpertParallelMoE
-        layer = ExpertParallelMoE(cfg, chunks=args.ep_chunks, comm_sms=args.comm_sms).to(dev)
+        layer = ExpertParallelMoE(cfg, chunks=args.ep_chunks, comm_sms=args.comm_sms,
+                                  transport=args.transport).to(dev)
         lo, hi = layer.expert_offset, layer.expert_offset + layer.local_experts
         w_gu, w_d = w_gu[lo:hi], w_d[lo:hi]
     else:

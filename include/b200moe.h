@@ -295,6 +295,55 @@ int b200moe_ep_weight_grad(const float* dw_rows, const int* inv_send, const long
                            long long T, int k, int experts_per_rank, int ranks, float* d_weights,
                            void* stream);
 
+/* ---- expert parallel over peer memory (NVLink / NVSwitch) ---------------
+ * The exchange of the expert-parallel layer without a collective library:
+ * rows are stored by these kernels straight into buffers of the other ranks
+ * that every rank has mapped (symmetric memory), and a bounded barrier over
+ * flag words in that memory orders the phases.  Per rank the mapped buffers are
+ * recv rows (P*T_cap, H) bf16 + recv meta (P*T_cap, k) uint32 (rows sent to
+ * this rank's experts) and back rows (P*T_cap, H) bf16 + back dw (P*T_cap, k)
+ * fp32 (results returned to this rank).  counts (P, ld) int32: row s = the
+ * unpadded rows rank s sends to each rank (gathered on every rank).  No
+ * counterpart in the reference, which is data-parallel only. */
+
+/* plan (2 + 4P ints) of this rank from the gathered counts: [0] rows received,
+ * [1, 1+P) where this rank's rows start at each owner, [1+P, 2+2P) where each
+ * source's rows start here (P+1 entries), [2+2P, 2+3P) where this rank's
+ * results for each source start in that source's back rows, [2+3P, 2+4P) where
+ * each owner's results start in this rank's back rows. */
+int b200moe_ep_p2p_plan(const int* counts, int ld, int me, int ranks, int* plan, void* stream);
+
+/* Source side: each token's row src[t] (T,H) bf16 is stored into the recv rows
+ * of every rank it selected (peer_rows[r] = rank r's recv rows, mapped here),
+ * at the row given by the send layout (inv_send (T*P), send_pad_offsets (P+1)
+ * from the dispatch of b200moe_ep_route's dest) and the plan; with selected
+ * (T,k) and weights (T,k) bf16, its k slot words go to peer_meta[r] likewise
+ * (selected == NULL: rows only).  ranks <= 32. */
+int b200moe_ep_p2p_send(const void* src, const int* inv_send, const int* send_pad_offsets,
+                        const int* plan, void* const* peer_rows, long long T, int H, int ranks,
+                        const long long* selected, const void* weights, int k,
+                        int experts_per_rank, unsigned int* const* peer_meta, void* stream);
+
+/* Owner side: the first plan[0] rows of rows (rows_cap, H) bf16 (and of dw_rows
+ * (rows_cap, k) fp32 if given) are stored into the back rows (back dw) of the
+ * ranks they came from, at the rows the plan gives. */
+int b200moe_ep_p2p_return(const void* rows, const float* dw_rows, const int* plan,
+                          void* const* peer_rows, float* const* peer_dw, long long rows_cap,
+                          int H, int k, int ranks, void* stream);
+
+/* inv_back (T*P) int32: the row of this rank's back rows that holds owner r's
+ * result for token t, or -1 (for b200moe_gather_rows_bwd with k = P). */
+int b200moe_ep_p2p_back_inv(const int* inv_send, const int* send_pad_offsets, const int* plan,
+                            long long T, int ranks, int* inv_back, void* stream);
+
+/* Group barrier over peer memory: writes epoch (> every earlier epoch) into
+ * every peer's flag word for this rank (system-scope release, after this
+ * stream's earlier stores into peers) and waits until every peer has written
+ * epoch into my_flags (ranks words).  Waits at most 4 s, then sets fault bit 1
+ * and returns.  ranks <= 32. */
+int b200moe_ep_barrier(unsigned long long* const* peer_flags, unsigned long long* my_flags, int me,
+                       int ranks, unsigned long long epoch, void* stream);
+
 /* ---- Muon on the packed expert weights (train.py:2877-3024) --------------
  * The optimizer step of the 3-D expert tensors (Muon groups, train.py:3066-3070):
  * momentum, then the batched Newton-Schulz orthogonalisation of each matrix,

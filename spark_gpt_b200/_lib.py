@@ -10,7 +10,7 @@ the first call raises.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_double, c_float, c_int, c_longlong, c_uint, c_void_p, c_char_p, POINTER
+from ctypes import c_double, c_float, c_int, c_longlong, c_uint, c_ulonglong, c_void_p, c_char_p, POINTER
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libb200moe.so"
@@ -57,6 +57,11 @@ PROTOTYPES = {
     "b200moe_ep_pack": (I, [P, P, P, P, L, I, I, I, P, P]),
     "b200moe_ep_unpack": (I, [P, L, I, P, P, P]),
     "b200moe_ep_weight_grad": (I, [P, P, P, L, I, I, I, P, P]),
+    "b200moe_ep_p2p_plan": (I, [P, I, I, I, P, P]),
+    "b200moe_ep_p2p_send": (I, [P, P, P, P, P, L, I, I, P, P, I, I, P, P]),
+    "b200moe_ep_p2p_return": (I, [P, P, P, P, P, L, I, I, I, P]),
+    "b200moe_ep_p2p_back_inv": (I, [P, P, P, L, I, P, P]),
+    "b200moe_ep_barrier": (I, [P, P, I, I, c_ulonglong, P]),
     "b200moe_muon_momentum": (I, [P, P, P, L, c_double, I, P]),
     "b200moe_newton_schulz_scratch_bytes": (L, [I, I, I]),
     "b200moe_newton_schulz": (I, [P, I, I, I, I, c_float, c_float, c_float, P, P, c_float, P, L,

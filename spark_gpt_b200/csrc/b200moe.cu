@@ -1134,6 +1134,77 @@ int b200moe_ep_weight_grad(const float* dw_rows, const int* inv_send, const long
   return check_launch("ep_weight_grad");
 }
 
+// ---------------------------------------------------------------- expert parallel, peer memory
+int b200moe_ep_p2p_plan(const int* counts, int ld, int me, int ranks, int* plan, void* stream) {
+  REQUIRE(counts && plan, "ep_p2p_plan: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= kEpMaxRanks && me >= 0 && me < ranks && ld >= ranks,
+          "ep_p2p_plan: bad ranks/me/ld");
+  ep_p2p_plan_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counts, ld, me, ranks, plan);
+  return check_launch("ep_p2p_plan");
+}
+
+int b200moe_ep_p2p_send(const void* src, const int* inv_send, const int* send_pad_offsets,
+                        const int* plan, void* const* peer_rows, long long T, int H, int ranks,
+                        const long long* selected, const void* weights, int k,
+                        int experts_per_rank, unsigned int* const* peer_meta, void* stream) {
+  REQUIRE(src && inv_send && send_pad_offsets && plan && peer_rows, "ep_p2p_send: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= 32 && H % 8 == 0 && H > 0 && T >= 0,
+          "ep_p2p_send: need 1 <= ranks <= 32, H % 8 == 0");
+  REQUIRE(selected == nullptr || (weights && peer_meta && k >= 1 && k <= 32 && experts_per_rank >= 1),
+          "ep_p2p_send: slot words need weights, peer_meta, 1 <= k <= 32");
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* sp = static_cast<const __nv_bfloat16*>(src);
+  auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
+  auto* wp = static_cast<const unsigned short*>(weights);
+  const int grid = grid_for(T, 8);
+  switch (H) {
+    case 1024: ep_p2p_send_kernel<4><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta); break;
+    case 2048: ep_p2p_send_kernel<8><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta); break;
+    default: ep_p2p_send_kernel<0><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta); break;
+  }
+  return check_launch("ep_p2p_send");
+}
+
+int b200moe_ep_p2p_return(const void* rows, const float* dw_rows, const int* plan,
+                          void* const* peer_rows, float* const* peer_dw, long long rows_cap,
+                          int H, int k, int ranks, void* stream) {
+  REQUIRE(rows && plan && peer_rows, "ep_p2p_return: null pointer");
+  REQUIRE(dw_rows == nullptr || (peer_dw && k >= 1 && k <= 32), "ep_p2p_return: bad dw arguments");
+  REQUIRE(ranks >= 1 && ranks <= kEpMaxRanks && H % 8 == 0 && H > 0 && rows_cap >= 0,
+          "ep_p2p_return: bad shape");
+  if (rows_cap == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* rp = static_cast<const __nv_bfloat16*>(rows);
+  auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
+  const int grid = grid_for(rows_cap, 8);
+  switch (H) {
+    case 1024: ep_p2p_return_kernel<4><<<grid, 256, 0, st>>>(rp, dw_rows, plan, pr, peer_dw, H, k, ranks); break;
+    case 2048: ep_p2p_return_kernel<8><<<grid, 256, 0, st>>>(rp, dw_rows, plan, pr, peer_dw, H, k, ranks); break;
+    default: ep_p2p_return_kernel<0><<<grid, 256, 0, st>>>(rp, dw_rows, plan, pr, peer_dw, H, k, ranks); break;
+  }
+  return check_launch("ep_p2p_return");
+}
+
+int b200moe_ep_p2p_back_inv(const int* inv_send, const int* send_pad_offsets, const int* plan,
+                            long long T, int ranks, int* inv_back, void* stream) {
+  REQUIRE(inv_send && send_pad_offsets && plan && inv_back, "ep_p2p_back_inv: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= kEpMaxRanks && T >= 0, "ep_p2p_back_inv: bad shape");
+  if (T == 0) return B200MOE_OK;
+  ep_p2p_back_inv_kernel<<<grid_for(T * ranks, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      inv_send, send_pad_offsets, plan, T, ranks, inv_back);
+  return check_launch("ep_p2p_back_inv");
+}
+
+int b200moe_ep_barrier(unsigned long long* const* peer_flags, unsigned long long* my_flags, int me,
+                       int ranks, unsigned long long epoch, void* stream) {
+  REQUIRE(peer_flags && my_flags, "ep_barrier: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= 32 && me >= 0 && me < ranks && epoch > 0, "ep_barrier: bad args");
+  ep_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(peer_flags, my_flags, me,
+                                                                     ranks, epoch);
+  return check_launch("ep_barrier");
+}
+
 // ---------------------------------------------------------------- Muon (packed experts)
 int b200moe_muon_momentum(const float* grad, float* momentum_buf, void* staged, long long n,
                           double momentum, int nesterov, void* stream) {
@@ -1180,13 +1251,21 @@ NsScratch ns_layout(void* base, int batch, int rows, int cols) {
   return s;
 }
 
-// One product of the Newton-Schulz step: out = alpha * A.B + beta * aux, over
-// `batch` groups.  K-major A rows are the stacked groups of `a_rows` rows.
+// One row-ragged product of the Newton-Schulz step: out = alpha * A.B + beta *
+// aux over `batch` groups (two-CTA pair tiles when the shape allows).
 template <bool B_MN>
 int ns_rows_product(const CUtensorMap& ta, const CUtensorMap& tb, int n, GemmParams p,
                     cudaStream_t st, const char* what) {
-  if (n % 256 == 0) return launch_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
-  return launch_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+  if (n % 256 == 0)
+    return launch_expert_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+  return launch_expert_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+}
+
+// Box height of a K-major B operand for an n-column row-ragged product: each CTA
+// of a pair tile stages half of the BN rows.
+int ns_b_box(int n, int batch) {
+  const int bn = n % 256 == 0 ? 256 : 128;
+  return use_pair(bn, kRowsRagged, batch, 0) ? bn / 2 : bn;
 }
 }  // namespace
 
@@ -1249,7 +1328,7 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
     p.n_tiles = g / bn_g;
     if (!tall) {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns gram a"))) return rc;
-      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, bn_g, "ns gram b"))) return rc;
+      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, ns_b_box(g, batch), "ns gram b"))) return rc;
       p.tile_expert = S.tile_r;
       p.pad_offsets = S.pad_r;
       p.k_blocks = cols / 64;
@@ -1264,14 +1343,14 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       p.m_valid = g;
       p.out_group_stride = static_cast<long long>(g) * g;
       rc = bn_g == 256
-               ? launch_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
-               : launch_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
+               ? launch_expert_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
+               : launch_expert_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
       if (rc) return rc;
     }
     // 2. P = c * A.A + b * A (A symmetric, so A.A = A.A^T)
     p = blank_params();
     if ((rc = make_tmap(&ta, S.gram, g, G, g, 64, 128, "ns poly a"))) return rc;
-    if ((rc = make_tmap(&tb, S.gram, g, G, g, 64, bn_g, "ns poly b"))) return rc;
+    if ((rc = make_tmap(&tb, S.gram, g, G, g, 64, ns_b_box(g, batch), "ns poly b"))) return rc;
     p.tile_expert = S.tile_g;
     p.pad_offsets = S.pad_g;
     p.num_groups = batch;
@@ -1315,7 +1394,7 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       if ((rc = ns_rows_product<true>(ta, tb, cols, p, st, "ns update"))) return rc;
     } else {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns update a"))) return rc;
-      if ((rc = make_tmap(&tb, S.poly, g, G, g, 64, bn_x, "ns update b"))) return rc;
+      if ((rc = make_tmap(&tb, S.poly, g, G, g, 64, ns_b_box(cols, batch), "ns update b"))) return rc;
       p.k_blocks = cols / 64;
       p.b_group_rows = g;
       if ((rc = ns_rows_product<false>(ta, tb, cols, p, st, "ns update"))) return rc;

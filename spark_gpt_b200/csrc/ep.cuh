@@ -117,3 +117,192 @@ __global__ void zero_skipped_slots_kernel(const int* __restrict__ inv_pad, long 
 }
 
 }  // namespace b200moe
+
+namespace b200moe {
+
+// ---------------------------------------------------------------------------
+// Peer-memory transport of the expert-parallel layer.  Every rank holds, in
+// memory mapped by all ranks of the group (NVLink / NVSwitch peer access):
+//   recv rows  (P*T_cap, H) bf16  rows other ranks send to this rank's experts
+//   recv meta  (P*T_cap, k) u32   their slot words
+//   back rows  (P*T_cap, H) bf16  partial rows the owners return to this rank
+//   back dw    (P*T_cap, k) f32   routing-weight gradients returned with them
+//   flags      (P) u64            barrier words, one per peer
+// C[s][d] = rows rank s sends to rank d (unpadded), gathered on every rank.
+// Layouts: at owner d, source s's rows start at recv_base[s] = sum_{s'<s}
+// C[s'][d]; at source s, the rows returned by owner d start at my_back_base[d]
+// = sum_{d'<d} C[s][d'] (rank-major, the source's send order).
+// ---------------------------------------------------------------------------
+// plan (ints): [0] n_recv | [1, 1+P) base_send[d] = sum_{s<me} C[s][d] |
+// [1+P, 2+2P) recv_base[s], s = 0..P | [2+2P, 2+3P) back_base[s] = sum_{d<me} C[s][d] |
+// [2+3P, 2+4P) my_back_base[d]
+constexpr int ep_plan_ints(int P) { return 2 + 4 * P; }
+
+__global__ void ep_p2p_plan_kernel(const int* __restrict__ counts, int ld, int me, int P,
+                                   int* __restrict__ plan) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  auto C = [&](int s, int d) { return counts[s * ld + d]; };
+  int n = 0;
+  for (int s = 0; s < P; ++s) {
+    plan[1 + P + s] = n;
+    n += C(s, me);
+  }
+  plan[1 + 2 * P] = n;
+  plan[0] = n;
+  for (int d = 0; d < P; ++d) {
+    int b = 0;
+    for (int s = 0; s < me; ++s) b += C(s, d);
+    plan[1 + d] = b;
+  }
+  for (int s = 0; s < P; ++s) {
+    int b = 0;
+    for (int d = 0; d < me; ++d) b += C(s, d);
+    plan[2 + 2 * P + s] = b;
+  }
+  int b = 0;
+  for (int d = 0; d < P; ++d) {
+    plan[2 + 3 * P + d] = b;
+    b += C(me, d);
+  }
+}
+
+// Source side: token t's row goes to every rank r it selected (dest row
+// inv_send[t*P+r] of the padded send layout -> row base_send[r] + (that row -
+// pad_offsets[r]) of rank r's recv rows), stored straight into the peer's
+// memory; with `sel`, its k slot words go to the peer's recv meta.
+template <int VPL>
+__global__ void ep_p2p_send_kernel(const __nv_bfloat16* __restrict__ src,
+                                   const int* __restrict__ inv_send,
+                                   const int* __restrict__ pad_offsets,
+                                   const int* __restrict__ plan,
+                                   __nv_bfloat16* const* __restrict__ peer_rows, long long T,
+                                   int H, int P, const long long* __restrict__ sel,
+                                   const unsigned short* __restrict__ w, int k, int E_loc,
+                                   unsigned* const* __restrict__ peer_meta) {
+  __shared__ int base_s[kEpMaxRanks], pad_s[kEpMaxRanks];
+  for (int r = threadIdx.x; r < P; r += blockDim.x) {
+    base_s[r] = plan[1 + r];
+    pad_s[r] = pad_offsets[r];
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       t < T; t += warps) {
+    const int pl = lane < P ? inv_send[t * P + lane] : -1;
+    const uint4* x = reinterpret_cast<const uint4*>(src + t * H);
+    uint4 v[VPL > 0 ? VPL : 1];
+    if (VPL > 0) {
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) v[j] = __ldg(x + lane + 32 * j);
+    }
+    long long e = -1;
+    unsigned short wb = 0;
+    if (sel != nullptr && lane < k) {
+      e = sel[t * k + lane];
+      wb = w[t * k + lane];
+    }
+    for (int r = 0; r < P; ++r) {
+      const int p = __shfl_sync(0xffffffffu, pl, r);
+      if (p < 0) continue;
+      const long long row = base_s[r] + (p - pad_s[r]);
+      uint4* dst = reinterpret_cast<uint4*>(peer_rows[r] + row * H);
+      if (VPL > 0) {
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) dst[lane + 32 * j] = v[j];
+      } else {
+        for (int i = lane; i < nvec; i += 32) dst[i] = __ldg(x + i);
+      }
+      if (sel != nullptr && lane < k) {
+        const long long lo = static_cast<long long>(r) * E_loc;
+        const unsigned word = (e >= lo && e < lo + E_loc)
+                                  ? ((static_cast<unsigned>(wb) << 16) | static_cast<unsigned>(e - lo))
+                                  : kEpNoExpert;
+        peer_meta[r][row * k + lane] = word;
+      }
+    }
+  }
+}
+
+// Owner side: received row i (< n_recv) came from source s (recv_base[s] <= i <
+// recv_base[s+1]); its result row goes back to row back_base[s] + (i -
+// recv_base[s]) of s's back rows, and its k routing-weight gradients (if given)
+// to the same row of s's back dw.
+template <int VPL>
+__global__ void ep_p2p_return_kernel(const __nv_bfloat16* __restrict__ rows,
+                                     const float* __restrict__ dw, const int* __restrict__ plan,
+                                     __nv_bfloat16* const* __restrict__ peer_rows,
+                                     float* const* __restrict__ peer_dw, int H, int k, int P) {
+  __shared__ int rb_s[kEpMaxRanks + 1], bb_s[kEpMaxRanks];
+  for (int r = threadIdx.x; r <= P; r += blockDim.x) {
+    rb_s[r] = plan[1 + P + r];
+    if (r < P) bb_s[r] = plan[2 + 2 * P + r];
+  }
+  __syncthreads();
+  const long long n = plan[0];
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       i < n; i += warps) {
+    int s = 0;
+    while (s + 1 < P && rb_s[s + 1] <= i) ++s;
+    const long long row = bb_s[s] + (i - rb_s[s]);
+    const uint4* x = reinterpret_cast<const uint4*>(rows + i * H);
+    uint4* dst = reinterpret_cast<uint4*>(peer_rows[s] + row * H);
+    if (VPL > 0) {
+      uint4 v[VPL > 0 ? VPL : 1];
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) v[j] = __ldg(x + lane + 32 * j);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) dst[lane + 32 * j] = v[j];
+    } else {
+      for (int j = lane; j < nvec; j += 32) dst[j] = __ldg(x + j);
+    }
+    if (dw != nullptr && lane < k) peer_dw[s][row * k + lane] = dw[i * k + lane];
+  }
+}
+
+// inv_back[t*P+r]: row of the source's back rows holding owner r's result for
+// token t (or -1): the padded send row minus its block start plus my_back_base[r].
+__global__ void ep_p2p_back_inv_kernel(const int* __restrict__ inv_send,
+                                       const int* __restrict__ pad_offsets,
+                                       const int* __restrict__ plan, long long T, int P,
+                                       int* __restrict__ inv_back) {
+  const long long n = T * P;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i % P);
+    const int p = inv_send[i];
+    inv_back[i] = p >= 0 ? p - pad_offsets[r] + plan[2 + 3 * P + r] : -1;
+  }
+}
+
+// Group barrier over peer memory: thread j writes `epoch` into peer j's flag
+// word for this rank (release, system scope: the rows this stream stored into
+// peers before are visible first), then waits until every peer has written
+// `epoch` into this rank's flags (acquire).  The wait is bounded: after the
+// limit it raises kFaultWaitTimeout and returns.
+__global__ void ep_barrier_kernel(unsigned long long* const* __restrict__ peer_flags,
+                                  unsigned long long* __restrict__ my_flags, int me, int P,
+                                  unsigned long long epoch) {
+  const int j = threadIdx.x;
+  if (j >= P) return;
+  __threadfence_system();
+  unsigned long long* dst = peer_flags[j] + me;
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(epoch) : "memory");
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(my_flags + j) : "memory");
+    if (v >= epoch) break;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      raise_fault(kFaultWaitTimeout);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
+}  // namespace b200moe

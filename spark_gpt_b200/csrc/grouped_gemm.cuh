@@ -196,6 +196,24 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
   }
 }
 
+// SwiGLU-backward epilogue: pull this lane's row of g and u for the tile's
+// column half into L2 before the accumulator is ready, so the epilogue's loads
+// of them (one chunk ahead) hit L2 instead of waiting on DRAM.
+template <int BN>
+__device__ __forceinline__ void prefetch_gu_row(const GemmParams& p, const TileInfo& T,
+                                                int row_in, int half) {
+  const long long row = static_cast<long long>(T.m) * 128 + row_in;
+  if (row >= p.m_valid) return;
+  const char* gu = reinterpret_cast<const char*>(static_cast<const __nv_bfloat16*>(p.aux) +
+                                                 row * p.ld_aux + T.n * BN + half * (BN / 2));
+  const long long up = static_cast<long long>(p.inter) * 2;
+#pragma unroll
+  for (int off = 0; off < BN; off += 128) {  // BN/2 columns = BN bytes, 128-byte lines
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(gu + off));
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(gu + up + off));
+  }
+}
+
 // Epilogue of a weight-gradient tile whose expert received no rows: zeros
 // (or nothing when accumulating).  Warps split the columns by `half`.
 template <int EPI, int BN>
@@ -840,6 +858,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
+      if (EPI == kEpiSwigluBwd) prefetch_gu_row<BN>(p, T, row_in, half);
       // every lane waits; the warp leaves together if any lane gave up (the TMEM
       // loads below are warp-collective)
       if (!__all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag))) break;

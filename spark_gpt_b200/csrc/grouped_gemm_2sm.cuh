@@ -392,6 +392,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
+      if (EPI == kEpiSwigluBwd && half_ok) prefetch_gu_row<BN>(p, T, row_in, half);
       B200_PROF(const long long w0 = clock64();)
       const bool got_acc = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag));
       B200_PROF(const long long w1 = clock64(); ew += w1 - w0;)

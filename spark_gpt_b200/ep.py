@@ -44,6 +44,7 @@ this rank's shard: gate_up_proj (E/P, 2I, H), down_proj (E/P, H, I).
 
 from __future__ import annotations
 
+import dataclasses
 from contextlib import nullcontext
 from types import SimpleNamespace
 
@@ -269,6 +270,152 @@ class _EPMoEFn(torch.autograd.Function):
         return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None, None)
 
 
+class PeerTransport:
+    """Peer-memory buffers of one process group for rows of width H with k slot
+    words, mapped by every rank (torch symmetric memory over NVLink/NVSwitch):
+    recv rows/meta (rows sent to this rank's experts), back rows/dw (results
+    returned to this rank) and the barrier flags.  Capacity T_cap tokens per
+    rank; grown collectively (every rank sees the same gathered token counts).
+    One transport serves every layer of the same (group, H, k): the phases of
+    a step are separated by barriers and each phase's data is consumed before
+    the next phase writes."""
+
+    _cache: dict = {}
+
+    @classmethod
+    def get(cls, group, H, k, device):
+        key = (id(group) if group is not None else None, H, k, str(device))
+        if key not in cls._cache:
+            cls._cache[key] = cls(group, H, k, device)
+        return cls._cache[key]
+
+    def __init__(self, group, H, k, device):
+        self.group, self.H, self.k, self.device = group, H, k, torch.device(device)
+        self.P = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        self.cap = 0
+        self.epoch = 0
+        self._buf = None
+
+    def ensure(self, tokens: int):
+        if tokens <= self.cap:
+            return
+        import torch.distributed._symmetric_memory as symm_mem
+        cap = max(1024, -(-tokens // 1024) * 1024)
+        rows = self.P * cap
+        H, k = self.H, self.k
+        sizes = [("recv_rows", rows * H * 2), ("recv_meta", rows * k * 4),
+                 ("back_rows", rows * H * 2), ("back_dw", rows * k * 4), ("flags", 8 * 32)]
+        offs, total = {}, 0
+        for name, nbytes in sizes:
+            offs[name] = total
+            total += -(-nbytes // 256) * 256
+        if self._buf is not None:
+            torch.cuda.synchronize(self.device)  # nothing in flight uses the old buffers
+        self._buf = None
+        buf = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
+        buf.zero_()
+        handle = symm_mem.rendezvous(buf, self.group)
+        ptrs = list(handle.buffer_ptrs)
+
+        def view(name, dtype, shape):
+            nbytes = sizes_d[name]
+            return buf[offs[name]: offs[name] + nbytes].view(dtype).view(*shape)
+
+        sizes_d = dict(sizes)
+        self.recv_rows = view("recv_rows", torch.bfloat16, (rows, H))
+        self.recv_meta = view("recv_meta", torch.int32, (rows, k))
+        self.back_rows = view("back_rows", torch.bfloat16, (rows, H))
+        self.back_dw = view("back_dw", torch.float32, (rows, k))
+        self.flags = view("flags", torch.int64, (32,))
+        table = lambda name: torch.tensor([q + offs[name] for q in ptrs], dtype=torch.int64,
+                                          device=self.device)
+        self.peer_recv_rows = table("recv_rows")
+        self.peer_recv_meta = table("recv_meta")
+        self.peer_back_rows = table("back_rows")
+        self.peer_back_dw = table("back_dw")
+        self.peer_flags = table("flags")
+        self._buf, self._handle = buf, handle
+        self.cap = cap
+        self.epoch = 0
+        torch.cuda.current_stream(self.device).synchronize()
+        dist.barrier(group=self.group)  # every rank's flags are zero before the first barrier
+
+    def barrier(self):
+        self.epoch += 1
+        ops.ep_barrier(self.peer_flags, self.flags, self.me, self.P, self.epoch)
+
+
+class _EPMoEP2PFn(torch.autograd.Function):
+    """The expert-parallel layer with its exchanges as peer-memory stores:
+    one kernel gathers each token's row and stores it into the owners' receive
+    buffers (with its slot words), one kernel stores the owners' result rows
+    into the sources' buffers, and bounded barriers over flag words separate the
+    phases.  One all-gather of the per-rank counts and one host read per step."""
+
+    @staticmethod
+    def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, transport):
+        P, me = transport.P, transport.me
+        E_loc = w_gu.shape[0]
+        T, H = x.shape
+        B = CudaExpertOps
+        xb = _as_bf16(x)
+        logits_buf, wr, sel, rw = B.router(xb, w_router, num_experts, top_k, norm)
+        dest, slots = ops.ep_route(sel, E_loc, P)
+        send = ops.dispatch(dest, P, partial=True)
+        counts = torch.cat([send.counts, slots, torch.full((1,), T, device=xb.device,
+                                                          dtype=torch.int32)])
+        gathered = torch.empty(P, 2 * P + 1, device=xb.device, dtype=torch.int32)
+        dist.all_gather_into_tensor(gathered, counts, group=group)
+        host = gathered.cpu()  # the one host read of the step
+        transport.ensure(int(host[:, 2 * P].max()))
+        n_recv = int(host[:, me].sum())
+        recv_slots = int(host[:, P + me].sum())
+        n_back = int(host[me, :P].sum())
+        plan = ops.ep_p2p_plan(gathered, me, P)
+        ops.ep_p2p_send(xb, send, plan, transport.peer_recv_rows, sel, rw, E_loc,
+                        transport.peer_recv_meta)
+        transport.barrier()
+        sel_loc, w_loc = B.unpack(transport.recv_meta[:n_recv])
+        wgu_b, wd_b = B.cast(w_gu), B.cast(w_d)
+        part, ectx = B.experts_fwd(transport.recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
+                                   recv_slots)
+        ops.ep_p2p_return(part, plan, transport.peer_back_rows, P)
+        transport.barrier()
+        back = dataclasses.replace(send, inv_pad=ops.ep_p2p_back_inv(send, plan))
+        out = ops.gather_rows_bwd(transport.back_rows[:n_back], back)
+        ctx.save_for_backward(xb, logits_buf, wr, sel)
+        ctx.meta = (send, back, plan, ectx, n_recv, n_back, transport, top_k, norm, num_experts,
+                    E_loc, H, w_gu.shape[1] // 2, x.dtype)
+        ctx.mark_non_differentiable(sel)
+        E = num_experts
+        logits = logits_buf if logits_buf.shape[1] == E else logits_buf[:, :E]
+        return out.to(x.dtype), logits, sel
+
+    @staticmethod
+    def backward(ctx, d_out, d_logits, _d_sel):
+        xb, logits_buf, wr, sel = ctx.saved_tensors
+        (send, back, plan, ectx, n_recv, n_back, transport, top_k, norm, num_experts, E_loc, H,
+         I, xdtype) = ctx.meta
+        B = CudaExpertOps
+        P = transport.P
+        if d_out is None:
+            d_out = torch.zeros(xb.shape, device=xb.device, dtype=xb.dtype)
+        ops.ep_p2p_send(_as_bf16(d_out), send, plan, transport.peer_recv_rows)
+        transport.barrier()
+        dx_rows, dw_rows, state = B.experts_dgrad(ectx, transport.recv_rows[:n_recv], top_k,
+                                                  xb.device)
+        ops.ep_p2p_return(dx_rows, plan, transport.peer_back_rows, P, dw_rows,
+                          transport.peer_back_dw)
+        g_gu, g_d = B.experts_wgrad(state, None, None, E_loc, H, I, xb.device)
+        transport.barrier()
+        d_rw = ops.ep_weight_grad(transport.back_dw[:n_back], back, sel, E_loc)
+        dx_router, g_router = B.router_bwd(xb, wr, logits_buf, sel, d_rw, d_logits, num_experts,
+                                           top_k, norm)
+        dx = ops.gather_rows_bwd(transport.back_rows[:n_back], back, addend=dx_router)
+        return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None)
+
+
 class ExpertParallelMoE(nn.Module):
     """SparseMoE with experts sharded over `group`.
 
@@ -277,8 +424,14 @@ class ExpertParallelMoE(nn.Module):
     data-parallel parameter); ``experts.gate_up_proj`` / ``down_proj`` hold
     this rank's E/P experts."""
 
-    def __init__(self, config, group=None, backend=CudaExpertOps, chunks=1, comm_sms=0):
+    def __init__(self, config, group=None, backend=CudaExpertOps, chunks=1, comm_sms=0,
+                 transport="nccl"):
         super().__init__()
+        if transport not in ("nccl", "p2p"):
+            raise ValueError(f"transport must be 'nccl' or 'p2p', got {transport!r}")
+        if transport == "p2p" and backend is not CudaExpertOps:
+            raise ValueError("the peer-memory transport runs the device kernels only")
+        self.transport = transport
         self.chunks = chunks
         self.comm_sms = comm_sms
         self.group = group
@@ -347,8 +500,14 @@ class ExpertParallelMoE(nn.Module):
             _require_cuda(hidden_states)
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
-        out, logits, sel = _EPMoEFn.apply(
-            x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
-            self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group,
-            self.backend, self.chunks, self.comm_sms)
+        if self.transport == "p2p":
+            tr = PeerTransport.get(self.group, shape[-1], self.gate.top_k, x.device)
+            out, logits, sel = _EPMoEP2PFn.apply(
+                x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
+                self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group, tr)
+        else:
+            out, logits, sel = _EPMoEFn.apply(
+                x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
+                self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group,
+                self.backend, self.chunks, self.comm_sms)
         return out.view(shape), logits.view(*shape[:-1], -1), sel.view(*shape[:-1], -1)

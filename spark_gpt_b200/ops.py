@@ -422,6 +422,47 @@ def ep_unpack(meta: torch.Tensor):
     return sel, w
 
 
+def ep_p2p_plan(counts: torch.Tensor, me: int, ranks: int) -> torch.Tensor:
+    """counts (P, ld) int32 gathered on every rank -> this rank's plan (2 + 4P ints)."""
+    plan = torch.empty(2 + 4 * ranks, device=counts.device, dtype=torch.int32)
+    _launch("ep_p2p_plan", 1, "b200moe_ep_p2p_plan", _p(counts), counts.stride(0), me, ranks,
+            _p(plan), _s(counts))
+    return plan
+
+
+def ep_p2p_send(src, send: Dispatch, plan, peer_rows, selected=None, weights=None,
+                experts_per_rank: int = 1, peer_meta=None):
+    """Store each token's row (and slot words) into the owners' receive buffers."""
+    _check(src, BF16, "ep_p2p_send src")
+    T, H = src.shape
+    k = selected.shape[1] if selected is not None else 0
+    _launch("ep_p2p_send", 1, "b200moe_ep_p2p_send", _p(src), _p(send.inv_pad),
+            _p(send.pad_offsets), _p(plan), _p(peer_rows), T, H, send.num_experts,
+            _p(selected), _p(weights), k, experts_per_rank, _p(peer_meta), _s(src))
+
+
+def ep_p2p_return(rows, plan, peer_rows, ranks: int, dw_rows=None, peer_dw=None):
+    """Store the owner's result rows (and routing-weight gradients) into the sources' back buffers."""
+    _check(rows, BF16, "ep_p2p_return rows")
+    n, H = rows.shape
+    k = dw_rows.shape[1] if dw_rows is not None else 0
+    _launch("ep_p2p_return", 1, "b200moe_ep_p2p_return", _p(rows), _p(dw_rows), _p(plan),
+            _p(peer_rows), _p(peer_dw), n, H, k, ranks, _s(rows))
+
+
+def ep_p2p_back_inv(send: Dispatch, plan) -> torch.Tensor:
+    T, P = send.num_tokens, send.num_experts
+    inv = torch.empty(max(T * P, 1), device=plan.device, dtype=torch.int32)
+    _launch("ep_p2p_back_inv", 1, "b200moe_ep_p2p_back_inv", _p(send.inv_pad),
+            _p(send.pad_offsets), _p(plan), T, P, _p(inv), _s(plan))
+    return inv[: T * P]
+
+
+def ep_barrier(peer_flags, my_flags, me: int, ranks: int, epoch: int):
+    _launch("ep_barrier", 1, "b200moe_ep_barrier", _p(peer_flags), _p(my_flags), me, ranks,
+            ctypes.c_ulonglong(epoch), _s(my_flags))
+
+
 def ep_weight_grad(dw_rows, send: Dispatch, selected, experts_per_rank: int,
                    out=None) -> torch.Tensor:
     T, k = selected.shape

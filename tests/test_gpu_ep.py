@@ -23,9 +23,11 @@ from tests.helpers import assert_bf16_close
 pytestmark = pytest.mark.gpu
 
 T, H, E, K, I = 2048, 1024, 16, 4, 256
-# one send plan per step, exchanges in sequence; and 3 token chunks with the
-# exchanges overlapped and 16 SMs left to NCCL
-VARIANTS = {"plain": dict(chunks=1, comm_sms=0), "overlap": dict(chunks=3, comm_sms=16)}
+# NCCL all-to-all: one send plan per step, exchanges in sequence; 3 token
+# chunks with the exchanges overlapped and 16 SMs left to NCCL; and the
+# peer-memory transport (rows stored straight into the other rank's buffers)
+VARIANTS = {"plain": dict(chunks=1, comm_sms=0), "overlap": dict(chunks=3, comm_sms=16),
+            "p2p": dict(transport="p2p")}
 
 
 def _cfg():
@@ -114,5 +116,8 @@ def test_expert_parallel_two_gpus_matches_single_gpu_layer():
             assert_bf16_close(dr_ep, dr_ref, f"{name} dW_router")
             assert_bf16_close(r["ep_gu"][name], r["ref_gu"], f"{name} dW_gate_up")
             assert_bf16_close(r["ep_d"][name], r["ref_d"], f"{name} dW_down")
-        # the chunked, overlapped schedule computes the same values
+        # the chunked, overlapped schedule and the peer-memory transport compute
+        # the same values as the plain NCCL schedule
         assert torch.equal(r["outs"]["plain"][0], r["outs"]["overlap"][0])
+        assert torch.equal(r["outs"]["plain"][0], r["outs"]["p2p"][0])
+        assert torch.equal(r["outs"]["plain"][2], r["outs"]["p2p"][2])

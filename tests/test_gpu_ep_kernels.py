@@ -10,11 +10,16 @@
    rank's output and input gradient match the single-GPU layer on its tokens,
    and every expert shard's weight gradients match the single-GPU layer's
    summed over all ranks' tokens, within the layer's bf16 tolerance.
+4. The same for the peer-memory transport (send / return kernels storing into
+   the other ranks' buffers), and its barrier: passing, and giving up after
+   its bounded wait with a fault bit instead of hanging.
 """
+
+import dataclasses
+from types import SimpleNamespace
 
 import pytest
 import torch
-from types import SimpleNamespace
 
 from tests.helpers import assert_bf16_close
 
@@ -232,3 +237,123 @@ def test_emulated_expert_parallel_matches_single_gpu_layer(ops, T, H, E, k, I, P
     assert_bf16_close(g_d, ref.experts.down_proj.grad, "dW_down")
     torch.cuda.synchronize()
     assert _lib.read_fault() == 0
+
+
+def _emulated_p2p(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
+    """The peer-memory transport with P ranks on one GPU: each rank's receive
+    and back buffers are ordinary device tensors and the 'peer' pointer tables
+    point at the other ranks' tensors, so the send / return kernels store
+    across ranks exactly as over NVLink (no barrier needed: one stream)."""
+    from spark_gpt_b200.ep import CudaExpertOps as B
+    E = w_gu.shape[0]
+    E_loc = E // P
+    I, H = w_d.shape[2], w_d.shape[1]
+    T = x_list[0].shape[0]
+    cap = P * T
+    bufs = [SimpleNamespace(recv_rows=torch.zeros(cap, H, device=DEV, dtype=torch.bfloat16),
+                            recv_meta=torch.zeros(cap, k, device=DEV, dtype=torch.int32),
+                            back_rows=torch.zeros(cap, H, device=DEV, dtype=torch.bfloat16),
+                            back_dw=torch.zeros(cap, k, device=DEV, dtype=torch.float32))
+            for _ in range(P)]
+    table = lambda name: torch.tensor([getattr(b, name).data_ptr() for b in bufs],
+                                      dtype=torch.int64, device=DEV)
+    peers = {n: table(n) for n in ("recv_rows", "recv_meta", "back_rows", "back_dw")}
+    st = []
+    for r in range(P):
+        logits_buf, wr, sel, rw = B.router(x_list[r], w_r, E, k, True)
+        dest, slots = ops.ep_route(sel, E_loc, P)
+        send = ops.dispatch(dest, P, partial=True)
+        st.append(SimpleNamespace(logits_buf=logits_buf, wr=wr, sel=sel, rw=rw, send=send,
+                                  counts=torch.cat([send.counts, slots])))
+    gathered = torch.stack([s.counts for s in st])            # (P, 2P)
+    host = gathered.cpu()
+    for r in range(P):
+        st[r].plan = ops.ep_p2p_plan(gathered, r, P)
+        ops.ep_p2p_send(x_list[r], st[r].send, st[r].plan, peers["recv_rows"], st[r].sel,
+                        st[r].rw, E_loc, peers["recv_meta"])
+    own = []
+    for o in range(P):
+        n_recv, slots_o = int(host[:, o].sum()), int(host[:, P + o].sum())
+        wgu_b = ops.cast_bf16(w_gu[o * E_loc:(o + 1) * E_loc].contiguous())
+        wd_b = ops.cast_bf16(w_d[o * E_loc:(o + 1) * E_loc].contiguous())
+        sel_loc, w_loc = B.unpack(bufs[o].recv_meta[:n_recv])
+        part, ectx = B.experts_fwd(bufs[o].recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
+                                   slots_o)
+        ops.ep_p2p_return(part, st[o].plan, peers["back_rows"], P)
+        own.append(SimpleNamespace(ectx=ectx, n_recv=n_recv))
+    outs = []
+    for r in range(P):
+        n_back = int(host[r, :P].sum())
+        st[r].back = dataclasses.replace(st[r].send, inv_pad=ops.ep_p2p_back_inv(st[r].send,
+                                                                                 st[r].plan))
+        st[r].n_back = n_back
+        outs.append(ops.gather_rows_bwd(bufs[r].back_rows[:n_back], st[r].back))
+    for r in range(P):
+        ops.ep_p2p_send(d_out_list[r], st[r].send, st[r].plan, peers["recv_rows"])
+    ggu, gd = [], []
+    for o in range(P):
+        d_recv = bufs[o].recv_rows[:own[o].n_recv]
+        dx_rows, dw_rows, state = B.experts_dgrad(own[o].ectx, d_recv, k, d_recv.device)
+        ops.ep_p2p_return(dx_rows, st[o].plan, peers["back_rows"], P, dw_rows, peers["back_dw"])
+        c, e = B.experts_wgrad(state, None, None, E_loc, H, I, d_recv.device)
+        ggu.append(c)
+        gd.append(e)
+    dxs, g_routers = [], []
+    for r in range(P):
+        s = st[r]
+        d_rw = ops.ep_weight_grad(bufs[r].back_dw[:s.n_back], s.back, s.sel, E_loc)
+        dx_router, g_router = B.router_bwd(x_list[r], s.wr, s.logits_buf, s.sel, d_rw, None, E,
+                                           k, True)
+        dxs.append(ops.gather_rows_bwd(bufs[r].back_rows[:s.n_back], s.back, addend=dx_router))
+        g_routers.append(g_router)
+    return outs, [s.sel for s in st], dxs, g_routers, torch.cat(ggu), torch.cat(gd)
+
+
+@pytest.mark.parametrize("T,H,E,k,I,P", [(2048, 1024, 32, 8, 256, 4), (1500, 2048, 16, 4, 128, 2),
+                                         (1024, 512, 64, 8, 192, 8)])
+def test_emulated_peer_memory_transport_matches_single_gpu_layer(ops, T, H, E, k, I, P):
+    from spark_gpt_b200 import SparseMoE, _lib
+    g = torch.Generator().manual_seed(E * 3 + P)
+    w_r = (torch.randn(E, H, generator=g) * 0.05).to(DEV)
+    w_gu = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(DEV)
+    w_d = (torch.randn(E, H, I, generator=g) * 0.02).to(DEV)
+    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV) for _ in range(P)]
+    ds = [(torch.randn(T, H, generator=g) * 1e-2).to(torch.bfloat16).to(DEV) for _ in range(P)]
+    outs, sels, dxs, g_routers, g_gu, g_d = _emulated_p2p(ops, xs, ds, w_r, w_gu, w_d, k, P)
+    cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=k,
+                          moe_intermediate_size=I, norm_topk_prob=True)
+    ref = SparseMoE(cfg).to(DEV)
+    with torch.no_grad():
+        ref.gate.weight.copy_(w_r)
+        ref.experts.gate_up_proj.copy_(w_gu)
+        ref.experts.down_proj.copy_(w_d)
+    for r in range(P):
+        xin = xs[r].clone().requires_grad_(True)
+        ref.gate.weight.grad = None
+        out, _, sel = ref(xin)
+        out.backward(ds[r])
+        assert torch.equal(sels[r], sel)
+        assert_bf16_close(outs[r], out, f"p2p out rank {r}")
+        assert_bf16_close(dxs[r], xin.grad, f"p2p dx rank {r}")
+        assert_bf16_close(g_routers[r], ref.gate.weight.grad, f"p2p dW_router rank {r}")
+    assert_bf16_close(g_gu, ref.experts.gate_up_proj.grad, "p2p dW_gate_up")
+    assert_bf16_close(g_d, ref.experts.down_proj.grad, "p2p dW_down")
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0
+
+
+def test_peer_barrier_passes_and_times_out_without_a_fault(ops):
+    """One rank: the barrier passes at once.  Two ranks emulated on one GPU
+    with only rank 0 arriving (a flag nothing sets): the bounded wait gives up
+    after its limit, records fault bit 1 and returns; the context stays usable."""
+    from spark_gpt_b200 import _lib
+    flags = [torch.zeros(32, device=DEV, dtype=torch.int64) for _ in range(2)]
+    table = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=DEV)
+    ops.ep_barrier(table[:1], flags[0], 0, 1, 1)
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0 and int(flags[0][0]) == 1
+    ops.ep_barrier(table, flags[0], 0, 2, 2)   # rank 1 never arrives
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 1
+    assert int(flags[1][0]) == 2               # rank 0 still signalled its peer
+    assert torch.equal(torch.ones(4, device=DEV).cumsum(0).cpu(), torch.arange(1, 5).float())
