@@ -71,7 +71,7 @@ def parse_args():
                     help="skip the Muon optimizer-step measurement of the expert tensors")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallel: token chunks pipelined against the exchanges")
-    ap.add_argument("--transport", default="nccl", choices=["nccl", "p2p"],
+    ap.add_argument("--transport", default="p2p", choices=["nccl", "p2p"],
                     help="expert parallel: NCCL all-to-all or peer-memory stores")
     ap.add_argument("--comm-sms", type=int, default=16,
                     help="expert parallel: SMs the persistent kernels leave to NCCL while an "

@@ -331,6 +331,17 @@ int b200moe_ep_p2p_return(const void* rows, const float* dw_rows, const int* pla
                           void* const* peer_rows, float* const* peer_dw, long long rows_cap,
                           int H, int k, int ranks, void* stream);
 
+/* Owner side, reduction fused with the return: for received row i < plan[0],
+ * sum_s bf16(rows[inv_pad[i*k+s]] * weights[i,s]) (the combine; weights (n,k)
+ * bf16) or sum_s rows[inv_pad[i*k+s]] (weights NULL: the gather backward),
+ * over the slots with inv_pad >= 0, fp32 in slot order, rounded once, is
+ * stored into the back rows of the rank row i came from; dw_rows (n,k) fp32,
+ * if given, into its back dw.  H in {256, 512, 1024, 2048}. */
+int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const void* weights, int k,
+                                 const float* dw_rows, const int* plan, void* const* peer_rows,
+                                 float* const* peer_dw, long long rows_cap, int H, int ranks,
+                                 void* stream);
+
 /* inv_back (T*P) int32: the row of this rank's back rows that holds owner r's
  * result for token t, or -1 (for b200moe_gather_rows_bwd with k = P). */
 int b200moe_ep_p2p_back_inv(const int* inv_send, const int* send_pad_offsets, const int* plan,

@@ -60,6 +60,7 @@ PROTOTYPES = {
     "b200moe_ep_p2p_plan": (I, [P, I, I, I, P, P]),
     "b200moe_ep_p2p_send": (I, [P, P, P, P, P, L, I, I, P, P, I, I, P, P]),
     "b200moe_ep_p2p_return": (I, [P, P, P, P, P, L, I, I, I, P]),
+    "b200moe_ep_p2p_reduce_return": (I, [P, P, P, I, P, P, P, P, L, I, I, P]),
     "b200moe_ep_p2p_back_inv": (I, [P, P, P, L, I, P, P]),
     "b200moe_ep_barrier": (I, [P, P, I, I, c_ulonglong, P]),
     "b200moe_muon_momentum": (I, [P, P, P, L, c_double, I, P]),

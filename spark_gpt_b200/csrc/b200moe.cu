@@ -1186,6 +1186,31 @@ int b200moe_ep_p2p_return(const void* rows, const float* dw_rows, const int* pla
   return check_launch("ep_p2p_return");
 }
 
+int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const void* weights, int k,
+                                 const float* dw_rows, const int* plan, void* const* peer_rows,
+                                 float* const* peer_dw, long long rows_cap, int H, int ranks,
+                                 void* stream) {
+  REQUIRE(rows && inv_pad && plan && peer_rows, "ep_p2p_reduce_return: null pointer");
+  REQUIRE(dw_rows == nullptr || peer_dw, "ep_p2p_reduce_return: dw needs peer_dw");
+  REQUIRE(k >= 1 && k <= 32 && ranks >= 1 && ranks <= kEpMaxRanks && rows_cap >= 0,
+          "ep_p2p_reduce_return: bad k/ranks");
+  REQUIRE(H == 256 || H == 512 || H == 1024 || H == 2048,
+          "ep_p2p_reduce_return: H must be 256, 512, 1024 or 2048");
+  if (rows_cap == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* yp = static_cast<const __nv_bfloat16*>(rows);
+  auto* wp = static_cast<const __nv_bfloat16*>(weights);
+  auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
+  const int grid = grid_for(rows_cap, 8);
+  switch (H) {
+    case 256: ep_p2p_reduce_return_kernel<1><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 512: ep_p2p_reduce_return_kernel<2><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 1024: ep_p2p_reduce_return_kernel<4><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    default: ep_p2p_reduce_return_kernel<8><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+  }
+  return check_launch("ep_p2p_reduce_return");
+}
+
 int b200moe_ep_p2p_back_inv(const int* inv_send, const int* send_pad_offsets, const int* plan,
                             long long T, int ranks, int* inv_back, void* stream) {
   REQUIRE(inv_send && send_pad_offsets && plan && inv_back, "ep_p2p_back_inv: null pointer");
@@ -1251,21 +1276,31 @@ NsScratch ns_layout(void* base, int batch, int rows, int cols) {
   return s;
 }
 
+// Newton-Schulz products run as two-CTA pair tiles for Gram sides >= 768 (the
+// Qwen3-30B-A3B expert shapes: measured faster) and as single-CTA tiles below
+// (cfg2-sized 256..512 matrices: the pair tiles' longer pipeline fill per short
+// K loop made them slower).
+bool ns_pair(int g) { return g >= 768; }
+
 // One row-ragged product of the Newton-Schulz step: out = alpha * A.B + beta *
-// aux over `batch` groups (two-CTA pair tiles when the shape allows).
+// aux over `batch` groups.
 template <bool B_MN>
-int ns_rows_product(const CUtensorMap& ta, const CUtensorMap& tb, int n, GemmParams p,
+int ns_rows_product(const CUtensorMap& ta, const CUtensorMap& tb, int n, bool pair, GemmParams p,
                     cudaStream_t st, const char* what) {
-  if (n % 256 == 0)
-    return launch_expert_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
-  return launch_expert_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+  if (pair) {
+    if (n % 256 == 0)
+      return launch_expert_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+    return launch_expert_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+  }
+  if (n % 256 == 0) return launch_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+  return launch_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
 }
 
 // Box height of a K-major B operand for an n-column row-ragged product: each CTA
 // of a pair tile stages half of the BN rows.
-int ns_b_box(int n, int batch) {
+int ns_b_box(int n, int batch, bool pair) {
   const int bn = n % 256 == 0 ? 256 : 128;
-  return use_pair(bn, kRowsRagged, batch, 0) ? bn / 2 : bn;
+  return pair && use_pair(bn, kRowsRagged, batch, 0) ? bn / 2 : bn;
 }
 }  // namespace
 
@@ -1312,6 +1347,7 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
   const long long G = static_cast<long long>(batch) * g;     // stacked rows of the Gram stack
   const int bn_g = g % 256 == 0 ? 256 : 128;
   const int bn_x = cols % 256 == 0 ? 256 : 128;
+  const bool pair = ns_pair(g);
   __nv_bfloat16* cur = X0;
   for (int it = 0; it < steps; ++it) {
     const bool last = it + 1 == steps;
@@ -1328,13 +1364,13 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
     p.n_tiles = g / bn_g;
     if (!tall) {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns gram a"))) return rc;
-      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, ns_b_box(g, batch), "ns gram b"))) return rc;
+      if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, ns_b_box(g, batch, pair), "ns gram b"))) return rc;
       p.tile_expert = S.tile_r;
       p.pad_offsets = S.pad_r;
       p.k_blocks = cols / 64;
       p.b_group_rows = rows;
       p.m_valid = R;
-      if ((rc = ns_rows_product<false>(ta, tb, g, p, st, "ns gram"))) return rc;
+      if ((rc = ns_rows_product<false>(ta, tb, g, pair, p, st, "ns gram"))) return rc;
     } else {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 64, "ns gram a"))) return rc;
       if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, 64, "ns gram b"))) return rc;
@@ -1342,15 +1378,19 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       p.m_tiles = g / 128;
       p.m_valid = g;
       p.out_group_stride = static_cast<long long>(g) * g;
-      rc = bn_g == 256
-               ? launch_expert_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
-               : launch_expert_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
+      if (pair)
+        rc = bn_g == 256
+                 ? launch_expert_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
+                 : launch_expert_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
+      else
+        rc = bn_g == 256 ? launch_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
+                         : launch_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
       if (rc) return rc;
     }
     // 2. P = c * A.A + b * A (A symmetric, so A.A = A.A^T)
     p = blank_params();
     if ((rc = make_tmap(&ta, S.gram, g, G, g, 64, 128, "ns poly a"))) return rc;
-    if ((rc = make_tmap(&tb, S.gram, g, G, g, 64, ns_b_box(g, batch), "ns poly b"))) return rc;
+    if ((rc = make_tmap(&tb, S.gram, g, G, g, 64, ns_b_box(g, batch, pair), "ns poly b"))) return rc;
     p.tile_expert = S.tile_g;
     p.pad_offsets = S.pad_g;
     p.num_groups = batch;
@@ -1365,7 +1405,7 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
     p.ld_aux = g;
     p.alpha = c;
     p.beta = b;
-    if ((rc = ns_rows_product<false>(ta, tb, g, p, st, "ns poly"))) return rc;
+    if ((rc = ns_rows_product<false>(ta, tb, g, pair, p, st, "ns poly"))) return rc;
     // 3. X' = P.X + a*X (wide) or X.P + a*X (tall), in X's layout
     p = blank_params();
     p.tile_expert = S.tile_r;
@@ -1391,13 +1431,13 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, 64, "ns update b"))) return rc;
       p.k_blocks = rows / 64;
       p.b_group_rows = rows;
-      if ((rc = ns_rows_product<true>(ta, tb, cols, p, st, "ns update"))) return rc;
+      if ((rc = ns_rows_product<true>(ta, tb, cols, pair, p, st, "ns update"))) return rc;
     } else {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns update a"))) return rc;
-      if ((rc = make_tmap(&tb, S.poly, g, G, g, 64, ns_b_box(cols, batch), "ns update b"))) return rc;
+      if ((rc = make_tmap(&tb, S.poly, g, G, g, 64, ns_b_box(cols, batch, pair), "ns update b"))) return rc;
       p.k_blocks = cols / 64;
       p.b_group_rows = g;
-      if ((rc = ns_rows_product<false>(ta, tb, cols, p, st, "ns update"))) return rc;
+      if ((rc = ns_rows_product<false>(ta, tb, cols, pair, p, st, "ns update"))) return rc;
     }
     cur = nxt;
   }

@@ -306,3 +306,99 @@ __global__ void ep_barrier_kernel(unsigned long long* const* __restrict__ peer_f
 }
 
 }  // namespace b200moe
+
+namespace b200moe {
+
+// Owner side, fused reduction + return: for received row i < plan[0], the sum
+// over its slots s with a row (inv_pad[i*k+s] >= 0) of bf16(y[row] * w[i,s])
+// (weights given: the combine) or of y[row] (no weights: the gather
+// backward), accumulated in fp32 in slot order and rounded once, is stored
+// straight into row back_base[src] + (i - recv_base[src]) of the source's back
+// rows; with dw (rows, k) fp32 its k routing-weight gradients go to the same
+// row of the source's back dw.  Warp per received row; the rows of the valid
+// slots are loaded two at a time.
+template <int VPL>
+__global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
+                                            const int* __restrict__ inv_pad,
+                                            const __nv_bfloat16* __restrict__ weights, int k,
+                                            const float* __restrict__ dw,
+                                            const int* __restrict__ plan,
+                                            __nv_bfloat16* const* __restrict__ peer_rows,
+                                            float* const* __restrict__ peer_dw, int H, int P) {
+  static_assert(VPL > 0, "H in {256, 512, 1024, 2048}");
+  __shared__ int rb_s[kEpMaxRanks + 1], bb_s[kEpMaxRanks];
+  for (int r = threadIdx.x; r <= P; r += blockDim.x) {
+    rb_s[r] = plan[1 + P + r];
+    if (r < P) bb_s[r] = plan[2 + 2 * P + r];
+  }
+  __syncthreads();
+  const long long n = plan[0];
+  const int lane = threadIdx.x & 31;
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       i < n; i += warps) {
+    const int rl = lane < k ? inv_pad[i * k + lane] : -1;
+    float wl = 1.f;
+    if (weights != nullptr && lane < k) wl = __bfloat162float(weights[i * k + lane]);
+    unsigned valid = __ballot_sync(0xffffffffu, rl >= 0);
+    float acc[VPL][8];
+#pragma unroll
+    for (int j = 0; j < VPL; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[j][e] = 0.f;
+    auto add_row = [&](const uint4* q, float w) {
+      const __nv_bfloat162 w2 = __float2bfloat162_rn(w);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        uint4 v = q[j];
+        if (weights != nullptr) {
+          // bf16 x bf16 product rounded once to bf16, as the combine
+          __nv_bfloat162* v2 = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v2[e] = __hmul2(v2[e], w2);
+        }
+        acc[j][0] += bf16_lo(v.x); acc[j][1] += bf16_hi(v.x);
+        acc[j][2] += bf16_lo(v.y); acc[j][3] += bf16_hi(v.y);
+        acc[j][4] += bf16_lo(v.z); acc[j][5] += bf16_hi(v.z);
+        acc[j][6] += bf16_lo(v.w); acc[j][7] += bf16_hi(v.w);
+      }
+    };
+    while (valid) {
+      const int s0 = __ffs(valid) - 1;
+      valid &= valid - 1;
+      const int s1 = valid ? __ffs(valid) - 1 : -1;
+      if (s1 >= 0) valid &= valid - 1;
+      const long long r0 = __shfl_sync(0xffffffffu, rl, s0);
+      const float w0 = __shfl_sync(0xffffffffu, wl, s0);
+      const long long r1 = __shfl_sync(0xffffffffu, rl, s1 >= 0 ? s1 : s0);
+      const float w1 = __shfl_sync(0xffffffffu, wl, s1 >= 0 ? s1 : s0);
+      uint4 a[VPL], b[VPL];
+      const uint4* p0 = reinterpret_cast<const uint4*>(y + r0 * H);
+      const uint4* p1 = reinterpret_cast<const uint4*>(y + r1 * H);
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) a[j] = __ldg(p0 + lane + 32 * j);
+      if (s1 >= 0) {
+#pragma unroll
+        for (int j = 0; j < VPL; ++j) b[j] = __ldg(p1 + lane + 32 * j);
+      }
+      add_row(a, w0);
+      if (s1 >= 0) add_row(b, w1);
+    }
+    int src = 0;
+    while (src + 1 < P && rb_s[src + 1] <= i) ++src;
+    const long long row = bb_s[src] + (i - rb_s[src]);
+    uint4* dst = reinterpret_cast<uint4*>(peer_rows[src] + row * H);
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      uint4 o;
+      o.x = pack_bf16x2(acc[j][0], acc[j][1]);
+      o.y = pack_bf16x2(acc[j][2], acc[j][3]);
+      o.z = pack_bf16x2(acc[j][4], acc[j][5]);
+      o.w = pack_bf16x2(acc[j][6], acc[j][7]);
+      dst[lane + 32 * j] = o;
+    }
+    if (dw != nullptr && lane < k) peer_dw[src][row * k + lane] = dw[i * k + lane];
+  }
+}
+
+}  // namespace b200moe

@@ -95,8 +95,9 @@ class CudaExpertOps:
         return ops.ep_unpack(meta)
 
     @staticmethod
-    def experts_fwd(rows, sel_loc, w_loc, w_gu, w_d, slots):
-        """partial[i] = sum over row i's local slots of bf16(expert(rows[i]) * w)."""
+    def experts_fwd(rows, sel_loc, w_loc, w_gu, w_d, slots, combine=True):
+        """partial[i] = sum over row i's local slots of bf16(expert(rows[i]) * w);
+        combine=False returns the expert outputs y (padded rows) instead."""
         E = w_gu.shape[0]
         if rows.shape[0] == 0 or slots == 0:
             return rows.new_zeros(rows.shape), None
@@ -104,12 +105,14 @@ class CudaExpertOps:
         xs = ops.gather_rows(rows, d)
         gu, h = ops.gate_up_fwd(xs, w_gu, d)
         y = ops.down_fwd(h, w_d, d)
-        part = ops.combine(y, d, w_loc)
-        return part, (d, w_loc, xs, gu, h, y, w_gu, w_d)
+        ctx = (d, w_loc, xs, gu, h, y, w_gu, w_d)
+        return (ops.combine(y, d, w_loc) if combine else y), ctx
 
     @staticmethod
-    def experts_dgrad(ctx, d_rows, k, device):
-        """-> (dx rows, d_weights (rows, k) fp32, state for experts_wgrad)."""
+    def experts_dgrad(ctx, d_rows, k, device, reduce=True):
+        """-> (dx rows, d_weights (rows, k) fp32, state for experts_wgrad);
+        reduce=False returns the slot input-gradients dxs (padded rows) instead
+        of their per-row sums."""
         n, H = d_rows.shape
         if ctx is None:
             return d_rows.new_zeros(n, H), torch.zeros(n, k, device=device), None
@@ -117,7 +120,7 @@ class CudaExpertOps:
         dy, dw = ops.combine_bwd(_as_bf16(d_rows), y, d, w_loc)
         d_gu = ops.down_dgrad_swiglu(dy, w_d, gu, d)
         dxs = ops.gate_up_dgrad(d_gu, w_gu, d)
-        return ops.gather_rows_bwd(dxs, d), dw, (d, dy, h, d_gu, xs)
+        return (ops.gather_rows_bwd(dxs, d) if reduce else dxs), dw, (d, dy, h, d_gu, xs)
 
     @staticmethod
     def experts_wgrad(state, g_gu, g_d, E, H, I, device):
@@ -315,7 +318,8 @@ class PeerTransport:
         self._buf = None
         buf = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
         buf.zero_()
-        handle = symm_mem.rendezvous(buf, self.group)
+        handle = symm_mem.rendezvous(buf, self.group if self.group is not None
+                                     else dist.group.WORLD)
         ptrs = list(handle.buffer_ptrs)
 
         def view(name, dtype, shape):
@@ -378,9 +382,10 @@ class _EPMoEP2PFn(torch.autograd.Function):
         transport.barrier()
         sel_loc, w_loc = B.unpack(transport.recv_meta[:n_recv])
         wgu_b, wd_b = B.cast(w_gu), B.cast(w_d)
-        part, ectx = B.experts_fwd(transport.recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
-                                   recv_slots)
-        ops.ep_p2p_return(part, plan, transport.peer_back_rows, P)
+        y, ectx = B.experts_fwd(transport.recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
+                                recv_slots, combine=False)
+        if ectx is not None:  # combine of each received row, stored into its source
+            ops.ep_p2p_reduce_return(y, ectx[0], plan, transport.peer_back_rows, P, weights=w_loc)
         transport.barrier()
         back = dataclasses.replace(send, inv_pad=ops.ep_p2p_back_inv(send, plan))
         out = ops.gather_rows_bwd(transport.back_rows[:n_back], back)
@@ -403,10 +408,11 @@ class _EPMoEP2PFn(torch.autograd.Function):
             d_out = torch.zeros(xb.shape, device=xb.device, dtype=xb.dtype)
         ops.ep_p2p_send(_as_bf16(d_out), send, plan, transport.peer_recv_rows)
         transport.barrier()
-        dx_rows, dw_rows, state = B.experts_dgrad(ectx, transport.recv_rows[:n_recv], top_k,
-                                                  xb.device)
-        ops.ep_p2p_return(dx_rows, plan, transport.peer_back_rows, P, dw_rows,
-                          transport.peer_back_dw)
+        dxs, dw_rows, state = B.experts_dgrad(ectx, transport.recv_rows[:n_recv], top_k,
+                                              xb.device, reduce=False)
+        if ectx is not None:  # per-row sums of the slot gradients, stored into the sources
+            ops.ep_p2p_reduce_return(dxs, ectx[0], plan, transport.peer_back_rows, P,
+                                     dw_rows=dw_rows, peer_dw=transport.peer_back_dw)
         g_gu, g_d = B.experts_wgrad(state, None, None, E_loc, H, I, xb.device)
         transport.barrier()
         d_rw = ops.ep_weight_grad(transport.back_dw[:n_back], back, sel, E_loc)

@@ -450,6 +450,16 @@ def ep_p2p_return(rows, plan, peer_rows, ranks: int, dw_rows=None, peer_dw=None)
             _p(peer_rows), _p(peer_dw), n, H, k, ranks, _s(rows))
 
 
+def ep_p2p_reduce_return(rows, d: Dispatch, plan, peer_rows, ranks: int, weights=None,
+                         dw_rows=None, peer_dw=None):
+    """Owner side: each received row's sum over its local slots (weighted: the
+    combine; unweighted: the gather backward) stored into the source's back rows."""
+    H = rows.shape[1]
+    _launch("ep_p2p_reduce_return", 1, "b200moe_ep_p2p_reduce_return", _p(rows), _p(d.inv_pad),
+            _p(weights), d.top_k, _p(dw_rows), _p(plan), _p(peer_rows), _p(peer_dw),
+            d.num_tokens, H, ranks, _s(rows))
+
+
 def ep_p2p_back_inv(send: Dispatch, plan) -> torch.Tensor:
     T, P = send.num_tokens, send.num_experts
     inv = torch.empty(max(T * P, 1), device=plan.device, dtype=torch.int32)

@@ -239,7 +239,7 @@ def test_emulated_expert_parallel_matches_single_gpu_layer(ops, T, H, E, k, I, P
     assert _lib.read_fault() == 0
 
 
-def _emulated_p2p(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
+def _emulated_p2p(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P, fused=True):
     """The peer-memory transport with P ranks on one GPU: each rank's receive
     and back buffers are ordinary device tensors and the 'peer' pointer tables
     point at the other ranks' tensors, so the send / return kernels store
@@ -277,9 +277,15 @@ def _emulated_p2p(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
         wgu_b = ops.cast_bf16(w_gu[o * E_loc:(o + 1) * E_loc].contiguous())
         wd_b = ops.cast_bf16(w_d[o * E_loc:(o + 1) * E_loc].contiguous())
         sel_loc, w_loc = B.unpack(bufs[o].recv_meta[:n_recv])
-        part, ectx = B.experts_fwd(bufs[o].recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
-                                   slots_o)
-        ops.ep_p2p_return(part, st[o].plan, peers["back_rows"], P)
+        if fused:   # the layer's path: combine fused with the return
+            y, ectx = B.experts_fwd(bufs[o].recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
+                                    slots_o, combine=False)
+            ops.ep_p2p_reduce_return(y, ectx[0], st[o].plan, peers["back_rows"], P,
+                                     weights=w_loc)
+        else:       # combine into a local buffer, then the plain return kernel
+            part, ectx = B.experts_fwd(bufs[o].recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
+                                       slots_o)
+            ops.ep_p2p_return(part, st[o].plan, peers["back_rows"], P)
         own.append(SimpleNamespace(ectx=ectx, n_recv=n_recv))
     outs = []
     for r in range(P):
@@ -293,8 +299,15 @@ def _emulated_p2p(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
     ggu, gd = [], []
     for o in range(P):
         d_recv = bufs[o].recv_rows[:own[o].n_recv]
-        dx_rows, dw_rows, state = B.experts_dgrad(own[o].ectx, d_recv, k, d_recv.device)
-        ops.ep_p2p_return(dx_rows, st[o].plan, peers["back_rows"], P, dw_rows, peers["back_dw"])
+        if fused:
+            dxs, dw_rows, state = B.experts_dgrad(own[o].ectx, d_recv, k, d_recv.device,
+                                                  reduce=False)
+            ops.ep_p2p_reduce_return(dxs, own[o].ectx[0], st[o].plan, peers["back_rows"], P,
+                                     dw_rows=dw_rows, peer_dw=peers["back_dw"])
+        else:
+            dx_rows, dw_rows, state = B.experts_dgrad(own[o].ectx, d_recv, k, d_recv.device)
+            ops.ep_p2p_return(dx_rows, st[o].plan, peers["back_rows"], P, dw_rows,
+                              peers["back_dw"])
         c, e = B.experts_wgrad(state, None, None, E_loc, H, I, d_recv.device)
         ggu.append(c)
         gd.append(e)
@@ -309,9 +322,11 @@ def _emulated_p2p(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
     return outs, [s.sel for s in st], dxs, g_routers, torch.cat(ggu), torch.cat(gd)
 
 
-@pytest.mark.parametrize("T,H,E,k,I,P", [(2048, 1024, 32, 8, 256, 4), (1500, 2048, 16, 4, 128, 2),
-                                         (1024, 512, 64, 8, 192, 8)])
-def test_emulated_peer_memory_transport_matches_single_gpu_layer(ops, T, H, E, k, I, P):
+@pytest.mark.parametrize("T,H,E,k,I,P,fused", [(2048, 1024, 32, 8, 256, 4, True),
+                                               (1500, 2048, 16, 4, 128, 2, True),
+                                               (1024, 512, 64, 8, 192, 8, True),
+                                               (1024, 1024, 32, 8, 128, 4, False)])
+def test_emulated_peer_memory_transport_matches_single_gpu_layer(ops, T, H, E, k, I, P, fused):
     from spark_gpt_b200 import SparseMoE, _lib
     g = torch.Generator().manual_seed(E * 3 + P)
     w_r = (torch.randn(E, H, generator=g) * 0.05).to(DEV)
@@ -319,7 +334,8 @@ def test_emulated_peer_memory_transport_matches_single_gpu_layer(ops, T, H, E, k
     w_d = (torch.randn(E, H, I, generator=g) * 0.02).to(DEV)
     xs = [torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV) for _ in range(P)]
     ds = [(torch.randn(T, H, generator=g) * 1e-2).to(torch.bfloat16).to(DEV) for _ in range(P)]
-    outs, sels, dxs, g_routers, g_gu, g_d = _emulated_p2p(ops, xs, ds, w_r, w_gu, w_d, k, P)
+    outs, sels, dxs, g_routers, g_gu, g_d = _emulated_p2p(ops, xs, ds, w_r, w_gu, w_d, k, P,
+                                                          fused)
     cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=k,
                           moe_intermediate_size=I, norm_topk_prob=True)
     ref = SparseMoE(cfg).to(DEV)
