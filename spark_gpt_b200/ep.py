@@ -286,8 +286,10 @@ class PeerTransport:
     _cache: dict = {}
 
     @classmethod
-    def get(cls, group, H, k, device):
-        key = (id(group) if group is not None else None, H, k, str(device))
+    def get(cls, group, H, k, device, slot=0):
+        """The transport of (group, H, k) on `device`; `slot` tells apart the
+        transports of a step's token chunks."""
+        key = (id(group) if group is not None else None, H, k, str(device), slot)
         if key not in cls._cache:
             cls._cache[key] = cls(group, H, k, device)
         return cls._cache[key]
@@ -350,48 +352,119 @@ class PeerTransport:
         ops.ep_barrier(self.peer_flags, self.flags, self.me, self.P, self.epoch)
 
 
+_COPY_STREAMS: dict = {}
+
+
+def _copy_stream(device):
+    key = str(device)
+    if key not in _COPY_STREAMS:
+        _COPY_STREAMS[key] = torch.cuda.Stream(device)
+    return _COPY_STREAMS[key]
+
+
 class _EPMoEP2PFn(torch.autograd.Function):
     """The expert-parallel layer with its exchanges as peer-memory stores:
     one kernel gathers each token's row and stores it into the owners' receive
-    buffers (with its slot words), one kernel stores the owners' result rows
-    into the sources' buffers, and bounded barriers over flag words separate the
-    phases.  One all-gather of the per-rank counts and one host read per step."""
+    buffers (with its slot words), one kernel reduces each received row's slots
+    and stores the result into the source's buffers, and bounded barriers over
+    flag words separate the phases.  One all-gather of the per-rank counts and
+    one host read per step.
+
+    Overlap (comm_sms > 0): the transfers run on a copy stream.  The tokens are
+    split into `chunks` ranges, each with its own send plan and its own
+    transport (buffers and barrier flags): chunk c+1's rows travel while chunk
+    c's experts compute, and chunk c's results travel back while chunk c+1
+    computes; in the backward the last results travel while the weight
+    gradients compute.  While transfers may run beside them the persistent
+    kernels leave comm_sms SMs free.  Every rank issues the same barriers in
+    the same order."""
 
     @staticmethod
-    def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, transport):
-        P, me = transport.P, transport.me
+    def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, transports,
+                comm_sms):
+        tr0 = transports[0]
+        P, me = tr0.P, tr0.me
+        C = len(transports)
         E_loc = w_gu.shape[0]
         T, H = x.shape
         B = CudaExpertOps
         xb = _as_bf16(x)
+        dev = xb.device
+        s0 = torch.cuda.current_stream(dev)
+        s1 = _copy_stream(dev) if comm_sms else s0
         logits_buf, wr, sel, rw = B.router(xb, w_router, num_experts, top_k, norm)
-        dest, slots = ops.ep_route(sel, E_loc, P)
-        send = ops.dispatch(dest, P, partial=True)
-        counts = torch.cat([send.counts, slots, torch.full((1,), T, device=xb.device,
-                                                          dtype=torch.int32)])
-        gathered = torch.empty(P, 2 * P + 1, device=xb.device, dtype=torch.int32)
-        dist.all_gather_into_tensor(gathered, counts, group=group)
+        span = [(T * c // C, T * (c + 1) // C) for c in range(C)]
+        sends, counts = [], []
+        for a, b in span:
+            dest, slots = ops.ep_route(sel[a:b], E_loc, P)
+            send = ops.dispatch(dest, P, partial=True)
+            sends.append(send)
+            counts.append(torch.cat([send.counts, slots,
+                                     torch.full((1,), b - a, device=dev, dtype=torch.int32)]))
+        W = 2 * P + 1
+        gathered = torch.empty(P, C * W, device=dev, dtype=torch.int32)
+        dist.all_gather_into_tensor(gathered, torch.cat(counts), group=group)
         host = gathered.cpu()  # the one host read of the step
-        transport.ensure(int(host[:, 2 * P].max()))
-        n_recv = int(host[:, me].sum())
-        recv_slots = int(host[:, P + me].sum())
-        n_back = int(host[me, :P].sum())
-        plan = ops.ep_p2p_plan(gathered, me, P)
-        ops.ep_p2p_send(xb, send, plan, transport.peer_recv_rows, sel, rw, E_loc,
-                        transport.peer_recv_meta)
-        transport.barrier()
-        sel_loc, w_loc = B.unpack(transport.recv_meta[:n_recv])
+        n_recv, slots_in, n_back, plans = [], [], [], []
+        for c in range(C):
+            hc = host[:, c * W:(c + 1) * W]
+            transports[c].ensure(int(hc[:, 2 * P].max()))
+            n_recv.append(int(hc[:, me].sum()))
+            slots_in.append(int(hc[:, P + me].sum()))
+            n_back.append(int(hc[me, :P].sum()))
+            plans.append(ops.ep_p2p_plan(gathered[:, c * W:], me, P))
         wgu_b, wd_b = B.cast(w_gu), B.cast(w_d)
-        y, ectx = B.experts_fwd(transport.recv_rows[:n_recv], sel_loc, w_loc, wgu_b, wd_b,
-                                recv_slots, combine=False)
-        if ectx is not None:  # combine of each received row, stored into its source
-            ops.ep_p2p_reduce_return(y, ectx[0], plan, transport.peer_back_rows, P, weights=w_loc)
-        transport.barrier()
-        back = dataclasses.replace(send, inv_pad=ops.ep_p2p_back_inv(send, plan))
-        out = ops.gather_rows_bwd(transport.back_rows[:n_back], back)
+
+        def send_rows(c):
+            a, b = span[c]
+            ops.ep_p2p_send(xb[a:b], sends[c], plans[c], transports[c].peer_recv_rows, sel[a:b],
+                            rw[a:b], E_loc, transports[c].peer_recv_meta)
+
+        ready = s0.record_event()
+        send_rows(0)
+        sent = [None] * C
+        if C > 1:
+            with torch.cuda.stream(s1):
+                s1.wait_event(ready)
+                for c in range(1, C):
+                    send_rows(c)
+                    sent[c] = s1.record_event()
+        ectxs, ret, keep = [None] * C, [None] * C, []
+        overlap = backend_overlap(comm_sms) if (comm_sms and C > 1) else nullcontext()
+        with overlap:
+            for c in range(C):
+                if sent[c] is not None:
+                    s0.wait_event(sent[c])
+                tr = transports[c]
+                tr.barrier()
+                sel_loc, w_loc = B.unpack(tr.recv_meta[:n_recv[c]])
+                y, ectxs[c] = B.experts_fwd(tr.recv_rows[:n_recv[c]], sel_loc, w_loc, wgu_b,
+                                            wd_b, slots_in[c], combine=False)
+                if ectxs[c] is None:
+                    continue
+                if C > 1:  # the combine + return of chunk c beside chunk c+1's experts
+                    done = s0.record_event()
+                    with torch.cuda.stream(s1):
+                        s1.wait_event(done)
+                        ops.ep_p2p_reduce_return(y, ectxs[c][0], plans[c], tr.peer_back_rows, P,
+                                                 weights=w_loc)
+                        ret[c] = s1.record_event()
+                    keep.append(w_loc)
+                else:
+                    ops.ep_p2p_reduce_return(y, ectxs[c][0], plans[c], tr.peer_back_rows, P,
+                                             weights=w_loc)
+        out = xb.new_empty(T, H)
+        backs = []
+        for c, (a, b) in enumerate(span):
+            if ret[c] is not None:
+                s0.wait_event(ret[c])
+            transports[c].barrier()
+            back = dataclasses.replace(sends[c], inv_pad=ops.ep_p2p_back_inv(sends[c], plans[c]))
+            backs.append(back)
+            ops.gather_rows_bwd(transports[c].back_rows[:n_back[c]], back, out=out[a:b])
         ctx.save_for_backward(xb, logits_buf, wr, sel)
-        ctx.meta = (send, back, plan, ectx, n_recv, n_back, transport, top_k, norm, num_experts,
-                    E_loc, H, w_gu.shape[1] // 2, x.dtype)
+        ctx.meta = (span, sends, backs, plans, ectxs, n_recv, n_back, transports, top_k, norm,
+                    num_experts, E_loc, H, w_gu.shape[1] // 2, x.dtype, comm_sms)
         ctx.mark_non_differentiable(sel)
         E = num_experts
         logits = logits_buf if logits_buf.shape[1] == E else logits_buf[:, :E]
@@ -400,26 +473,76 @@ class _EPMoEP2PFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, d_out, d_logits, _d_sel):
         xb, logits_buf, wr, sel = ctx.saved_tensors
-        (send, back, plan, ectx, n_recv, n_back, transport, top_k, norm, num_experts, E_loc, H,
-         I, xdtype) = ctx.meta
+        (span, sends, backs, plans, ectxs, n_recv, n_back, transports, top_k, norm, num_experts,
+         E_loc, H, I, xdtype, comm_sms) = ctx.meta
         B = CudaExpertOps
-        P = transport.P
+        C = len(span)
+        P = transports[0].P
+        dev = xb.device
+        s0 = torch.cuda.current_stream(dev)
+        s1 = _copy_stream(dev) if comm_sms else s0
         if d_out is None:
-            d_out = torch.zeros(xb.shape, device=xb.device, dtype=xb.dtype)
-        ops.ep_p2p_send(_as_bf16(d_out), send, plan, transport.peer_recv_rows)
-        transport.barrier()
-        dxs, dw_rows, state = B.experts_dgrad(ectx, transport.recv_rows[:n_recv], top_k,
-                                              xb.device, reduce=False)
-        if ectx is not None:  # per-row sums of the slot gradients, stored into the sources
-            ops.ep_p2p_reduce_return(dxs, ectx[0], plan, transport.peer_back_rows, P,
-                                     dw_rows=dw_rows, peer_dw=transport.peer_back_dw)
-        g_gu, g_d = B.experts_wgrad(state, None, None, E_loc, H, I, xb.device)
-        transport.barrier()
-        d_rw = ops.ep_weight_grad(transport.back_dw[:n_back], back, sel, E_loc)
+            d_out = torch.zeros(xb.shape, device=dev, dtype=xb.dtype)
+        d_out = _as_bf16(d_out)
+
+        def send_rows(c):
+            a, b = span[c]
+            ops.ep_p2p_send(d_out[a:b], sends[c], plans[c], transports[c].peer_recv_rows)
+
+        ready = s0.record_event()
+        send_rows(0)
+        sent = [None] * C
+        if C > 1:
+            with torch.cuda.stream(s1):
+                s1.wait_event(ready)
+                for c in range(1, C):
+                    send_rows(c)
+                    sent[c] = s1.record_event()
+        ret, states, keep = [None] * C, [None] * C, []
+        g_gu = g_d = None
+        overlap = backend_overlap(comm_sms) if comm_sms else nullcontext()
+        with overlap:
+            for c in range(C):
+                if sent[c] is not None:
+                    s0.wait_event(sent[c])
+                tr = transports[c]
+                tr.barrier()
+                dxs, dw_rows, states[c] = B.experts_dgrad(ectxs[c], tr.recv_rows[:n_recv[c]],
+                                                          top_k, dev, reduce=False)
+                if ectxs[c] is None:
+                    continue
+                if comm_sms:  # the return of chunk c beside the next GEMMs
+                    done = s0.record_event()
+                    with torch.cuda.stream(s1):
+                        s1.wait_event(done)
+                        ops.ep_p2p_reduce_return(dxs, ectxs[c][0], plans[c], tr.peer_back_rows,
+                                                 P, dw_rows=dw_rows, peer_dw=tr.peer_back_dw)
+                        ret[c] = s1.record_event()
+                    keep.append((dxs, dw_rows))
+                else:
+                    ops.ep_p2p_reduce_return(dxs, ectxs[c][0], plans[c], tr.peer_back_rows, P,
+                                             dw_rows=dw_rows, peer_dw=tr.peer_back_dw)
+            for c in range(C):
+                g_gu, g_d = B.experts_wgrad(states[c], g_gu, g_d, E_loc, H, I, dev)
+        d_rw = torch.empty(xb.shape[0], top_k, device=dev, dtype=torch.float32)
+        for c, (a, b) in enumerate(span):
+            if ret[c] is not None:
+                s0.wait_event(ret[c])
+            transports[c].barrier()
+            ops.ep_weight_grad(transports[c].back_dw[:n_back[c]], backs[c], sel[a:b], E_loc,
+                               out=d_rw[a:b])
+        del keep
         dx_router, g_router = B.router_bwd(xb, wr, logits_buf, sel, d_rw, d_logits, num_experts,
                                            top_k, norm)
-        dx = ops.gather_rows_bwd(transport.back_rows[:n_back], back, addend=dx_router)
-        return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None)
+        dx = xb.new_empty(xb.shape)
+        for c, (a, b) in enumerate(span):
+            ops.gather_rows_bwd(transports[c].back_rows[:n_back[c]], backs[c],
+                                addend=dx_router[a:b], out=dx[a:b])
+        return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None)
+
+
+def backend_overlap(comm_sms):
+    return CudaExpertOps.overlap(comm_sms)
 
 
 class ExpertParallelMoE(nn.Module):
@@ -507,10 +630,12 @@ class ExpertParallelMoE(nn.Module):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
         if self.transport == "p2p":
-            tr = PeerTransport.get(self.group, shape[-1], self.gate.top_k, x.device)
+            trs = tuple(PeerTransport.get(self.group, shape[-1], self.gate.top_k, x.device, c)
+                        for c in range(max(1, self.chunks)))
             out, logits, sel = _EPMoEP2PFn.apply(
                 x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
-                self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group, tr)
+                self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group, trs,
+                self.comm_sms)
         else:
             out, logits, sel = _EPMoEFn.apply(
                 x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
