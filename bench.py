@@ -374,7 +374,8 @@ def main():
                                       "dispatch", "router_topk", "router_topk_bwd", "cast",
                                       "lb_stats", "lb_grad", "lb_finalize"]
     if c.get("ep"):
-        names += ["ep_route", "ep_pack", "ep_unpack", "ep_weight_grad"]
+        names += ["ep_route", "ep_pack", "ep_unpack", "ep_weight_grad", "ep_p2p_send",
+                  "ep_p2p_reduce_return", "ep_barrier"]
     timing = ops.set_timing(names)
     launches0 = ops.LAUNCHES["count"]
     barrier()

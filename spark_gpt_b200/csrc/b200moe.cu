@@ -1201,12 +1201,11 @@ int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const voi
   auto* yp = static_cast<const __nv_bfloat16*>(rows);
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
-  const int grid = grid_for(rows_cap, 8);
-  switch (H) {
-    case 256: ep_p2p_reduce_return_kernel<1><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    case 512: ep_p2p_reduce_return_kernel<2><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    case 1024: ep_p2p_reduce_return_kernel<4><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    default: ep_p2p_reduce_return_kernel<8><<<grid, 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+  switch (H) {  // a warp handles at most 1024 columns (4 vectors per lane)
+    case 256: ep_p2p_reduce_return_kernel<1, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 512: ep_p2p_reduce_return_kernel<2, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    default: ep_p2p_reduce_return_kernel<4, 2><<<grid_for(2 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
   }
   return check_launch("ep_p2p_reduce_return");
 }

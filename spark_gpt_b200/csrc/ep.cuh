@@ -315,9 +315,11 @@ namespace b200moe {
 // backward), accumulated in fp32 in slot order and rounded once, is stored
 // straight into row back_base[src] + (i - recv_base[src]) of the source's back
 // rows; with dw (rows, k) fp32 its k routing-weight gradients go to the same
-// row of the source's back dw.  Warp per received row; the rows of the valid
-// slots are loaded two at a time.
-template <int VPL>
+// row of the source's back dw.  A warp takes one of SPLIT column parts of a
+// received row (VPL 16-byte vectors per lane), so the fp32 accumulators stay
+// few enough for three 256-thread blocks per SM; the rows of the valid slots
+// are loaded two at a time.
+template <int VPL, int SPLIT>
 __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
                                             const int* __restrict__ inv_pad,
                                             const __nv_bfloat16* __restrict__ weights, int k,
@@ -332,11 +334,14 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
     if (r < P) bb_s[r] = plan[2 + 2 * P + r];
   }
   __syncthreads();
-  const long long n = plan[0];
+  const long long n = plan[0] * static_cast<long long>(SPLIT);
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
-       i < n; i += warps) {
+  for (long long item = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       item < n; item += warps) {
+    const long long i = item / SPLIT;
+    const int part = static_cast<int>(item - i * SPLIT);
+    const int col0 = part * (H / SPLIT);  // first column of this part
     const int rl = lane < k ? inv_pad[i * k + lane] : -1;
     float wl = 1.f;
     if (weights != nullptr && lane < k) wl = __bfloat162float(weights[i * k + lane]);
@@ -373,8 +378,8 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
       const long long r1 = __shfl_sync(0xffffffffu, rl, s1 >= 0 ? s1 : s0);
       const float w1 = __shfl_sync(0xffffffffu, wl, s1 >= 0 ? s1 : s0);
       uint4 a[VPL], b[VPL];
-      const uint4* p0 = reinterpret_cast<const uint4*>(y + r0 * H);
-      const uint4* p1 = reinterpret_cast<const uint4*>(y + r1 * H);
+      const uint4* p0 = reinterpret_cast<const uint4*>(y + r0 * H + col0);
+      const uint4* p1 = reinterpret_cast<const uint4*>(y + r1 * H + col0);
 #pragma unroll
       for (int j = 0; j < VPL; ++j) a[j] = __ldg(p0 + lane + 32 * j);
       if (s1 >= 0) {
@@ -387,7 +392,7 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
     int src = 0;
     while (src + 1 < P && rb_s[src + 1] <= i) ++src;
     const long long row = bb_s[src] + (i - rb_s[src]);
-    uint4* dst = reinterpret_cast<uint4*>(peer_rows[src] + row * H);
+    uint4* dst = reinterpret_cast<uint4*>(peer_rows[src] + row * H + col0);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {
       uint4 o;
@@ -397,7 +402,7 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
       o.w = pack_bf16x2(acc[j][6], acc[j][7]);
       dst[lane + 32 * j] = o;
     }
-    if (dw != nullptr && lane < k) peer_dw[src][row * k + lane] = dw[i * k + lane];
+    if (dw != nullptr && part == 0 && lane < k) peer_dw[src][row * k + lane] = dw[i * k + lane];
   }
 }
 
