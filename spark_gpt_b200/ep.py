@@ -8,9 +8,8 @@ tokens.  Per forward:
      its k experts (one row per (token, destination rank), not one per slot),
      with k packed slot words (local expert id + bf16 routing weight, or "no
      expert here") beside the row; rank-major, token order within a rank;
-  3. the rows and slot words cross the NVLink/NVSwitch fabric with NCCL
-     all_to_all_single (one host read of the per-rank row and slot counts
-     sizes the receive buffers);
+  3. the rows and slot words cross the NVLink/NVSwitch fabric (one host read
+     of the per-rank counts sizes every buffer);
   4. the owner runs its local experts on the received rows as a k-slot layer
      whose foreign slots are skipped (dispatch, gate_up GEMM + SwiGLU, down
      GEMM) and combines each row's local slots with their routing weights
@@ -23,19 +22,26 @@ owner computes the combine backward (slot gradients and routing-weight
 gradients), its experts' dgrads, and sums each row's slot input-gradients
 into one row; rows and routing-weight gradients travel back (while the owner
 computes its expert weight gradients, which stay local) and the source adds
-them to the router's input gradient.
+them to the router's input gradient.  The load-balancing counts are
+all-reduced by global_load_balancing_loss as in the data-parallel layout
+(train.py:3162).
 
-Overlap: the tokens may be split into chunks with one send plan each, so that
-one chunk's exchange runs while another chunk's experts compute (see
-_EPMoEFn); the persistent kernels can leave SMs to the collective.  The load-balancing counts are all-reduced by
-global_load_balancing_loss as in the data-parallel layout (train.py:3162).
+Two transports carry steps 3 and 5:
+  * "nccl": all_to_all_single of packed send buffers (_EPMoEFn); the tokens
+    may be split into chunks so one chunk's exchange runs while another's
+    experts compute, the persistent kernels leaving SMs to the collective;
+  * "p2p": this library's kernels store the rows straight into buffers every
+    rank has mapped (torch symmetric memory over NVLink/NVSwitch), the gather
+    of the send plan and the owner's combine fused with the transfers, and
+    bounded barriers over flag words separate the phases (_EPMoEP2PFn).
 
 Each (token, rank) row crosses the fabric once per pass instead of once per
 slot: with top-8 of 128 experts a token reaches about 5.3 of 8 ranks (2 of
 2), so each of the four exchanges moves a third (three quarters) less than a
 per-slot exchange.  Results agree with the single-GPU layer within bf16
 rounding: the owner's partial sums are rounded to bf16 before the source adds
-them (one extra rounding when a token's experts span ranks).
+them (one extra rounding when a token's experts span ranks); both transports
+give the same bits.
 
 The reference trains data-parallel only (experts replicated, DDP); this module
 is the expert-parallel layout of the same layer.  Expert parameters here are
@@ -641,4 +647,5 @@ class ExpertParallelMoE(nn.Module):
                 x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
                 self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group,
                 self.backend, self.chunks, self.comm_sms)
-        return out.view(shape), logits.view(*shape[:-1], -1), sel.view(*shape[:-1], -1)
+        lead = shape[:-1]
+        return out.view(shape), logits.view(*lead, logits.shape[-1]), sel.view(*lead, sel.shape[-1])

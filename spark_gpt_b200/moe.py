@@ -140,8 +140,9 @@ class TopKRouter(nn.Module):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
         logits, rw, sel = _RouterFn.apply(x, self.weight, self.top_k, self.norm_topk_prob)
-        return (logits.view(*shape[:-1], -1), rw.view(*shape[:-1], -1),
-                sel.view(*shape[:-1], -1))
+        lead = shape[:-1]
+        return (logits.view(*lead, logits.shape[-1]), rw.view(*lead, rw.shape[-1]),
+                sel.view(*lead, sel.shape[-1]))
 
 
 class Experts(nn.Module):
@@ -180,4 +181,5 @@ class SparseMoE(nn.Module):
         out, logits, sel = sparse_moe(
             x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
             self.gate.top_k, self.gate.norm_topk_prob)
-        return out.view(shape), logits.view(*shape[:-1], -1), sel.view(*shape[:-1], -1)
+        lead = shape[:-1]
+        return out.view(shape), logits.view(*lead, logits.shape[-1]), sel.view(*lead, sel.shape[-1])

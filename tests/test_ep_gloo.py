@@ -6,7 +6,10 @@ send plan, the all_to_all_single exchanges, the owner-side partial combine and
 the backward's reverse exchanges are checked on CPU: every rank's output and
 input gradient must equal the single-process oracle layer on that rank's
 tokens, and each rank's expert-shard gradients must equal the oracle's
-gradients of those experts summed over all ranks' tokens.  Test infrastructure only: the product path runs the CUDA kernels.
+gradients of those experts summed over all ranks' tokens.  Also: ranks with
+different token counts (one with none), and a rank that fails before its
+first exchange (its peer gets an error, not a hang).  Test infrastructure
+only: the product path runs the CUDA kernels.
 """
 
 import contextlib
@@ -149,12 +152,12 @@ def full_weights():
             torch.randn(E, H, I, generator=g) * 0.2)
 
 
-def rank_inputs(rank):
+def rank_inputs(rank, tokens=T):
     g = torch.Generator().manual_seed(100 + rank)
-    return torch.randn(T, H, generator=g), torch.randn(T, H, generator=g)
+    return torch.randn(tokens, H, generator=g), torch.randn(tokens, H, generator=g)
 
 
-def _worker(rank, world, port, results, chunks):
+def _worker(rank, world, port, results, chunks, tokens=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -169,7 +172,7 @@ def _worker(rank, world, port, results, chunks):
             m.gate.weight.copy_(w_r)
             m.experts.gate_up_proj.copy_(w_gu[lo:hi])
             m.experts.down_proj.copy_(w_d[lo:hi])
-        x, d_out = rank_inputs(rank)
+        x, d_out = rank_inputs(rank, tokens[rank] if tokens else T)
         xin = x.clone().requires_grad_(True)
         out, logits, sel = m(xin)
         out.backward(d_out)
@@ -267,3 +270,72 @@ def test_expert_shards_round_trip_to_the_full_layout(world):
         assert torch.equal(r["m2_gu"], w_gu[r["lo"]:r["hi"]])
         assert "_extra_state" in r["keys"]
         assert r["mismatch"] is not None and "cannot load" in r["mismatch"]
+
+
+@pytest.mark.parametrize("tokens", [(48, 17), (0, 48), (31, 48, 5, 0)])
+def test_expert_parallel_ranks_with_different_token_counts(tokens):
+    """Ranks holding different numbers of tokens (one of them none): the counts
+    exchange sizes every buffer, and each rank's results still equal the
+    single-process oracle on its own tokens."""
+    world = len(tokens)
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_worker, args=(world, _free_port(), results, 1, list(tokens)),
+                       nprocs=world, join=True, start_method="spawn")
+    w_r, w_gu, w_d = full_weights()
+    sum_gu = torch.zeros_like(w_gu)
+    sum_d = torch.zeros_like(w_d)
+    for rank in range(world):
+        r = results[rank]
+        assert r["out"].shape == (tokens[rank], H) and r["dx"].shape == (tokens[rank], H)
+        if tokens[rank] == 0:
+            continue
+        x, d_out = rank_inputs(rank, tokens[rank])
+        ref = O.layer_forward_backward(x, w_r, w_gu, w_d, K, d_out)
+        torch.testing.assert_close(r["out"], ref["out"], rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(r["dx"], ref["dx"], rtol=1e-5, atol=1e-6)
+        sum_gu += ref["dW_gate_up"]
+        sum_d += ref["dW_down"]
+    for rank in range(world):
+        r = results[rank]
+        torch.testing.assert_close(r["dW_gu"], sum_gu[r["lo"]:r["hi"]], rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(r["dW_d"], sum_d[r["lo"]:r["hi"]], rtol=1e-5, atol=1e-6)
+
+
+def _failing_worker(rank, world, port, results):
+    """Rank 1 raises before its first exchange; rank 0 must get an error from
+    the process group (its short timeout, or the closed connection) instead of
+    waiting for good."""
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    from spark_gpt_b200.ep import ExpertParallelMoE
+    cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=K,
+                          moe_intermediate_size=I, norm_topk_prob=True)
+    m = ExpertParallelMoE(cfg, backend=OracleOps)
+    w_r, w_gu, w_d = full_weights()
+    with torch.no_grad():
+        m.gate.weight.copy_(w_r)
+        m.experts.gate_up_proj.copy_(w_gu[m.expert_offset:m.expert_offset + m.local_experts])
+        m.experts.down_proj.copy_(w_d[m.expert_offset:m.expert_offset + m.local_experts])
+    if rank == 1:
+        results[rank] = {"error": "planted failure before the first exchange", "seconds": 0.0}
+        return  # leaves without joining any collective (no destroy, no barrier)
+    t0 = time.monotonic()
+    try:
+        m(rank_inputs(rank)[0])
+        results[rank] = {"error": None, "seconds": time.monotonic() - t0}
+    except Exception as e:  # noqa: BLE001 - the failure is the point
+        results[rank] = {"error": f"{type(e).__name__}: {e}", "seconds": time.monotonic() - t0}
+
+
+def test_a_rank_that_fails_surfaces_as_an_error_not_a_hang():
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_failing_worker, args=(2, _free_port(), results), nprocs=2, join=True,
+                       start_method="spawn")
+    assert results[1]["error"].startswith("planted")
+    assert results[0]["error"] is not None, "rank 0 finished an exchange its peer never joined"
+    assert results[0]["seconds"] < 60
