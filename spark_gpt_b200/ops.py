@@ -207,6 +207,11 @@ def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None 
     dev = selected.device
     cap = padded_rows(R if routed_slots is None else routed_slots, num_experts)
     i32 = dict(device=dev, dtype=torch.int32)
+    if R == 0:  # no slots: every expert empty, every row padding (nothing to launch)
+        z = lambda n: torch.zeros(n, **i32)  # noqa: E731
+        return Dispatch(z(num_experts), z(num_experts), z(num_experts + 1),
+                        torch.full((cap,), -1, **i32), z(0), z(cap // 128), cap, T, k,
+                        num_experts, partial or routed_slots is not None)
     counts = torch.empty(num_experts, **i32)
     offsets = torch.empty(num_experts, **i32)
     pad = torch.empty(num_experts + 1, **i32)
@@ -228,6 +233,8 @@ def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None 
 def gather_rows(x: torch.Tensor, d: Dispatch) -> torch.Tensor:
     _check(x, BF16, "gather_rows x")
     H = x.shape[1]
+    if d.num_tokens == 0:  # only padding rows
+        return torch.zeros(d.rows_cap, H, device=x.device, dtype=BF16)
     xs = torch.empty(d.rows_cap, H, device=x.device, dtype=BF16)
     _launch("gather", 1, "b200moe_gather_rows", _p(x), _p(d.row_flat),
             _p(d.inv_pad) if d.inv_pad.numel() else None, _p(d.pad_offsets), d.num_tokens,
@@ -265,6 +272,9 @@ def combine(y, d: Dispatch, weights, token_major=False) -> torch.Tensor:
 def combine_bwd(d_out, y, d: Dispatch, weights, token_major=False):
     _check(d_out, BF16, "combine_bwd d_out")
     H = y.shape[1]
+    if d.num_tokens == 0:  # only padding rows, no routing weights
+        return (torch.zeros(d.rows_cap, H, device=y.device, dtype=BF16),
+                torch.zeros(0, d.top_k, device=y.device, dtype=torch.float32))
     dy = torch.empty(d.rows_cap, H, device=y.device, dtype=BF16)
     dw = torch.empty(d.num_tokens, d.top_k, device=y.device, dtype=torch.float32)
     _launch("combine_bwd", 2 if token_major else 1, "b200moe_combine_bwd", _p(d_out), _p(y),
@@ -395,6 +405,8 @@ def ep_route(selected: torch.Tensor, experts_per_rank: int, ranks: int):
     T, k = selected.shape
     dest = torch.empty(T, ranks, device=selected.device, dtype=torch.int64)
     slots = torch.empty(ranks, device=selected.device, dtype=torch.int32)
+    if T == 0:
+        return dest, slots.zero_()
     _launch("ep_route", 1, "b200moe_ep_route", _p(selected), T, k, experts_per_rank, ranks,
             _p(dest), _p(slots), _s(selected))
     return dest, slots
@@ -404,6 +416,8 @@ def ep_pack(selected, weights, send: Dispatch, experts_per_rank: int) -> torch.T
     """(send.rows_cap, k) int32 slot words of the send rows."""
     _check(weights, BF16, "ep_pack weights")
     k = selected.shape[1]
+    if selected.shape[0] == 0:  # no rows to send: every slot word says "no expert"
+        return torch.full((send.rows_cap, k), 0xFFFF, device=selected.device, dtype=torch.int32)
     meta = torch.empty(send.rows_cap, k, device=selected.device, dtype=torch.int32)
     _launch("ep_pack", 1, "b200moe_ep_pack", _p(selected), _p(weights), _p(send.row_flat),
             _p(send.pad_offsets), send.rows_cap, k, experts_per_rank, send.num_experts,
@@ -435,6 +449,8 @@ def ep_p2p_send(src, send: Dispatch, plan, peer_rows, selected=None, weights=Non
     """Store each token's row (and slot words) into the owners' receive buffers."""
     _check(src, BF16, "ep_p2p_send src")
     T, H = src.shape
+    if T == 0:
+        return
     k = selected.shape[1] if selected is not None else 0
     _launch("ep_p2p_send", 1, "b200moe_ep_p2p_send", _p(src), _p(send.inv_pad),
             _p(send.pad_offsets), _p(plan), _p(peer_rows), T, H, send.num_experts,
@@ -446,6 +462,8 @@ def ep_p2p_return(rows, plan, peer_rows, ranks: int, dw_rows=None, peer_dw=None)
     _check(rows, BF16, "ep_p2p_return rows")
     n, H = rows.shape
     k = dw_rows.shape[1] if dw_rows is not None else 0
+    if n == 0:
+        return
     _launch("ep_p2p_return", 1, "b200moe_ep_p2p_return", _p(rows), _p(dw_rows), _p(plan),
             _p(peer_rows), _p(peer_dw), n, H, k, ranks, _s(rows))
 
@@ -463,6 +481,8 @@ def ep_p2p_reduce_return(rows, d: Dispatch, plan, peer_rows, ranks: int, weights
 def ep_p2p_back_inv(send: Dispatch, plan) -> torch.Tensor:
     T, P = send.num_tokens, send.num_experts
     inv = torch.empty(max(T * P, 1), device=plan.device, dtype=torch.int32)
+    if T == 0:
+        return inv[:0]
     _launch("ep_p2p_back_inv", 1, "b200moe_ep_p2p_back_inv", _p(send.inv_pad),
             _p(send.pad_offsets), _p(plan), T, P, _p(inv), _s(plan))
     return inv[: T * P]

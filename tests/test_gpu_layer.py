@@ -103,6 +103,33 @@ def test_layer_matches_oracle(T, H, E, k, I, norm, filler):
     assert m.experts.gate_up_proj.grad.dtype == torch.float32
 
 
+@pytest.mark.parametrize("shape", [(0, 256), (2, 0, 256), (7, 256), (3, 5, 256)])
+def test_empty_and_ragged_batches(shape):
+    """An empty batch (a rank or micro-batch without tokens), a 3-D hidden
+    state and batches smaller than one 128-row tile: outputs keep the input's
+    leading shape, gradients are finite, the expert and router gradients of
+    an empty batch are zero, and nothing sets the fault word."""
+    from spark_gpt_b200 import SparseMoE, _lib
+    torch.manual_seed(0)
+    m = SparseMoE(cfg(256, 8, 2, 128)).to(DEV)
+    with torch.no_grad():
+        m.gate.weight.normal_(0, 0.05)
+        m.experts.gate_up_proj.normal_(0, 0.02)
+        m.experts.down_proj.normal_(0, 0.02)
+    x = torch.randn(*shape, device=DEV).to(torch.bfloat16).requires_grad_(True)
+    out, logits, sel = m(x)
+    assert out.shape == x.shape
+    assert logits.shape == (*shape[:-1], 8) and sel.shape == (*shape[:-1], 2)
+    out.float().square().sum().backward()
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0
+    assert x.grad.shape == x.shape and torch.isfinite(x.grad.float()).all()
+    for p in m.parameters():
+        assert p.grad is not None and torch.isfinite(p.grad).all()
+        if x.numel() == 0:
+            assert torch.all(p.grad == 0)
+
+
 def test_unused_experts_have_zero_finite_gradients():
     """Analogue of the reference's tests/test_moe.py:452-472."""
     from spark_gpt_b200 import Experts
