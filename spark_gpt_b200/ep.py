@@ -59,7 +59,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from . import ops
-from .moe import BF16, TopKRouter, _as_bf16, _extra_logit_grad, _require_cuda
+from .moe import TopKRouter, _as_bf16, _extra_logit_grad, _require_cuda
 
 MAX_RANKS = 16  # the source-side sum over ranks reduces at most 16 rows per token
 

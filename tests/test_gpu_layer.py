@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from oracle import moe_oracle as O
-from tests.helpers import assert_bf16_close, rel_errors
+from tests.helpers import assert_bf16_close
 
 pytestmark = pytest.mark.gpu
 
