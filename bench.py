@@ -17,7 +17,11 @@ moe_intermediate 256, 65,536 tokens per GPU, near-uniform routing).
 
 --impl reference times the reference's CPU path (the oracle port of
 train.py's torch MoE path, fp32) on the host cores on a bounded token sample
-of the same shapes; rank 0 alone runs it.
+of the same shapes; rank 0 alone runs it.  Its step is the forward, the
+load-balancing loss and the backward of out . g + 1e-3 * aux for a fixed
+upstream gradient g (the MoE work of one training step).  The GPU arm's `e2e`
+figure times a training step with the reference's loss, mean(out^2) + 1e-3 *
+aux, with x copied from pinned host memory every step and the loss read back.
 """
 
 from __future__ import annotations
@@ -411,28 +415,42 @@ def main():
     gemm_ms = sum(per_op.get(n, 0.0) * len(timing.get(n, [])) / args.steps for n in flops)
 
     # ---------------- end to end: host buffers, copies inside the timed region.
-    # Each step's x and d_out come from pinned host memory; as a training
-    # input pipeline does, the copy of step i+1's inputs runs on a copy stream
-    # while step i computes (two device buffers, ordered by events), and each
-    # step's aux loss is read back to pinned host memory.  Every copy lies
-    # inside the timed region.
+    # The step of the reference arm and of the CPU baseline: forward, loss =
+    # mean(out^2) + 1e-3 * aux, backward; its one input, x, comes from pinned
+    # host memory every step and the loss is read back to pinned host memory.
+    # As a training input pipeline does, the copy of step i+1's x runs on a
+    # copy stream while step i computes (two device buffers, ordered by
+    # events).  Every copy lies inside the timed region.
+    def loss_step(xb):
+        for p in layer.parameters():
+            p.grad = None
+        xin = xb.detach().requires_grad_(True)
+        out, logits, sel = layer(xin)
+        aux, _ = global_load_balancing_loss((logits,), (sel,), valid, num_experts=c["E"],
+                                            top_k=c["k"])
+        loss = out.float().square().mean() + AUX_COEF * aux
+        loss.backward()
+        return loss
+
     e2e = None
     if not args.no_e2e:
-        aux_h = torch.empty((), dtype=torch.float32).pin_memory()
+        loss_h = torch.empty((), dtype=torch.float32).pin_memory()
         comp = torch.cuda.current_stream(dev)
         copy = torch.cuda.Stream(dev)
-        bufs = [(torch.empty_like(x), torch.empty_like(d_out)) for _ in range(2)]
+        bufs = [torch.empty_like(x) for _ in range(2)]
         copied = [torch.cuda.Event() for _ in range(2)]
         freed = [torch.cuda.Event() for _ in range(2)]
 
         def prefetch(i):
-            xb, db = bufs[i % 2]
+            xb = bufs[i % 2]
             with torch.cuda.stream(copy):
                 if i >= 2:
                     copy.wait_event(freed[i % 2])  # step i-2 is done with this buffer
                 xb.copy_(x_pin, non_blocking=True)
-                db.copy_(d_pin, non_blocking=True)
                 copied[i % 2].record(copy)
+
+        for _ in range(2):
+            loss_step(x)  # warm the loss's own kernels
 
         torch.cuda.synchronize()
         barrier()
@@ -444,17 +462,18 @@ def main():
             if i + 1 < args.steps:
                 prefetch(i + 1)
             comp.wait_event(copied[i % 2])
-            xb, db = bufs[i % 2]
-            aux = step(xb, db)
+            loss = loss_step(bufs[i % 2])
             freed[i % 2].record(comp)
-            aux_h.copy_(aux.detach(), non_blocking=True)
+            loss_h.copy_(loss.detach(), non_blocking=True)
         e1.record(comp)
         torch.cuda.synchronize()
         barrier()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
         e2e = {"value": world * T / (e2e_ms / 1e3), "unit": "tokens/s",
-               "h2d_bytes_per_step": x_pin.numel() * 2 + d_pin.numel() * 2,
-               "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": x_pin.numel() * 2, "d2h_bytes_per_step": 4,
+               "ms_per_step": e2e_ms,
+               "step": "forward, loss = mean(out^2) + 1e-3*aux, backward (the reference arm's "
+                       "step); x from pinned host memory, the loss read back",
                "pipeline": "next step's H2D overlapped with this step's compute (copy stream, "
                            "double-buffered inputs)"}
 
