@@ -92,3 +92,24 @@ def test_hf_export_keys_match_the_reference_model(train):
     b = {k: tuple(v.shape) for k, v in train.export_unfused_state_dict(ours).items()}
     assert a == b
     assert a["layers.0.mlp.experts.gate_up_proj"] == (8, 128, 128)
+
+
+def test_hf_export_of_the_swapped_model_strictly_loads_as_qwen3_moe(train, tmp_path):
+    """The reference's export_hf (train.py:2614-2691) on the model with this
+    layer swapped in writes a directory that transformers strictly loads as
+    Qwen3MoeForCausalLM, with every tensor equal to the reference model's own
+    export under the same init (the reference's tests/test_moe.py:260-290)."""
+    transformers = pytest.importorskip("transformers")
+    cfg, ref, ours = _models(train)
+    for model in (ref, ours):
+        torch.manual_seed(2)
+        train.apply_mup_init(model, base_dim=64, emb_std=0.02, hidden_std=0.02)
+    train.export_hf(ours, tmp_path)
+    loaded = transformers.AutoModelForCausalLM.from_pretrained(tmp_path)
+    assert loaded.__class__.__name__ == "Qwen3MoeForCausalLM"
+    actual = loaded.state_dict()
+    expected = {(k if k == "lm_head.weight" else "model." + k): v
+                for k, v in train.export_unfused_state_dict(ref).items()}
+    assert set(actual) == set(expected)
+    for key, value in expected.items():
+        torch.testing.assert_close(actual[key], value)
