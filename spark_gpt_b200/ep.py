@@ -162,6 +162,21 @@ class CudaExpertOps:
             torch.cuda.current_device()).multi_processor_count - comm_sms))
 
 
+def _layer_signature(num_experts, top_k, H, I, chunks):
+    """What every rank of the group must agree on: a rank configured
+    differently would route rows to experts that another rank does not hold."""
+    return [num_experts, top_k, H, I, chunks]
+
+
+def _check_signatures(received, mine):
+    """received: one signature per rank (host ints); raise on every rank alike."""
+    bad = [r for r, sig in enumerate(received) if list(sig) != list(mine)]
+    if bad:
+        raise ValueError(f"expert-parallel ranks disagree on the layer configuration "
+                         f"(experts, top_k, hidden, intermediate, chunks): this rank has {mine}, "
+                         f"rank(s) {bad} have {[list(received[r]) for r in bad]}")
+
+
 def _start(buf, send_counts, recv_counts, group):
     """Asynchronous all_to_all_single of row blocks -> (receive buffer, work)."""
     out = buf.new_empty((sum(recv_counts), *buf.shape[1:]))
@@ -198,10 +213,14 @@ class _EPMoEFn(torch.autograd.Function):
             plans.append(plan)
             sizes.append(sz)
         x_sends = [backend.pack_rows(xb[a:b], plans[c]) for c, (a, b) in enumerate(span)]
-        sizes_t = torch.stack(sizes).transpose(0, 1).contiguous()     # (P, C, 2)
+        sizes_t = torch.stack(sizes).transpose(0, 1)                  # (P, C, 2)
+        sig = _layer_signature(num_experts, top_k, H, w_gu.shape[1] // 2, C)
+        sig_t = torch.tensor(sig, dtype=sizes_t.dtype, device=sizes_t.device)
+        sizes_t = torch.cat([sizes_t, sig_t.expand(P, C, len(sig))], 2).contiguous()
         recv_t = torch.empty_like(sizes_t)
         dist.all_to_all_single(recv_t, sizes_t, group=group)
         host = torch.stack([sizes_t, recv_t]).cpu()  # the one host read of the step
+        _check_signatures(host[1, :, 0, 2:].tolist(), sig)
         send_rows = [host[0, :, c, 0].tolist() for c in range(C)]
         recv_rows = [host[1, :, c, 0].tolist() for c in range(C)]
         recv_slots = [int(host[1, :, c, 1].sum()) for c in range(C)]
@@ -408,9 +427,12 @@ class _EPMoEP2PFn(torch.autograd.Function):
             counts.append(torch.cat([send.counts, slots,
                                      torch.full((1,), b - a, device=dev, dtype=torch.int32)]))
         W = 2 * P + 1
-        gathered = torch.empty(P, C * W, device=dev, dtype=torch.int32)
+        sig = _layer_signature(num_experts, top_k, H, w_gu.shape[1] // 2, C)
+        counts.append(torch.tensor(sig, device=dev, dtype=torch.int32))
+        gathered = torch.empty(P, C * W + len(sig), device=dev, dtype=torch.int32)
         dist.all_gather_into_tensor(gathered, torch.cat(counts), group=group)
         host = gathered.cpu()  # the one host read of the step
+        _check_signatures(host[:, C * W:].tolist(), sig)
         n_recv, slots_in, n_back, plans = [], [], [], []
         for c in range(C):
             hc = host[:, c * W:(c + 1) * W]

@@ -339,3 +339,40 @@ def test_a_rank_that_fails_surfaces_as_an_error_not_a_hang():
     assert results[1]["error"].startswith("planted")
     assert results[0]["error"] is not None, "rank 0 finished an exchange its peer never joined"
     assert results[0]["seconds"] < 60
+
+
+def _mismatch_worker(rank, world, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=20))
+    try:
+        from spark_gpt_b200.ep import ExpertParallelMoE
+        experts = E if rank == 0 else 2 * E     # rank 1 is configured differently
+        cfg = SimpleNamespace(hidden_size=H, num_experts=experts, num_experts_per_tok=K,
+                              moe_intermediate_size=I, norm_topk_prob=True)
+        m = ExpertParallelMoE(cfg, backend=OracleOps)
+        g = torch.Generator().manual_seed(rank)
+        with torch.no_grad():
+            for p in m.parameters():
+                p.copy_(torch.randn(p.shape, generator=g) * 0.1)
+        try:
+            m(rank_inputs(rank)[0])
+            results[rank] = None
+        except ValueError as e:
+            results[rank] = str(e)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ranks_with_different_layer_configurations_all_raise():
+    """A rank built with a different number of experts (so a different expert
+    -> rank map): every rank sees it in the counts exchange and raises the same
+    error before any row moves, instead of routing rows to experts that are
+    not there."""
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_mismatch_worker, args=(2, _free_port(), results), nprocs=2, join=True,
+                       start_method="spawn")
+    for rank in range(2):
+        assert results[rank] is not None and "disagree on the layer configuration" in results[rank]
