@@ -62,6 +62,7 @@ from . import ops
 from .moe import TopKRouter, _as_bf16, _extra_logit_grad, _require_cuda
 
 MAX_RANKS = 16  # the source-side sum over ranks reduces at most 16 rows per token
+P2P_HIDDEN_SIZES = (256, 512, 1024, 2048)  # b200moe_ep_p2p_reduce_return
 
 
 class CudaExpertOps:
@@ -588,6 +589,10 @@ class ExpertParallelMoE(nn.Module):
             raise ValueError(f"transport must be 'nccl' or 'p2p', got {transport!r}")
         if transport == "p2p" and backend is not CudaExpertOps:
             raise ValueError("the peer-memory transport runs the device kernels only")
+        if transport == "p2p" and config.hidden_size not in P2P_HIDDEN_SIZES:
+            raise ValueError(f"the peer-memory transport takes hidden sizes {P2P_HIDDEN_SIZES} "
+                             f"(its combine-and-return kernel); hidden {config.hidden_size} "
+                             f"runs with transport='nccl'")
         self.transport = transport
         self.chunks = chunks
         self.comm_sms = comm_sms

@@ -376,3 +376,25 @@ def test_ranks_with_different_layer_configurations_all_raise():
                        start_method="spawn")
     for rank in range(2):
         assert results[rank] is not None and "disagree on the layer configuration" in results[rank]
+
+
+def test_construction_rejects_what_a_transport_cannot_run():
+    """Checked on the host before any collective: experts that do not split
+    over the ranks, and the peer-memory transport at a hidden size its
+    combine-and-return kernel does not take."""
+    from datetime import timedelta
+    from spark_gpt_b200.ep import ExpertParallelMoE
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("gloo", rank=0, world_size=1, timeout=timedelta(seconds=20))
+    try:
+        cfg = SimpleNamespace(hidden_size=768, num_experts=8, num_experts_per_tok=2,
+                              moe_intermediate_size=384, norm_topk_prob=True)
+        with pytest.raises(ValueError, match="transport='nccl'"):
+            ExpertParallelMoE(cfg, transport="p2p")
+        m = ExpertParallelMoE(cfg, transport="nccl")
+        assert m.local_experts == 8
+        with pytest.raises(ValueError, match="transport must be"):
+            ExpertParallelMoE(cfg, transport="shm")
+    finally:
+        dist.destroy_process_group()
