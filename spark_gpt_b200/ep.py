@@ -315,7 +315,9 @@ class PeerTransport:
     def get(cls, group, H, k, device, slot=0):
         """The transport of (group, H, k) on `device`; `slot` tells apart the
         transports of a step's token chunks."""
-        key = (id(group) if group is not None else None, H, k, str(device), slot)
+        # by the group's name: an id() could be reused by a later group object
+        name = (group if group is not None else dist.group.WORLD).group_name
+        key = (name, H, k, str(device), slot)
         if key not in cls._cache:
             cls._cache[key] = cls(group, H, k, device)
         return cls._cache[key]

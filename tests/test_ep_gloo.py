@@ -398,3 +398,26 @@ def test_construction_rejects_what_a_transport_cannot_run():
             ExpertParallelMoE(cfg, transport="shm")
     finally:
         dist.destroy_process_group()
+
+
+def test_peer_transports_are_kept_per_group_shape_and_chunk():
+    """One transport per (group, H, k, device, chunk slot), found again by the
+    group's name; creating one allocates nothing (buffers come with the first
+    forward)."""
+    from datetime import timedelta
+    from spark_gpt_b200.ep import PeerTransport
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(_free_port())
+    dist.init_process_group("gloo", rank=0, world_size=1, timeout=timedelta(seconds=20))
+    try:
+        sub = dist.new_group([0])
+        a = PeerTransport.get(None, 1024, 8, "cpu")
+        assert PeerTransport.get(dist.group.WORLD, 1024, 8, "cpu") is a
+        assert PeerTransport.get(None, 1024, 8, "cpu", slot=1) is not a
+        assert PeerTransport.get(None, 2048, 8, "cpu") is not a
+        b = PeerTransport.get(sub, 1024, 8, "cpu")
+        assert b is not a and PeerTransport.get(sub, 1024, 8, "cpu") is b
+        assert a.cap == 0 and a.P == 1 and a.me == 0
+    finally:
+        PeerTransport._cache.clear()
+        dist.destroy_process_group()
