@@ -531,28 +531,34 @@ class _EPMoEP2PFn(torch.autograd.Function):
                     sent[c] = s1.record_event()
         ret, states, keep = [None] * C, [None] * C, []
         g_gu = g_d = None
-        overlap = backend_overlap(comm_sms) if comm_sms else nullcontext()
-        with overlap:
-            for c in range(C):
-                if sent[c] is not None:
-                    s0.wait_event(sent[c])
-                tr = transports[c]
-                tr.barrier()
-                dxs, dw_rows, states[c] = B.experts_dgrad(ectxs[c], tr.recv_rows[:n_recv[c]],
-                                                          top_k, dev, reduce=False)
-                if ectxs[c] is None:
-                    continue
-                if comm_sms:  # the return of chunk c beside the next GEMMs
-                    done = s0.record_event()
-                    with torch.cuda.stream(s1):
-                        s1.wait_event(done)
-                        ops.ep_p2p_reduce_return(dxs, ectxs[c][0], plans[c], tr.peer_back_rows,
-                                                 P, dw_rows=dw_rows, peer_dw=tr.peer_back_dw)
-                        ret[c] = s1.record_event()
-                    keep.append((dxs, dw_rows))
-                else:
-                    ops.ep_p2p_reduce_return(dxs, ectxs[c][0], plans[c], tr.peer_back_rows, P,
-                                             dw_rows=dw_rows, peer_dw=tr.peer_back_dw)
+
+        def beside_transfers(busy):
+            """The SM limit while a transfer may run on the copy stream."""
+            return backend_overlap(comm_sms) if (comm_sms and busy) else nullcontext()
+
+        for c in range(C):
+            if sent[c] is not None:
+                s0.wait_event(sent[c])
+            tr = transports[c]
+            tr.barrier()
+            # beside chunk c's dgrads: later chunks' sends and earlier chunks' returns
+            with beside_transfers(C > 1):
+                dxs, dw_rows, states[c] = B.experts_dgrad(
+                    ectxs[c], tr.recv_rows[:n_recv[c]], top_k, dev, reduce=False)
+            if ectxs[c] is None:
+                continue
+            if comm_sms:  # the return of chunk c beside the next GEMMs
+                done = s0.record_event()
+                with torch.cuda.stream(s1):
+                    s1.wait_event(done)
+                    ops.ep_p2p_reduce_return(dxs, ectxs[c][0], plans[c], tr.peer_back_rows,
+                                             P, dw_rows=dw_rows, peer_dw=tr.peer_back_dw)
+                    ret[c] = s1.record_event()
+                keep.append((dxs, dw_rows))
+            else:
+                ops.ep_p2p_reduce_return(dxs, ectxs[c][0], plans[c], tr.peer_back_rows, P,
+                                         dw_rows=dw_rows, peer_dw=tr.peer_back_dw)
+        with beside_transfers(True):  # the returns run beside the weight gradients
             for c in range(C):
                 g_gu, g_d = B.experts_wgrad(states[c], g_gu, g_d, E_loc, H, I, dev)
         d_rw = torch.empty(xb.shape[0], top_k, device=dev, dtype=torch.float32)
