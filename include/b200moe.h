@@ -135,6 +135,9 @@ int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* 
  * <= 262144 (e.g. T*k <= 16.7M slots at E = 64, <= 4.19M at E = 256); larger sizes are
  * rejected with B200MOE_ERR_INVALID_ARG.  The first call on a device looks up the array's
  * device address (cudaGetSymbolAddress); make that first call before any stream capture.
+ * The address is kept per device ordinal until the process exits, so resetting a device
+ * (cudaDeviceReset, or releasing and re-creating its primary context) after that first
+ * call is not supported: the next call would write through the old context's address.
  * All calls share the array: calls that overlap on the GPU (different streams, or different
  * host threads, without ordering between them) race and give wrong results.  No call
  * allocates or frees device memory. */

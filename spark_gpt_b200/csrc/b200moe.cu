@@ -531,7 +531,8 @@ int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* 
 // device array instead of caller-provided scratch.  1 MiB; every GPU that loads the library
 // keeps it until the process exits.  Host code must not pass the array's name to a kernel
 // (on the host it is only a stand-in, not a device address): its device address is looked
-// up once per device with cudaGetSymbolAddress and cached.
+// up once per device with cudaGetSymbolAddress and cached until exit (a device reset after
+// the first call is not supported: the cached address belongs to the old context).
 namespace {
 constexpr long long kNoAllocDispatchInts = 262144;
 static __device__ __align__(256) int g_noalloc_dispatch_counts[kNoAllocDispatchInts];

@@ -315,15 +315,24 @@ class PeerTransport:
     def get(cls, group, H, k, device, slot=0):
         """The transport of (group, H, k) on `device`; `slot` tells apart the
         transports of a step's token chunks."""
-        # by the group's name: an id() could be reused by a later group object
-        name = (group if group is not None else dist.group.WORLD).group_name
-        key = (name, H, k, str(device), slot)
-        if key not in cls._cache:
-            cls._cache[key] = cls(group, H, k, device)
-        return cls._cache[key]
+        # Keyed by the group's name, and checked against the group object
+        # itself: torch restarts its group-name counter when the process group
+        # is destroyed, so a group created after destroy_process_group and a
+        # new init can carry the name of a destroyed one.  A transport bound to
+        # another group object is dropped (with its peer mappings) and rebuilt.
+        pg = group if group is not None else dist.group.WORLD
+        key = (pg.group_name, H, k, str(device), slot)
+        cached = cls._cache.get(key)
+        if cached is not None and cached.pg is not pg:
+            cached.release()
+            cached = None
+        if cached is None:
+            cached = cls._cache[key] = cls(group, H, k, device)
+        return cached
 
     def __init__(self, group, H, k, device):
         self.group, self.H, self.k, self.device = group, H, k, torch.device(device)
+        self.pg = group if group is not None else dist.group.WORLD
         self.P = dist.get_world_size(group)
         self.me = dist.get_rank(group)
         self.cap = 0
@@ -374,6 +383,11 @@ class PeerTransport:
         self.epoch = 0
         torch.cuda.current_stream(self.device).synchronize()
         dist.barrier(group=self.group)  # every rank's flags are zero before the first barrier
+
+    def release(self):
+        """Drop the mapped buffers (the group they were mapped over is gone)."""
+        self._buf = self._handle = None
+        self.cap = 0
 
     def barrier(self):
         self.epoch += 1

@@ -2,7 +2,8 @@
 
 Run in a container that has the reference checkout (never on the GPU box):
 
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
+    (or SPARK_GPT_REFERENCE=PATH python tests/golden/make_golden.py)
 
 It imports ``train.py`` from the reference checkout (not copied), runs its
 ``SparseMoE`` (train.py:2325-2334) and ``global_load_balancing_loss``
@@ -121,11 +122,14 @@ def make_muon_golden(train, out_path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SPARK_GPT_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SPARK_GPT_REFERENCE"),
+                    help="reference checkout holding train.py (default: $SPARK_GPT_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "moe_golden.pt"))
     ap.add_argument("--muon-out", default=str(HERE / "muon_golden.pt"))
     ap.add_argument("--only", choices=["moe", "muon"], default=None)
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference checkout with --reference or SPARK_GPT_REFERENCE")
     sys.dont_write_bytecode = True
     sys.path.insert(0, args.reference)
     import train  # the reference module, imported in place

@@ -1,14 +1,15 @@
 """Drop-in check against the reference's own training code (CPU, structure only).
 
 The reference's ByteLM is built with sparse blocks and every block's mlp is
-swapped for spark_gpt_b200.SparseMoE (the edit INTEGRATION.md describes).  The
+swapped for spark_gpt_b200.SparseMoE (the two-line edit a trainer makes).  The
 reference's own build_optimizer (train.py:3056-3095), apply_mup_init
 (:2718-2745) and export_unfused_state_dict (:2540-2558) must then see the same
 tensors as with its own SparseMoE: the same parameter names, shapes and
 dtypes, the same optimizer groups, the same init draws under one seed and the
 same export keys.  The layer's forward needs a B200 and is covered by the GPU
-tests.  Skipped where the reference checkout is absent (it never travels to a
-GPU box).
+tests.  The reference checkout is named by the SPARK_GPT_REFERENCE environment
+variable (the directory holding its train.py); the test is skipped when the
+variable is unset or the checkout is absent (it never travels to a GPU box).
 """
 
 import os
@@ -19,11 +20,14 @@ from types import SimpleNamespace
 import pytest
 import torch
 
-REF = Path(os.environ.get("SPARK_GPT_REFERENCE", "/root/reference"))
+REF_ENV = os.environ.get("SPARK_GPT_REFERENCE")
+REF = Path(REF_ENV) if REF_ENV else None
 
 
 @pytest.fixture(scope="module")
 def train():
+    if REF is None:
+        pytest.skip("SPARK_GPT_REFERENCE is unset (path of the reference checkout)")
     if not (REF / "train.py").exists():
         pytest.skip("reference checkout not present")
     old = sys.dont_write_bytecode

@@ -421,3 +421,31 @@ def test_peer_transports_are_kept_per_group_shape_and_chunk():
     finally:
         PeerTransport._cache.clear()
         dist.destroy_process_group()
+
+
+def test_peer_transport_is_rebuilt_for_a_group_created_after_destroy():
+    """torch restarts its group-name counter in destroy_process_group, so the
+    WORLD group of a second init carries the name of the first one.  The cache
+    must not hand back the first group's transport (its peer mappings belong
+    to a destroyed group): get() returns a new transport bound to the new
+    group object."""
+    from datetime import timedelta
+    from spark_gpt_b200.ep import PeerTransport
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    try:
+        os.environ["MASTER_PORT"] = str(_free_port())
+        dist.init_process_group("gloo", rank=0, world_size=1, timeout=timedelta(seconds=20))
+        first = PeerTransport.get(None, 1024, 8, "cpu")
+        first_pg = dist.group.WORLD
+        dist.destroy_process_group()
+        os.environ["MASTER_PORT"] = str(_free_port())
+        dist.init_process_group("gloo", rank=0, world_size=1, timeout=timedelta(seconds=20))
+        assert dist.group.WORLD is not first_pg
+        second = PeerTransport.get(None, 1024, 8, "cpu")
+        assert second is not first
+        assert second.pg is dist.group.WORLD
+        assert PeerTransport.get(None, 1024, 8, "cpu") is second
+    finally:
+        PeerTransport._cache.clear()
+        if dist.is_initialized():
+            dist.destroy_process_group()
