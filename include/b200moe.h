@@ -55,6 +55,13 @@ const char* b200moe_last_error(void);
  * 4 = inconsistent sizes.  Kernels never trap; they record and return. */
 int b200moe_fault_read_and_clear(unsigned int* fault);
 
+/* Enqueues on `stream` an asynchronous copy of the device fault word into
+ * *dst (pinned host memory, or device memory); nothing is cleared and the
+ * host is not synchronised.  The layer ends every call with one, and checks
+ * the copy at its next call.  Replaces the reference's only failure signal on
+ * this path, a collective that times out (train.py:3561-3562, :3655). */
+int b200moe_fault_snapshot(unsigned int* dst, void* stream);
+
 /* Rows of the padded routed-row buffers: R + E*127 rounded up to 128. */
 long long b200moe_padded_rows(long long routed_rows, int num_experts);
 

@@ -5,8 +5,11 @@ TEST INFRASTRUCTURE ONLY.  This module is the parity checker: only ``tests/``,
 import it.  The product path (``spark_gpt_b200``) never imports it and has no CPU
 fallback.
 
-It restates, in plain fp32 torch-CPU arithmetic (dense math) and numpy (integer
-dispatch), the MoE path of spark-gpt's ``train.py``:
+It restates, in plain fp32 torch arithmetic (dense math) and numpy (integer
+dispatch), the MoE path of spark-gpt's ``train.py``.  The dense math runs on
+the device its inputs live on: the CPU for the golden and small cases, a GPU
+in fp32 (TF32 off) for the full-size parity cases, which would take the CPU
+minutes per case; the integer dispatch and top-k always run in numpy.
 
 * router                    train.py:2144-2158  (TopKRouter.forward)
 * dispatch sort/histogram   train.py:2271-2290  (Experts.forward)
@@ -23,12 +26,23 @@ Parity pin: ``tests/golden/make_golden.py`` runs the reference module itself on
 seeded inputs and stores its outputs under ``tests/golden/``;
 ``tests/test_oracle_golden.py`` checks this file against them.
 
-Top-k tie rule: the selected set is the k largest probabilities, ties broken
-toward the LOWER expert index, listed in (probability desc, index asc) order.
-torch CUDA's radix-select top-k takes the lowest indices among values equal to
-the k-th; torch CPU's partial sort does not (``topk([.5,1,1,1,.2], 2)`` gives
-indices [1, 3] on CPU).  The golden vectors carry no ties, so they pin the
-rule-independent part; the tie rule itself is stated here and in the tests.
+Top-k tie rule: the reference trains on CUDA, where ``torch.topk``
+(train.py:2147) is torch's radix-select top-k (torch 2.11.0 here; the
+reference tested 2.12): the selected set is the k largest probabilities with
+ties at the k-th value broken toward the LOWER expert index, and the k winners
+are listed in the order that torch's sort of the k results leaves them.  That
+sort is a 32-slot bitonic key/value sort (descending; unstable), run on the
+winners gathered as [values above the k-th, by ascending index] + [values
+equal to the k-th, by ascending index]; equal values come out in a fixed,
+shape-dependent order (all-equal rows: k=2 -> [1, 0], k=4 -> [1, 0, 2, 3],
+k=8 -> [7, 6, 4, 5, 1, 0, 2, 3]).  ``topk_cuda_order`` restates those three
+steps (torch sources: aten/src/ATen/native/cuda/TensorTopK.cu, gatherTopK;
+Sort.cu, sortKeyValueInplace -> SmallBitonicSort; SortUtils.cuh, bitonicSort
+and bitonicSwap).  It is pinned against ``torch.topk`` on a B200 by
+``tests/test_gpu_fullsize.py`` (tie-heavy bf16 logits at E = 8..256).  torch
+CPU's partial sort breaks ties differently (``topk([.5,1,1,1,.2], 2)`` gives
+indices [1, 3] on CPU); the golden vectors, made on the CPU, carry no ties,
+so they pin the rule-independent part.
 """
 
 from __future__ import annotations
@@ -51,17 +65,71 @@ def softmax_fp32(logits: torch.Tensor) -> torch.Tensor:
     return e / e.sum(dim=-1, keepdim=True)
 
 
-def topk_lowest_index(probs: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
-    """k largest entries per row, ties toward the lower index (see module doc).
+def _bitonic32_desc(keys: np.ndarray, vals: np.ndarray, valid: np.ndarray):
+    """torch's 32-slot bitonic key/value sort, descending, on every row at once
+    (SortUtils.cuh bitonicSort with bitonicSwap and a greater-than
+    comparator; 16 threads, each owning one compare-exchange per substep)."""
+    K, V, ok = keys.copy(), vals.copy(), valid.copy()
+    t = np.arange(16)
 
-    Returns (values fp32 (T,k), indices int64 (T,k)) in (value desc, index asc)
-    order.  Stand-in for ``torch.topk(router_probs, k)`` at train.py:2147.
-    """
-    p = probs.detach().float().numpy()
-    # stable sort of -p keeps the lower index first among equal values
+    def substep(stride, flags):
+        pos = 2 * t - (t & (stride - 1))
+        a, b = pos, pos + stride
+        ka, kb, oa, ob = K[:, a], K[:, b], ok[:, a], ok[:, b]
+        swap = ((ka > kb) & oa) | ~ob
+        x = swap == flags[None, :]
+        for arr in (K, V, ok):
+            va, vb = arr[:, a].copy(), arr[:, b].copy()
+            arr[:, a] = np.where(x, vb, va)
+            arr[:, b] = np.where(x, va, vb)
+
+    size = 2
+    while size < 32:
+        flags = (t & (size // 2)) != 0
+        stride = size // 2
+        while stride > 0:
+            substep(stride, flags)
+            stride //= 2
+        size *= 2
+    stride = 16
+    while stride > 0:
+        substep(stride, np.zeros(16, dtype=bool))
+        stride //= 2
+    return K, V
+
+
+def topk_cuda_order(probs: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """``torch.topk(probs, k)`` as torch's CUDA kernel computes it (see the
+    module doc): the k largest entries per row, ties at the k-th value toward
+    the lower index, listed in the order torch's bitonic sort of the gathered
+    winners leaves them.  Returns (values fp32 (T,k), indices int64 (T,k)) on
+    the device of ``probs``.  k <= 32."""
+    assert 1 <= k <= 32
+    p = probs.detach().float().cpu().numpy()
+    T = p.shape[0]
+    # the set: stable sort of -p keeps the lower index first among equal values
     order = np.argsort(-p, axis=-1, kind="stable")[:, :k]
     vals = np.take_along_axis(p, order, axis=-1)
-    return torch.from_numpy(vals.copy()), torch.from_numpy(order.astype(np.int64))
+    # gathered order: winners above the k-th value by index, then those equal to it
+    above = vals > vals[:, k - 1:k]
+    key = np.where(above, 0, 1).astype(np.int64) * (p.shape[1] + 1) + order
+    g = np.argsort(key, axis=-1, kind="stable")
+    gi = np.take_along_axis(order, g, axis=-1)
+    gv = np.take_along_axis(vals, g, axis=-1)
+    # rows without a tie among their winners sort to the unique descending
+    # order; only rows with one need the network
+    tie = np.nonzero((vals[:, 1:] == vals[:, :-1]).any(axis=-1))[0]
+    if tie.size:
+        n = tie.size
+        keys = np.zeros((n, 32), dtype=np.float32)
+        ids = np.zeros((n, 32), dtype=np.int64)
+        valid = np.zeros((n, 32), dtype=bool)
+        keys[:, :k], ids[:, :k], valid[:, :k] = gv[tie], gi[tie], True
+        K, V = _bitonic32_desc(keys, ids, valid)
+        vals[tie], order[tie] = K[:, :k], V[:, :k]
+    dev = probs.device
+    return (torch.from_numpy(np.ascontiguousarray(vals)).to(dev),
+            torch.from_numpy(np.ascontiguousarray(order.astype(np.int64))).to(dev))
 
 
 def router_select(logits: torch.Tensor, top_k: int, norm_topk_prob: bool = True):
@@ -72,7 +140,7 @@ def router_select(logits: torch.Tensor, top_k: int, norm_topk_prob: bool = True)
     dtype afterwards (train.py:2156).
     """
     probs = softmax_fp32(logits)
-    w, sel = topk_lowest_index(probs, top_k)
+    w, sel = topk_cuda_order(probs, top_k)
     if norm_topk_prob:
         w = w / w.sum(dim=-1, keepdim=True)
     return probs, w, sel
@@ -134,6 +202,8 @@ def dispatch(selected: torch.Tensor | np.ndarray, num_experts: int) -> Dispatch:
     Rows end up ordered by (expert, flat index t*k+s); the histogram counts
     every routed row, filler tokens included.
     """
+    if isinstance(selected, torch.Tensor):
+        selected = selected.detach().cpu()
     sel = np.asarray(selected, dtype=np.int64)
     top_k = sel.shape[-1]
     flat = sel.reshape(-1)
@@ -143,6 +213,13 @@ def dispatch(selected: torch.Tensor | np.ndarray, num_experts: int) -> Dispatch:
     counts = np.bincount(flat, minlength=num_experts).astype(np.int64)
     offsets = np.cumsum(counts).astype(np.int32)
     return Dispatch(perm, perm // top_k, inv, counts, offsets, top_k)
+
+
+def _index(a: np.ndarray, like: torch.Tensor) -> torch.Tensor:
+    """An integer index array as a tensor on the device of ``like`` (the dense
+    math runs on whichever device its inputs live on: CPU, or fp32 on a GPU
+    for the full-size parity cases)."""
+    return torch.from_numpy(a).to(like.device)
 
 
 def expert_ranges(offsets):
@@ -157,25 +234,25 @@ def expert_ranges(offsets):
 # --------------------------------------------------------------------------- #
 def gather_forward(x, d: Dispatch):
     """sorted_hidden = x[token_index] (train.py:2206)."""
-    return x.float()[torch.from_numpy(d.token_index)]
+    return x.float()[_index(d.token_index, x)]
 
 
 def gather_backward(d_rows, d: Dispatch):
     """dx[t] = sum_s d_rows[inverse[t*k+s]] (train.py:2209-2217)."""
-    rows = d_rows.float()[torch.from_numpy(d.inverse)]
+    rows = d_rows.float()[_index(d.inverse, d_rows)]
     return rows.view(-1, d.top_k, rows.shape[-1]).sum(dim=1)
 
 
 def combine_forward(y, sorted_weights, d: Dispatch):
     """out[t] = sum_s w[j] * y[j], j = inverse[t*k+s] (train.py:2229-2233)."""
     weighted = y.float() * sorted_weights.float().unsqueeze(-1)
-    rows = weighted[torch.from_numpy(d.inverse)]
+    rows = weighted[_index(d.inverse, weighted)]
     return rows.view(-1, d.top_k, rows.shape[-1]).sum(dim=1)
 
 
 def combine_backward(y, sorted_weights, d: Dispatch, d_out):
     """(dy, d_sorted_weights) of combine_forward (train.py:2235-2241)."""
-    g = d_out.float()[torch.from_numpy(d.token_index)]
+    g = d_out.float()[_index(d.token_index, d_out)]
     dy = g * sorted_weights.float().unsqueeze(-1)
     dw_sorted = (g * y.float()).sum(dim=-1)
     return dy, dw_sorted
@@ -279,10 +356,11 @@ def load_balancing_loss(logits_layers, selected_layers, valid_mask, *, num_exper
     if not logits_layers:
         z = torch.zeros(())
         return z, {}, []
-    soft = torch.zeros(num_experts)
-    hard = torch.zeros(num_experts)
-    ent = torch.zeros(())
-    rows = torch.zeros(())
+    dev = logits_layers[0].device
+    soft = torch.zeros(num_experts, device=dev)
+    hard = torch.zeros(num_experts, device=dev)
+    ent = torch.zeros((), device=dev)
+    rows = torch.zeros((), device=dev)
     for lg, sel in zip(logits_layers, selected_layers):
         s, h, e_, r = lb_partials(lg, sel, valid_mask, num_experts, top_k)
         soft, hard, ent, rows = soft + s, hard + h, ent + e_, rows + r
@@ -339,7 +417,7 @@ def layer_forward_backward(x, w_router, w_gu, w_down, top_k, d_out, *,
     if weights is not None:
         w_sel = weights.float()
     d = dispatch(sel, E)
-    sorted_w = w_sel.reshape(-1)[torch.from_numpy(d.permutation)]
+    sorted_w = w_sel.reshape(-1)[_index(d.permutation, w_sel)]
     xs = gather_forward(x, d)
     gu, h = swiglu_forward(xs, w_gu, d.offsets)
     y = grouped_linear_forward(h, w_down, d.offsets)
@@ -349,8 +427,8 @@ def layer_forward_backward(x, w_router, w_gu, w_down, top_k, d_out, *,
     dh, dw_down = grouped_linear_backward(h, w_down, dy, d.offsets)
     dxs, dw_gu, d_gu = swiglu_backward(xs, w_gu, gu, dh, d.offsets)
     dx_gather = gather_backward(dxs, d)
-    d_weights = torch.empty(d.permutation.size)
-    d_weights[torch.from_numpy(d.permutation)] = dw_sorted
+    d_weights = torch.empty(d.permutation.size, device=x.device)
+    d_weights[_index(d.permutation, x)] = dw_sorted
     d_weights = d_weights.view(-1, top_k)
     d_logits, dx_router, dw_r = router_backward(
         x, w_router, probs, w_sel, sel, d_weights, norm_topk_prob, d_logits_extra)

@@ -26,6 +26,7 @@ PROTOTYPES = {
     "b200moe_set_pair_gemm": (I, [I]),
     "b200moe_set_persistent_sm_limit": (I, [I]),
     "b200moe_fault_read_and_clear": (I, [POINTER(c_uint)]),
+    "b200moe_fault_snapshot": (I, [P, P]),
     "b200moe_padded_rows": (L, [L, I]),
     "b200moe_router_width": (I, [I]),
     "b200moe_cast_f32_to_bf16": (I, [P, L, L, L, P, P]),

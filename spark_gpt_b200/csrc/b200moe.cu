@@ -310,6 +310,14 @@ int b200moe_fault_read_and_clear(unsigned int* fault) {
   return B200MOE_OK;
 }
 
+int b200moe_fault_snapshot(unsigned int* dst, void* stream) {
+  REQUIRE(dst, "fault_snapshot: null pointer");
+  cudaError_t e = cudaMemcpyFromSymbolAsync(dst, g_fault, sizeof(unsigned int), 0,
+                                            cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "fault snapshot: %s", cudaGetErrorString(e));
+  return B200MOE_OK;
+}
+
 long long b200moe_padded_rows(long long routed_rows, int num_experts) {
   const long long r = routed_rows + static_cast<long long>(num_experts) * (kRowTile - 1);
   return (r + kRowTile - 1) / kRowTile * kRowTile;

@@ -125,6 +125,82 @@ struct GroupTokens {
   }
 };
 
+// The order torch.topk on CUDA lists its k winners in (the reference's router,
+// train.py:2147; torch 2.11: TensorTopK.cu gatherTopK, Sort.cu SmallBitonicSort,
+// SortUtils.cuh bitonicSort / bitonicSwap).  The winners are gathered as
+// [values above the k-th, by ascending index] + [values equal to the k-th, by
+// ascending index] into 32 slots (slots >= k invalid) and sorted by a bitonic
+// key/value network, descending and unstable, so equal values come out in a
+// fixed, shape-dependent order.  In: (sv, si) in (value desc, index asc) order,
+// as the selection produces them.  Out: the same winners in torch's order.
+// Only called for rows with a tie among their winners (without one the order
+// is the unique descending order); every index below is static.
+__device__ __forceinline__ void torch_topk_order(float (&sv)[kMaxTopK], int (&si)[kMaxTopK],
+                                                 int k) {
+  const float kth = sv[k - 1];
+  // rank of each winner in the gathered order
+  int rank[kMaxTopK];
+#pragma unroll
+  for (int i = 0; i < kMaxTopK; ++i) {
+    int r = 0;
+    const bool ai = sv[i] > kth;
+#pragma unroll
+    for (int j = 0; j < kMaxTopK; ++j) {
+      if (j >= k) continue;
+      const bool aj = sv[j] > kth;
+      // above-kth winners first, each group by ascending expert index
+      r += (aj && !ai) || (aj == ai && si[j] < si[i]) ? 1 : 0;
+    }
+    rank[i] = r;
+  }
+  float K[32];
+  int V[32];  // -1: an invalid slot (sorts to the end)
+#pragma unroll
+  for (int d = 0; d < 32; ++d) {
+    K[d] = 0.f;
+    V[d] = -1;
+  }
+#pragma unroll
+  for (int d = 0; d < kMaxTopK; ++d) {
+#pragma unroll
+    for (int i = 0; i < kMaxTopK; ++i) {
+      if (i < k && rank[i] == d) {
+        K[d] = sv[i];
+        V[d] = si[i];
+      }
+    }
+  }
+  // 16 "threads" t, each owning one compare-exchange (pos, pos + stride) per
+  // substep; swap when (K[a] > K[b] && a valid) || b invalid equals the
+  // substep's direction flag
+#pragma unroll
+  for (int size = 2; size <= 32; size *= 2) {
+#pragma unroll
+    for (int stride = size / 2; stride > 0; stride /= 2) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const bool flag = size < 32 && (t & (size / 2)) != 0;
+        const int a = 2 * t - (t & (stride - 1));
+        const int b = a + stride;
+        const bool sw = (K[a] > K[b] && V[a] >= 0) || V[b] < 0;
+        if (sw == flag) {
+          const float tk = K[a];
+          K[a] = K[b];
+          K[b] = tk;
+          const int tv = V[a];
+          V[a] = V[b];
+          V[b] = tv;
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kMaxTopK; ++r) {
+    sv[r] = K[r];
+    si[r] = V[r];
+  }
+}
+
 template <int L, typename LT>
 __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long ld, long long T,
                                        int E, int k, int norm, int vec,
@@ -173,6 +249,11 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
         si[r] = bi;
       }
     }
+    bool tie = false;
+#pragma unroll
+    for (int r = 0; r + 1 < kMaxTopK; ++r)
+      if (r + 1 < k) tie |= sv[r] == sv[r + 1];
+    if (tie) torch_topk_order(sv, si, k);
     float sum = 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxTopK; ++r)

@@ -14,11 +14,12 @@ register_autograd wires the backward op in.
 
 from __future__ import annotations
 
+from contextlib import nullcontext
 from typing import Optional
 
 import torch
 
-from . import ops
+from . import faults, ops
 
 BF16 = torch.bfloat16
 
@@ -64,6 +65,7 @@ def sparse_moe_fwd(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Ten
     variants read x rows inside the GEMM instead of materialising xs; on B200
     their per-row TMA requests ran slower than the streaming gather kernel,
     so this path materialises.)"""
+    faults.raise_pending(x.device)
     E = w_gate_up.shape[0]
     W = ops.router_width(E)
     xb = x if x.dtype == BF16 else x.to(BF16)
@@ -80,6 +82,7 @@ def sparse_moe_fwd(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Ten
     gu, h = ops.gate_up_fwd(xs, wgu, d)
     y = ops.down_fwd(h, wd, d, token_major=TOKEN_MAJOR)
     out = ops.combine(y, d, rw, token_major=TOKEN_MAJOR).to(x.dtype)
+    faults.snapshot(x.device)
     return (out, logits_buf, sel, wr, wgu, wd, rw, xs, gu, h, y, d.counts, d.offsets,
             d.pad_offsets, d.row_flat, d.inv_pad, d.tile_expert)
 
@@ -99,28 +102,43 @@ def _(x, w_router, w_gate_up, w_down, top_k, norm):
             e(T * top_k, dt=i32), e(cap // 128, dt=i32))
 
 
-@torch.library.custom_op("b200moe::sparse_moe_bwd", mutates_args=(), device_types="cuda")
-def sparse_moe_bwd(d_out: torch.Tensor, d_logits: Optional[torch.Tensor], xb: torch.Tensor,
-                   logits_buf: torch.Tensor, sel: torch.Tensor, wr: torch.Tensor,
-                   wgu: torch.Tensor, wd: torch.Tensor, rw: torch.Tensor, xs: torch.Tensor,
-                   gu: torch.Tensor, h: torch.Tensor, y: torch.Tensor, counts: torch.Tensor,
-                   offsets: torch.Tensor, pad_offsets: torch.Tensor, row_flat: torch.Tensor,
-                   inv_pad: torch.Tensor, tile_expert: torch.Tensor, top_k: int, norm: bool,
-                   num_experts: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
-                                              torch.Tensor]:
+def moe_backward(d_out, d_logits, xb, logits_buf, sel, wr, wgu, wd, rw, xs, gu, h, y,
+                 d: "ops.Dispatch", top_k: int, norm: bool, num_experts: int, grads=None):
+    """Router + experts + combine backward: combine backward -> down dgrad with
+    the SwiGLU backward in its epilogue -> both weight gradients -> gate_up
+    dgrad -> top-k/softmax backward -> router dgrad, folded into the
+    row-gather backward -> router wgrad (train.py:2331-2334 under autograd).
+
+    `grads` (optional, grad_sync.GradSync) supplies the fp32 destinations of
+    the three weight gradients, whether to accumulate into them, and two
+    callbacks: one when the expert gradients are final (it may start their
+    all-reduce on another stream and returns a context that limits the SMs of
+    the GEMM running beside it) and one when the router gradient is.  With
+    `grads` the gate_up weight gradient runs before the gate_up dgrad, so that
+    both expert gradients are final while the dgrad, the router backward and
+    the row-gather backward still run; without it the dgrad runs first (its
+    input, d_gu, is then partly still in L2)."""
     T = xb.shape[0]
     E = num_experts
     W = wr.shape[0]
-    if xb.data_ptr() % 16:
-        xb = xb.clone()
-    d = _dispatch_from(counts, offsets, pad_offsets, row_flat, inv_pad, tile_expert, T, top_k, E)
+    out_r = out_gu = out_d = None
+    acc = (False, False, False)
+    if grads is not None:
+        out_r, out_gu, out_d = grads.router, grads.gate_up, grads.down
+        acc = grads.accumulate
     d_out = d_out.to(BF16).contiguous()
     dy, d_rw = ops.combine_bwd(d_out, y, d, rw, token_major=TOKEN_MAJOR)
     d_gu = ops.down_dgrad_swiglu(dy, wd, gu, d)
-    g_down = ops.wgrad(dy, h, d, name="down_wgrad")
+    g_down = ops.wgrad(dy, h, d, name="down_wgrad", out=out_d, accumulate=acc[2])
     del dy
-    dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
-    g_gate_up = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad")
+    if grads is None:
+        dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
+        g_gate_up = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad")
+    else:
+        g_gate_up = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad", out=out_gu, accumulate=acc[1])
+        beside = grads.experts_ready()
+        with beside if beside is not None else nullcontext():
+            dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
     del d_gu
     extra = None
     if d_logits is not None:
@@ -133,8 +151,30 @@ def sparse_moe_bwd(d_out: torch.Tensor, d_logits: Optional[torch.Tensor], xb: to
     dl = ops.router_topk_bwd(logits_buf, sel, d_rw, extra, E, top_k, norm)
     dx_router = ops.router_dgrad(dl, wr)
     dx = ops.gather_rows_bwd(dxs, d, addend=dx_router, token_major=TOKEN_MAJOR)
-    g_router = ops.router_wgrad(xb, dl, E)
+    g_router = ops.router_wgrad(xb, dl, E, out=out_r, accumulate=acc[0])
+    if grads is not None:
+        grads.router_ready()
     return dx, g_router, g_gate_up, g_down
+
+
+@torch.library.custom_op("b200moe::sparse_moe_bwd", mutates_args=(), device_types="cuda")
+def sparse_moe_bwd(d_out: torch.Tensor, d_logits: Optional[torch.Tensor], xb: torch.Tensor,
+                   logits_buf: torch.Tensor, sel: torch.Tensor, wr: torch.Tensor,
+                   wgu: torch.Tensor, wd: torch.Tensor, rw: torch.Tensor, xs: torch.Tensor,
+                   gu: torch.Tensor, h: torch.Tensor, y: torch.Tensor, counts: torch.Tensor,
+                   offsets: torch.Tensor, pad_offsets: torch.Tensor, row_flat: torch.Tensor,
+                   inv_pad: torch.Tensor, tile_expert: torch.Tensor, top_k: int, norm: bool,
+                   num_experts: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor,
+                                              torch.Tensor]:
+    faults.raise_pending(xb.device)
+    if xb.data_ptr() % 16:
+        xb = xb.clone()
+    d = _dispatch_from(counts, offsets, pad_offsets, row_flat, inv_pad, tile_expert,
+                       xb.shape[0], top_k, num_experts)
+    res = moe_backward(d_out, d_logits, xb, logits_buf, sel, wr, wgu, wd, rw, xs, gu, h, y, d,
+                       top_k, norm, num_experts)
+    faults.snapshot(xb.device)
+    return res
 
 
 @sparse_moe_bwd.register_fake

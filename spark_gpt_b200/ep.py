@@ -58,7 +58,7 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
-from . import ops
+from . import faults, ops
 from .moe import TopKRouter, _as_bf16, _extra_logit_grad, _require_cuda
 
 MAX_RANKS = 16  # the source-side sum over ranks reduces at most 16 rows per token
@@ -157,10 +157,27 @@ class CudaExpertOps:
         return ops.cast_bf16(w)
 
     @staticmethod
+    def raise_pending(device):
+        """Raise the fault a kernel of an earlier call recorded (faults.py)."""
+        faults.raise_pending(device)
+
+    @staticmethod
+    def snapshot(device):
+        """Queue the copy of the device fault word that the next call checks."""
+        faults.snapshot(device)
+
+    @staticmethod
     def overlap(comm_sms):
         """Persistent kernels leave `comm_sms` SMs to the all-to-all beside them."""
         return ops.persistent_sm_limit(max(2, torch.cuda.get_device_properties(
             torch.cuda.current_device()).multi_processor_count - comm_sms))
+
+
+def _backend_call(backend, name, device):
+    """A backend's fault hook (raise_pending / snapshot), if it has one."""
+    fn = getattr(backend, name, None)
+    if fn is not None:
+        fn(device)
 
 
 def _layer_signature(num_experts, top_k, H, I, chunks):
@@ -200,6 +217,7 @@ class _EPMoEFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, backend, chunks,
                 comm_sms):
+        _backend_call(backend, "raise_pending", x.device)
         P = dist.get_world_size(group)
         E_loc = w_gu.shape[0]
         T, H = x.shape
@@ -250,6 +268,7 @@ class _EPMoEFn(torch.autograd.Function):
             rows, w = backs[c]
             w.wait()
             backend.reduce_rows(rows, plans[c], out=out[a:b])
+        _backend_call(backend, "snapshot", x.device)
         ctx.save_for_backward(xb, logits_buf, wr, sel)
         ctx.meta = (plans, ectxs, span, send_rows, recv_rows, group, backend, top_k, norm,
                     num_experts, E_loc, H, w_gu.shape[1] // 2, x.dtype, comm_sms)
@@ -263,6 +282,7 @@ class _EPMoEFn(torch.autograd.Function):
         xb, logits_buf, wr, sel = ctx.saved_tensors
         (plans, ectxs, span, send_rows, recv_rows, group, backend, top_k, norm, num_experts,
          E_loc, H, I, xdtype, comm_sms) = ctx.meta
+        _backend_call(backend, "raise_pending", xb.device)
         C = len(span)
         T = xb.shape[0]
         if d_out is None:
@@ -296,6 +316,7 @@ class _EPMoEFn(torch.autograd.Function):
         dx = xb.new_empty(T, H)
         for c, (a, b) in enumerate(span):
             backend.reduce_rows(rets[c][0][0], plans[c], addend=dx_router[a:b], out=dx[a:b])
+        _backend_call(backend, "snapshot", xb.device)
         return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None, None)
 
 
@@ -390,8 +411,11 @@ class PeerTransport:
         self.cap = 0
 
     def barrier(self):
+        """The bounded rank barrier of a phase, then the fault-word snapshot
+        that the next call checks (a peer that never arrives sets bit 1)."""
         self.epoch += 1
         ops.ep_barrier(self.peer_flags, self.flags, self.me, self.P, self.epoch)
+        faults.snapshot(self.device)
 
 
 _COPY_STREAMS: dict = {}
@@ -424,6 +448,7 @@ class _EPMoEP2PFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, transports,
                 comm_sms):
+        faults.raise_pending(x.device)
         tr0 = transports[0]
         P, me = tr0.P, tr0.me
         C = len(transports)
@@ -520,6 +545,7 @@ class _EPMoEP2PFn(torch.autograd.Function):
         xb, logits_buf, wr, sel = ctx.saved_tensors
         (span, sends, backs, plans, ectxs, n_recv, n_back, transports, top_k, norm, num_experts,
          E_loc, H, I, xdtype, comm_sms) = ctx.meta
+        faults.raise_pending(xb.device)
         B = CudaExpertOps
         C = len(span)
         P = transports[0].P
@@ -589,6 +615,7 @@ class _EPMoEP2PFn(torch.autograd.Function):
         for c, (a, b) in enumerate(span):
             ops.gather_rows_bwd(transports[c].back_rows[:n_back[c]], backs[c],
                                 addend=dx_router[a:b], out=dx[a:b])
+        faults.snapshot(dev)
         return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None)
 
 

@@ -20,8 +20,8 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from . import ops
-from .custom_ops import TOKEN_MAJOR, sparse_moe
+from . import faults, ops
+from .custom_ops import TOKEN_MAJOR, _dispatch_from, moe_backward, sparse_moe
 
 BF16 = torch.bfloat16
 
@@ -63,12 +63,14 @@ class _RouterFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w_router, top_k, norm):
         _require_cuda(x, w_router)
+        faults.raise_pending(x.device)
         E = w_router.shape[0]
         W = ops.router_width(E)
         xb = _as_bf16(x)
         wr = ops.cast_bf16(w_router, W)
         logits_buf = ops.router_logits(xb, wr)
         sel, rw = ops.router_topk(logits_buf, E, top_k, norm)
+        faults.snapshot(x.device)
         ctx.save_for_backward(xb, wr, logits_buf, sel)
         ctx.cfg = (E, W, top_k, norm, x.dtype)
         ctx.mark_non_differentiable(sel)
@@ -78,6 +80,7 @@ class _RouterFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, d_logits, d_rw, _d_sel):
         xb, wr, logits_buf, sel = ctx.saved_tensors
+        faults.raise_pending(xb.device)
         E, W, top_k, norm, xdtype = ctx.cfg
         T = xb.shape[0]
         if d_rw is None:
@@ -87,6 +90,7 @@ class _RouterFn(torch.autograd.Function):
         dl = ops.router_topk_bwd(logits_buf, sel, d_rw, extra, E, top_k, norm)
         dx = ops.router_dgrad(dl, wr)
         g_router = ops.router_wgrad(xb, dl, E) if ctx.needs_input_grad[1] else None
+        faults.snapshot(xb.device)
         return dx.to(xdtype), g_router, None, None
 
 
@@ -96,6 +100,7 @@ class _ExpertsFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, selected, weights, w_gate_up, w_down):
         _require_cuda(x, selected, weights, w_gate_up, w_down)
+        faults.raise_pending(x.device)
         E = w_gate_up.shape[0]
         xb = _as_bf16(x)
         rw = _as_bf16(weights)
@@ -107,6 +112,7 @@ class _ExpertsFn(torch.autograd.Function):
         gu, h = ops.gate_up_fwd(xs, wgu, d)
         y = ops.down_fwd(h, wd, d, token_major=TOKEN_MAJOR)
         out = ops.combine(y, d, rw, token_major=TOKEN_MAJOR)
+        faults.snapshot(x.device)
         ctx.save_for_backward(rw, wgu, wd, xs, gu, h, y)
         ctx.dispatch = d
         ctx.cfg = (x.dtype, weights.dtype)
@@ -115,6 +121,7 @@ class _ExpertsFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, d_out):
         rw, wgu, wd, xs, gu, h, y = ctx.saved_tensors
+        faults.raise_pending(xs.device)
         d = ctx.dispatch
         xdtype, wdtype = ctx.cfg
         dy, d_rw = ops.combine_bwd(_as_bf16(d_out), y, d, rw, token_major=TOKEN_MAJOR)
@@ -123,7 +130,45 @@ class _ExpertsFn(torch.autograd.Function):
         dxs = ops.gate_up_dgrad(d_gu, wgu, d, token_major=TOKEN_MAJOR)
         g_gu = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad") if ctx.needs_input_grad[3] else None
         dx = ops.gather_rows_bwd(dxs, d, token_major=TOKEN_MAJOR)
+        faults.snapshot(xs.device)
         return dx.to(xdtype), None, d_rw.to(wdtype), g_gu, g_down
+
+
+class _GradSyncMoEFn(torch.autograd.Function):
+    """The fused layer with its weight gradients handed to a GradSync
+    (grad_sync.py): written or accumulated into the sync's flat buffer, the
+    expert bucket's all-reduce started as soon as it is final.  The
+    parameters' .grad is that buffer, so no gradient is returned for them."""
+
+    @staticmethod
+    def forward(ctx, x, w_router, w_gate_up, w_down, top_k, norm, sync):
+        out, logits_buf, sel, *saved = torch.ops.b200moe.sparse_moe_fwd(
+            x, w_router, w_gate_up, w_down, top_k, norm)
+        ctx.save_for_backward(x, logits_buf, sel, *saved)
+        ctx.set_materialize_grads(False)
+        ctx.cfg = (top_k, norm, w_gate_up.shape[0], x.dtype)
+        ctx.sync = sync
+        ctx.mark_non_differentiable(sel)
+        E = w_gate_up.shape[0]
+        logits = logits_buf if logits_buf.shape[1] == E else logits_buf[:, :E]
+        return out, logits, sel
+
+    @staticmethod
+    def backward(ctx, d_out, d_logits, _d_sel):
+        x, logits_buf, sel, wr, wgu, wd, rw, xs, gu, h, y, counts, offsets, pad_offsets, \
+            row_flat, inv_pad, tile_expert = ctx.saved_tensors
+        top_k, norm, E, xdt = ctx.cfg
+        xb = _as_bf16(x)
+        faults.raise_pending(xb.device)
+        if d_out is None:
+            d_out = torch.zeros_like(xb)
+        d = _dispatch_from(counts, offsets, pad_offsets, row_flat, inv_pad, tile_expert,
+                           xb.shape[0], top_k, E)
+        grads = ctx.sync.begin()
+        dx, _, _, _ = moe_backward(d_out, d_logits, xb, logits_buf, sel, wr, wgu, wd, rw, xs, gu,
+                                   h, y, d, top_k, norm, E, grads=grads)
+        faults.snapshot(xb.device)
+        return dx.to(xdt), None, None, None, None, None, None
 
 
 class TopKRouter(nn.Module):
@@ -173,13 +218,19 @@ class SparseMoE(nn.Module):
         super().__init__()
         self.gate = TopKRouter(config)
         self.experts = Experts(config)
+        self._grad_sync = None  # set by grad_sync.GradSync
 
     def forward(self, hidden_states: torch.Tensor):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
         _require_cuda(x)
-        out, logits, sel = sparse_moe(
-            x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
-            self.gate.top_k, self.gate.norm_topk_prob)
+        if self._grad_sync is not None and torch.is_grad_enabled():
+            out, logits, sel = _GradSyncMoEFn.apply(
+                x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
+                self.gate.top_k, self.gate.norm_topk_prob, self._grad_sync)
+        else:
+            out, logits, sel = sparse_moe(
+                x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
+                self.gate.top_k, self.gate.norm_topk_prob)
         lead = shape[:-1]
         return out.view(shape), logits.view(*lead, logits.shape[-1]), sel.view(*lead, sel.shape[-1])

@@ -25,7 +25,7 @@ import ctypes
 
 import torch
 
-from . import _lib
+from . import _lib, faults
 from .ops import _launch, _p, _s
 
 NS_COEFFS = (3.4445, -4.7750, 2.0315)  # train.py:2899
@@ -74,16 +74,22 @@ def muon_step_packed(params, momentum_buffers, lr: float, momentum: float = 0.95
 
     momentum_buffers: one fp32 tensor per parameter (zeros at the first step),
     updated in place."""
+    dev = None
     for p, v in zip(params, momentum_buffers):
         if p.grad is None:
             continue
         if p.dim() != 3 or p.dtype != torch.float32 or not p.is_contiguous():
             raise RuntimeError("muon_step_packed: parameters must be contiguous fp32 (E, rows, cols)")
+        if dev is None:
+            dev = p.device
+            faults.raise_pending(dev)
         g = p.grad.float().contiguous()
         staged = momentum_stage(g, v, momentum, nesterov)
         rows, cols = p.shape[-2], p.shape[-1]
         lr_eff = lr * max(1, rows / cols) ** 0.5
         newton_schulz(staged, ns_steps, update=p.data, neg_lr=-lr_eff)
+    if dev is not None:
+        faults.snapshot(dev)
 
 
 class PackedExpertMuon(torch.optim.Optimizer):

@@ -19,8 +19,9 @@ MEAN_REL = 2e-3
 
 
 def rel_errors(a: torch.Tensor, b: torch.Tensor):
-    a = a.detach().double().cpu()
-    b = b.detach().double().cpu()
+    """In float64, on b's device (full-size cases compare on the GPU)."""
+    b = b.detach().double()
+    a = a.detach().double().to(b.device)
     diff = (a - b).abs()
     scale = b.abs().max().clamp_min(1e-30)
     return {

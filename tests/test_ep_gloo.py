@@ -449,3 +449,67 @@ def test_peer_transport_is_rebuilt_for_a_group_created_after_destroy():
         PeerTransport._cache.clear()
         if dist.is_initialized():
             dist.destroy_process_group()
+
+
+class FaultingOps(OracleOps):
+    """OracleOps whose fault hooks stand in for the device fault word: the
+    snapshot at the end of rank 1's first forward "lands" bit 1 (a bounded
+    wait that gave up), as b200moe_fault_snapshot would after a peer barrier
+    timed out."""
+
+    landed = 0
+    rank = 0
+
+    @classmethod
+    def snapshot(cls, device):
+        if cls.rank == 1:
+            cls.landed = 1
+
+    @classmethod
+    def raise_pending(cls, device):
+        from spark_gpt_b200.faults import DeviceFault
+        if cls.landed:
+            word, cls.landed = cls.landed, 0
+            raise DeviceFault(word, device)
+
+
+def _fault_worker(rank, world, port, results):
+    import time
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=5))
+    from spark_gpt_b200.ep import ExpertParallelMoE
+    FaultingOps.rank = rank
+    cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=K,
+                          moe_intermediate_size=I, norm_topk_prob=True)
+    m = ExpertParallelMoE(cfg, backend=FaultingOps)
+    w_r, w_gu, w_d = full_weights()
+    with torch.no_grad():
+        m.gate.weight.copy_(w_r)
+        m.experts.gate_up_proj.copy_(w_gu[m.expert_offset:m.expert_offset + m.local_experts])
+        m.experts.down_proj.copy_(w_d[m.expert_offset:m.expert_offset + m.local_experts])
+    x = rank_inputs(rank)[0]
+    m(x)  # the first step completes on both ranks; rank 1's snapshot records the fault
+    t0 = time.monotonic()
+    try:
+        m(x)
+        results[rank] = {"error": None, "type": None, "seconds": time.monotonic() - t0}
+    except Exception as e:  # noqa: BLE001 - the failure is the point
+        results[rank] = {"error": str(e), "type": type(e).__name__,
+                         "seconds": time.monotonic() - t0}
+
+
+def test_a_recorded_device_fault_raises_on_the_next_call():
+    """A fault word recorded during one step raises DeviceFault (a
+    RuntimeError naming the fault) at the start of that rank's next layer
+    call, before it issues any collective; its peer then gets an error from
+    the process group's short timeout instead of waiting for good."""
+    mgr = mp.get_context("spawn").Manager()
+    results = mgr.dict()
+    mp.start_processes(_fault_worker, args=(2, _free_port(), results), nprocs=2, join=True,
+                       start_method="spawn")
+    assert results[1]["type"] == "DeviceFault"
+    assert "bounded device wait gave up" in results[1]["error"]
+    assert results[0]["error"] is not None, "rank 0 finished an exchange its peer never joined"
+    assert results[0]["seconds"] < 60

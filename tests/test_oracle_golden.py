@@ -115,7 +115,7 @@ def test_config1_matches_reference(golden):
     assert torch.allclose(sums, c["input_sums"], rtol=1e-12, atol=1e-9), "RNG drifted"
     valid = torch.ones(T, dtype=torch.bool)
     logits = x @ w_r.t()
-    _, sel0 = O.topk_lowest_index(O.softmax_fp32(logits), k)
+    _, sel0 = O.topk_cuda_order(O.softmax_fp32(logits), k)
     aux, stats, g_aux = O.load_balancing_loss((logits,), (sel0,), valid, num_experts=E, top_k=k)
     res = O.layer_forward_backward(x, w_r, w_gu, w_d, k, probe, d_logits_extra=1e-3 * g_aux[0])
     assert torch.equal(res["selected"].to(torch.int8), c["selected"])
@@ -131,12 +131,34 @@ def test_config1_matches_reference(golden):
         assert abs(float(res[key].double().norm()) / float(c[key + "_norm"]) - 1) < 1e-5
 
 
-def test_topk_tie_rule_lowest_index():
+# torch.topk of an all-equal row on a B200 (torch 2.11.0): the order its bitonic
+# sort of the k winners leaves them in (the live comparison with torch.topk on
+# tie-heavy logits is tests/test_gpu_fullsize.py::test_topk_matches_torch_cuda)
+CUDA_ALL_TIE_ORDER = {
+    2: [1, 0], 3: [2, 1, 0], 4: [1, 0, 2, 3], 8: [7, 6, 4, 5, 1, 0, 2, 3],
+    16: [7, 6, 4, 5, 1, 0, 2, 3, 11, 10, 8, 9, 13, 12, 14, 15],
+}
+
+
+@pytest.mark.parametrize("k", sorted(CUDA_ALL_TIE_ORDER))
+def test_topk_cuda_order_of_an_all_tie_row(k):
+    for E in (k, 32, 256):
+        if E >= k:
+            _, i = O.topk_cuda_order(torch.ones(3, E), k)
+            assert i.tolist() == [CUDA_ALL_TIE_ORDER[k]] * 3
+
+
+def test_topk_tie_rule_set_and_order():
+    # the set: lowest indices among the values equal to the k-th
     p = torch.tensor([[0.5, 1.0, 1.0, 1.0, 0.2]])
-    v, i = O.topk_lowest_index(p, 2)
-    assert i.tolist() == [[1, 2]]
-    v, i = O.topk_lowest_index(torch.tensor([[0.1, 0.3, 0.3, 0.2]]), 3)
-    assert i.tolist() == [[1, 2, 3]]
+    v, i = O.topk_cuda_order(p, 2)
+    assert sorted(i[0].tolist()) == [1, 2] and i.tolist() == [[2, 1]]
+    v, i = O.topk_cuda_order(torch.tensor([[0.1, 0.3, 0.3, 0.2]]), 3)
+    assert i.tolist() == [[2, 1, 3]]
+    assert torch.allclose(v, torch.tensor([[0.3, 0.3, 0.2]]))
+    # no ties: plain descending order
+    v, i = O.topk_cuda_order(torch.tensor([[0.1, 0.4, 0.2, 0.3]]), 3)
+    assert i.tolist() == [[1, 3, 2]]
 
 
 def test_dispatch_empty_and_all_one_expert():
