@@ -92,8 +92,9 @@ def parse_args():
                     help="skip the Muon optimizer-step measurement of the expert tensors")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallel: token chunks pipelined against the exchanges")
-    ap.add_argument("--transport", default="p2p", choices=["nccl", "p2p"],
-                    help="expert parallel: NCCL all-to-all or peer-memory stores")
+    ap.add_argument("--transport", default="p2p_pipe", choices=["nccl", "p2p", "p2p_pipe"],
+                    help="expert parallel: NCCL all-to-all, peer-memory stores with group "
+                         "barriers, or peer-memory stores pipelined per source rank")
     ap.add_argument("--comm-sms", type=int, default=16,
                     help="SMs the persistent kernels leave to a transfer or collective "
                          "running beside them (expert-parallel exchanges, the data-parallel "
@@ -320,6 +321,9 @@ def config_block(args, c, n, grad_sync=False):
         elif args.transport == "p2p":
             par = (f"ep{n} (experts sharded, one row per (token, rank) stored into the owners' "
                    f"peer memory by the gather / combine kernels, bounded barriers)")
+        elif args.transport == "p2p_pipe":
+            par = (f"ep{n} (experts sharded, peer-memory stores pipelined per source rank: own "
+                   f"rows first, transfers beside the experts, point-to-point flags)")
         else:
             par = (f"ep{n} (experts sharded, NCCL all_to_all, one row per (token, rank), "
                    f"{args.ep_chunks} token chunks overlapped, {args.comm_sms} SMs left to NCCL)")
@@ -554,7 +558,7 @@ def ep_block(run, args, pk):
     if run.world == 1:
         return res
     from spark_gpt_b200.ep import ExpertParallelMoE
-    for transport in ("p2p", "nccl"):
+    for transport in ("p2p_pipe", "p2p", "nccl"):
         layer = ExpertParallelMoE(layer_cfg(c), chunks=1, comm_sms=args.comm_sms,
                                   transport=transport).to(run.dev)
         lo, hi = layer.expert_offset, layer.expert_offset + layer.local_experts

@@ -169,6 +169,32 @@ int b200moe_gather_rows(const void* x, const int* row_flat, const int* inv_pad,
 int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* addend, long long T,
                             int k, int H, int partial, void* dx, void* stream);
 
+/* ---- post-attention RMSNorm folded into the layer ------------------------ */
+/* Replaces the block's RMSNorm (train.py:162-170) applied to the layer's input
+ * (Block.forward, train.py:2370).
+ *
+ * x_n (T,H) bf16 = bf16(bf16(x * r) * bf16(w)), r = rsqrt(sum(x^2) * (1/H) + eps)
+ * per token, written to rstd (T) fp32; x bf16, w (H) fp32.  H % 8 == 0. */
+int b200moe_rmsnorm_fwd(const void* x, const float* w, long long T, int H, float eps, void* x_n,
+                        float* rstd, void* stream);
+
+/* Scratch of b200moe_gather_rows_bwd_rmsnorm: per-block partial rows of the
+ * norm weight's gradient. */
+long long b200moe_gather_rows_bwd_rmsnorm_scratch_bytes(long long T, int H);
+
+/* b200moe_gather_rows_bwd with the RMSNorm backward folded in: with
+ * g = bf16(sum_s dxs[inv_pad[t*k+s]] + addend[t]) (the norm output's gradient,
+ * not written), dx (T,H) bf16 = the norm input's gradient
+ * bf16(r * dy - (r^3/H) * x * <dy, x>), dy = bf16(g * bf16(w)), and dw (H) fp32
+ * = sum_t g * bf16(x * r) (deterministic order).  x, w, rstd as given to and
+ * returned by b200moe_rmsnorm_fwd.  Needs H % 32 == 0, H <= 4096 and
+ * H * k <= 18432 (the shared-memory row ring); other shapes return
+ * B200MOE_ERR_UNSUPPORTED. */
+int b200moe_gather_rows_bwd_rmsnorm(const void* dxs, const int* inv_pad, const void* addend,
+                                    const void* x, const float* w, const float* rstd, long long T,
+                                    int k, int H, int partial, void* dx, float* dw, void* scratch,
+                                    long long scratch_bytes, void* stream);
+
 /* ---- combine: _CombineTopK (train.py:2220-2241) -------------------------- */
 
 /* out (T,H) bf16 = sum_s bf16(y[inv_pad[t*k+s]] * weights[t,s]).  With
@@ -351,6 +377,37 @@ int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const voi
                                  const float* dw_rows, const int* plan, void* const* peer_rows,
                                  float* const* peer_dw, long long rows_cap, int H, int ranks,
                                  void* stream);
+
+/* Pipelined exchange (no counterpart in the reference, which is data-parallel
+ * only).  b200moe_ep_p2p_send with a destination filter: dest_mode 0 stores
+ * every row, 1 only the rows of this rank (`me`) itself, 2 only the other
+ * ranks' rows -- so a rank's own share is copied at once and the rest crosses
+ * NVLink beside the experts' compute. */
+int b200moe_ep_p2p_send_part(const void* src, const int* inv_send, const int* send_pad_offsets,
+                             const int* plan, void* const* peer_rows, long long T, int H,
+                             int ranks, const long long* selected, const void* weights, int k,
+                             int experts_per_rank, unsigned int* const* peer_meta, int me,
+                             int dest_mode, void* stream);
+
+/* b200moe_ep_p2p_reduce_return for one source's rows only: rows [0, n_rows)
+ * (inv_pad and weights indexed by that chunk) all came from rank `src`; row i
+ * goes to row back_base[src] + i of src's back rows (and back dw). */
+int b200moe_ep_p2p_reduce_return_src(const void* rows, const int* inv_pad, const void* weights,
+                                     int k, const float* dw_rows, const int* plan,
+                                     void* const* peer_rows, float* const* peer_dw,
+                                     long long n_rows, int src, int H, int ranks, void* stream);
+
+/* Point-to-point completion flags: each rank's flag area holds one u64 per
+ * (phase 1..4, source rank) at flags[phase * 64 + source].  ep_signal writes
+ * epoch into word (phase, me) of peer `dest` (every peer when dest < 0),
+ * system-scope release after this stream's earlier stores into that peer.
+ * ep_wait waits until word (phase, src) of my_flags -- every source's word
+ * when src < 0 -- reaches epoch (acquire); at most 4 s, then fault bit 1 and
+ * return.  ranks <= 32. */
+int b200moe_ep_signal(unsigned long long* const* peer_flags, int phase, int me, int ranks,
+                      int dest, unsigned long long epoch, void* stream);
+int b200moe_ep_wait(const unsigned long long* my_flags, int phase, int src, int ranks,
+                    unsigned long long epoch, void* stream);
 
 /* inv_back (T*P) int32: the row of this rank's back rows that holds owner r's
  * result for token t, or -1 (for b200moe_gather_rows_bwd with k = P). */

@@ -18,6 +18,7 @@ minutes per case; the integer dispatch and top-k always run in numpy.
 * down projection           train.py:2161-2192, 1746-1896
 * combine + its backward    train.py:2220-2241  (_CombineTopK)
 * load-balancing loss       train.py:3098-3197  (global_load_balancing_loss)
+* post-attention RMSNorm    train.py:162-170    (RMSNorm, applied at :2370)
 
 Every backward is written out explicitly (no autograd) so each GPU kernel can be
 checked against the matching oracle function on its own.
@@ -440,6 +441,44 @@ def layer_forward_backward(x, w_router, w_gu, w_down, top_k, d_out, *,
         "dx": dx_gather + dx_router, "dW_router": dw_r, "dW_gate_up": dw_gu,
         "dW_down": dw_down,
     }
+
+
+# --------------------------------------------------------------------------- #
+# post-attention RMSNorm (train.py:162-170, applied before the layer at :2370)
+# --------------------------------------------------------------------------- #
+def rmsnorm_forward(x, w, eps):
+    """RMSNorm.forward: r = rsqrt(mean(x^2) + eps) in fp32; for bf16 input the
+    result is bf16(bf16(x * r) * bf16(w)) (the cast back to the input dtype,
+    then the product with the weight cast to it).  Returns (x_n fp32 holding
+    the input dtype's values, r (T,))."""
+    xf = x.float()
+    r = torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    if x.dtype == torch.bfloat16:
+        y1 = (xf * r).to(torch.bfloat16).float()
+        x_n = (y1 * w.to(torch.bfloat16).float()).to(torch.bfloat16).float()
+    else:
+        x_n = (xf * r) * w.float()
+    return x_n, r.squeeze(-1)
+
+
+def rmsnorm_backward(x, w, r, g, bf16_io=True):
+    """(dx, dw) of rmsnorm_forward for the upstream gradient g, in fp32 (the
+    casts' backwards are identities): dy = g * w; dx = r * dy - (r^3 / H) *
+    x * <dy, x>; dw = sum_t g * (x * r), with x * r rounded to bf16 when the
+    input is bf16 (the value the weight multiplies)."""
+    xf = x.float()
+    g = g.float()
+    H = xf.shape[-1]
+    rr = r.float().unsqueeze(-1)
+    wv = w.to(torch.bfloat16).float() if bf16_io else w.float()
+    dy = g * wv
+    dot = (dy * xf).sum(dim=-1, keepdim=True)
+    dx = rr * dy - (rr ** 3 / H) * xf * dot
+    y1 = xf * rr
+    if bf16_io:
+        y1 = y1.to(torch.bfloat16).float()
+    dw = (g * y1).sum(dim=0)
+    return dx, dw
 
 
 def mup_std(hidden, base_dim=256, hidden_std=0.02, num_layers=12):

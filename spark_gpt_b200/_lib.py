@@ -42,6 +42,9 @@ PROTOTYPES = {
     "b200moe_gather_rows": (I, [P, P, P, P, L, I, I, I, L, P, P]),
     "b200moe_gather_rows_bwd": (I, [P, P, P, L, I, I, I, P, P]),
     "b200moe_combine_fwd": (I, [P, P, P, L, I, I, I, P, P]),
+    "b200moe_rmsnorm_fwd": (I, [P, P, L, I, c_float, P, P, P]),
+    "b200moe_gather_rows_bwd_rmsnorm_scratch_bytes": (L, [L, I]),
+    "b200moe_gather_rows_bwd_rmsnorm": (I, [P, P, P, P, P, P, L, I, I, I, P, P, P, L, P]),
     "b200moe_combine_bwd": (I, [P, P, P, P, P, P, I, L, I, I, L, I, P, P, P]),
     "b200moe_expert_gate_up_fwd": (I, [P, P, P, P, L, I, I, I, P, P, P]),
     "b200moe_expert_down_fwd": (I, [P, P, P, P, P, L, I, I, I, P, P]),
@@ -64,6 +67,10 @@ PROTOTYPES = {
     "b200moe_ep_p2p_reduce_return": (I, [P, P, P, I, P, P, P, P, L, I, I, P]),
     "b200moe_ep_p2p_back_inv": (I, [P, P, P, L, I, P, P]),
     "b200moe_ep_barrier": (I, [P, P, I, I, c_ulonglong, P]),
+    "b200moe_ep_p2p_send_part": (I, [P, P, P, P, P, L, I, I, P, P, I, I, P, I, I, P]),
+    "b200moe_ep_p2p_reduce_return_src": (I, [P, P, P, I, P, P, P, P, L, I, I, I, P]),
+    "b200moe_ep_signal": (I, [P, I, I, I, I, c_ulonglong, P]),
+    "b200moe_ep_wait": (I, [P, I, I, I, c_ulonglong, P]),
     "b200moe_muon_momentum": (I, [P, P, P, L, c_double, I, P]),
     "b200moe_newton_schulz_scratch_bytes": (L, [I, I, I]),
     "b200moe_newton_schulz": (I, [P, I, I, I, I, c_float, c_float, c_float, P, P, c_float, P, L,

@@ -255,25 +255,46 @@ int lanes_for(long long width) {
 // Returns -1 when one token's k rows do not fit a ring slot (caller falls back).
 constexpr int kReduceSmemPerBlock = 72 * 1024;  // three blocks per SM
 
+// Blocks of the row reduction: three per SM (kReduceSmemPerBlock), at most T.
+long long row_reduce_blocks(long long T, int sms) {
+  return std::min<long long>(3LL * sms, std::max<long long>(T, 1));
+}
+
 int launch_row_reduce(const __nv_bfloat16* rows, const int* inv_pad,
                       const __nv_bfloat16* weights, const __nv_bfloat16* addend, long long T,
                       int k, int H, __nv_bfloat16* out, cudaStream_t st, const char* what,
-                      bool partial) {
+                      bool partial, const NormBwd* norm = nullptr, long long* grid_out = nullptr) {
   const long long slot_bytes = 2LL * H * k;
   // slots: a multiple of the consumer-group count, at least one per group
   const int min_slots = kReduceGroups;
   if (slot_bytes * min_slots > kReduceSmemPerBlock || H % (8 * kReduceWarpsPerToken) != 0 ||
       k > kMaxTopK)
     return -1;
+  // vectors per lane of the fused norm backward: one per 1024 columns
+  const int nv = norm ? (H + 1023) / 1024 : 0;
+  if (nv > kNormVecsMax) return -1;
   int slots = kMaxReduceSlots;
   while (slots > min_slots && slots * slot_bytes > kReduceSmemPerBlock) slots -= kReduceGroups;
   const size_t smem = static_cast<size_t>(slots) * slot_bytes + 2 * slots * sizeof(uint64_t);
-  auto kern = partial && inv_pad ? row_reduce_kernel<true> : row_reduce_kernel<false>;
+  const bool skip = partial && inv_pad;
+  decltype(&row_reduce_kernel<false, 0>) kern;
+  switch (nv) {
+    case 0: kern = skip ? row_reduce_kernel<true, 0> : row_reduce_kernel<false, 0>; break;
+    case 1: kern = skip ? row_reduce_kernel<true, 1> : row_reduce_kernel<false, 1>; break;
+    case 2: kern = skip ? row_reduce_kernel<true, 2> : row_reduce_kernel<false, 2>; break;
+    default: kern = skip ? row_reduce_kernel<true, 4> : row_reduce_kernel<false, 4>; break;
+  }
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-  const long long grid = std::min<long long>(3LL * persistent_sms(), std::max<long long>(T, 1));
+  // resident blocks per SM: three (the plain reduction and H <= 1024), fewer
+  // when the fused norm backward holds more columns per lane
+  const int per_sm = nv <= 1 ? 3 : (nv == 2 ? 2 : 1);
+  const long long grid = std::min<long long>(row_reduce_blocks(T, persistent_sms()),
+                                             static_cast<long long>(per_sm) * persistent_sms());
+  if (grid_out) *grid_out = grid;
   kern<<<static_cast<int>(grid), kReduceThreads, smem, st>>>(rows, inv_pad, weights, addend, T, k,
-                                                              H, slots, out);
+                                                              H, slots, out,
+                                                              norm ? *norm : NormBwd{});
   return check_launch(what);
 }
 
@@ -431,6 +452,15 @@ int b200moe_router_dgrad(const void* d_logits, const void* w, long long T, int H
   p.out = dx;
   p.ld_out = H;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256 && g_pair_gemm) {
+    // K = W is one or a few 64-column blocks, so the tile's time is its epilogue: the
+    // two-CTA kernel writes it through shared memory with TMA stores (rows >= T are
+    // clipped by the tensor map; the rows of the tile past T load as zeros)
+    CUtensorMap to;
+    if ((rc = make_out_tmap(&to, dx, H, T, "router_dgrad dx"))) return rc;
+    return launch_gemm_pair<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, to, to, p, st,
+                                                                          "router_dgrad");
+  }
   if (BN == 256) return launch_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_dgrad");
   return launch_gemm<128, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "router_dgrad");
 }
@@ -661,6 +691,59 @@ int b200moe_gather_rows_bwd(const void* dxs, const int* inv_pad, const void* add
       static_cast<const __nv_bfloat16*>(dxs), inv_pad, static_cast<const __nv_bfloat16*>(addend), T,
       k, H, static_cast<__nv_bfloat16*>(dx));
   return check_launch("gather_rows_bwd");
+}
+
+int b200moe_rmsnorm_fwd(const void* x, const float* w, long long T, int H, float eps, void* x_n,
+                        float* rstd, void* stream) {
+  REQUIRE(x && w && x_n && rstd, "rmsnorm_fwd: null pointer");
+  REQUIRE(H % 8 == 0 && H > 0, "rmsnorm_fwd: H must be a positive multiple of 8");
+  REQUIRE(aligned16(x) && aligned16(x_n), "rmsnorm_fwd: x and x_n must be 16-byte aligned");
+  if (T == 0) return B200MOE_OK;
+  rmsnorm_fwd_kernel<<<grid_for(T, 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), w, T, H, eps, static_cast<__nv_bfloat16*>(x_n), rstd);
+  return check_launch("rmsnorm_fwd");
+}
+
+long long b200moe_gather_rows_bwd_rmsnorm_scratch_bytes(long long T, int H) {
+  return row_reduce_blocks(T, num_sms()) * kReduceGroups * static_cast<long long>(H) *
+         static_cast<long long>(sizeof(float));
+}
+
+int b200moe_gather_rows_bwd_rmsnorm(const void* dxs, const int* inv_pad, const void* addend,
+                                    const void* x, const float* w, const float* rstd, long long T,
+                                    int k, int H, int partial, void* dx, float* dw, void* scratch,
+                                    long long scratch_bytes, void* stream) {
+  REQUIRE(dxs && x && w && rstd && dx && dw && scratch, "gather_rows_bwd_rmsnorm: null pointer");
+  REQUIRE(H % 8 == 0 && H > 0 && k >= 1 && k <= kMaxTopK, "gather_rows_bwd_rmsnorm: bad shape");
+  REQUIRE(aligned16(dxs) && aligned16(x) && aligned16(dx) && (!addend || aligned16(addend)),
+          "gather_rows_bwd_rmsnorm: 16-byte aligned rows needed");
+  REQUIRE(scratch_bytes >= b200moe_gather_rows_bwd_rmsnorm_scratch_bytes(T, H),
+          "gather_rows_bwd_rmsnorm: scratch too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (T == 0) {
+    const cudaError_t e = cudaMemsetAsync(dw, 0, static_cast<size_t>(H) * sizeof(float), st);
+    if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "gather_rows_bwd_rmsnorm: %s", cudaGetErrorString(e));
+    return B200MOE_OK;
+  }
+  NormBwd nb;
+  nb.x = static_cast<const __nv_bfloat16*>(x);
+  nb.w = w;
+  nb.rstd = rstd;
+  nb.dw_part = static_cast<float*>(scratch);
+  nb.inv_h = 1.0f / static_cast<float>(H);
+  long long grid = 0;
+  int rc = launch_row_reduce(static_cast<const __nv_bfloat16*>(dxs), inv_pad, nullptr,
+                             static_cast<const __nv_bfloat16*>(addend), T, k, H,
+                             static_cast<__nv_bfloat16*>(dx), st, "gather_rows_bwd_rmsnorm",
+                             partial != 0, &nb, &grid);
+  if (rc < 0)
+    return fail(B200MOE_ERR_UNSUPPORTED,
+                "gather_rows_bwd_rmsnorm: H*k = %lld does not fit the shared-memory row ring "
+                "(H*k <= 18432, H <= 4096, H %% 32 == 0)", static_cast<long long>(H) * k);
+  if (rc) return rc;
+  sum_columns_kernel<<<(H + 255) / 256, 256, 0, st>>>(static_cast<const float*>(scratch),
+                                                      static_cast<int>(grid * kReduceGroups), H, dw);
+  return check_launch("rmsnorm_weight_grad");
 }
 
 int b200moe_combine_fwd(const void* y, const int* inv_pad, const void* weights, long long T, int k,
@@ -1175,6 +1258,79 @@ int b200moe_ep_p2p_send(const void* src, const int* inv_send, const int* send_pa
   return check_launch("ep_p2p_send");
 }
 
+int b200moe_ep_p2p_send_part(const void* src, const int* inv_send, const int* send_pad_offsets,
+                             const int* plan, void* const* peer_rows, long long T, int H,
+                             int ranks, const long long* selected, const void* weights, int k,
+                             int experts_per_rank, unsigned int* const* peer_meta, int me,
+                             int dest_mode, void* stream) {
+  REQUIRE(src && inv_send && send_pad_offsets && plan && peer_rows,
+          "ep_p2p_send_part: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= 32 && H % 8 == 0 && H > 0 && T >= 0 && me >= 0 && me < ranks,
+          "ep_p2p_send_part: need 1 <= ranks <= 32, 0 <= me < ranks, H % 8 == 0");
+  REQUIRE(dest_mode >= 0 && dest_mode <= 2, "ep_p2p_send_part: dest_mode must be 0, 1 or 2");
+  REQUIRE(selected == nullptr || (weights && peer_meta && k >= 1 && k <= 32 && experts_per_rank >= 1),
+          "ep_p2p_send_part: slot words need weights, peer_meta, 1 <= k <= 32");
+  if (T == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* sp = static_cast<const __nv_bfloat16*>(src);
+  auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
+  auto* wp = static_cast<const unsigned short*>(weights);
+  const int grid = grid_for(T, 8);
+  switch (H) {
+    case 1024: ep_p2p_send_kernel<4><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
+    case 2048: ep_p2p_send_kernel<8><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
+    default: ep_p2p_send_kernel<0><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
+  }
+  return check_launch("ep_p2p_send_part");
+}
+
+int b200moe_ep_p2p_reduce_return_src(const void* rows, const int* inv_pad, const void* weights,
+                                     int k, const float* dw_rows, const int* plan,
+                                     void* const* peer_rows, float* const* peer_dw,
+                                     long long n_rows, int src, int H, int ranks, void* stream) {
+  REQUIRE(rows && inv_pad && plan && peer_rows, "ep_p2p_reduce_return_src: null pointer");
+  REQUIRE(dw_rows == nullptr || peer_dw, "ep_p2p_reduce_return_src: dw needs peer_dw");
+  REQUIRE(k >= 1 && k <= 32 && ranks >= 1 && ranks <= kEpMaxRanks && n_rows >= 0 && src >= 0 &&
+              src < ranks,
+          "ep_p2p_reduce_return_src: bad k/ranks/src");
+  REQUIRE(H == 256 || H == 512 || H == 1024 || H == 2048,
+          "ep_p2p_reduce_return_src: H must be 256, 512, 1024 or 2048");
+  if (n_rows == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* yp = static_cast<const __nv_bfloat16*>(rows);
+  auto* wp = static_cast<const __nv_bfloat16*>(weights);
+  auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
+  switch (H) {
+    case 256: ep_p2p_reduce_return_kernel<1, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 512: ep_p2p_reduce_return_kernel<2, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    default: ep_p2p_reduce_return_kernel<4, 2><<<grid_for(2 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+  }
+  return check_launch("ep_p2p_reduce_return_src");
+}
+
+int b200moe_ep_signal(unsigned long long* const* peer_flags, int phase, int me, int ranks,
+                      int dest, unsigned long long epoch, void* stream) {
+  REQUIRE(peer_flags, "ep_signal: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= 32 && me >= 0 && me < ranks && epoch > 0 && phase >= 1 &&
+              phase < kEpFlagPhases && dest < ranks,
+          "ep_signal: bad args");
+  ep_signal_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(peer_flags, phase, me, ranks,
+                                                                    dest, epoch);
+  return check_launch("ep_signal");
+}
+
+int b200moe_ep_wait(const unsigned long long* my_flags, int phase, int src, int ranks,
+                    unsigned long long epoch, void* stream) {
+  REQUIRE(my_flags, "ep_wait: null pointer");
+  REQUIRE(ranks >= 1 && ranks <= 32 && epoch > 0 && phase >= 1 && phase < kEpFlagPhases &&
+              src < ranks,
+          "ep_wait: bad args");
+  ep_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(my_flags, phase, src, ranks,
+                                                                  epoch);
+  return check_launch("ep_wait");
+}
+
 int b200moe_ep_p2p_return(const void* rows, const float* dw_rows, const int* plan,
                           void* const* peer_rows, float* const* peer_dw, long long rows_cap,
                           int H, int k, int ranks, void* stream) {
@@ -1453,9 +1609,20 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
 }
 
 // ---------------------------------------------------------------- load balancing
+// Blocks of lb_partials_kernel: one token per lane group of 256 / lanes_for(E)
+// per block and round, capped at kLbMaxBlocks.
+static long long lb_blocks(long long T, int E) {
+  const long long groups = kLbThreads / lanes_for(E);
+  long long nblk = (T + groups - 1) / groups;
+  if (nblk > kLbMaxBlocks) nblk = kLbMaxBlocks;
+  return nblk > 0 ? nblk : 1;
+}
+
 long long b200moe_lb_scratch_bytes(long long T, int E) {
-  const long long nblk = (T + kLbTokensPerBlock - 1) / kLbTokensPerBlock;
-  return (nblk > 0 ? nblk : 1) * (2LL * E + 2) * static_cast<long long>(sizeof(float));
+  // per-block partial rows, then the level-one sums of kLbRowsPerSum rows each
+  const long long nblk = lb_blocks(T, E);
+  const long long level1 = (nblk + kLbRowsPerSum - 1) / kLbRowsPerSum;
+  return (nblk + level1) * (2LL * E + 2) * static_cast<long long>(sizeof(float));
 }
 
 int b200moe_lb_stats(const void* logits, long long ld, const long long* selected,
@@ -1467,7 +1634,7 @@ int b200moe_lb_stats(const void* logits, long long ld, const long long* selected
   REQUIRE(scratch_bytes >= b200moe_lb_scratch_bytes(T, E), "lb_stats: scratch too small");
   if (T == 0) return B200MOE_OK;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int nblk = static_cast<int>((T + kLbTokensPerBlock - 1) / kLbTokensPerBlock);
+  const int nblk = static_cast<int>(lb_blocks(T, E));
   float* part = static_cast<float*>(scratch);
   auto* lg = static_cast<const __nv_bfloat16*>(logits);
   B200_SWITCH_LANES(E, {
@@ -1476,9 +1643,13 @@ int b200moe_lb_stats(const void* logits, long long ld, const long long* selected
   })
   int rc = check_launch("lb_partials");
   if (rc) return rc;
-  lb_accumulate_kernel<<<1, 512, 16 * (2 * E + 2) * sizeof(float), st>>>(part, nblk, 2 * E + 2,
-                                                                          packed);
-  return check_launch("lb_accumulate");
+  const int W = 2 * E + 2;
+  const int level1 = (nblk + kLbRowsPerSum - 1) / kLbRowsPerSum;
+  float* sums = part + static_cast<long long>(nblk) * W;
+  lb_sum_rows_kernel<<<level1, 256, 0, st>>>(part, nblk, W, sums, 0);
+  if ((rc = check_launch("lb_sum_rows"))) return rc;
+  lb_sum_rows_kernel<<<1, 256, 0, st>>>(sums, level1, W, packed, 1);
+  return check_launch("lb_sum_rows");
 }
 
 int b200moe_lb_finalize(const float* packed, int E, int k, int world, float* aux, float* stats,

@@ -178,7 +178,8 @@ __global__ void ep_p2p_send_kernel(const __nv_bfloat16* __restrict__ src,
                                    __nv_bfloat16* const* __restrict__ peer_rows, long long T,
                                    int H, int P, const long long* __restrict__ sel,
                                    const unsigned short* __restrict__ w, int k, int E_loc,
-                                   unsigned* const* __restrict__ peer_meta) {
+                                   unsigned* const* __restrict__ peer_meta, int me = 0,
+                                   int dest_mode = 0) {
   __shared__ int base_s[kEpMaxRanks], pad_s[kEpMaxRanks];
   for (int r = threadIdx.x; r < P; r += blockDim.x) {
     base_s[r] = plan[1 + r];
@@ -206,6 +207,8 @@ __global__ void ep_p2p_send_kernel(const __nv_bfloat16* __restrict__ src,
     for (int r = 0; r < P; ++r) {
       const int p = __shfl_sync(0xffffffffu, pl, r);
       if (p < 0) continue;
+      // dest_mode 1: only this rank's own rows; 2: only the other ranks'
+      if ((dest_mode == 1 && r != me) || (dest_mode == 2 && r == me)) continue;
       const long long row = base_s[r] + (p - pad_s[r]);
       uint4* dst = reinterpret_cast<uint4*>(peer_rows[r] + row * H);
       if (VPL > 0) {
@@ -305,6 +308,43 @@ __global__ void ep_barrier_kernel(unsigned long long* const* __restrict__ peer_f
   }
 }
 
+// Point-to-point completion flags of the pipelined exchange.  Each rank's flag
+// area holds one word per (phase, source rank): flags[phase * kEpMaxRanks + s].
+// ep_signal: thread j writes `epoch` into peer j's word (phase, me) -- every
+// peer (dest < 0) or only peer `dest` -- with a system-scope release store, so
+// the rows this stream stored into that peer before are visible first.
+// ep_wait: waits until this rank's word (phase, src) -- or, with src < 0,
+// every source's word of the phase -- reaches `epoch` (acquire), at most
+// kWaitLimitNs; then it raises kFaultWaitTimeout and returns.
+constexpr int kEpFlagPhases = 5;  // 0: the group barrier, 1-4: the pipelined phases
+
+__global__ void ep_signal_kernel(unsigned long long* const* __restrict__ peer_flags, int phase,
+                                 int me, int P, int dest, unsigned long long epoch) {
+  const int j = threadIdx.x;
+  if (j >= P || (dest >= 0 && j != dest)) return;
+  __threadfence_system();
+  unsigned long long* dst = peer_flags[j] + phase * kEpMaxRanks + me;
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(dst), "l"(epoch) : "memory");
+}
+
+__global__ void ep_wait_kernel(const unsigned long long* __restrict__ my_flags, int phase, int src,
+                               int P, unsigned long long epoch) {
+  const int j = threadIdx.x;
+  if (j >= P || (src >= 0 && j != src)) return;
+  const unsigned long long* w = my_flags + phase * kEpMaxRanks + j;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(w) : "memory");
+    if (v >= epoch) break;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      raise_fault(kFaultWaitTimeout);
+      break;
+    }
+    __nanosleep(64);
+  }
+}
+
 }  // namespace b200moe
 
 namespace b200moe {
@@ -326,7 +366,8 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
                                             const float* __restrict__ dw,
                                             const int* __restrict__ plan,
                                             __nv_bfloat16* const* __restrict__ peer_rows,
-                                            float* const* __restrict__ peer_dw, int H, int P) {
+                                            float* const* __restrict__ peer_dw, int H, int P,
+                                            long long n_src_rows = 0, int src_fixed = -1) {
   static_assert(VPL > 0, "H in {256, 512, 1024, 2048}");
   __shared__ int rb_s[kEpMaxRanks + 1], bb_s[kEpMaxRanks];
   for (int r = threadIdx.x; r <= P; r += blockDim.x) {
@@ -334,7 +375,11 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
     if (r < P) bb_s[r] = plan[2 + 2 * P + r];
   }
   __syncthreads();
-  const long long n = plan[0] * static_cast<long long>(SPLIT);
+  // src_fixed >= 0: the rows are the n_src_rows rows received from that source
+  // alone (one per-source chunk of the owner's work), row i returning to row
+  // back_base[src] + i; otherwise all received rows, each to its source.
+  const long long n = (src_fixed >= 0 ? n_src_rows : static_cast<long long>(plan[0])) *
+                      static_cast<long long>(SPLIT);
   const int lane = threadIdx.x & 31;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   for (long long item = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -390,8 +435,14 @@ __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
       if (s1 >= 0) add_row(b, w1);
     }
     int src = 0;
-    while (src + 1 < P && rb_s[src + 1] <= i) ++src;
-    const long long row = bb_s[src] + (i - rb_s[src]);
+    long long row;
+    if (src_fixed >= 0) {
+      src = src_fixed;
+      row = bb_s[src] + i;
+    } else {
+      while (src + 1 < P && rb_s[src + 1] <= i) ++src;
+      row = bb_s[src] + (i - rb_s[src]);
+    }
     uint4* dst = reinterpret_cast<uint4*>(peer_rows[src] + row * H + col0);
 #pragma unroll
     for (int j = 0; j < VPL; ++j) {

@@ -440,14 +440,14 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
   }
 }
 // ---------------------------------------------------------------------------
-// Epilogue through shared memory + TMA stores: each warp owns a ring of four
+// Epilogue through shared memory + TMA stores: each warp owns a ring of kOutRing
 // 2 KB buffers; a 32-row x 32-column bf16 chunk of its rows is written there
 // (64-byte swizzle, conflict-free) and stored with one TMA tensor store, so
 // global writes are full, coalesced rows and asynchronous.  The output tensor
 // maps have a {32, 32} box and the 64-byte swizzle.
 // ---------------------------------------------------------------------------
 #ifndef B200MOE_OUT_RING
-#define B200MOE_OUT_RING 4  // 2 KB staging buffers per epilogue warp
+#define B200MOE_OUT_RING 2  // 2 KB staging buffers per epilogue warp (2: six operand stages fit)
 #endif
 constexpr int kOutRing = B200MOE_OUT_RING;
 

@@ -142,8 +142,10 @@ __device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* 
       if (pair_start[mid] <= pt) lo = mid; else hi = mid;
     }
     T.g = lo;
-    const int first_tile = __ldg(p.pad_offsets + lo) / 128;
-    const int ntiles = __ldg(p.pad_offsets + lo + 1) / 128 - first_tile;
+    // without pad_offsets: one group of m_tiles row tiles (the router dgrad)
+    const int first_tile = p.pad_offsets ? __ldg(p.pad_offsets + lo) / 128 : 0;
+    const int ntiles = p.pad_offsets ? __ldg(p.pad_offsets + lo + 1) / 128 - first_tile
+                                     : p.m_tiles;
     const int local = 2 * (pt - pair_start[lo]) + static_cast<int>(rank);
     half_ok = local < ntiles;
     T.m = first_tile + local;
@@ -221,7 +223,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int e = e0 + lane;
       int v = 0;
       if (e < p.num_groups) {
-        const int nt = (__ldg(p.pad_offsets + e + 1) - __ldg(p.pad_offsets + e)) / 128;
+        const int nt = p.pad_offsets
+                           ? (__ldg(p.pad_offsets + e + 1) - __ldg(p.pad_offsets + e)) / 128
+                           : p.m_tiles;
         v = (nt + 1) / 2;
       }
       int incl = v;

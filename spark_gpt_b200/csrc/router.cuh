@@ -14,6 +14,7 @@
 namespace b200moe {
 
 constexpr int kMaxTopK = 16;
+constexpr int kRouterThreads = 256;  // threads per block of the router kernels
 constexpr int kVpt = 8;  // logits per lane
 
 template <typename T>
@@ -131,73 +132,151 @@ struct GroupTokens {
 // [values above the k-th, by ascending index] + [values equal to the k-th, by
 // ascending index] into 32 slots (slots >= k invalid) and sorted by a bitonic
 // key/value network, descending and unstable, so equal values come out in a
-// fixed, shape-dependent order.  In: (sv, si) in (value desc, index asc) order,
-// as the selection produces them.  Out: the same winners in torch's order.
-// Only called for rows with a tie among their winners (without one the order
-// is the unique descending order); every index below is static.
-__device__ __forceinline__ void torch_topk_order(float (&sv)[kMaxTopK], int (&si)[kMaxTopK],
-                                                 int k) {
-  const float kth = sv[k - 1];
-  // rank of each winner in the gathered order
-  int rank[kMaxTopK];
+// fixed, shape-dependent order.
+//
+// Here the L lanes of a token's group hold the 32 slots (32/L each: slot s in
+// lane s / (32/L)) and run that network together: a compare-exchange whose
+// slots lie in one lane is done in registers, one across lanes by a shuffle
+// with the partner lane (both lanes evaluate the same comparison).  The
+// gathered order is built from the lanes' own experts: lane `sub` holds the
+// probabilities of experts 8*sub .. 8*sub+7 (`pe`, as the selection saw them),
+// so the winners above the k-th value in ascending index order are each
+// lane's such experts placed after those of the lower lanes (a prefix sum of
+// per-lane counts), and likewise the first k - above experts equal to it.
+// In: `kth` the k-th largest probability.  Out: this lane's slots (K, V) in
+// torch's order; V = -1 marks a slot >= k.  `sh_k`, `sh_v`: the group's
+// 32-slot shared-memory staging area.  Every lane of the warp must call it.
+template <int L>
+__device__ __forceinline__ int lane_exclusive_sum(int v, int sub) {
+  int incl = v;
 #pragma unroll
-  for (int i = 0; i < kMaxTopK; ++i) {
-    int r = 0;
-    const bool ai = sv[i] > kth;
-#pragma unroll
-    for (int j = 0; j < kMaxTopK; ++j) {
-      if (j >= k) continue;
-      const bool aj = sv[j] > kth;
-      // above-kth winners first, each group by ascending expert index
-      r += (aj && !ai) || (aj == ai && si[j] < si[i]) ? 1 : 0;
-    }
-    rank[i] = r;
+  for (int o = 1; o < L; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o, L);
+    if (sub >= o) incl += u;
   }
-  float K[32];
-  int V[32];  // -1: an invalid slot (sorts to the end)
+  return incl - v;
+}
+
+template <int L>
+__device__ __forceinline__ void stage_gathered_winners(const float (&pe)[kVpt], float kth, int k,
+                                                       int sub, float* sh_k, int* sh_v) {
+  int n_above = 0, n_equal = 0;
 #pragma unroll
-  for (int d = 0; d < 32; ++d) {
-    K[d] = 0.f;
-    V[d] = -1;
+  for (int j = 0; j < kVpt; ++j) {
+    n_above += pe[j] > kth ? 1 : 0;
+    n_equal += pe[j] == kth ? 1 : 0;
   }
+  int above_at = lane_exclusive_sum<L>(n_above, sub);
+  int equal_at = lane_exclusive_sum<L>(n_equal, sub);
+  const int above_total = __shfl_sync(0xffffffffu, above_at + n_above, L - 1, L);
+  equal_at += above_total;
 #pragma unroll
-  for (int d = 0; d < kMaxTopK; ++d) {
-#pragma unroll
-    for (int i = 0; i < kMaxTopK; ++i) {
-      if (i < k && rank[i] == d) {
-        K[d] = sv[i];
-        V[d] = si[i];
+  for (int j = 0; j < kVpt; ++j) {
+    if (pe[j] > kth) {
+      sh_k[above_at] = pe[j];
+      sh_v[above_at] = sub * kVpt + j;
+      ++above_at;
+    } else if (pe[j] == kth) {
+      if (equal_at < k) {
+        sh_k[equal_at] = pe[j];
+        sh_v[equal_at] = sub * kVpt + j;
       }
+      ++equal_at;
     }
   }
-  // 16 "threads" t, each owning one compare-exchange (pos, pos + stride) per
-  // substep; swap when (K[a] > K[b] && a valid) || b invalid equals the
-  // substep's direction flag
+  __syncwarp();
+}
+
+// The general case (any k <= 16, any L): 32 slots over the group's lanes.
+template <int L>
+__device__ __forceinline__ void torch_topk_order(const float (&pe)[kVpt], float kth, int k, int sub,
+                                                 float* sh_k, int* sh_v, float (&K)[32 / L],
+                                                 int (&V)[32 / L]) {
+  constexpr int SPL = 32 / L;  // slots per lane
+  stage_gathered_winners<L>(pe, kth, k, sub, sh_k, sh_v);
+#pragma unroll
+  for (int j = 0; j < SPL; ++j) {
+    const int d = sub * SPL + j;
+    K[j] = d < k ? sh_k[d] : 0.f;
+    V[j] = d < k ? sh_v[d] : -1;
+  }
+  __syncwarp();  // the staging area is free for the next token
+  // pair (a, a + stride) exchanges when (K[a] > K[b] && a valid) || b invalid
+  // equals the direction flag, which is bit `size` of a (false in the last merge)
 #pragma unroll
   for (int size = 2; size <= 32; size *= 2) {
 #pragma unroll
     for (int stride = size / 2; stride > 0; stride /= 2) {
+      if (stride >= SPL) {
+        const int lane_mask = stride / SPL;
 #pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const bool flag = size < 32 && (t & (size / 2)) != 0;
-        const int a = 2 * t - (t & (stride - 1));
-        const int b = a + stride;
-        const bool sw = (K[a] > K[b] && V[a] >= 0) || V[b] < 0;
-        if (sw == flag) {
-          const float tk = K[a];
-          K[a] = K[b];
-          K[b] = tk;
-          const int tv = V[a];
-          V[a] = V[b];
-          V[b] = tv;
+        for (int j = 0; j < SPL; ++j) {
+          const float ok = __shfl_xor_sync(0xffffffffu, K[j], lane_mask);
+          const int ov = __shfl_xor_sync(0xffffffffu, V[j], lane_mask);
+          const int slot = sub * SPL + j;
+          const bool lower = (slot & stride) == 0;
+          const bool flag = size < 32 && (slot & size) != 0;
+          const float ka = lower ? K[j] : ok, kb = lower ? ok : K[j];
+          const int va = lower ? V[j] : ov, vb = lower ? ov : V[j];
+          const bool sw = (ka > kb && va >= 0) || vb < 0;
+          if (sw == flag) {
+            K[j] = ok;
+            V[j] = ov;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < SPL; ++j) {
+          if ((j & stride) == 0) {
+            const bool flag = size < 32 && ((sub * SPL + j) & size) != 0;
+            const bool sw = (K[j] > K[j + stride] && V[j] >= 0) || V[j + stride] < 0;
+            if (sw == flag) {
+              const float tk = K[j];
+              K[j] = K[j + stride];
+              K[j + stride] = tk;
+              const int tv = V[j];
+              V[j] = V[j + stride];
+              V[j + stride] = tv;
+            }
+          }
         }
       }
     }
   }
+}
+
+// k a power of two and k <= L (every MoE shape here: top-2/4/8/16): the valid
+// slots never leave [0, k) -- an invalid slot always sorts behind a valid one,
+// and a pair (a, a + stride >= k) has direction flag bit `size` of a < k, i.e.
+// false, so it never exchanges -- so the network reduces to its substeps with
+// stride < k on lanes 0..k-1, one winner per lane.  Out: lane `sub` < k holds
+// slot `sub` (K, V).
+template <int L>
+__device__ __forceinline__ void torch_topk_order_small(const float (&pe)[kVpt], float kth, int k,
+                                                       int sub, float* sh_k, int* sh_v, float& K,
+                                                       int& V) {
+  stage_gathered_winners<L>(pe, kth, k, sub, sh_k, sh_v);
+  K = sub < k ? sh_k[sub] : 0.f;
+  V = sub < k ? sh_v[sub] : -1;
+  __syncwarp();  // the staging area is free for the next token
 #pragma unroll
-  for (int r = 0; r < kMaxTopK; ++r) {
-    sv[r] = K[r];
-    si[r] = V[r];
+  for (int size = 2; size <= 32; size *= 2) {
+#pragma unroll
+    for (int stride = size / 2; stride > 0; stride /= 2) {
+      if (stride < L) {  // (stride < k is checked at run time: k <= L)
+        const float ok = __shfl_xor_sync(0xffffffffu, K, stride);
+        const int ov = __shfl_xor_sync(0xffffffffu, V, stride);
+        if (stride < k) {
+          const bool lower = (sub & stride) == 0;
+          const bool flag = size < 32 && (sub & size) != 0;
+          const float ka = lower ? K : ok, kb = lower ? ok : K;
+          if ((ka > kb) == flag) {
+            K = ok;
+            V = ov;
+          }
+        }
+      }
+    }
   }
 }
 
@@ -206,6 +285,8 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
                                        int E, int k, int norm, int vec,
                                        long long* __restrict__ selected,
                                        __nv_bfloat16* __restrict__ weights) {
+  __shared__ float sh_k[kRouterThreads / L][32];  // tie-order staging, 32 slots per token group
+  __shared__ int sh_v[kRouterThreads / L][32];
   const int sub = threadIdx.x & (L - 1);
   const GroupTokens gt = GroupTokens::make<L>(T);
   for (long long rnd = 0; rnd < gt.rounds; ++rnd) {
@@ -216,8 +297,12 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
 #pragma unroll
     for (int j = 0; j < kVpt; ++j)
       if (sub * kVpt + j >= E) p[j] = -1.f;
+    float pe[kVpt];  // the probabilities as selected (entries >= E: -1)
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) pe[j] = p[j];
     float sv[kMaxTopK];
     int si[kMaxTopK];
+    float kth = 0.f;  // the k-th largest probability
 #pragma unroll
     for (int r = 0; r < kMaxTopK; ++r) {
       sv[r] = 0.f;
@@ -247,23 +332,52 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
           if (sub * kVpt + j == bi) p[j] = -3.f;
         sv[r] = bv;
         si[r] = bi;
+        if (r == k - 1) kth = bv;
       }
     }
-    bool tie = false;
-#pragma unroll
-    for (int r = 0; r + 1 < kMaxTopK; ++r)
-      if (r + 1 < k) tie |= sv[r] == sv[r + 1];
-    if (tie) torch_topk_order(sv, si, k);
     float sum = 0.f;
 #pragma unroll
     for (int r = 0; r < kMaxTopK; ++r)
       if (r < k) sum += sv[r];
-    if (valid) {
+    // winners with equal probabilities leave in torch's order; the network
+    // runs (warp-uniformly) only when some token of the warp has such a tie
+    bool tie = false;
 #pragma unroll
-      for (int r = 0; r < kMaxTopK; ++r) {
-        if (r < k && (r & (L - 1)) == sub) {
-          selected[t * k + r] = si[r];
-          weights[t * k + r] = __float2bfloat16_rn(norm ? sv[r] / sum : sv[r]);
+    for (int r = 0; r + 1 < kMaxTopK; ++r)
+      if (r + 1 < k) tie |= sv[r] == sv[r + 1];
+    if (!__any_sync(0xffffffffu, valid && tie)) {
+      if (valid) {
+#pragma unroll
+        for (int r = 0; r < kMaxTopK; ++r) {
+          if (r < k && (r & (L - 1)) == sub) {
+            selected[t * k + r] = si[r];
+            weights[t * k + r] = __float2bfloat16_rn(norm ? sv[r] / sum : sv[r]);
+          }
+        }
+      }
+    } else if ((k & (k - 1)) == 0 && k <= L) {
+      float K;
+      int V;
+      const int grp = threadIdx.x / L;
+      torch_topk_order_small<L>(pe, kth, k, sub, sh_k[grp], sh_v[grp], K, V);
+      if (valid && sub < k) {
+        selected[t * k + sub] = V;
+        weights[t * k + sub] = __float2bfloat16_rn(norm ? K / sum : K);
+      }
+    } else {
+      constexpr int SPL = 32 / L;
+      float K[SPL];
+      int V[SPL];
+      const int grp = threadIdx.x / L;
+      torch_topk_order<L>(pe, kth, k, sub, sh_k[grp], sh_v[grp], K, V);
+      if (valid) {
+#pragma unroll
+        for (int j = 0; j < SPL; ++j) {
+          const int d = sub * SPL + j;
+          if (d < k) {
+            selected[t * k + d] = V[j];
+            weights[t * k + d] = __float2bfloat16_rn(norm ? K[j] / sum : K[j]);
+          }
         }
       }
     }
@@ -380,7 +494,10 @@ __global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits,
 //   partials[b][2E]    entropy sum, partials[b][2E+1] valid rows
 // ---------------------------------------------------------------------------
 constexpr int kLbThreads = 256;
-constexpr int kLbTokensPerBlock = 256;
+// Blocks of the statistics kernel: one token per lane group and round, at
+// most 8 blocks per SM of B200's 148 (more tokens loop over the grid in
+// rounds), so the partials stay under 1184 rows.
+constexpr int kLbMaxBlocks = 148 * 8;
 
 template <int L>
 __global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
@@ -403,9 +520,10 @@ __global__ void lb_partials_kernel(const __nv_bfloat16* __restrict__ logits, lon
   for (int j = 0; j < kVpt; ++j) soft[j] = 0.f;
   float ent = 0.f, rows = 0.f;
   const float tiny = 1.17549435e-38f;
-  const long long t0 = static_cast<long long>(blockIdx.x) * kLbTokensPerBlock;
-  for (int i = grp; i < kLbTokensPerBlock; i += kGroups) {  // uniform trip count per warp
-    const long long t = t0 + i;
+  const long long stride = static_cast<long long>(gridDim.x) * kGroups;
+  const long long rounds = (T + stride - 1) / stride;  // the same for every warp
+  for (long long rnd = 0; rnd < rounds; ++rnd) {
+    const long long t = rnd * stride + static_cast<long long>(blockIdx.x) * kGroups + grp;
     const bool valid = t < T && (valid_mask == nullptr || valid_mask[t] != 0);
     float p[kVpt];
     softmax_group<L, true>(logits + (valid ? t : 0) * ld, E, sub, valid, vec != 0, p);
@@ -457,27 +575,25 @@ constexpr size_t lb_partials_smem(int E) {
          sizeof(float);
 }
 
-// packed[i] += sum over blocks of partials[b][i], fixed block order.
-// packed[i] += sum over blocks of partials[b][i]: warp w sums the blocks
-// b = w (mod warps) for its lane's columns, then the warps' sums are added in
-// warp order (a fixed order: deterministic).  Shared memory: warps * W floats.
-__global__ void lb_accumulate_kernel(const float* __restrict__ partials, int nblk, int W,
-                                     float* __restrict__ packed) {
-  extern __shared__ float acc_sh[];
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int nw = blockDim.x >> 5;
-  for (int i = lane; i < W; i += 32) {
-    float a = 0.f;
-#pragma unroll 4
-    for (int b = warp; b < nblk; b += nw) a += partials[static_cast<long long>(b) * W + i];
-    acc_sh[warp * W + i] = a;
-  }
-  __syncthreads();
+// Deterministic two-level sum of the per-block partial rows (W floats each):
+// block b of level one adds rows [kLbRowsPerSum*b, kLbRowsPerSum*(b+1)) in row
+// order into out[b]; level two (one block, accumulate = 1) adds those rows in
+// order into packed.  Each thread owns columns i = threadIdx.x + blockDim.x*j,
+// so a row is read coalesced and every sum has a fixed order.
+constexpr int kLbRowsPerSum = 32;
+
+__global__ void lb_sum_rows_kernel(const float* __restrict__ rows_in, int nrows, int W,
+                                   float* __restrict__ out, int accumulate) {
+  const int r0 = blockIdx.x * kLbRowsPerSum;
+  const int r1 = min(nrows, r0 + kLbRowsPerSum);
   for (int i = threadIdx.x; i < W; i += blockDim.x) {
     float a = 0.f;
-    for (int w = 0; w < nw; ++w) a += acc_sh[w * W + i];
-    packed[i] += a;
+#pragma unroll 8
+    for (int r = r0; r < r1; ++r) a += rows_in[static_cast<long long>(r) * W + i];
+    if (accumulate)
+      out[i] += a;
+    else
+      out[static_cast<long long>(blockIdx.x) * W + i] = a;
   }
 }
 

@@ -645,15 +645,77 @@ constexpr int kReduceGroups = 2;
 constexpr int kMaxReduceSlots = 4 * kReduceGroups;
 constexpr int kReduceThreads = 32 * (1 + kReduceGroups * kReduceWarpsPerToken);
 
+// The post-attention RMSNorm's backward fused into the gather backward
+// (NORM = true).  The reference normalises before the layer (train.py:162-170,
+// :2370): x_n = bf16(bf16(x * r) * bf16(w)), r = rsqrt(mean(x^2) + eps).  With
+// g = bf16(sum of the token's rows + addend) = dL/dx_n (the plain gather
+// backward's output, never written here):
+//   dy_j   = bf16(g_j * bf16(w_j))                 (d of the bf16 product)
+//   dx_j   = bf16(r * dy_j - (r^3 / H) * x_j * sum_i dy_i x_i)
+//   dw_j  += g_j * bf16(x_j * r)                   (summed over tokens)
+// The row-wide sum needs the whole row: the kReduceWarpsPerToken warps of a
+// group each add their columns, exchange the partial sums through shared
+// memory and a per-group mbarrier (bounded wait), and make a second pass over
+// the slot's rows (still in shared memory) to write dx.  Each group keeps its
+// columns' dw sums in registers and writes one partial row at the end.
+struct NormBwd {
+  const __nv_bfloat16* x;  // (T, H) the norm's input
+  const float* w;          // (H,) norm weight (fp32 master, used as bf16)
+  const float* rstd;       // (T,) r of the forward
+  float* dw_part;          // (gridDim.x * kReduceGroups, H) partial weight gradients
+  float inv_h;             // 1 / H
+};
+constexpr int kNormVecsMax = 4;  // 16-byte column vectors per lane: H <= 4096
+
+__device__ __forceinline__ void unpack8(const uint4 a, float (&f)[8]) {
+  f[0] = bf16_lo(a.x); f[1] = bf16_hi(a.x); f[2] = bf16_lo(a.y); f[3] = bf16_hi(a.y);
+  f[4] = bf16_lo(a.z); f[5] = bf16_hi(a.z); f[6] = bf16_lo(a.w); f[7] = bf16_hi(a.w);
+}
+
+// g = bf16(sum over the token's rows in the ring slot + addend row) for the 8
+// columns of 16-byte vector v (fp32 in slot order, one rounding)
+template <bool SKIP>
+__device__ __forceinline__ void norm_row_sum(const uint8_t* slot, uint32_t row_bytes, int k,
+                                             unsigned have, const uint4* arow, int v,
+                                             float (&g)[8]) {
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+  for (int r = 0; r < kMaxTopK; ++r) {
+    if (r < k && (!SKIP || ((have >> r) & 1u))) {
+      float f[8];
+      unpack8(*reinterpret_cast<const uint4*>(slot + r * row_bytes + v * 16), f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    }
+  }
+  if (arow) {
+    float f[8];
+    unpack8(__ldg(arow + v), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] += f[j];
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) g[j] = bf16_round(acc[j]);
+}
+
 // SKIP: some slots may have no row (inv_pad -1, the expert-parallel layouts);
 // without it every one of a token's k slots is copied and summed.
-template <bool SKIP>
-__global__ void __launch_bounds__(kReduceThreads)
+// NV > 0: the RMSNorm backward is fused in, with NV 16-byte column vectors per
+// lane (H <= NV * 1024); the plain reduction keeps three blocks per SM.
+template <bool SKIP, int NV = 0>
+__global__ void __launch_bounds__(kReduceThreads, NV == 0 ? 3 : (NV == 1 ? 3 : (NV == 2 ? 2 : 1)))
     row_reduce_kernel(const __nv_bfloat16* __restrict__ rows, const int* __restrict__ inv_pad,
                       const __nv_bfloat16* __restrict__ weights,
                       const __nv_bfloat16* __restrict__ addend, long long T, int k, int H,
-                      int slots, __nv_bfloat16* __restrict__ out) {
+                      int slots, __nv_bfloat16* __restrict__ out, NormBwd nb = NormBwd{}) {
   extern __shared__ __align__(128) uint8_t rsm[];
+  constexpr bool kNorm = NV > 0;
+  // NORM: per group, the row-dot partials of its warps (two token buffers) and
+  // the mbarrier their exchange completes on
+  __shared__ float red_sh[kReduceGroups][2][kReduceWarpsPerToken];
+  __shared__ __align__(8) uint64_t red_bar[kReduceGroups];
   const uint32_t row_bytes = static_cast<uint32_t>(H) * 2;
   const uint32_t slot_bytes = row_bytes * k;
   uint64_t* full = reinterpret_cast<uint64_t*>(rsm + static_cast<size_t>(slots) * slot_bytes);
@@ -670,6 +732,8 @@ __global__ void __launch_bounds__(kReduceThreads)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kReduceWarpsPerToken);
     }
+    if (kNorm)
+      for (int g = 0; g < kReduceGroups; ++g) mbar_init(&red_bar[g], kReduceWarpsPerToken);
     abort_flag_s = 0;
     fence_mbar_init();
   }
@@ -724,6 +788,22 @@ __global__ void __launch_bounds__(kReduceThreads)
     const int nvec = H / 8;
     const int v0 = part * (nvec / kReduceWarpsPerToken);
     const int v1 = (part + 1 == kReduceWarpsPerToken) ? nvec : v0 + nvec / kReduceWarpsPerToken;
+    // NORM: this lane's columns' weight (as bf16) and weight-gradient sums
+    constexpr bool NORM = NV > 0;
+    constexpr int kNormVecs = NV > 0 ? NV : 1;
+    float wb[kNormVecs][8], dw[kNormVecs][8];
+    if constexpr (NORM) {
+#pragma unroll
+      for (int q = 0; q < kNormVecs; ++q) {
+        const int v = v0 + lane + 32 * q;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          wb[q][j] = v < v1 ? bf16_round(nb.w[v * 8 + j]) : 0.f;
+          dw[q][j] = 0.f;
+        }
+      }
+    }
+    uint32_t red_phase = 0;
     for (long long i = group; i < n; i += kReduceGroups) {
       const int s = static_cast<int>(i % slots);
       const uint32_t ph = static_cast<uint32_t>((i / slots) & 1);
@@ -741,6 +821,59 @@ __global__ void __launch_bounds__(kReduceThreads)
       for (int r = 0; r < kMaxTopK; ++r)
         wr[r] = __float2bfloat162_rn(__shfl_sync(0xffffffffu, wv, r));
       const uint8_t* slot = rsm + static_cast<size_t>(s) * slot_bytes;
+      if constexpr (NORM) {
+        const float r = nb.rstd[t];
+        const uint4* xrow = reinterpret_cast<const uint4*>(nb.x + t * H);
+        const uint4* arow = addend ? reinterpret_cast<const uint4*>(addend + t * H) : nullptr;
+        float dot = 0.f;
+#pragma unroll
+        for (int q = 0; q < kNormVecs; ++q) {
+          const int v = v0 + lane + 32 * q;
+          if (v < v1) {
+            float g[8], xf[8];
+            norm_row_sum<SKIP>(slot, row_bytes, k, have, arow, v, g);
+            unpack8(__ldg(xrow + v), xf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              dot += bf16_round(g[j] * wb[q][j]) * xf[j];
+              dw[q][j] += g[j] * bf16_round(xf[j] * r);
+            }
+          }
+        }
+        // the group's row-wide sum: each warp's partial through shared memory
+        dot = warp_sum(dot);
+        const int buf = static_cast<int>(red_phase & 1u);
+        if (lane == 0) {
+          red_sh[group][buf][part] = dot;
+          mbar_arrive(&red_bar[group]);
+        }
+        if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[group], red_phase, abort_flag))) break;
+        red_phase ^= 1u;
+        float row_dot = 0.f;
+#pragma unroll
+        for (int w2 = 0; w2 < kReduceWarpsPerToken; ++w2) row_dot += red_sh[group][buf][w2];
+        const float c = r * r * r * nb.inv_h * row_dot;
+#pragma unroll
+        for (int q = 0; q < kNormVecs; ++q) {
+          const int v = v0 + lane + 32 * q;
+          if (v < v1) {
+            float g[8], xf[8];
+            norm_row_sum<SKIP>(slot, row_bytes, k, have, arow, v, g);
+            unpack8(__ldg(xrow + v), xf);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) g[j] = r * bf16_round(g[j] * wb[q][j]) - c * xf[j];
+            uint4 o;
+            o.x = pack_bf16x2(g[0], g[1]);
+            o.y = pack_bf16x2(g[2], g[3]);
+            o.z = pack_bf16x2(g[4], g[5]);
+            o.w = pack_bf16x2(g[6], g[7]);
+            reinterpret_cast<uint4*>(out + t * H)[v] = o;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        continue;
+      }
       for (int v = v0 + lane; v < v1; v += 32) {
         float acc[8];
 #pragma unroll
@@ -777,6 +910,71 @@ __global__ void __launch_bounds__(kReduceThreads)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if constexpr (NORM) {
+      float* dst = nb.dw_part + (static_cast<long long>(blockIdx.x) * kReduceGroups + group) * H;
+#pragma unroll
+      for (int q = 0; q < kNormVecs; ++q) {
+        const int v = v0 + lane + 32 * q;
+        if (v < v1) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) dst[v * 8 + j] = dw[q][j];
+        }
+      }
+    }
+  }
+}
+
+// out[c] = sum over rows r of part[r][c], r in order (deterministic column sums
+// of per-block partials: the RMSNorm weight gradient).
+__global__ void sum_columns_kernel(const float* __restrict__ part, int rows, int cols,
+                                   float* __restrict__ out) {
+  for (int c = blockIdx.x * blockDim.x + threadIdx.x; c < cols; c += gridDim.x * blockDim.x) {
+    float a = 0.f;
+#pragma unroll 8
+    for (int r = 0; r < rows; ++r) a += part[static_cast<long long>(r) * cols + c];
+    out[c] = a;
+  }
+}
+
+// x_n = bf16(bf16(x * r) * bf16(w)), r = rsqrt(mean(x^2) + eps) per token
+// (the reference's RMSNorm, train.py:162-170: the mean as the sum times 1/H).
+// Warp per token, 16-byte vectors; r is kept for the backward.
+__global__ void rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
+                                   const float* __restrict__ w, long long T, int H, float eps,
+                                   __nv_bfloat16* __restrict__ x_n, float* __restrict__ rstd) {
+  const int lane = threadIdx.x & 31;
+  const int nvec = H / 8;
+  const float inv_h = 1.0f / static_cast<float>(H);
+  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
+  for (long long t = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
+       t < T; t += warps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + t * H);
+    float ss = 0.f;
+    for (int v = lane; v < nvec; v += 32) {
+      const uint4 a = __ldg(xr + v);
+      const float f[8] = {bf16_lo(a.x), bf16_hi(a.x), bf16_lo(a.y), bf16_hi(a.y),
+                          bf16_lo(a.z), bf16_hi(a.z), bf16_lo(a.w), bf16_hi(a.w)};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss * inv_h + eps);
+    if (lane == 0) rstd[t] = r;
+    uint4* o = reinterpret_cast<uint4*>(x_n + t * H);
+    for (int v = lane; v < nvec; v += 32) {
+      const uint4 a = __ldg(xr + v);
+      const float f[8] = {bf16_lo(a.x), bf16_hi(a.x), bf16_lo(a.y), bf16_hi(a.y),
+                          bf16_lo(a.z), bf16_hi(a.z), bf16_lo(a.w), bf16_hi(a.w)};
+      float y[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) y[j] = bf16_round(f[j] * r) * bf16_round(w[v * 8 + j]);
+      uint4 q;
+      q.x = pack_bf16x2(y[0], y[1]);
+      q.y = pack_bf16x2(y[2], y[3]);
+      q.z = pack_bf16x2(y[4], y[5]);
+      q.w = pack_bf16x2(y[6], y[7]);
+      o[v] = q;
     }
   }
 }

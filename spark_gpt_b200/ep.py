@@ -62,6 +62,11 @@ from . import faults, ops
 from .moe import TopKRouter, _as_bf16, _extra_logit_grad, _require_cuda
 
 MAX_RANKS = 16  # the source-side sum over ranks reduces at most 16 rows per token
+# flag words of a peer-memory transport: the group barrier's (phase 0) and the
+# pipelined exchange's point-to-point completion flags, 64 words per phase
+# (include/b200moe.h, b200moe_ep_signal)
+FLAG_WORDS = 5 * 64
+PH_FWD_SEND, PH_FWD_RETURN, PH_BWD_SEND, PH_BWD_RETURN = 1, 2, 3, 4
 P2P_HIDDEN_SIZES = (256, 512, 1024, 2048)  # b200moe_ep_p2p_reduce_return
 
 
@@ -358,6 +363,7 @@ class PeerTransport:
         self.me = dist.get_rank(group)
         self.cap = 0
         self.epoch = 0
+        self.step = 0
         self._buf = None
 
     def ensure(self, tokens: int):
@@ -368,7 +374,8 @@ class PeerTransport:
         rows = self.P * cap
         H, k = self.H, self.k
         sizes = [("recv_rows", rows * H * 2), ("recv_meta", rows * k * 4),
-                 ("back_rows", rows * H * 2), ("back_dw", rows * k * 4), ("flags", 8 * 32)]
+                 ("back_rows", rows * H * 2), ("back_dw", rows * k * 4),
+                 ("flags", 8 * FLAG_WORDS)]
         offs, total = {}, 0
         for name, nbytes in sizes:
             offs[name] = total
@@ -391,7 +398,7 @@ class PeerTransport:
         self.recv_meta = view("recv_meta", torch.int32, (rows, k))
         self.back_rows = view("back_rows", torch.bfloat16, (rows, H))
         self.back_dw = view("back_dw", torch.float32, (rows, k))
-        self.flags = view("flags", torch.int64, (32,))
+        self.flags = view("flags", torch.int64, (FLAG_WORDS,))
         table = lambda name: torch.tensor([q + offs[name] for q in ptrs], dtype=torch.int64,
                                           device=self.device)
         self.peer_recv_rows = table("recv_rows")
@@ -402,6 +409,7 @@ class PeerTransport:
         self._buf, self._handle = buf, handle
         self.cap = cap
         self.epoch = 0
+        self.step = 0  # epoch of the pipelined exchange's point-to-point flags
         torch.cuda.current_stream(self.device).synchronize()
         dist.barrier(group=self.group)  # every rank's flags are zero before the first barrier
 
@@ -619,6 +627,151 @@ class _EPMoEP2PFn(torch.autograd.Function):
         return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None)
 
 
+class _EPMoEPipeFn(torch.autograd.Function):
+    """The expert-parallel layer over peer memory, pipelined per source rank.
+
+    Each owner works through the rows it receives one source rank at a time,
+    its own rows first (a local copy, available at once) and then the others
+    in the order they arrive (rank me-1, me-2, ...: each source stores to the
+    ranks after it first), while the rest of the rows still cross NVLink on a
+    copy stream; each source chunk's results go back to that source on the
+    copy stream while the next chunk computes.  Completion is signalled point
+    to point instead of by group barriers: a source sets a flag word at every
+    owner when all its rows are stored, an owner sets one at a source when
+    that source's results are stored (b200moe_ep_signal / _wait, bounded
+    waits).  The backward mirrors it with the upstream gradient rows; the
+    expert weight gradients accumulate over the chunks and run beside the
+    last returns.  Every buffer is reused only after the flag that orders it:
+    a source stores the backward's rows only after its forward has received
+    every owner's results, which each owner signals after it consumed that
+    source's forward rows (and likewise from one step to the next)."""
+
+    @staticmethod
+    def forward(ctx, x, w_router, w_gu, w_d, top_k, norm, num_experts, group, tr, comm_sms):
+        faults.raise_pending(x.device)
+        P, me = tr.P, tr.me
+        E_loc = w_gu.shape[0]
+        T, H = x.shape
+        B = CudaExpertOps
+        xb = _as_bf16(x)
+        dev = xb.device
+        s0 = torch.cuda.current_stream(dev)
+        s1 = _copy_stream(dev)
+        logits_buf, wr, sel, rw = B.router(xb, w_router, num_experts, top_k, norm)
+        dest, slots = ops.ep_route(sel, E_loc, P)
+        send = ops.dispatch(dest, P, partial=True)
+        sig = _layer_signature(num_experts, top_k, H, w_gu.shape[1] // 2, 1)
+        counts = torch.cat([send.counts, slots, torch.full((1,), T, device=dev, dtype=torch.int32),
+                            torch.tensor(sig, device=dev, dtype=torch.int32)])
+        W = 2 * P + 1
+        gathered = torch.empty(P, W + len(sig), device=dev, dtype=torch.int32)
+        dist.all_gather_into_tensor(gathered, counts, group=group)
+        host = gathered.cpu()  # the one host read of the step
+        _check_signatures(host[:, W:].tolist(), sig)
+        tr.ensure(int(host[:, 2 * P].max()))
+        rows_from = [int(v) for v in host[:, me]]
+        slots_from = [int(v) for v in host[:, P + me]]
+        base = [sum(rows_from[:s]) for s in range(P)]
+        n_back = int(host[me, :P].sum())
+        plan = ops.ep_p2p_plan(gathered, me, P)
+        tr.step += 1
+        step = tr.step
+        wgu_b, wd_b = B.cast(w_gu), B.cast(w_d)
+        # this rank's own rows: a local copy, ready for the first chunk
+        ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 1, sel, rw, E_loc,
+                             tr.peer_recv_meta)
+        ready = s0.record_event()
+        with torch.cuda.stream(s1):
+            s1.wait_event(ready)
+            ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 2, sel, rw, E_loc,
+                                 tr.peer_recv_meta)
+            ops.ep_signal(tr.peer_flags, PH_FWD_SEND, me, P, step)
+        order = [(me - j) % P for j in range(P)]
+        ectxs, keep = [None] * P, []
+        with backend_overlap(comm_sms) if (comm_sms and P > 1) else nullcontext():
+            for s in order:
+                if s != me:
+                    ops.ep_wait(tr.flags, PH_FWD_SEND, P, step, src=s)
+                n = rows_from[s]
+                rows = tr.recv_rows[base[s]:base[s] + n]
+                sel_loc, w_loc = B.unpack(tr.recv_meta[base[s]:base[s] + n])
+                y, ectxs[s] = B.experts_fwd(rows, sel_loc, w_loc, wgu_b, wd_b, slots_from[s],
+                                            combine=False)
+                done = s0.record_event()
+                with torch.cuda.stream(s1):
+                    s1.wait_event(done)
+                    if ectxs[s] is not None:
+                        ops.ep_p2p_reduce_return_src(y, ectxs[s][0], plan, tr.peer_back_rows, P,
+                                                     s, weights=w_loc)
+                    ops.ep_signal(tr.peer_flags, PH_FWD_RETURN, me, P, step, dest=s)
+                keep.append((y, w_loc))
+        s0.wait_stream(s1)
+        del keep
+        ops.ep_wait(tr.flags, PH_FWD_RETURN, P, step)
+        back = dataclasses.replace(send, inv_pad=ops.ep_p2p_back_inv(send, plan))
+        out = ops.gather_rows_bwd(tr.back_rows[:n_back], back)
+        faults.snapshot(dev)
+        ctx.save_for_backward(xb, logits_buf, wr, sel)
+        ctx.meta = (send, back, plan, ectxs, rows_from, base, n_back, tr, step, top_k, norm,
+                    num_experts, E_loc, H, w_gu.shape[1] // 2, x.dtype, comm_sms)
+        ctx.mark_non_differentiable(sel)
+        E = num_experts
+        logits = logits_buf if logits_buf.shape[1] == E else logits_buf[:, :E]
+        return out.to(x.dtype), logits, sel
+
+    @staticmethod
+    def backward(ctx, d_out, d_logits, _d_sel):
+        xb, logits_buf, wr, sel = ctx.saved_tensors
+        (send, back, plan, ectxs, rows_from, base, n_back, tr, step, top_k, norm, num_experts,
+         E_loc, H, I, xdtype, comm_sms) = ctx.meta
+        faults.raise_pending(xb.device)
+        B = CudaExpertOps
+        P, me = tr.P, tr.me
+        dev = xb.device
+        s0 = torch.cuda.current_stream(dev)
+        s1 = _copy_stream(dev)
+        if d_out is None:
+            d_out = torch.zeros(xb.shape, device=dev, dtype=xb.dtype)
+        d_out = _as_bf16(d_out)
+        ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 1)
+        ready = s0.record_event()
+        with torch.cuda.stream(s1):
+            s1.wait_event(ready)
+            ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 2)
+            ops.ep_signal(tr.peer_flags, PH_BWD_SEND, me, P, step)
+        order = [(me - j) % P for j in range(P)]
+        states, keep = [None] * P, []
+        with backend_overlap(comm_sms) if (comm_sms and P > 1) else nullcontext():
+            for s in order:
+                if s != me:
+                    ops.ep_wait(tr.flags, PH_BWD_SEND, P, step, src=s)
+                d_rows = tr.recv_rows[base[s]:base[s] + rows_from[s]]
+                dxs, dw_rows, states[s] = B.experts_dgrad(ectxs[s], d_rows, top_k, dev,
+                                                          reduce=False)
+                done = s0.record_event()
+                with torch.cuda.stream(s1):
+                    s1.wait_event(done)
+                    if ectxs[s] is not None:
+                        ops.ep_p2p_reduce_return_src(dxs, ectxs[s][0], plan, tr.peer_back_rows,
+                                                     P, s, dw_rows=dw_rows,
+                                                     peer_dw=tr.peer_back_dw)
+                    ops.ep_signal(tr.peer_flags, PH_BWD_RETURN, me, P, step, dest=s)
+                keep.append((dxs, dw_rows))
+            # the expert weight gradients run beside the last returns
+            g_gu = g_d = None
+            for s in order:
+                g_gu, g_d = B.experts_wgrad(states[s], g_gu, g_d, E_loc, H, I, dev)
+        s0.wait_stream(s1)
+        del keep
+        ops.ep_wait(tr.flags, PH_BWD_RETURN, P, step)
+        d_rw = ops.ep_weight_grad(tr.back_dw[:n_back], back, sel, E_loc)
+        dx_router, g_router = B.router_bwd(xb, wr, logits_buf, sel, d_rw, d_logits, num_experts,
+                                           top_k, norm)
+        dx = ops.gather_rows_bwd(tr.back_rows[:n_back], back, addend=dx_router)
+        faults.snapshot(dev)
+        return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None)
+
+
 def backend_overlap(comm_sms):
     return CudaExpertOps.overlap(comm_sms)
 
@@ -634,11 +787,11 @@ class ExpertParallelMoE(nn.Module):
     def __init__(self, config, group=None, backend=CudaExpertOps, chunks=1, comm_sms=0,
                  transport="nccl"):
         super().__init__()
-        if transport not in ("nccl", "p2p"):
-            raise ValueError(f"transport must be 'nccl' or 'p2p', got {transport!r}")
-        if transport == "p2p" and backend is not CudaExpertOps:
+        if transport not in ("nccl", "p2p", "p2p_pipe"):
+            raise ValueError(f"transport must be 'nccl', 'p2p' or 'p2p_pipe', got {transport!r}")
+        if transport.startswith("p2p") and backend is not CudaExpertOps:
             raise ValueError("the peer-memory transport runs the device kernels only")
-        if transport == "p2p" and config.hidden_size not in P2P_HIDDEN_SIZES:
+        if transport.startswith("p2p") and config.hidden_size not in P2P_HIDDEN_SIZES:
             raise ValueError(f"the peer-memory transport takes hidden sizes {P2P_HIDDEN_SIZES} "
                              f"(its combine-and-return kernel); hidden {config.hidden_size} "
                              f"runs with transport='nccl'")
@@ -711,7 +864,13 @@ class ExpertParallelMoE(nn.Module):
             _require_cuda(hidden_states)
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
-        if self.transport == "p2p":
+        if self.transport == "p2p_pipe":
+            tr = PeerTransport.get(self.group, shape[-1], self.gate.top_k, x.device)
+            out, logits, sel = _EPMoEPipeFn.apply(
+                x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
+                self.gate.top_k, self.gate.norm_topk_prob, self.num_experts, self.group, tr,
+                self.comm_sms)
+        elif self.transport == "p2p":
             trs = tuple(PeerTransport.get(self.group, shape[-1], self.gate.top_k, x.device, c)
                         for c in range(max(1, self.chunks)))
             out, logits, sel = _EPMoEP2PFn.apply(

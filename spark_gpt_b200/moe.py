@@ -21,7 +21,7 @@ import torch
 import torch.nn as nn
 
 from . import faults, ops
-from .custom_ops import TOKEN_MAJOR, _dispatch_from, moe_backward, sparse_moe
+from .custom_ops import TOKEN_MAJOR, _dispatch_from, moe_backward, norm_sparse_moe, sparse_moe
 
 BF16 = torch.bfloat16
 
@@ -232,5 +232,28 @@ class SparseMoE(nn.Module):
             out, logits, sel = sparse_moe(
                 x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
                 self.gate.top_k, self.gate.norm_topk_prob)
+        lead = shape[:-1]
+        return out.view(shape), logits.view(*lead, logits.shape[-1]), sel.view(*lead, sel.shape[-1])
+
+    def forward_normed(self, hidden_states: torch.Tensor, norm: nn.Module):
+        """self(norm(hidden_states)) with the block's post-attention RMSNorm
+        (train.py:162-170, applied at :2370) folded into the layer: one pass
+        writes the normalised rows and r per token, and the norm's backward
+        (its input and weight gradients) runs inside the row-gather backward,
+        so the normalised rows' gradient is never written.  `norm` is the
+        reference's RMSNorm module (its .weight and .eps); its weight gets its
+        gradient as with the unfused call.  Block.forward's
+        `self.mlp(self.post_attention_layernorm(h))` becomes
+        `self.mlp.forward_normed(h, self.post_attention_layernorm)`."""
+        shape = hidden_states.shape
+        x = hidden_states.reshape(-1, shape[-1])
+        _require_cuda(x)
+        H = shape[-1]
+        if H % 32 or H > 4096 or H * self.gate.top_k > 18432 or self._grad_sync is not None:
+            # beyond the fused backward's shared-memory row ring: the plain composition
+            return self(norm(hidden_states))
+        out, logits, sel = norm_sparse_moe(
+            x, norm.weight, norm.eps, self.gate.weight, self.experts.gate_up_proj,
+            self.experts.down_proj, self.gate.top_k, self.gate.norm_topk_prob)
         lead = shape[:-1]
         return out.view(shape), logits.view(*lead, logits.shape[-1]), sel.view(*lead, sel.shape[-1])

@@ -258,6 +258,35 @@ def gather_rows_bwd(dxs, d: Dispatch, addend=None, token_major=False, out=None) 
     return dx
 
 
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float):
+    """The reference's RMSNorm (train.py:162-170) on bf16 rows: (x_n bf16, r fp32 per row)."""
+    _check(x, BF16, "rmsnorm x")
+    T, H = x.shape
+    wf = w.detach().float().contiguous()
+    x_n = torch.empty_like(x)
+    rstd = torch.empty(T, device=x.device, dtype=torch.float32)
+    if T:
+        _launch("rmsnorm", 1, "b200moe_rmsnorm_fwd", _p(x), _p(wf), T, H, ctypes.c_float(eps),
+                _p(x_n), _p(rstd), _s(x))
+    return x_n, rstd
+
+
+def gather_rows_bwd_rmsnorm(dxs, d: Dispatch, addend, x, w, rstd, token_major=False):
+    """The gather backward (dxs rows summed per token + addend) with the
+    RMSNorm backward folded in: (d x (T, H) bf16, d w (H,) fp32)."""
+    H = dxs.shape[1]
+    dev = dxs.device
+    dx = torch.empty(d.num_tokens, H, device=dev, dtype=BF16)
+    dw = torch.empty(H, device=dev, dtype=torch.float32)
+    nbytes = int(_lib.value("b200moe_gather_rows_bwd_rmsnorm_scratch_bytes", d.num_tokens, H))
+    scratch = torch.empty(max(nbytes, 16), device=dev, dtype=torch.uint8)
+    _launch("gather_bwd", 2, "b200moe_gather_rows_bwd_rmsnorm", _p(dxs),
+            None if token_major else _p(d.inv_pad), _p(addend), _p(x), _p(w), _p(rstd),
+            d.num_tokens, d.top_k, H, int(d.partial), _p(dx), _p(dw), _p(scratch), nbytes,
+            _s(dxs))
+    return dx, dw
+
+
 def combine(y, d: Dispatch, weights, token_major=False) -> torch.Tensor:
     _check(weights, BF16, "combine weights")
     H = y.shape[1]
@@ -457,6 +486,41 @@ def ep_p2p_send(src, send: Dispatch, plan, peer_rows, selected=None, weights=Non
             _p(selected), _p(weights), k, experts_per_rank, _p(peer_meta), _s(src))
 
 
+def ep_p2p_send_part(src, send: Dispatch, plan, peer_rows, me: int, dest_mode: int,
+                     selected=None, weights=None, experts_per_rank: int = 1, peer_meta=None):
+    """ep_p2p_send restricted to this rank's own rows (dest_mode 1) or to the
+    other ranks' rows (dest_mode 2)."""
+    _check(src, BF16, "ep_p2p_send_part src")
+    T, H = src.shape
+    if T == 0:
+        return
+    k = selected.shape[1] if selected is not None else 0
+    _launch("ep_p2p_send", 1, "b200moe_ep_p2p_send_part", _p(src), _p(send.inv_pad),
+            _p(send.pad_offsets), _p(plan), _p(peer_rows), T, H, send.num_experts,
+            _p(selected), _p(weights), k, experts_per_rank, _p(peer_meta), me, dest_mode,
+            _s(src))
+
+
+def ep_p2p_reduce_return_src(rows, d: Dispatch, plan, peer_rows, ranks: int, src: int,
+                             weights=None, dw_rows=None, peer_dw=None):
+    """Owner side, one source's chunk: each of its rows' local-slot sum stored
+    into the source's back rows (and the routing-weight gradients into its back dw)."""
+    H = rows.shape[1]
+    _launch("ep_p2p_reduce_return", 1, "b200moe_ep_p2p_reduce_return_src", _p(rows),
+            _p(d.inv_pad), _p(weights), d.top_k, _p(dw_rows), _p(plan), _p(peer_rows),
+            _p(peer_dw), d.num_tokens, src, H, ranks, _s(rows))
+
+
+def ep_signal(peer_flags, phase: int, me: int, ranks: int, epoch: int, dest: int = -1):
+    _launch("ep_signal", 1, "b200moe_ep_signal", _p(peer_flags), phase, me, ranks, dest,
+            ctypes.c_ulonglong(epoch), _s(peer_flags))
+
+
+def ep_wait(my_flags, phase: int, ranks: int, epoch: int, src: int = -1):
+    _launch("ep_wait", 1, "b200moe_ep_wait", _p(my_flags), phase, src, ranks,
+            ctypes.c_ulonglong(epoch), _s(my_flags))
+
+
 def ep_p2p_return(rows, plan, peer_rows, ranks: int, dw_rows=None, peer_dw=None):
     """Store the owner's result rows (and routing-weight gradients) into the sources' back buffers."""
     _check(rows, BF16, "ep_p2p_return rows")
@@ -511,7 +575,7 @@ def lb_stats(logits, selected, valid_u8, num_experts, top_k, packed):
     nbytes = int(_lib.value("b200moe_lb_scratch_bytes", T, num_experts))
     scratch = torch.empty(nbytes, device=logits.device, dtype=torch.uint8)
     if T:
-        _launch("lb_stats", 2, "b200moe_lb_stats", _p(logits), logits.stride(0), _p(selected),
+        _launch("lb_stats", 3, "b200moe_lb_stats", _p(logits), logits.stride(0), _p(selected),
                 _p(valid_u8), T, num_experts, top_k, _p(packed), _p(scratch), nbytes,
                 _s(logits))
     return packed

@@ -12,7 +12,9 @@ It imports ``train.py`` from the reference checkout (not copied), runs its
 ``tests/golden/moe_golden.pt``; it also runs two ``MuonAdamWHybrid`` steps
 (train.py:2930-3024) on seeded packed expert tensors and the batched
 Newton-Schulz iteration (train.py:2877-2927) on its own, stored in
-``tests/golden/muon_golden.pt`` (``--only muon`` writes just that file).  The large config-1 case stores its inputs as a
+``tests/golden/muon_golden.pt`` (``--only muon`` writes just that file); and it runs
+the reference's ``RMSNorm`` (train.py:162-170) forward and backward into
+``tests/golden/norm_golden.pt`` (``--only norm``).  The large config-1 case stores its inputs as a
 seed plus checksums and keeps only slices and norms of the float outputs, so
 the fixture stays small.
 """
@@ -120,13 +122,39 @@ def make_muon_golden(train, out_path):
     print(f"wrote {out_path}: {', '.join(cases)}")
 
 
+def make_norm_golden(train, out_path):
+    """The reference's RMSNorm (train.py:162-170) forward and backward on
+    seeded inputs: bf16 rows (as under autocast) and an fp32 weight, in fp32
+    (autograd), plus the fp32-input case."""
+    cases = {}
+    for name, (T, H, seed, dtype) in {
+        "norm_bf16": (64, 256, 11, torch.bfloat16),
+        "norm_f32": (48, 768, 12, torch.float32),
+    }.items():
+        g = torch.Generator().manual_seed(seed)
+        x = (torch.randn(T, H, generator=g) * 2.0).to(dtype)
+        w = 1.0 + 0.1 * torch.randn(H, generator=g)
+        probe = torch.randn(T, H, generator=g).to(dtype)
+        norm = train.RMSNorm(H, eps=1e-6)
+        with torch.no_grad():
+            norm.weight.copy_(w)
+        xin = x.clone().requires_grad_(True)
+        out = norm(xin)
+        (out.float() * probe.float()).sum().backward()
+        cases[name] = {"x": x, "w": w, "eps": torch.tensor(1e-6), "probe": probe,
+                       "out": out.detach(), "dx": xin.grad, "dw": norm.weight.grad.clone()}
+    torch.save(cases, out_path)
+    print(f"wrote {out_path}: {', '.join(cases)}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPARK_GPT_REFERENCE"),
                     help="reference checkout holding train.py (default: $SPARK_GPT_REFERENCE)")
     ap.add_argument("--out", default=str(HERE / "moe_golden.pt"))
     ap.add_argument("--muon-out", default=str(HERE / "muon_golden.pt"))
-    ap.add_argument("--only", choices=["moe", "muon"], default=None)
+    ap.add_argument("--norm-out", default=str(HERE / "norm_golden.pt"))
+    ap.add_argument("--only", choices=["moe", "muon", "norm"], default=None)
     args = ap.parse_args()
     if not args.reference:
         ap.error("name the reference checkout with --reference or SPARK_GPT_REFERENCE")
@@ -135,6 +163,10 @@ def main():
     import train  # the reference module, imported in place
     import torch.nn.functional as F
 
+    if args.only in (None, "norm"):
+        make_norm_golden(train, args.norm_out)
+    if args.only == "norm":
+        return
     if args.only != "moe":
         make_muon_golden(train, args.muon_out)
     if args.only == "muon":

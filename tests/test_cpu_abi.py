@@ -45,7 +45,10 @@ def test_host_helpers(lib):
         [64, 64, 64, 128, 128, 256, 256]
     from spark_gpt_b200 import _lib
     assert _lib.value("b200moe_dispatch_scratch_bytes", 65536, 8, 64) == 128 * 64 * 4
-    assert _lib.value("b200moe_lb_scratch_bytes", 65536, 64) == 256 * 130 * 4
+    # load-balance statistics: 1184 block partial rows (8 per SM of 148), then
+    # 37 level-one sums of 32 rows, 2E+2 floats each
+    assert _lib.value("b200moe_lb_scratch_bytes", 65536, 64) == (1184 + 37) * 130 * 4
+    assert _lib.value("b200moe_lb_scratch_bytes", 100, 64) == (4 + 1) * 130 * 4  # 32 tokens a block
 
 
 def test_entry_points_reject_bad_arguments_without_touching_the_gpu(lib):

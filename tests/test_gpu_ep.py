@@ -26,10 +26,12 @@ T, H, E, K, I = 2048, 1024, 16, 4, 256
 # NCCL all-to-all: one send plan per step, exchanges in sequence; 3 token
 # chunks with the exchanges overlapped and 16 SMs left to NCCL; and the
 # peer-memory transport (rows stored straight into the other rank's buffers),
-# plain and with 2 token chunks pipelined on a copy stream
+# plain, with 2 token chunks pipelined on a copy stream, and pipelined per
+# source rank with point-to-point completion flags
 VARIANTS = {"plain": dict(chunks=1, comm_sms=0), "overlap": dict(chunks=3, comm_sms=16),
             "p2p": dict(transport="p2p"),
-            "p2p_overlap": dict(transport="p2p", chunks=2, comm_sms=16)}
+            "p2p_overlap": dict(transport="p2p", chunks=2, comm_sms=16),
+            "p2p_pipe": dict(transport="p2p_pipe", comm_sms=16)}
 
 
 def _cfg():
@@ -125,3 +127,6 @@ def test_expert_parallel_two_gpus_matches_single_gpu_layer():
         assert torch.equal(r["outs"]["plain"][2], r["outs"]["p2p"][2])
         assert torch.equal(r["outs"]["plain"][0], r["outs"]["p2p_overlap"][0])
         assert torch.equal(r["outs"]["plain"][2], r["outs"]["p2p_overlap"][2])
+        # per-source chunks: every row's result is computed as without them
+        assert torch.equal(r["outs"]["p2p"][0], r["outs"]["p2p_pipe"][0])
+        assert torch.equal(r["outs"]["p2p"][2], r["outs"]["p2p_pipe"][2])

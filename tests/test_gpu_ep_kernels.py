@@ -358,6 +358,162 @@ def test_emulated_peer_memory_transport_matches_single_gpu_layer(ops, T, H, E, k
     assert _lib.read_fault() == 0
 
 
+def _emulated_pipe(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
+    """The per-source pipelined peer-memory exchange (_EPMoEPipeFn's kernels)
+    with P ranks on one GPU, run phase by phase in one stream: every rank's
+    sends and send flags first, then each owner's source chunks (own rows
+    first, then me-1, me-2, ...), each returned with its own flag, then each
+    source's wait for all owners' flags and its sum over them; the same for
+    the backward.  The point-to-point flags live in per-rank device tensors
+    reached through a peer table, as over NVLink."""
+    from spark_gpt_b200.ep import (CudaExpertOps as B, FLAG_WORDS, PH_BWD_RETURN,
+                                   PH_BWD_SEND, PH_FWD_RETURN, PH_FWD_SEND)
+    E = w_gu.shape[0]
+    E_loc = E // P
+    I, H = w_d.shape[2], w_d.shape[1]
+    T = x_list[0].shape[0]
+    cap = P * T
+    bufs = [SimpleNamespace(recv_rows=torch.zeros(cap, H, device=DEV, dtype=torch.bfloat16),
+                            recv_meta=torch.zeros(cap, k, device=DEV, dtype=torch.int32),
+                            back_rows=torch.zeros(cap, H, device=DEV, dtype=torch.bfloat16),
+                            back_dw=torch.zeros(cap, k, device=DEV, dtype=torch.float32),
+                            flags=torch.zeros(FLAG_WORDS, device=DEV, dtype=torch.int64))
+            for _ in range(P)]
+    table = lambda name: torch.tensor([getattr(b, name).data_ptr() for b in bufs],
+                                      dtype=torch.int64, device=DEV)
+    peers = {n: table(n) for n in ("recv_rows", "recv_meta", "back_rows", "back_dw", "flags")}
+    step = 1
+    st = []
+    for r in range(P):
+        logits_buf, wr, sel, rw = B.router(x_list[r], w_r, E, k, True)
+        dest, slots = ops.ep_route(sel, E_loc, P)
+        send = ops.dispatch(dest, P, partial=True)
+        st.append(SimpleNamespace(logits_buf=logits_buf, wr=wr, sel=sel, rw=rw, send=send,
+                                  counts=torch.cat([send.counts, slots])))
+    gathered = torch.stack([s.counts for s in st])            # (P, 2P)
+    host = gathered.cpu()
+    for r in range(P):
+        st[r].plan = ops.ep_p2p_plan(gathered, r, P)
+        for mode in (1, 2):
+            ops.ep_p2p_send_part(x_list[r], st[r].send, st[r].plan, peers["recv_rows"], r, mode,
+                                 st[r].sel, st[r].rw, E_loc, peers["recv_meta"])
+        ops.ep_signal(peers["flags"], PH_FWD_SEND, r, P, step)
+    own = []
+    for o in range(P):
+        rows_from = [int(v) for v in host[:, o]]
+        slots_from = [int(v) for v in host[:, P + o]]
+        base = [sum(rows_from[:s]) for s in range(P)]
+        wgu_b = ops.cast_bf16(w_gu[o * E_loc:(o + 1) * E_loc].contiguous())
+        wd_b = ops.cast_bf16(w_d[o * E_loc:(o + 1) * E_loc].contiguous())
+        ectxs = [None] * P
+        for s in [(o - j) % P for j in range(P)]:
+            if s != o:
+                ops.ep_wait(bufs[o].flags, PH_FWD_SEND, P, step, src=s)
+            n = rows_from[s]
+            sel_loc, w_loc = B.unpack(bufs[o].recv_meta[base[s]:base[s] + n])
+            y, ectxs[s] = B.experts_fwd(bufs[o].recv_rows[base[s]:base[s] + n], sel_loc, w_loc,
+                                        wgu_b, wd_b, slots_from[s], combine=False)
+            if ectxs[s] is not None:
+                ops.ep_p2p_reduce_return_src(y, ectxs[s][0], st[o].plan, peers["back_rows"], P,
+                                             s, weights=w_loc)
+            ops.ep_signal(peers["flags"], PH_FWD_RETURN, o, P, step, dest=s)
+        own.append(SimpleNamespace(ectxs=ectxs, rows_from=rows_from, base=base))
+    outs = []
+    for r in range(P):
+        ops.ep_wait(bufs[r].flags, PH_FWD_RETURN, P, step)
+        n_back = int(host[r, :P].sum())
+        st[r].back = dataclasses.replace(st[r].send, inv_pad=ops.ep_p2p_back_inv(st[r].send,
+                                                                                 st[r].plan))
+        st[r].n_back = n_back
+        outs.append(ops.gather_rows_bwd(bufs[r].back_rows[:n_back], st[r].back))
+    for r in range(P):
+        for mode in (1, 2):
+            ops.ep_p2p_send_part(d_out_list[r], st[r].send, st[r].plan, peers["recv_rows"], r,
+                                 mode)
+        ops.ep_signal(peers["flags"], PH_BWD_SEND, r, P, step)
+    ggu, gd = [], []
+    for o in range(P):
+        g_gu = g_d = None
+        for s in [(o - j) % P for j in range(P)]:
+            if s != o:
+                ops.ep_wait(bufs[o].flags, PH_BWD_SEND, P, step, src=s)
+            e = own[o].ectxs[s]
+            d_rows = bufs[o].recv_rows[own[o].base[s]:own[o].base[s] + own[o].rows_from[s]]
+            dxs, dw_rows, state = B.experts_dgrad(e, d_rows, k, DEV, reduce=False)
+            if e is not None:
+                ops.ep_p2p_reduce_return_src(dxs, e[0], st[o].plan, peers["back_rows"], P, s,
+                                             dw_rows=dw_rows, peer_dw=peers["back_dw"])
+            ops.ep_signal(peers["flags"], PH_BWD_RETURN, o, P, step, dest=s)
+            g_gu, g_d = B.experts_wgrad(state, g_gu, g_d, E_loc, H, I, DEV)
+        ggu.append(g_gu)
+        gd.append(g_d)
+    dxs, g_routers = [], []
+    for r in range(P):
+        ops.ep_wait(bufs[r].flags, PH_BWD_RETURN, P, step)
+        s = st[r]
+        d_rw = ops.ep_weight_grad(bufs[r].back_dw[:s.n_back], s.back, s.sel, E_loc)
+        dx_router, g_router = B.router_bwd(x_list[r], s.wr, s.logits_buf, s.sel, d_rw, None, E,
+                                           k, True)
+        dxs.append(ops.gather_rows_bwd(bufs[r].back_rows[:s.n_back], s.back, addend=dx_router))
+        g_routers.append(g_router)
+    return outs, [s.sel for s in st], dxs, g_routers, torch.cat(ggu), torch.cat(gd)
+
+
+@pytest.mark.parametrize("T,H,E,k,I,P", [(2048, 1024, 32, 8, 256, 4),
+                                         (1500, 2048, 16, 4, 128, 2),
+                                         (1024, 512, 64, 8, 192, 8)])
+def test_emulated_pipelined_exchange_matches_single_gpu_layer(ops, T, H, E, k, I, P):
+    """Per-source chunks, the one-source return kernel and the point-to-point
+    flags give the single-GPU layer's routing and, within the bf16 contract,
+    its outputs and gradients (one extra rounding of an owner's partial sum)."""
+    from spark_gpt_b200 import SparseMoE, _lib
+    g = torch.Generator().manual_seed(E * 7 + P)
+    w_r = (torch.randn(E, H, generator=g) * 0.05).to(DEV)
+    w_gu = (torch.randn(E, 2 * I, H, generator=g) * 0.02).to(DEV)
+    w_d = (torch.randn(E, H, I, generator=g) * 0.02).to(DEV)
+    xs = [torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV) for _ in range(P)]
+    ds = [(torch.randn(T, H, generator=g) * 1e-2).to(torch.bfloat16).to(DEV) for _ in range(P)]
+    outs, sels, dxs, g_routers, g_gu, g_d = _emulated_pipe(ops, xs, ds, w_r, w_gu, w_d, k, P)
+    cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=k,
+                          moe_intermediate_size=I, norm_topk_prob=True)
+    ref = SparseMoE(cfg).to(DEV)
+    with torch.no_grad():
+        ref.gate.weight.copy_(w_r)
+        ref.experts.gate_up_proj.copy_(w_gu)
+        ref.experts.down_proj.copy_(w_d)
+    for r in range(P):
+        xin = xs[r].clone().requires_grad_(True)
+        ref.gate.weight.grad = None
+        out, _, sel = ref(xin)
+        out.backward(ds[r])
+        assert torch.equal(sels[r], sel)
+        assert_bf16_close(outs[r], out, f"pipe out rank {r}")
+        assert_bf16_close(dxs[r], xin.grad, f"pipe dx rank {r}")
+        assert_bf16_close(g_routers[r], ref.gate.weight.grad, f"pipe dW_router rank {r}")
+    assert_bf16_close(g_gu, ref.experts.gate_up_proj.grad, "pipe dW_gate_up")
+    assert_bf16_close(g_d, ref.experts.down_proj.grad, "pipe dW_down")
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0
+
+
+def test_point_to_point_flags_pass_and_time_out_without_a_fault(ops):
+    """A signalled flag passes at once; a wait on a flag nothing sets gives up
+    after its limit with fault bit 1, and the context stays usable."""
+    from spark_gpt_b200 import _lib
+    from spark_gpt_b200.ep import FLAG_WORDS, PH_FWD_SEND
+    flags = [torch.zeros(FLAG_WORDS, device=DEV, dtype=torch.int64) for _ in range(2)]
+    table = torch.tensor([f.data_ptr() for f in flags], dtype=torch.int64, device=DEV)
+    ops.ep_signal(table, PH_FWD_SEND, 0, 2, 3, dest=1)       # rank 0 -> rank 1
+    ops.ep_wait(flags[1], PH_FWD_SEND, 2, 3, src=0)
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 0
+    assert int(flags[1][PH_FWD_SEND * 64 + 0]) == 3 and int(flags[0].abs().sum()) == 0
+    ops.ep_wait(flags[1], PH_FWD_SEND, 2, 3, src=1)          # rank 1 never signalled
+    torch.cuda.synchronize()
+    assert _lib.read_fault() == 1
+    assert torch.equal(torch.ones(4, device=DEV).cumsum(0).cpu(), torch.arange(1, 5).float())
+
+
 def test_peer_barrier_passes_and_times_out_without_a_fault(ops):
     """One rank: the barrier passes at once.  Two ranks emulated on one GPU
     with only rank 0 arriving (a flag nothing sets): the bounded wait gives up

@@ -204,3 +204,26 @@ def test_newton_schulz_oracle_matches_reference(muon_golden, name):
     out = M.newton_schulz(ns_case_input(shape, seed), steps=5)
     assert out.dtype == torch.bfloat16 and out.shape == shape
     assert_bf16_close(out, muon_golden[name]["out"], name)
+
+
+@pytest.mark.parametrize("case", ["norm_bf16", "norm_f32"])
+def test_rmsnorm_oracle_matches_reference(case):
+    """The oracle's RMSNorm against the reference's own RMSNorm module
+    (tests/golden/norm_golden.pt, made by make_golden.py --only norm): the
+    forward bit-exact; the backward, which the reference runs through bf16
+    autograd ops for bf16 input, within the layer's bf16 contract (max 2e-2 /
+    mean 2e-3 of the reference tensor's scale), and to fp32 rounding for fp32
+    input."""
+    from tests.conftest import ROOT
+    from tests.helpers import assert_bf16_close
+    c = torch.load(ROOT / "tests" / "golden" / "norm_golden.pt", weights_only=True)[case]
+    bf = c["x"].dtype == torch.bfloat16
+    x_n, r = O.rmsnorm_forward(c["x"], c["w"], float(c["eps"]))
+    assert torch.equal(x_n, c["out"].float())
+    dx, dw = O.rmsnorm_backward(c["x"], c["w"], r, c["probe"], bf16_io=bf)
+    if bf:
+        assert_bf16_close(dx, c["dx"].float(), "dx")
+        assert_bf16_close(dw, c["dw"].float(), "dw")
+    else:
+        torch.testing.assert_close(dx, c["dx"], rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(dw, c["dw"], rtol=1e-5, atol=1e-6)
