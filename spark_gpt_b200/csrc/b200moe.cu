@@ -202,6 +202,25 @@ int make_out_tmap(CUtensorMap* m, const void* base, long long cols, long long ro
   return B200MOE_OK;
 }
 
+// Output tensor maps of the fp32 TMA-store epilogue: a {16, 32} box (64 bytes
+// of fp32 per row) with the 64-byte swizzle over a (rows, cols) fp32 matrix.
+int make_out_tmap_f32(CUtensorMap* m, const void* base, long long cols, long long rows,
+                      const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 4)};
+  cuuint32_t box[2] = {16, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
 int launch_expert_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                        cudaStream_t st, const char* what, const CUtensorMap* to0 = nullptr,
@@ -994,6 +1013,18 @@ int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* 
   p.accumulate = accumulate;
   p.out_group_stride = static_cast<long long>(M) * N;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN >= 128 && use_pair(BN, kKRagged, E, p.m_tiles)) {
+    // two-CTA tiles whose fp32 output leaves through shared memory with TMA
+    // stores (reduce-adds when accumulating): coalesced and asynchronous
+    CUtensorMap to;
+    if ((rc = make_out_tmap_f32(&to, dw, N, static_cast<long long>(E) * M, "expert_wgrad dw")))
+      return rc;
+    if (BN == 256)
+      return launch_gemm_pair<256, true, true, kEpiStoreF32Tma, kKRagged>(ta, tb, to, to, p, st,
+                                                                          "expert_wgrad");
+    return launch_gemm_pair<128, true, true, kEpiStoreF32Tma, kKRagged>(ta, tb, to, to, p, st,
+                                                                        "expert_wgrad");
+  }
   if (BN == 256) return launch_expert_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   if (BN == 128) return launch_expert_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   return launch_expert_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");

@@ -44,6 +44,7 @@ enum Epilogue : int {
   kEpiStoreF32T = 4,
   kEpiSwigluBwdCombine = 5,  // down dgrad from gathered d_out: combine backward fused in
   kEpiAxpby = 6,             // bf16 out = alpha*acc + beta*aux, or fp32 update += neg_lr*bf16(..)
+  kEpiStoreF32Tma = 7,       // kEpiStoreF32 through shared memory and TMA stores / reduce-adds
 };
 
 // Which operand is gathered row by row from a token-major tensor (x or d_out)
@@ -221,8 +222,8 @@ __device__ __forceinline__ void epilogue_empty_tile(const GemmParams& p, const T
                                                     int row_in, int half) {
   constexpr int BM = 128;
   // a weight-gradient tile of an expert that received no rows
-  if ((EPI == kEpiStoreF32 || EPI == kEpiStoreF32T) && !p.accumulate) {
-    if (EPI == kEpiStoreF32) {
+  if ((EPI == kEpiStoreF32 || EPI == kEpiStoreF32Tma || EPI == kEpiStoreF32T) && !p.accumulate) {
+    if (EPI == kEpiStoreF32 || EPI == kEpiStoreF32Tma) {
       float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
                  static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
       float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -484,6 +485,19 @@ __device__ __forceinline__ void ring_put(const OutRing& ring, int slot, const fl
   }
 }
 
+// Chunk `slot` of the group: this lane's row of 16 fp32 values (64 bytes) in
+// the 64-byte-swizzled 32 x 16 fp32 box.
+__device__ __forceinline__ void ring_put_f32(const OutRing& ring, int slot, const float* v,
+                                             int lane) {
+  uint8_t* buf = ring.base + ((ring.next + slot) % kOutRing) * 2048;
+  uint4* rowp = reinterpret_cast<uint4*>(buf + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    rowp[j ^ sw] = make_uint4(__float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                              __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+}
+
 template <int G>
 __device__ __forceinline__ void ring_flush(OutRing& ring, const CUtensorMap* const* tm,
                                            const int* col, int row0, int lane) {
@@ -519,7 +533,37 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
                                                   unsigned long long* prof = nullptr) {
   constexpr int BM = 128;
   const int row0 = T.m * BM + quarter * 32;
-  if (EPI == kEpiStoreBf16) {
+  if (EPI == kEpiStoreF32Tma) {
+    // fp32 weight-gradient tile: each 32-column TMEM chunk leaves as two 32 x 16
+    // boxes, stored (or reduce-added into the gradient when accumulating)
+    const int rowg = T.g * p.m_tiles * BM + row0;  // (E*M, N) view of the output
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        ring_acquire<1>(lane);
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[16 * part + j]);
+        ring_put_f32(ring, 0, v, lane);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          const uint8_t* buf = ring.base + ring.next * 2048;
+          const int col = T.n * BN + c * 32 + 16 * part;
+          if (p.accumulate)
+            tma_reduce_add_2d(tmO0, buf, col, rowg);
+          else
+            tma_store_2d(tmO0, buf, col, rowg);
+          bulk_commit_group();
+        }
+        ring.next = (ring.next + 1) % kOutRing;
+      }
+    }
+  } else if (EPI == kEpiStoreBf16) {
     constexpr int G = B200MOE_EPI_GROUP < BN / 64 ? B200MOE_EPI_GROUP : BN / 64;
 #pragma unroll 1
     for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c += G) {

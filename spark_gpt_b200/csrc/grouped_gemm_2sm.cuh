@@ -110,8 +110,8 @@ constexpr int kMaxPairExperts = 256;  // the library takes E <= 256
 // Epilogues whose bf16 output goes through shared memory and TMA stores.
 template <int EPI>
 struct TmaOut {
-  static constexpr bool value =
-      EPI == kEpiStoreBf16 || EPI == kEpiSwigluFwd || EPI == kEpiSwigluBwd;
+  static constexpr bool value = EPI == kEpiStoreBf16 || EPI == kEpiSwigluFwd ||
+                                EPI == kEpiSwigluBwd || EPI == kEpiStoreF32Tma;
 };
 
 template <int BN, int STAGES, bool TMA_OUT>

@@ -6,7 +6,8 @@ norm's backward inside the row-gather backward.  Checked on the device:
 
 * the norm kernel against the oracle's RMSNorm (pinned to the reference's
   own module): x_n bit-exact except where the fp32 sum of squares, added in a
-  different order, moves r by an ulp (then x_n by one bf16 unit);
+  different order, moves r by an ulp (then x_n by at most two bf16 units, on
+  fewer than 0.1% of the elements);
 * the whole fused layer, forward + load-balancing loss + backward, against
   the oracle composition RMSNorm -> layer -> layer backward -> RMSNorm
   backward, with the device's routing injected: out, d h, the norm weight's
@@ -70,9 +71,10 @@ def test_norm_kernel_matches_oracle(T, H):
     ref, ref_r = O.rmsnorm_forward(x, w, 1e-6)
     assert torch.allclose(r, ref_r, rtol=1e-6, atol=0)
     d = (x_n.float() - ref).abs()
-    # one bf16 unit where r differs by an ulp
+    # where r differs by an ulp, x * r and then its product with w may each
+    # round to the neighbouring bf16 value: at most two units, on few elements
     assert float((d > 0).float().mean()) < 1e-3
-    assert bool((d <= 2 ** -7 * ref.abs().clamp_min(2 ** -100)).all())
+    assert bool((d <= 2 ** -6 * ref.abs().clamp_min(2 ** -100)).all())
 
 
 LAYERS = [
