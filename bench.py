@@ -532,6 +532,178 @@ def sub_block(name, run, args, pk):
     }
 
 
+# --------------------------------------------------------------------------- #
+# On-box GPU comparator: the reference's stock-torch GPU path, not the product
+# --------------------------------------------------------------------------- #
+class _TorchGatherRows(torch.autograd.Function):
+    """rows = x[token] with the backward as a gather of each token's k rows
+    and a sum (the reference's _GatherTopK, train.py:2195-2217)."""
+
+    @staticmethod
+    def forward(ctx, x, token, inv, k):
+        ctx.save_for_backward(inv)
+        ctx.k = k
+        return x[token]
+
+    @staticmethod
+    def backward(ctx, g):
+        (inv,) = ctx.saved_tensors
+        return g[inv].view(-1, ctx.k, g.shape[-1]).sum(dim=1), None, None, None
+
+
+class _TorchCombineRows(torch.autograd.Function):
+    """out[t] = sum of w * y over token t's k rows, gathers both ways (the
+    reference's _CombineTopK, train.py:2220-2241)."""
+
+    @staticmethod
+    def forward(ctx, y, w, inv, token, k):
+        ctx.save_for_backward(y, w, token)
+        weighted = y * w.unsqueeze(-1)
+        return weighted[inv].view(-1, k, y.shape[-1]).sum(dim=1)
+
+    @staticmethod
+    def backward(ctx, g):
+        y, w, token = ctx.saved_tensors
+        g_rows = g[token]
+        return g_rows * w.unsqueeze(-1), (g_rows * y).sum(dim=-1), None, None, None
+
+
+def torch_path_step(layer, c, valid, coef):
+    """One step of the reference's GPU path with FUSED_SWIGLU off, in stock
+    torch ops on the same fp32 master weights: router F.linear + fp32 softmax
+    + torch.topk + renorm (train.py:2144-2158), sort / inverse / histc /
+    cumsum (:2271-2290), F.grouped_mm on the bf16 view of each expert tensor
+    (:2160-2181) with SiLU(gate) * up between (:2312-2318), the gather-based
+    combine, and the load-balancing loss (:3098-3197) as autograd over the
+    softmax.  cuBLAS / CUTLASS library kernels throughout: this is the GPU bar
+    the hand-written layer is compared against, under autocast(bf16) as the
+    reference's training step runs it."""
+    import torch.nn.functional as F
+    E, k = c["E"], c["k"]
+    w_r = layer.gate.weight
+    w_gu, w_d = layer.experts.gate_up_proj, layer.experts.down_proj
+
+    def step(xb, db):
+        for p in layer.parameters():
+            p.grad = None
+        xin = xb.detach().requires_grad_(True)
+        with torch.autocast("cuda", dtype=torch.bfloat16):
+            logits = F.linear(xin, w_r)
+        probs = F.softmax(logits, dtype=torch.float32, dim=-1)
+        rw, sel = torch.topk(probs, k, dim=-1)
+        rw = (rw / rw.sum(dim=-1, keepdim=True)).to(logits.dtype)
+        flat = sel.reshape(-1)
+        sorted_e, perm = torch.sort(flat)
+        token = perm // k
+        inv = torch.empty_like(perm)
+        inv[perm] = torch.arange(perm.numel(), device=perm.device)
+        counts = torch.histc(sorted_e.int() if sorted_e.is_cuda else sorted_e.float(),
+                             bins=E, min=0, max=E - 1)
+        offs = torch.cumsum(counts, dim=0, dtype=torch.int32)
+        xs = _TorchGatherRows.apply(xin, token, inv, k)
+        gu = F.grouped_mm(xs, w_gu.to(xs.dtype).transpose(-2, -1), offs=offs)
+        gate, up = gu.chunk(2, dim=-1)
+        y = F.grouped_mm(F.silu(gate) * up, w_d.to(xs.dtype).transpose(-2, -1), offs=offs)
+        out = _TorchCombineRows.apply(y, rw.reshape(-1)[perm], inv, token, k).to(xin.dtype)
+        rows = valid.sum().clamp_min(1).float()
+        frac = torch.bincount(flat, minlength=E).float() / rows
+        soft = (probs * valid.unsqueeze(-1)).sum(dim=0) / rows
+        aux = E * torch.dot(frac, soft)
+        torch.autograd.backward([out, aux], [db, coef])
+        return out, xin
+    return step
+
+
+def torch_path_block(run, args, pk):
+    """cfg2 through the stock-torch comparator on this GPU, timed like the
+    product (same weights and inputs), with its agreement against the
+    product layer on one step (bf16 contract: relative to the product's
+    max magnitude)."""
+    c = dict(CONFIGS[args.config])
+    T = c["T"]
+    layer = make_layer(c, run)
+    _, _, x, d_out = make_inputs(c, T, run)
+    valid = torch.ones(T, dtype=torch.bool, device=run.dev)
+    coef = torch.tensor(AUX_COEF, device=run.dev)
+    step = torch_path_step(layer, c, valid, coef)
+    try:
+        out_t, x_t = step(x, d_out)
+    except (RuntimeError, NotImplementedError) as e:  # grouped_mm unsupported here
+        return {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+    ref = (out_t.detach().float(), x_t.grad.float(), layer.experts.gate_up_proj.grad.clone())
+    mine = layer_step(layer, c, valid, coef)
+    xin = x.detach().requires_grad_(True)
+    from spark_gpt_b200 import global_load_balancing_loss
+    for p in layer.parameters():
+        p.grad = None
+    out, logits, sel = layer(xin)
+    aux, _ = global_load_balancing_loss((logits,), (sel,), valid, num_experts=c["E"],
+                                        top_k=c["k"])
+    torch.autograd.backward([out, aux], [d_out, coef])
+
+    def rel(a, b):
+        return float((a.float() - b).abs().max() / b.abs().max().clamp_min(1e-30))
+    agree = {"out": rel(out.detach(), ref[0]), "dx": rel(xin.grad, ref[1]),
+             "dW_gate_up": rel(layer.experts.gate_up_proj.grad, ref[2])}
+    del out, logits, sel, aux, xin, out_t, x_t, ref
+    ms_t, _, _, _ = time_steps(run, lambda: step(x, d_out), args.sub_steps,
+                               max(3, args.warmup), [])
+    ms_m, _, _, _ = time_steps(run, lambda: mine(x, d_out), args.sub_steps,
+                               max(3, args.warmup), [])
+    lf = layer_flops(c, T)
+    del layer, x, d_out, step, mine
+    dense = dense_gemm_block(c, T, pk)
+    return {
+        "workload": f"{args.config}, {T} tokens: the reference's GPU path with "
+                    f"FUSED_SWIGLU off (F.grouped_mm, train.py:2160-2181) in stock torch ops",
+        "steps": args.sub_steps,
+        "torch_ms_per_step": ms_t, "torch_tokens_per_s": T / (ms_t / 1e3),
+        "torch_layer_frac_of_burst": lf / (ms_t / 1e3) / 1e12 / pk["bf16"],
+        "b200_ms_per_step": ms_m, "b200_tokens_per_s": T / (ms_m / 1e3),
+        "speedup": ms_t / ms_m,
+        "max_rel_diff_vs_b200": agree,
+        "cublas_dense_same_shapes": dense,
+        "note": "the reference's Triton fused path (train.py:2304-2310) cannot run here: the "
+                "reference checkout is not on the GPU box and its kernels are not copied",
+    }
+
+
+def dense_gemm_block(c, T, pk, reps=10):
+    """cuBLAS (torch.mm, bf16) on one dense GEMM of each expert GEMM's total
+    shape -- all R routed rows against one expert's weight -- the library's
+    rate on this M/N/K without the grouping: what the grouped kernels' frac
+    of the square-GEMM burst peak should be read against."""
+    R, H, I = T * c["k"], c["H"], c["I"]
+    shapes = {  # name: (M, N, K) of the output M x N with reduction K
+        "gate_up_fwd": (R, 2 * I, H), "down_fwd": (R, H, I), "down_dgrad": (R, I, H),
+        "gate_up_dgrad": (R, H, 2 * I), "gate_up_wgrad": (2 * I, H, R), "down_wgrad": (H, I, R),
+    }
+    out = {}
+    for n, (M, N, K) in shapes.items():
+        if n.endswith("wgrad"):   # dW = A^T B with the rows as the reduction (column-major A)
+            a = torch.randn(K, M, device="cuda", dtype=torch.bfloat16).t()
+        else:
+            a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
+        o = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        for _ in range(3):
+            torch.mm(a, b, out=o)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            torch.mm(a, b, out=o)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        tf = 2 * M * N * K / (ms / 1e3) / 1e12
+        out[n] = {"mnk": [M, N, K], "ms": round(ms, 5), "tflops": round(tf, 1),
+                  "frac_of_burst": round(tf / pk["bf16"], 3)}
+        del a, b, o
+    return out
+
+
 def ep_block(run, args, pk):
     """BASELINE config 5 at this N: the single-GPU layer at cfg5's per-GPU
     shape on every rank (the baseline), then the expert-parallel layer over
@@ -670,9 +842,14 @@ def main():
     del layer, step
 
     subs = {}
+    torch_path = None
     if world == 1 and args.config == "cfg2" and not args.no_extra:
         for name in ("cfg3", "cfg4"):
             subs[name] = sub_block(name, run, args, pk)
+        try:
+            torch_path = torch_path_block(run, args, pk)
+        except Exception as e:  # a comparator failure must not cost the product's line
+            torch_path = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
     ep = None
     if not args.no_ep and not c.get("ep"):
         ep = ep_block(run, args, pk)
@@ -704,6 +881,7 @@ def main():
         "e2e": e2e,
         "muon_step": muon_line,
         "configs": subs or None,
+        "torch_gpu_path": torch_path,
         "ep": ep,
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / max(args.steps, 1),

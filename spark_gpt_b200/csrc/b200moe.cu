@@ -420,12 +420,21 @@ int b200moe_router_topk_fwd(const void* logits, int logits_f32, long long ld, lo
   const int vec = aligned16(logits) && (ld * (logits_f32 ? 4 : 2)) % 16 == 0;
   B200_SWITCH_LANES(E, {
     const int grid = grid_for(T, 256 / L);
-    if (logits_f32)
-      router_topk_fwd_kernel<L, float><<<grid, 256, 0, st>>>(
-          static_cast<const float*>(logits), ld, T, E, k, norm, vec, selected, w);
-    else
-      router_topk_fwd_kernel<L, __nv_bfloat16><<<grid, 256, 0, st>>>(
-          static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, vec, selected, w);
+    if (logits_f32) {
+      if (k <= 8)
+        router_topk_fwd_kernel<L, 8, float><<<grid, 256, 0, st>>>(
+            static_cast<const float*>(logits), ld, T, E, k, norm, vec, selected, w);
+      else
+        router_topk_fwd_kernel<L, kMaxTopK, float><<<grid, 256, 0, st>>>(
+            static_cast<const float*>(logits), ld, T, E, k, norm, vec, selected, w);
+    } else {
+      if (k <= 8)
+        router_topk_fwd_kernel<L, 8, __nv_bfloat16><<<grid, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, vec, selected, w);
+      else
+        router_topk_fwd_kernel<L, kMaxTopK, __nv_bfloat16><<<grid, 256, 0, st>>>(
+            static_cast<const __nv_bfloat16*>(logits), ld, T, E, k, norm, vec, selected, w);
+    }
   })
   return check_launch("router_topk_fwd");
 }
@@ -444,8 +453,12 @@ int b200moe_router_topk_bwd(const void* logits, long long ld, const long long* s
   const int vec = aligned16(lg) && aligned16(out) && (ex == nullptr || aligned16(ex)) &&
                   (ld * 2) % 16 == 0;
   B200_SWITCH_LANES(ld, {
-    router_topk_bwd_kernel<L><<<grid_for(T, 256 / L), 256, 0, st>>>(lg, ld, selected, d_weights,
-                                                                    ex, T, E, k, norm, vec, out);
+    if (k <= 8)
+      router_topk_bwd_kernel<L, 8><<<grid_for(T, 256 / L), 256, 0, st>>>(
+          lg, ld, selected, d_weights, ex, T, E, k, norm, vec, out);
+    else
+      router_topk_bwd_kernel<L, kMaxTopK><<<grid_for(T, 256 / L), 256, 0, st>>>(
+          lg, ld, selected, d_weights, ex, T, E, k, norm, vec, out);
   })
   return check_launch("router_topk_bwd");
 }
@@ -551,6 +564,45 @@ long long b200moe_dispatch_scratch_bytes(long long T, int k, int E) {
   return (nblk > 0 ? nblk : 1) * E * static_cast<long long>(sizeof(int));
 }
 
+}  // extern "C"
+
+namespace {
+
+// count -> scan -> scatter over nblk chunks of kDispatchChunk slots; `base`
+// holds nblk * E ints.
+template <int WARPS>
+int launch_dispatch_scatter(const long long* selected, long long R, int E, int nblk,
+                            const int* base, int* row_flat, int* inv_pad, cudaStream_t st,
+                            const char* tag) {
+  const size_t shm = static_cast<size_t>(WARPS) * E * sizeof(int);
+  if (shm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(dispatch_scatter_kernel<WARPS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
+    if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s scatter: %s", tag, cudaGetErrorString(e));
+  }
+  dispatch_scatter_kernel<WARPS><<<nblk, WARPS * 32, shm, st>>>(selected, R, E, nblk, base,
+                                                                row_flat, inv_pad);
+  return check_launch(tag);
+}
+
+int launch_dispatch(const long long* selected, long long R, int E, int nblk, int* base,
+                    int* counts, int* offsets, int* pad_offsets, int* row_flat, int* inv_pad,
+                    int* tile_expert, cudaStream_t st, const char* tag) {
+  dispatch_count_kernel<<<nblk, kDispatchThreads, E * sizeof(int), st>>>(selected, R, E, nblk, base);
+  int rc = check_launch(tag);
+  if (rc) return rc;
+  dispatch_scan_kernel<<<1, 1024, (2 * E + 1) * sizeof(int), st>>>(base, nblk, E, counts, offsets,
+                                                                   pad_offsets, row_flat, tile_expert);
+  if ((rc = check_launch(tag))) return rc;
+  // 32 warps per chunk while their expert tables fit (E <= 1024: 128 KB), else 8
+  return E <= 1024 ? launch_dispatch_scatter<32>(selected, R, E, nblk, base, row_flat, inv_pad, st, tag)
+                   : launch_dispatch_scatter<8>(selected, R, E, nblk, base, row_flat, inv_pad, st, tag);
+}
+
+}  // namespace
+
+extern "C" {
+
 int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* counts,
                      int* offsets, int* pad_offsets, int* row_flat, int* inv_pad, int* tile_expert,
                      void* scratch, long long scratch_bytes, void* stream) {
@@ -563,22 +615,8 @@ int b200moe_dispatch(const long long* selected, long long T, int k, int E, int* 
   REQUIRE(scratch_bytes >= b200moe_dispatch_scratch_bytes(T, k, E), "dispatch: scratch too small");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int nblk = static_cast<int>(R > 0 ? (R + kDispatchChunk - 1) / kDispatchChunk : 1);
-  int* base = static_cast<int*>(scratch);
-  dispatch_count_kernel<<<nblk, kDispatchThreads, E * sizeof(int), st>>>(selected, R, E, nblk, base);
-  int rc = check_launch("dispatch_count");
-  if (rc) return rc;
-  dispatch_scan_kernel<<<1, 1024, (2 * E + 1) * sizeof(int), st>>>(base, nblk, E, counts, offsets,
-                                                                   pad_offsets, row_flat, tile_expert);
-  if ((rc = check_launch("dispatch_scan"))) return rc;
-  const size_t shm = (kDispatchThreads / 32) * E * sizeof(int);
-  if (shm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(dispatch_scatter_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
-    if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "dispatch_scatter: %s", cudaGetErrorString(e));
-  }
-  dispatch_scatter_kernel<<<nblk, kDispatchThreads, shm, st>>>(selected, R, E, nblk, base, row_flat,
-                                                               inv_pad);
-  return check_launch("dispatch_scatter");
+  return launch_dispatch(selected, R, E, nblk, static_cast<int*>(scratch), counts, offsets,
+                         pad_offsets, row_flat, inv_pad, tile_expert, st, "dispatch");
 }
 
 }  // extern "C"
@@ -639,21 +677,8 @@ int b200moe_dispatch_noalloc(const long long* selected, long long T, int k, int 
   const int nblk = static_cast<int>(nblk_ll);
   // the count kernel writes every one of the nblk*E entries before the scan reads them, so
   // whatever an earlier call left in the array needs no clearing
-  dispatch_count_kernel<<<nblk, kDispatchThreads, E * sizeof(int), st>>>(selected, R, E, nblk, base);
-  if ((rc = check_launch("dispatch_noalloc count"))) return rc;
-  dispatch_scan_kernel<<<1, 1024, (2 * E + 1) * sizeof(int), st>>>(base, nblk, E, counts, offsets,
-                                                                   pad_offsets, row_flat, tile_expert);
-  if ((rc = check_launch("dispatch_noalloc scan"))) return rc;
-  const size_t shm = (kDispatchThreads / 32) * E * sizeof(int);
-  if (shm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(dispatch_scatter_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)shm);
-    if (e != cudaSuccess)
-      return fail(B200MOE_ERR_CUDA, "dispatch_noalloc scatter: %s", cudaGetErrorString(e));
-  }
-  dispatch_scatter_kernel<<<nblk, kDispatchThreads, shm, st>>>(selected, R, E, nblk, base, row_flat,
-                                                               inv_pad);
-  return check_launch("dispatch_noalloc scatter");
+  return launch_dispatch(selected, R, E, nblk, base, counts, offsets, pad_offsets, row_flat,
+                         inv_pad, tile_expert, st, "dispatch_noalloc");
 }
 
 // ---------------------------------------------------------------- gather / combine

@@ -280,7 +280,9 @@ __device__ __forceinline__ void torch_topk_order_small(const float (&pe)[kVpt], 
   }
 }
 
-template <int L, typename LT>
+// KMAX: the largest k this instantiation takes (8 or KMAX): fewer registers
+// for the common top-8, so more tokens are in flight per SM.
+template <int L, int KMAX, typename LT>
 __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long ld, long long T,
                                        int E, int k, int norm, int vec,
                                        long long* __restrict__ selected,
@@ -300,11 +302,11 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
     float pe[kVpt];  // the probabilities as selected (entries >= E: -1)
 #pragma unroll
     for (int j = 0; j < kVpt; ++j) pe[j] = p[j];
-    float sv[kMaxTopK];
-    int si[kMaxTopK];
+    float sv[KMAX];
+    int si[KMAX];
     float kth = 0.f;  // the k-th largest probability
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
+    for (int r = 0; r < KMAX; ++r) {
       sv[r] = 0.f;
       si[r] = 0;
       if (r < k) {
@@ -337,18 +339,18 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
     }
     float sum = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r)
+    for (int r = 0; r < KMAX; ++r)
       if (r < k) sum += sv[r];
     // winners with equal probabilities leave in torch's order; the network
     // runs (warp-uniformly) only when some token of the warp has such a tie
     bool tie = false;
 #pragma unroll
-    for (int r = 0; r + 1 < kMaxTopK; ++r)
+    for (int r = 0; r + 1 < KMAX; ++r)
       if (r + 1 < k) tie |= sv[r] == sv[r + 1];
     if (!__any_sync(0xffffffffu, valid && tie)) {
       if (valid) {
 #pragma unroll
-        for (int r = 0; r < kMaxTopK; ++r) {
+        for (int r = 0; r < KMAX; ++r) {
           if (r < k && (r & (L - 1)) == sub) {
             selected[t * k + r] = si[r];
             weights[t * k + r] = __float2bfloat16_rn(norm ? sv[r] / sum : sv[r]);
@@ -387,14 +389,14 @@ __global__ void router_topk_fwd_kernel(const LT* __restrict__ logits, long long 
 // d logits (T, ld) of the router from d(routing weights) (T,k) fp32 in slot
 // order, plus an optional extra bf16 logit gradient (the load-balancing loss);
 // columns in [E, ld) are written as zero.  8L >= ld.
-template <int L>
+template <int L, int KMAX>
 __global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits, long long ld,
                                        const long long* __restrict__ selected,
                                        const float* __restrict__ d_weights,
                                        const __nv_bfloat16* __restrict__ d_extra, long long T,
                                        int E, int k, int norm, int vec,
                                        __nv_bfloat16* __restrict__ d_logits) {
-  constexpr int kSlots = (kMaxTopK + L - 1) / L;  // slots r = sub + L*i held by this lane
+  constexpr int kSlots = (KMAX + L - 1) / L;  // slots r = sub + L*i held by this lane
   const int sub = threadIdx.x & (L - 1);
   const int e0 = sub * kVpt;
   const GroupTokens gt = GroupTokens::make<L>(T);
@@ -413,11 +415,11 @@ __global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits,
       sl[i] = on ? static_cast<int>(selected[tt * k + r]) : -1;
       dl[i] = on ? d_weights[tt * k + r] : 0.f;
     }
-    int si[kMaxTopK];
-    float ps[kMaxTopK], dw[kMaxTopK];
+    int si[KMAX];
+    float ps[KMAX], dw[KMAX];
     float s = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
+    for (int r = 0; r < KMAX; ++r) {
       si[r] = -1;
       ps[r] = 0.f;
       dw[r] = 0.f;
@@ -434,13 +436,13 @@ __global__ void router_topk_bwd_kernel(const __nv_bfloat16* __restrict__ logits,
     const float inv_s = 1.0f / s;
     float dot = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r)
+    for (int r = 0; r < KMAX; ++r)
       if (r < k) dot += dw[r] * (ps[r] * inv_s);
     float g[kVpt];
 #pragma unroll
     for (int j = 0; j < kVpt; ++j) g[j] = 0.f;
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r) {
+    for (int r = 0; r < KMAX; ++r) {
       if (r < k) {
         const float dp = norm ? (dw[r] - dot) * inv_s : dw[r];
 #pragma unroll

@@ -15,7 +15,7 @@ namespace b200moe {
 
 constexpr int kRowTile = 128;       // padding granule of an expert's row block
 constexpr int kDispatchChunk = 4096;  // flat routed slots per dispatch block
-constexpr int kDispatchThreads = 256;
+constexpr int kDispatchThreads = 1024;  // count kernel: 4 slots per thread
 
 // ---------------------------------------------------------------------------
 // fp32 master -> bf16 compute copy, rows >= rows_in zero-filled
@@ -182,11 +182,15 @@ __global__ void dispatch_scan_kernel(int* __restrict__ block_base, int nblk, int
   }
 }
 
-__global__ void dispatch_scatter_kernel(const long long* __restrict__ sel, long long R, int E,
-                                        int nblk, const int* __restrict__ block_base,
-                                        int* __restrict__ row_flat, int* __restrict__ inv_pad) {
+// WARPS warps per chunk, each placing a contiguous run of 4096 / WARPS slots
+// (32 warps while their per-warp expert tables fit in shared memory).
+template <int WARPS>
+__global__ void __launch_bounds__(WARPS * 32)
+    dispatch_scatter_kernel(const long long* __restrict__ sel, long long R, int E, int nblk,
+                            const int* __restrict__ block_base, int* __restrict__ row_flat,
+                            int* __restrict__ inv_pad) {
   extern __shared__ int wbase[];  // [warps][E]
-  constexpr int kWarps = kDispatchThreads / 32;
+  constexpr int kWarps = WARPS;
   constexpr int kPerWarp = kDispatchChunk / kWarps;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -870,10 +874,7 @@ __global__ void __launch_bounds__(kReduceThreads, NV == 0 ? 3 : (NV == 1 ? 3 : (
             reinterpret_cast<uint4*>(out + t * H)[v] = o;
           }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
-        continue;
-      }
+      } else {
       for (int v = v0 + lane; v < v1; v += 32) {
         float acc[8];
 #pragma unroll
@@ -907,6 +908,7 @@ __global__ void __launch_bounds__(kReduceThreads, NV == 0 ? 3 : (NV == 1 ? 3 : (
         o.z = pack_bf16x2(acc[4], acc[5]);
         o.w = pack_bf16x2(acc[6], acc[7]);
         reinterpret_cast<uint4*>(out + t * H)[v] = o;
+      }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[s]);
