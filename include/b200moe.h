@@ -251,6 +251,80 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gate_up, const 
 int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets,
                          int E, long long rows_cap, float* dw, int accumulate, void* stream);
 
+/* ---- the fp8 expert path: _FP8Experts (train.py:1543-1604) --------------
+ * spark-gpt's --fp8-mlp on MoE layers.  x, gu, h and the expert weights are
+ * e4m3, d_gu and the rows' gradient dy e5m2.  `scale` points at the layer's
+ * five delayed per-site scales (x, gu, h, d_gu, dy: the Experts module's
+ * fp8_scale buffer) and `amax` at its five amax slots (fp8_amax), which the
+ * kernels raise with the absolute maxima of the unquantized values
+ * (train.py:914-946).  Quantization is clamp(v * scale) with a round to
+ * nearest even; every dequantization divides by powers of two.  Shapes:
+ * H % 256 == 0, I % 128 == 0, E <= 256; fp8 buffers are one byte per element
+ * in the padded expert-order row layout of b200moe_dispatch. */
+
+long long b200moe_fp8_quantize_experts_scratch_bytes(int E);
+
+/* Per-expert e4m3 copies of fp32 master weights w (E, per_expert):
+ * q[e] = 2^floor(log2(448 / max|w_e|)), w8 = e4m3(w * q[e]).  Replaces
+ * _fp8_quantize_experts (train.py:1536-1540). */
+int b200moe_fp8_quantize_experts(const float* w, int E, long long per_expert, void* w8, float* q,
+                                 void* scratch, long long scratch_bytes, void* stream);
+
+/* x8 (Rcap,H) e4m3 = e4m3(x[token] * scale[0]) in padded expert order,
+ * padding rows zero; amax[0] raised.  Replaces _fp8_moe_gather_quant_kernel
+ * (train.py:1301-1313). */
+int b200moe_fp8_gather_quant(const void* x, const int* row_flat, const int* inv_pad,
+                             const int* pad_offsets, long long T, int E, int k, int H,
+                             long long rows_cap, const float* scale, float* amax, void* x8,
+                             void* stream);
+
+/* dst (rows,cols) fp8 = fp8(src * scale[0]) for a bf16 src, amax[0] raised;
+ * fmt 0 = e4m3, 1 = e5m2.  The e5m2 copy of the rows' gradient that the down
+ * weight gradient reads (the in-register quantization of
+ * _fp8_moe_wgrad_rows_kernel, train.py:1504-1530). */
+int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const float* scale,
+                              float* amax, int fmt, void* dst, void* stream);
+
+/* gu = x8 . W8_gu[e]^T / (scale[0] q_gu[e]) rounded to bf16, h = silu(g) u;
+ * gu8 (Rcap,2I), h8 (Rcap,I) e4m3 with scale[1], scale[2]; amax[1], amax[2]
+ * raised.  Replaces _fp8_moe_swiglu_fwd_kernel (train.py:1317-1354). */
+int b200moe_fp8_expert_gate_up_fwd(const void* x8, const void* w8_gate_up, const float* q_gu,
+                                   const int* tile_expert, const int* pad_offsets,
+                                   long long rows_cap, int E, int H, int I, const float* scale,
+                                   float* amax, void* gu8, void* h8, void* stream);
+
+/* y (Rcap,H) bf16 = h8 . W8_d[e]^T / (scale[2] q_d[e]).  Replaces
+ * _fp8_moe_down_fwd_kernel (train.py:1357-1379). */
+int b200moe_fp8_expert_down_fwd(const void* h8, const void* w8_down, const float* q_d,
+                                const int* tile_expert, const int* pad_offsets, long long rows_cap,
+                                int E, int H, int I, const float* scale, void* y, void* stream);
+
+/* dh = bf16(dy . W_d[e]) (bf16 operands); g, u = gu8 / scale[1]; the SwiGLU
+ * backward; d_gu8 (Rcap,2I) e5m2 with scale[3]; amax[3] raised.  Replaces
+ * _fp8_moe_down_dgrad_swiglu_kernel (train.py:1382-1423); the dy amax it
+ * records comes from b200moe_fp8_quantize_rows. */
+int b200moe_fp8_expert_down_dgrad_swiglu(const void* dy, const void* w_down, const void* gu8,
+                                         const int* tile_expert, const int* pad_offsets,
+                                         long long rows_cap, int E, int H, int I,
+                                         const float* scale, float* amax, void* d_gu8,
+                                         void* stream);
+
+/* dxs (Rcap,H) bf16 = d_gu8 . W8_gu[e] / (scale[3] q_gu[e]).  Replaces
+ * _fp8_moe_dgrad_kernel (train.py:1426-1448). */
+int b200moe_fp8_expert_gate_up_dgrad(const void* d_gu8, const void* w8_gate_up, const float* q_gu,
+                                     const int* tile_expert, const int* pad_offsets,
+                                     long long rows_cap, int E, int H, int I, const float* scale,
+                                     void* dxs, void* stream);
+
+/* dw (E,M,N) fp32 (+)= a8_e^T . b8_e / (scale_a[0] scale_b[0]) over the padded
+ * rows of expert e; a8 (Rcap,M) e4m3 (a_fmt 0) or e5m2 (1), b8 (Rcap,N) e4m3;
+ * M % 256 == 0, N % 128 == 0.  Replaces _fp8_moe_wgrad_kernel (train.py:1451-1478)
+ * and _fp8_moe_wgrad_rows_kernel (:1504-1530). */
+int b200moe_fp8_expert_wgrad(const void* a8, int a_fmt, int M, const void* b8, int N,
+                             const int* pad_offsets, int E, long long rows_cap,
+                             const float* scale_a, const float* scale_b, float* dw, int accumulate,
+                             void* stream);
+
 /* ---- expert products with the row gather / combine backward fused in ----
  * These read token-major tensors (x, d_out) row by row with TMA tile::gather4
  * in the GEMM's load stage, so the gathered (Rcap,H) copies of the reference's

@@ -11,7 +11,8 @@ built with ``python -m spark_gpt_b200.build``.
 
 from .aux_loss import global_load_balancing_loss
 from .faults import DeviceFault, check_faults
+from .fp8 import fp8_update_scales
 from .moe import Experts, SparseMoE, TopKRouter
 
 __all__ = ["SparseMoE", "TopKRouter", "Experts", "global_load_balancing_loss", "DeviceFault",
-           "check_faults"]
+           "check_faults", "fp8_update_scales"]

@@ -15,6 +15,7 @@
 #include "routing.cuh"
 #include "ep.cuh"
 #include "muon.cuh"
+#include "fp8.cuh"
 
 namespace b200moe {
 namespace {
@@ -103,6 +104,30 @@ int make_tmap(CUtensorMap* m, const void* base, long long inner, long long outer
   return B200MOE_OK;
 }
 
+// 2-D fp8 (one byte per element) tensor map with the 128-byte swizzle: a
+// K-major box of 128 elements x box_outer rows, or an MN-major box of
+// 128 x 128.
+int make_tmap_u8(CUtensorMap* m, const void* base, long long inner, long long outer,
+                 long long ld, int box_inner, int box_outer, const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: base pointer not 16-byte aligned", what);
+  if (ld % 16 != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: row stride not a multiple of 16 bytes", what);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
 // Tensor map for row gathers (tile::gather4) from a token-major (rows, cols)
 // bf16 matrix: box of one row by 64 columns.
 int make_gather_tmap(CUtensorMap* m, const void* base, long long cols, long long rows,
@@ -147,13 +172,13 @@ constexpr int pair_stages() {
 // parity tests of the two kernels against each other).
 int g_pair_gemm = 1;
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int OP = kOpBf16>
 int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to0,
                      const CUtensorMap& to1, const GemmParams& p, cudaStream_t st,
                      const char* what) {
   constexpr bool kTmaOut = TmaOut<EPI>::value;
   constexpr int STAGES = pair_stages<BN, kTmaOut>();
-  auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES>;
+  auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES, OP>;
   const int smem = static_cast<int>(PairSmem<BN, STAGES, kTmaOut>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -1053,6 +1078,263 @@ int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* 
   if (BN == 256) return launch_expert_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   if (BN == 128) return launch_expert_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   return launch_expert_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+}
+
+// ---------------------------------------------------------------- fp8 expert path
+// spark-gpt's --fp8-mlp on MoE layers (train.py:1301-1604): e4m3 x, gu, h and
+// weights, e5m2 d_gu and dy, delayed per-site scales (scale[0..4] = x, gu, h,
+// d_gu, dy) read from device memory, amax slots raised by the kernels that
+// quantize.  Every GEMM is a two-CTA pair kernel; shapes as the reference's
+// gate (H a multiple of 256 here, I of 128, E <= 256).
+static int check_fp8_shape(const char* what, long long rows_cap, int E, int H, int I) {
+  REQUIRE(E >= 1 && E <= kMaxPairExperts, "%s: fp8 expert GEMMs take 1 <= E <= %d", what,
+          kMaxPairExperts);
+  REQUIRE(H > 0 && H % 256 == 0, "%s: fp8 path needs H a multiple of 256", what);
+  REQUIRE(I > 0 && I % 128 == 0, "%s: fp8 path needs I a multiple of 128", what);
+  REQUIRE(rows_cap > 0 && rows_cap % 128 == 0 && rows_cap < 0x7fffffffLL,
+          "%s: rows_cap must be a positive multiple of 128", what);
+  REQUIRE(static_cast<long long>(E) * 2 * I < 0x7fffffffLL && static_cast<long long>(E) * H < 0x7fffffffLL,
+          "%s: weights too large", what);
+  REQUIRE(g_pair_gemm, "%s: the fp8 path runs only as two-CTA pair tiles", what);
+  return B200MOE_OK;
+}
+
+long long b200moe_fp8_quantize_experts_scratch_bytes(int E) {
+  return static_cast<long long>(E > 0 ? E : 1) * 64 * static_cast<long long>(sizeof(float));
+}
+
+int b200moe_fp8_quantize_experts(const float* w, int E, long long per_expert, void* w8, float* q,
+                                 void* scratch, long long scratch_bytes, void* stream) {
+  REQUIRE(w && w8 && q && scratch, "fp8_quantize_experts: null pointer");
+  REQUIRE(E >= 1 && E <= 65535 && per_expert > 0 && per_expert % 4 == 0,
+          "fp8_quantize_experts: need 1 <= E <= 65535 and a per-expert size that is a "
+          "multiple of 4");
+  REQUIRE(aligned16(w) && aligned16(w8), "fp8_quantize_experts: pointers must be 16-byte aligned");
+  REQUIRE(scratch_bytes >= b200moe_fp8_quantize_experts_scratch_bytes(E),
+          "fp8_quantize_experts: scratch too small");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // splits per expert: about four blocks per SM over all experts, at most 64
+  int splits = static_cast<int>((4LL * num_sms() + E - 1) / E);
+  splits = std::max(1, std::min(64, splits));
+  float* partial = static_cast<float*>(scratch);
+  fp8_weight_amax_kernel<<<dim3(splits, E), kWeightAmaxThreads, 0, st>>>(w, per_expert, splits,
+                                                                          partial);
+  int rc = check_launch("fp8_quantize_experts amax");
+  if (rc) return rc;
+  fp8_weight_scale_kernel<<<(E + 127) / 128, 128, 0, st>>>(partial, E, splits, q);
+  if ((rc = check_launch("fp8_quantize_experts scale"))) return rc;
+  const long long total = static_cast<long long>(E) * per_expert;
+  fp8_weight_quant_kernel<<<grid_for(total / 4, 256), 256, 0, st>>>(w, per_expert, total, q,
+                                                                    static_cast<uint8_t*>(w8));
+  return check_launch("fp8_quantize_experts quant");
+}
+
+int b200moe_fp8_gather_quant(const void* x, const int* row_flat, const int* inv_pad,
+                             const int* pad_offsets, long long T, int E, int k, int H,
+                             long long rows_cap, const float* scale, float* amax, void* x8,
+                             void* stream) {
+  REQUIRE(x && row_flat && inv_pad && pad_offsets && scale && amax && x8,
+          "fp8_gather_quant: null pointer");
+  REQUIRE(H > 0 && H % 16 == 0 && k >= 1 && k <= 32 && T >= 0,
+          "fp8_gather_quant: need H a multiple of 16 and 1 <= k <= 32");
+  REQUIRE(aligned16(x) && aligned16(x8), "fp8_gather_quant: pointers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(T > rows_cap / 32 ? T : rows_cap / 32, 8);
+  fp8_gather_quant_kernel<<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(x), inv_pad,
+                                                row_flat, pad_offsets + E, T, k, H, scale, amax,
+                                                static_cast<uint8_t*>(x8));
+  return check_launch("fp8_gather_quant");
+}
+
+int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const float* scale,
+                              float* amax, int fmt, void* dst, void* stream) {
+  REQUIRE(src && scale && amax && dst, "fp8_quantize_rows: null pointer");
+  REQUIRE(rows >= 0 && cols > 0 && cols % 8 == 0, "fp8_quantize_rows: cols must be a multiple of 8");
+  REQUIRE(fmt == 0 || fmt == 1, "fp8_quantize_rows: fmt 0 (e4m3) or 1 (e5m2)");
+  REQUIRE(aligned16(src) && aligned16(dst), "fp8_quantize_rows: pointers must be 16-byte aligned");
+  const long long n8 = rows * cols / 8;
+  if (n8 == 0) return B200MOE_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(n8, 256);
+  if (fmt == 0)
+    fp8_quantize_rows_kernel<kE4M3><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), n8,
+                                                         scale, amax, static_cast<uint8_t*>(dst));
+  else
+    fp8_quantize_rows_kernel<kE5M2><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), n8,
+                                                         scale, amax, static_cast<uint8_t*>(dst));
+  return check_launch("fp8_quantize_rows");
+}
+
+int b200moe_fp8_expert_gate_up_fwd(const void* x8, const void* w8_gu, const float* q_gu,
+                                   const int* tile_expert, const int* pad_offsets,
+                                   long long rows_cap, int E, int H, int I, const float* scale,
+                                   float* amax, void* gu8, void* h8, void* stream) {
+  REQUIRE(x8 && w8_gu && q_gu && tile_expert && pad_offsets && scale && amax && gu8 && h8,
+          "fp8_gate_up_fwd: null pointer");
+  int rc = check_fp8_shape("fp8_gate_up_fwd", rows_cap, E, H, I);
+  if (rc) return rc;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap_u8(&ta, x8, H, rows_cap, H, 128, 128, "fp8_gate_up_fwd x8"))) return rc;
+  if ((rc = make_tmap_u8(&tb, w8_gu, H, static_cast<long long>(E) * 2 * I, H, 128, 128,
+                         "fp8_gate_up_fwd w8")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = I / 128;
+  p.k_blocks = H / 128;
+  p.b_group_rows = 2 * I;
+  p.b_half_offset = I;
+  p.m_valid = rows_cap;
+  p.n_valid = I;
+  p.out = gu8;
+  p.ld_out = 2 * I;
+  p.out2 = h8;
+  p.ld_out2 = I;
+  p.inter = I;
+  p.fp8_scale = scale;
+  p.fp8_amax = amax;
+  p.deq_a = scale;  // x
+  p.deq_g = q_gu;
+  return launch_gemm_pair<256, false, false, kEpiSwigluFwdF8, kRowsRagged, kOpE4m3>(
+      ta, tb, ta, ta, p, static_cast<cudaStream_t>(stream), "fp8_gate_up_fwd");
+}
+
+int b200moe_fp8_expert_down_fwd(const void* h8, const void* wd8, const float* q_d,
+                                const int* tile_expert, const int* pad_offsets, long long rows_cap,
+                                int E, int H, int I, const float* scale, void* y, void* stream) {
+  REQUIRE(h8 && wd8 && q_d && tile_expert && pad_offsets && scale && y, "fp8_down_fwd: null pointer");
+  int rc = check_fp8_shape("fp8_down_fwd", rows_cap, E, H, I);
+  if (rc) return rc;
+  CUtensorMap ta, tb, to0;
+  if ((rc = make_tmap_u8(&ta, h8, I, rows_cap, I, 128, 128, "fp8_down_fwd h8"))) return rc;
+  if ((rc = make_tmap_u8(&tb, wd8, I, static_cast<long long>(E) * H, I, 128, 128, "fp8_down_fwd w8")))
+    return rc;
+  if ((rc = make_out_tmap(&to0, y, H, rows_cap, "fp8_down_fwd y"))) return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = H / 256;
+  p.k_blocks = I / 128;
+  p.b_group_rows = H;
+  p.m_valid = rows_cap;
+  p.n_valid = H;
+  p.out = y;
+  p.ld_out = H;
+  p.deq_a = scale + 2;  // h
+  p.deq_g = q_d;
+  return launch_gemm_pair<256, false, false, kEpiStoreBf16, kRowsRagged, kOpE4m3>(
+      ta, tb, to0, to0, p, static_cast<cudaStream_t>(stream), "fp8_down_fwd");
+}
+
+int b200moe_fp8_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void* gu8,
+                                         const int* tile_expert, const int* pad_offsets,
+                                         long long rows_cap, int E, int H, int I,
+                                         const float* scale, float* amax, void* d_gu8,
+                                         void* stream) {
+  REQUIRE(dy && w_d && gu8 && tile_expert && pad_offsets && scale && amax && d_gu8,
+          "fp8_down_dgrad: null pointer");
+  int rc = check_fp8_shape("fp8_down_dgrad", rows_cap, E, H, I);
+  if (rc) return rc;
+  REQUIRE(aligned16(gu8) && aligned16(d_gu8), "fp8_down_dgrad: pointers must be 16-byte aligned");
+  const int BN = (I % 256 == 0) ? 256 : 128;
+  CUtensorMap ta, tb;
+  if ((rc = make_tmap(&ta, dy, H, rows_cap, H, 64, 128, "fp8_down_dgrad dy"))) return rc;
+  if ((rc = make_tmap(&tb, w_d, I, static_cast<long long>(E) * H, I, 64, 64, "fp8_down_dgrad w")))
+    return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = I / BN;
+  p.k_blocks = H / 64;
+  p.b_group_rows = H;
+  p.m_valid = rows_cap;
+  p.n_valid = I;
+  p.out = d_gu8;
+  p.ld_out = 2 * I;
+  p.aux = gu8;
+  p.ld_aux = 2 * I;
+  p.inter = I;
+  p.fp8_scale = scale;
+  p.fp8_amax = amax;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256)
+    return launch_gemm_pair<256, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, ta, ta, p, st,
+                                                                            "fp8_down_dgrad");
+  return launch_gemm_pair<128, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, ta, ta, p, st,
+                                                                          "fp8_down_dgrad");
+}
+
+int b200moe_fp8_expert_gate_up_dgrad(const void* d_gu8, const void* w8_gu, const float* q_gu,
+                                     const int* tile_expert, const int* pad_offsets,
+                                     long long rows_cap, int E, int H, int I, const float* scale,
+                                     void* dxs, void* stream) {
+  REQUIRE(d_gu8 && w8_gu && q_gu && tile_expert && pad_offsets && scale && dxs,
+          "fp8_gate_up_dgrad: null pointer");
+  int rc = check_fp8_shape("fp8_gate_up_dgrad", rows_cap, E, H, I);
+  if (rc) return rc;
+  CUtensorMap ta, tb, to0;
+  if ((rc = make_tmap_u8(&ta, d_gu8, 2 * I, rows_cap, 2 * I, 128, 128, "fp8_gate_up_dgrad d_gu8")))
+    return rc;
+  // B[n=h][k=j] = W8_gu[e][j][h]: MN-major, rows (e*2I + j), columns h
+  if ((rc = make_tmap_u8(&tb, w8_gu, H, static_cast<long long>(E) * 2 * I, H, 128, 128,
+                         "fp8_gate_up_dgrad w8")))
+    return rc;
+  if ((rc = make_out_tmap(&to0, dxs, H, rows_cap, "fp8_gate_up_dgrad dxs"))) return rc;
+  GemmParams p = blank_params();
+  p.tile_expert = tile_expert;
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.n_tiles = H / 256;
+  p.k_blocks = 2 * I / 128;
+  p.b_group_rows = 2 * I;
+  p.m_valid = rows_cap;
+  p.n_valid = H;
+  p.out = dxs;
+  p.ld_out = H;
+  p.deq_a = scale + 3;  // d_gu
+  p.deq_g = q_gu;
+  return launch_gemm_pair<256, false, true, kEpiStoreBf16, kRowsRagged, kOpE5m2E4m3>(
+      ta, tb, to0, to0, p, static_cast<cudaStream_t>(stream), "fp8_gate_up_dgrad");
+}
+
+int b200moe_fp8_expert_wgrad(const void* a8, int a_fmt, int M, const void* b8, int N,
+                             const int* pad_offsets, int E, long long rows_cap,
+                             const float* scale_a, const float* scale_b, float* dw, int accumulate,
+                             void* stream) {
+  REQUIRE(a8 && b8 && pad_offsets && scale_a && scale_b && dw, "fp8_wgrad: null pointer");
+  REQUIRE(a_fmt == 0 || a_fmt == 1, "fp8_wgrad: a_fmt 0 (e4m3) or 1 (e5m2)");
+  REQUIRE(M > 0 && M % 256 == 0, "fp8_wgrad: M must be a multiple of 256");
+  REQUIRE(N > 0 && N % 128 == 0, "fp8_wgrad: N must be a multiple of 128");
+  REQUIRE(E >= 1 && E <= kMaxPairExperts && rows_cap > 0 && rows_cap % 128 == 0,
+          "fp8_wgrad: bad rows/E");
+  REQUIRE(g_pair_gemm, "fp8_wgrad: the fp8 path runs only as two-CTA pair tiles");
+  CUtensorMap ta, tb, to;
+  int rc;
+  if ((rc = make_tmap_u8(&ta, a8, M, rows_cap, M, 128, 128, "fp8_wgrad a"))) return rc;
+  if ((rc = make_tmap_u8(&tb, b8, N, rows_cap, N, 128, 128, "fp8_wgrad b"))) return rc;
+  if ((rc = make_out_tmap_f32(&to, dw, N, static_cast<long long>(E) * M, "fp8_wgrad dw"))) return rc;
+  GemmParams p = blank_params();
+  p.pad_offsets = pad_offsets;
+  p.num_groups = E;
+  p.m_tiles = M / 128;
+  p.n_tiles = (N + 255) / 256;  // a last half tile reads zero columns; its stores are clipped
+  p.n_valid = N;
+  p.out = dw;
+  p.ld_out = N;
+  p.accumulate = accumulate;
+  p.out_group_stride = static_cast<long long>(M) * N;
+  p.deq_a = scale_a;
+  p.deq_b = scale_b;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (a_fmt == 1)
+    return launch_gemm_pair<256, true, true, kEpiStoreF32Tma, kKRagged, kOpE5m2E4m3>(
+        ta, tb, to, to, p, st, "fp8_wgrad");
+  return launch_gemm_pair<256, true, true, kEpiStoreF32Tma, kKRagged, kOpE4m3>(ta, tb, to, to, p,
+                                                                             st, "fp8_wgrad");
 }
 
 // ---------------------------------------------------------------- gathered-operand GEMMs

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
 namespace b200moe {
@@ -293,6 +294,57 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn_m
   return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
          (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
          (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// Instruction descriptor, kind::f8f6f4: fp32 accumulator; a_fmt / b_fmt 0 = e4m3,
+// 1 = e5m2 (MN-major operands are valid for both 8-bit formats).
+__host__ __device__ constexpr uint32_t make_idesc_f8(int M, int N, uint32_t a_fmt, uint32_t b_fmt,
+                                                     bool a_mn_major, bool b_mn_major) {
+  return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | (static_cast<uint32_t>(a_mn_major) << 15) |
+         (static_cast<uint32_t>(b_mn_major) << 16) | (static_cast<uint32_t>(N >> 3) << 17) |
+         (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// fp8 conversions (round to nearest even, saturating to the finite range:
+// the same values as clamp(v, -max, max) followed by a rounding cast)
+// ---------------------------------------------------------------------------
+enum Fp8Format : int { kE4M3 = 0, kE5M2 = 1 };
+
+template <int FMT>
+__device__ __forceinline__ uint32_t f32x2_to_fp8x2(float lo, float hi) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE,
+                                                        FMT == kE4M3 ? __NV_E4M3 : __NV_E5M2));
+}
+
+// four floats -> four fp8 bytes (little-endian: v[0] in the lowest byte)
+template <int FMT>
+__device__ __forceinline__ uint32_t pack_fp8x4(float a, float b, float c, float d) {
+  return f32x2_to_fp8x2<FMT>(a, b) | (f32x2_to_fp8x2<FMT>(c, d) << 16);
+}
+
+template <int FMT>
+__device__ __forceinline__ float2 fp8x2_to_f32x2(uint32_t two) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(two & 0xffffu),
+                                                   FMT == kE4M3 ? __NV_E4M3 : __NV_E5M2);
+  return __half22float2(*reinterpret_cast<const __half2*>(&h));
+}
+
+// four fp8 bytes -> four floats (exact)
+template <int FMT>
+__device__ __forceinline__ void unpack_fp8x4(uint32_t w, float* v) {
+  const float2 a = fp8x2_to_f32x2<FMT>(w);
+  const float2 b = fp8x2_to_f32x2<FMT>(w >> 16);
+  v[0] = a.x;
+  v[1] = a.y;
+  v[2] = b.x;
+  v[3] = b.y;
+}
+
+// Running absolute maxima recorded with an integer atomic max on the float's
+// bits (exact ordering for non-negative values).
+__device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
+  atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
 }
 
 }  // namespace b200moe

@@ -45,6 +45,25 @@ enum Epilogue : int {
   kEpiSwigluBwdCombine = 5,  // down dgrad from gathered d_out: combine backward fused in
   kEpiAxpby = 6,             // bf16 out = alpha*acc + beta*aux, or fp32 update += neg_lr*bf16(..)
   kEpiStoreF32Tma = 7,       // kEpiStoreF32 through shared memory and TMA stores / reduce-adds
+  kEpiSwigluFwdF8 = 8,       // fp8 gate_up: gu, h stored e4m3 with the delayed scales
+  kEpiSwigluBwdF8 = 9,       // down dgrad, SwiGLU backward against e4m3 gu, d_gu stored e5m2
+};
+
+// Operand kinds of the expert GEMMs: bf16 (tcgen05.mma kind::f16), or fp8
+// (kind::f8f6f4) with A and B formats e4m3 x e4m3 or e5m2 x e4m3.  An fp8
+// K block holds 128 elements, so a stage's shared-memory tiles have the same
+// bytes and the same 128-byte swizzle as a 64-element bf16 K block.
+enum OperandKind : int {
+  kOpBf16 = 0,
+  kOpE4m3 = 1,     // A e4m3, B e4m3
+  kOpE5m2E4m3 = 2  // A e5m2, B e4m3
+};
+
+template <int OP>
+struct OpTraits {
+  static constexpr int kBK = OP == kOpBf16 ? 64 : 128;   // elements per K block
+  static constexpr int kMmaK = OP == kOpBf16 ? 16 : 32;  // elements per MMA
+  static constexpr uint32_t kAFmt = OP == kOpE5m2E4m3 ? 1u : 0u;
 };
 
 // Which operand is gathered row by row from a token-major tensor (x or d_out)
@@ -105,7 +124,24 @@ struct GemmParams {
   float alpha, beta, neg_lr;
   float* update;
   long long ld_update;
+  // fp8 path (spark-gpt train.py:1301-1530): the delayed per-site scales
+  // (x, gu, h, d_gu, dy) and the amax slots the epilogues raise.  An output is
+  // multiplied by 1 / (deq_a[0] * deq_b[0] * deq_g[group]) over the pointers
+  // that are set: products of powers of two, so the scaling is exact.
+  const float* fp8_scale;
+  float* fp8_amax;
+  const float* deq_a;
+  const float* deq_b;
+  const float* deq_g;
 };
+
+__device__ __forceinline__ float deq_factor(const GemmParams& p, int g) {
+  float d = 1.f;
+  if (p.deq_a) d *= __ldg(p.deq_a);
+  if (p.deq_b) d *= __ldg(p.deq_b);
+  if (p.deq_g) d *= __ldg(p.deq_g + g);
+  return 1.0f / d;
+}
 
 __device__ __forceinline__ int gather_token(const GemmParams& p, int row) {
   const int f = __ldg(p.gather_rows + row);
@@ -227,7 +263,7 @@ __device__ __forceinline__ void epilogue_empty_tile(const GemmParams& p, const T
       float* o = static_cast<float*>(p.out) + T.g * p.out_group_stride +
                  static_cast<long long>(T.m * BM + row_in) * p.ld_out + T.n * BN;
       float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 4)
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2) && T.n * BN + c < p.n_valid; c += 4)
         *reinterpret_cast<float4*>(o + c) = z;
     } else {
       for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); ++c) {
@@ -326,6 +362,113 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
         store_bf16x32(dgu + p.inter + col, du);
       }
     }
+  } else if (EPI == kEpiSwigluFwdF8) {
+    // gu = x8 . W8[e]^T / (s_x q_e) rounded to bf16; h = silu(g) u; gu and h
+    // leave as e4m3 with the gu / h scales; amax of the unquantized values
+    // (train.py:1317-1354)
+    constexpr int HALF = BN / 2;
+    const int lane = row_in & 31;
+    const long long row = static_cast<long long>(T.m) * BM + row_in;
+    const bool row_ok = row < p.m_valid;
+    uint8_t* gu = static_cast<uint8_t*>(p.out) + row * p.ld_out;
+    uint8_t* hh = static_cast<uint8_t*>(p.out2) + row * p.ld_out2;
+    const float deq = deq_factor(p, T.g);
+    const float s_gu = __ldg(p.fp8_scale + 1), s_h = __ldg(p.fp8_scale + 2);
+    float m_gu = 0.f, m_h = 0.f;
+#pragma unroll 1
+    for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(taddr + c * 32, rg);
+      tmem_ld32(taddr + HALF + c * 32, ru);
+      tmem_wait_ld();
+      if (row_ok) {
+        const int col = T.n * HALF + c * 32;
+        uint32_t wg[8], wu[8], wh[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float g[4], u[4], h[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            g[j] = bf16_round(__uint_as_float(rg[4 * q + j]) * deq);
+            u[j] = bf16_round(__uint_as_float(ru[4 * q + j]) * deq);
+            h[j] = g[j] * sigmoidf_(g[j]) * u[j];
+            m_gu = fmaxf(m_gu, fmaxf(fabsf(g[j]), fabsf(u[j])));
+            m_h = fmaxf(m_h, fabsf(h[j]));
+          }
+          wg[q] = pack_fp8x4<kE4M3>(g[0] * s_gu, g[1] * s_gu, g[2] * s_gu, g[3] * s_gu);
+          wu[q] = pack_fp8x4<kE4M3>(u[0] * s_gu, u[1] * s_gu, u[2] * s_gu, u[3] * s_gu);
+          wh[q] = pack_fp8x4<kE4M3>(h[0] * s_h, h[1] * s_h, h[2] * s_h, h[3] * s_h);
+        }
+        uint4* dg = reinterpret_cast<uint4*>(gu + col);
+        uint4* du = reinterpret_cast<uint4*>(gu + p.inter + col);
+        uint4* dh = reinterpret_cast<uint4*>(hh + col);
+        dg[0] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+        dg[1] = make_uint4(wg[4], wg[5], wg[6], wg[7]);
+        du[0] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+        du[1] = make_uint4(wu[4], wu[5], wu[6], wu[7]);
+        dh[0] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+        dh[1] = make_uint4(wh[4], wh[5], wh[6], wh[7]);
+      }
+    }
+    m_gu = warp_max(m_gu);
+    m_h = warp_max(m_h);
+    if (lane == 0) {
+      atomic_max_nonneg(p.fp8_amax + 1, m_gu);
+      atomic_max_nonneg(p.fp8_amax + 2, m_h);
+    }
+  } else if (EPI == kEpiSwigluBwdF8) {
+    // dh = bf16(dy . W_d[e]); g, u from the e4m3 gu (x 1/s_gu); the SwiGLU
+    // backward; d_gu leaves as e5m2 with the d_gu scale; its amax recorded
+    // (train.py:1382-1423)
+    const int lane = row_in & 31;
+    const long long row = static_cast<long long>(T.m) * BM + row_in;
+    const bool row_ok = row < p.m_valid;
+    const uint8_t* gu = static_cast<const uint8_t*>(p.aux) + row * p.ld_aux;
+    uint8_t* dgu = static_cast<uint8_t*>(p.out) + row * p.ld_out;
+    const float inv_s_gu = 1.0f / __ldg(p.fp8_scale + 1);
+    const float s_dgu = __ldg(p.fp8_scale + 3);
+    float m_d = 0.f;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      if (row_ok) {
+        const int col = T.n * BN + c * 32;
+        const uint4* gs = reinterpret_cast<const uint4*>(gu + col);
+        const uint4* us = reinterpret_cast<const uint4*>(gu + p.inter + col);
+        const uint4 g0 = gs[0], g1 = gs[1], u0 = us[0], u1 = us[1];
+        const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+        const uint32_t uw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+        uint32_t wg[8], wu[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float g[4], u[4], dg[4], du[4];
+          unpack_fp8x4<kE4M3>(gw[q], g);
+          unpack_fp8x4<kE4M3>(uw[q], u);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            g[j] *= inv_s_gu;
+            u[j] *= inv_s_gu;
+            const float dh = bf16_round(__uint_as_float(r[4 * q + j]));
+            const float sig = sigmoidf_(g[j]);
+            dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+            du[j] = dh * g[j] * sig;
+            m_d = fmaxf(m_d, fmaxf(fabsf(dg[j]), fabsf(du[j])));
+          }
+          wg[q] = pack_fp8x4<kE5M2>(dg[0] * s_dgu, dg[1] * s_dgu, dg[2] * s_dgu, dg[3] * s_dgu);
+          wu[q] = pack_fp8x4<kE5M2>(du[0] * s_dgu, du[1] * s_dgu, du[2] * s_dgu, du[3] * s_dgu);
+        }
+        uint4* og = reinterpret_cast<uint4*>(dgu + col);
+        uint4* ou = reinterpret_cast<uint4*>(dgu + p.inter + col);
+        og[0] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
+        og[1] = make_uint4(wg[4], wg[5], wg[6], wg[7]);
+        ou[0] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+        ou[1] = make_uint4(wu[4], wu[5], wu[6], wu[7]);
+      }
+    }
+    m_d = warp_max(m_d);
+    if (lane == 0) atomic_max_nonneg(p.fp8_amax + 3, m_d);
   } else if (EPI == kEpiSwigluBwdCombine) {
     // acc = d_out[token] . W_d[e] (unscaled).  dh = bf16(w * acc); the routing
     // weight's gradient <d_out[token], y[row]> = <acc, h[row]> is summed here;
@@ -525,7 +668,8 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
 
 // The bf16-output epilogues (plain store, SwiGLU forward, SwiGLU backward) with
 // TMA stores.  Outputs: O0 = out (or gu / d_gu), O1 = h (SwiGLU forward).
-template <int EPI, int BN>
+// SCALED: multiply the accumulator by deq_factor (the fp8 GEMMs' dequantization).
+template <int EPI, int BN, bool SCALED = false>
 __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const TileInfo& T,
                                                   int quarter, int lane, int half,
                                                   uint32_t taddr, const CUtensorMap* tmO0,
@@ -537,8 +681,11 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
     // fp32 weight-gradient tile: each 32-column TMEM chunk leaves as two 32 x 16
     // boxes, stored (or reduce-added into the gradient when accumulating)
     const int rowg = T.g * p.m_tiles * BM + row0;  // (E*M, N) view of the output
+    const float sc = SCALED ? deq_factor(p, T.g) : 1.f;
 #pragma unroll 1
     for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      // columns past N (a last tile wider than what is left of N) are not stored
+      if (T.n * BN + c * 32 >= p.n_valid) break;
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_wait_ld();
@@ -547,7 +694,8 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
         ring_acquire<1>(lane);
         float v[16];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[16 * part + j]);
+        for (int j = 0; j < 16; ++j) v[j] = SCALED ? __uint_as_float(r[16 * part + j]) * sc
+                                                   : __uint_as_float(r[16 * part + j]);
         ring_put_f32(ring, 0, v, lane);
         fence_proxy_async_smem();
         __syncwarp();
@@ -565,6 +713,7 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
     }
   } else if (EPI == kEpiStoreBf16) {
     constexpr int G = B200MOE_EPI_GROUP < BN / 64 ? B200MOE_EPI_GROUP : BN / 64;
+    const float sc = SCALED ? deq_factor(p, T.g) : 1.f;
 #pragma unroll 1
     for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c += G) {
       uint32_t r[G][32];
@@ -581,7 +730,8 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
       for (int g = 0; g < G; ++g) {
         float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[g][j]);
+        for (int j = 0; j < 32; ++j) v[j] = SCALED ? __uint_as_float(r[g][j]) * sc
+                                                   : __uint_as_float(r[g][j]);
         ring_put(ring, g, v, lane);
         tms[g] = tmO0;
         cols[g] = T.n * BN + (c + g) * 32;

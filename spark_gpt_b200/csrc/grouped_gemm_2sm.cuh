@@ -95,6 +95,16 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t d_tmem, uint64_t adesc, 
       : "memory");
 }
 
+__device__ __forceinline__ void umma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on the barrier at this shared-memory offset in both CTAs of the pair
 // once the issuing thread's prior tcgen05 operations have completed.
 __device__ __forceinline__ void umma_commit_pair_both(uint64_t* bar) {
@@ -128,7 +138,7 @@ struct PairSmem {
 
 // This CTA's 128-row tile of pair tile t.  `half_ok` is false for the second
 // half of an expert's last pair when the expert has an odd tile count.
-template <int SCHED>
+template <int SCHED, int BK = 64>
 __device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* pair_start,
                                                 int t, uint32_t rank, bool& half_ok) {
   TileInfo T;
@@ -162,12 +172,16 @@ __device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* 
     const int s = __ldg(p.pad_offsets + T.g);
     const int e = __ldg(p.pad_offsets + T.g + 1);
     T.krow0 = s;
-    T.kblocks = (e - s) / 64;
+    T.kblocks = (e - s) / BK;
   }
   return T;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES>
+// OP: operand kind (OperandKind).  An fp8 stage carries 128 K elements in the
+// bytes of a 64-element bf16 stage; MN-major fp8 tiles are one 128-element
+// (128-byte) swizzle column wide, so their TMA box is 128 x 128 and the MMA's
+// 32-row K step advances 4 KB.  fp8 pair tiles need BN = 256 for MN-major B.
+template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED, int STAGES, int OP = kOpBf16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
@@ -175,12 +189,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                              const __grid_constant__ CUtensorMap tmO1, const GemmParams p) {
   static_assert(BN == 128 || BN == 256, "BN");
   static_assert(SCHED == kRowsRagged ? !A_MN : (A_MN && B_MN), "operand majors vs schedule");
+  static_assert(OP == kOpBf16 || !B_MN || BN == 256, "fp8 MN-major B needs BN = 256");
   constexpr int BM = 128;
-  constexpr int BK = 64;
+  constexpr bool kF8 = OP != kOpBf16;
+  constexpr int BK = OpTraits<OP>::kBK;
+  constexpr int kMmaK = OpTraits<OP>::kMmaK;
   constexpr bool kTmaOut = TmaOut<EPI>::value;
   using S = PairSmem<BN, STAGES, kTmaOut>;
   constexpr uint32_t kTmemCols = TmemCols<BN>::value;
-  constexpr uint32_t kIdesc = make_idesc_bf16(2 * BM, BN, A_MN, B_MN);
+  constexpr uint32_t kIdesc = kF8 ? make_idesc_f8(2 * BM, BN, OpTraits<OP>::kAFmt, 0u, A_MN, B_MN)
+                                  : make_idesc_bf16(2 * BM, BN, A_MN, B_MN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -272,7 +290,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       B200_PROF(unsigned long long pw = 0; const long long pt0 = clock64();)
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         bool half_ok;
-        const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
+        const TileInfo T = decode_pair<SCHED, BK>(p, pair_start, t, rank, half_ok);
         for (int kb = 0; kb < T.kblocks; ++kb) {
           B200_PROF(const long long w0 = clock64();)
           const bool got = mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
@@ -290,12 +308,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
             const int krow = T.krow0 + kb * BK;
             tma_load_2d_pair(a, &tmA, full_leader, T.m * BM, krow);
-            tma_load_2d_pair(a + 8192, &tmA, full_leader, T.m * BM + 64, krow);
+            if (!kF8) tma_load_2d_pair(a + 8192, &tmA, full_leader, T.m * BM + 64, krow);
           }
           if (!B_MN) {
             // this CTA's BN/2 rows of B: the gate (leader) or up (follower) rows for
             // SwiGLU, else the leader's or follower's half of the BN rows
-            const int row = (EPI == kEpiSwigluFwd)
+            const int row = (EPI == kEpiSwigluFwd || EPI == kEpiSwigluFwdF8)
                                 ? T.g * p.b_group_rows + static_cast<int>(rank) * p.b_half_offset +
                                       T.n * (BN / 2)
                                 : T.g * p.b_group_rows + T.n * BN + static_cast<int>(rank) * (BN / 2);
@@ -303,10 +321,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           } else {
             const int krow =
                 (SCHED == kKRagged) ? (T.krow0 + kb * BK) : (T.g * p.b_group_rows + kb * BK);
+            if (kF8) {
+              tma_load_2d_pair(b, &tmB, full_leader, T.n * BN + static_cast<int>(rank) * (BN / 2),
+                               krow);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j)
-              tma_load_2d_pair(b + j * 8192, &tmB, full_leader,
-                               T.n * BN + static_cast<int>(rank) * (BN / 2) + 64 * j, krow);
+              for (int j = 0; j < BN / 128; ++j)
+                tma_load_2d_pair(b + j * 8192, &tmB, full_leader,
+                                 T.n * BN + static_cast<int>(rank) * (BN / 2) + 64 * j, krow);
+            }
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -335,7 +358,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       B200_PROF(unsigned long long we = 0, wf = 0; const long long mt0 = clock64();)
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         bool half_ok;
-        const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
+        const TileInfo T = decode_pair<SCHED, BK>(p, pair_start, t, rank, half_ok);
         if (T.kblocks == 0) continue;
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -358,12 +381,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           const uint32_t a0 = smem_u32(sA + stage * S::kABytes);
           const uint32_t b0 = smem_u32(sB + stage * S::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            const uint64_t ad =
-                A_MN ? make_sdesc(a0 + kk * 2048, 8192, 1024) : make_sdesc(a0 + kk * 32, 16, 1024);
-            const uint64_t bd =
-                B_MN ? make_sdesc(b0 + kk * 2048, 8192, 1024) : make_sdesc(b0 + kk * 32, 16, 1024);
-            umma_bf16_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int kk = 0; kk < BK / kMmaK; ++kk) {
+            // K-major: 32 bytes per MMA step; MN-major: kMmaK rows of 128 bytes
+            const uint64_t ad = A_MN ? make_sdesc(a0 + kk * kMmaK * 128, 8192, 1024)
+                                     : make_sdesc(a0 + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sdesc(b0 + kk * kMmaK * 128, 8192, 1024)
+                                     : make_sdesc(b0 + kk * 32, 16, 1024);
+            if (kF8)
+              umma_f8_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+            else
+              umma_bf16_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit_pair_both(&empty[stage]);
           if (++stage == STAGES) {
@@ -388,7 +415,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               unsigned long long pacc[3] = {0, 0, 0};)
     for (int t = cluster_id; t < num_tiles; t += num_clusters) {
       bool half_ok;
-      const TileInfo T = decode_pair<SCHED>(p, pair_start, t, rank, half_ok);
+      const TileInfo T = decode_pair<SCHED, BK>(p, pair_start, t, rank, half_ok);
       if (T.kblocks == 0) {
         epilogue_empty_tile<EPI, BN>(p, T, row_in, half);
         continue;
@@ -405,7 +432,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * BN;
       if (half_ok) {
         if (tma_out)
-          epilogue_tile_tma<EPI, BN>(p, T, q, lane, half, taddr, &tmO0, &tmO1, ring
+          epilogue_tile_tma<EPI, BN, kF8>(p, T, q, lane, half, taddr, &tmO0, &tmO1, ring
                                      B200_PROF(, pacc));
         else
           epilogue_tile<EPI, BN>(p, T, row_in, half, taddr);

@@ -20,7 +20,7 @@ from __future__ import annotations
 import torch
 import torch.nn as nn
 
-from . import faults, ops
+from . import faults, fp8, ops
 from .custom_ops import TOKEN_MAJOR, _dispatch_from, moe_backward, norm_sparse_moe, sparse_moe
 
 BF16 = torch.bfloat16
@@ -202,11 +202,16 @@ class Experts(nn.Module):
             self.num_experts, 2 * self.intermediate_dim, self.hidden_dim))
         self.down_proj = nn.Parameter(torch.empty(
             self.num_experts, self.hidden_dim, self.intermediate_dim))
-        # kept so code that scans modules for the reference's fp8 state still works
+        # the fp8 path's delayed scales and amax slots (x, gu, h, d_gu, dy),
+        # train.py:2258-2260; see spark_gpt_b200.fp8
         self.register_buffer("fp8_scale", torch.ones(5), persistent=False)
         self.register_buffer("fp8_amax", torch.zeros(5), persistent=False)
 
     def forward(self, hidden_states, selected_experts, routing_weights):
+        if fp8.use_fp8(self, hidden_states):  # train.py:2292-2300
+            return fp8.FP8ExpertsFn.apply(hidden_states, selected_experts, routing_weights,
+                                          self.gate_up_proj, self.down_proj, self.fp8_scale,
+                                          self.fp8_amax)
         return _ExpertsFn.apply(hidden_states, selected_experts, routing_weights,
                                 self.gate_up_proj, self.down_proj)
 
@@ -224,7 +229,11 @@ class SparseMoE(nn.Module):
         shape = hidden_states.shape
         x = hidden_states.reshape(-1, shape[-1])
         _require_cuda(x)
-        if self._grad_sync is not None and torch.is_grad_enabled():
+        if fp8.use_fp8(self.experts, x):
+            # router in bf16, experts on the fp8 path (train.py:2292-2300)
+            logits, rw, sel = self.gate(x)
+            out = self.experts(x, sel, rw)
+        elif self._grad_sync is not None and torch.is_grad_enabled():
             out, logits, sel = _GradSyncMoEFn.apply(
                 x, self.gate.weight, self.experts.gate_up_proj, self.experts.down_proj,
                 self.gate.top_k, self.gate.norm_topk_prob, self._grad_sync)

@@ -367,6 +367,143 @@ def wgrad(a, b, d: Dispatch, name="wgrad", out=None, accumulate=False):
 
 
 # --------------------------------------------------------------------------- #
+# fp8 expert path (spark-gpt --fp8-mlp, train.py:1301-1604)
+# --------------------------------------------------------------------------- #
+E4M3 = torch.float8_e4m3fn
+E5M2 = torch.float8_e5m2
+_FP8_FMT = {E4M3: 0, E5M2: 1}
+
+
+def _check_fp8(t: torch.Tensor, name, dtypes=(E4M3, E5M2)):
+    if not t.is_cuda:
+        raise RuntimeError(f"{name}: the B200 MoE kernels need CUDA tensors (no CPU path)")
+    if t.dtype not in dtypes:
+        raise RuntimeError(f"{name}: expected one of {dtypes}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name}: expected a contiguous tensor")
+
+
+def _check_scales(scale, amax=None):
+    _check(scale, torch.float32, "fp8 scale")
+    if scale.numel() < 5:
+        raise RuntimeError("fp8 scale: expected the five per-site scales")
+    if amax is not None:
+        _check(amax, torch.float32, "fp8 amax")
+        if amax.numel() < 5:
+            raise RuntimeError("fp8 amax: expected the five amax slots")
+
+
+def fp8_quantize_experts(w: torch.Tensor):
+    """(e4m3 copy of w * q_e, q (E,) fp32) of fp32 (E, rows, cols) master
+    weights, q_e = 2^floor(log2(448 / max|w_e|)) (train.py:1536-1540)."""
+    w = w.detach().float().contiguous()
+    E = w.shape[0]
+    per = w[0].numel() if E else 0
+    w8 = torch.empty(w.shape, device=w.device, dtype=E4M3)
+    q = torch.empty(E, device=w.device, dtype=torch.float32)
+    if E and per:
+        nbytes = int(_lib.value("b200moe_fp8_quantize_experts_scratch_bytes", E))
+        scratch = torch.empty(nbytes, device=w.device, dtype=torch.uint8)
+        _launch("fp8_quantize", 3, "b200moe_fp8_quantize_experts", _p(w), E, per, _p(w8), _p(q),
+                _p(scratch), nbytes, _s(w))
+    return w8, q
+
+
+def fp8_gather_quant(x: torch.Tensor, d: Dispatch, scale, amax) -> torch.Tensor:
+    """x8 (Rcap, H) e4m3 = e4m3(x[token] * scale[0]), padding rows zero; amax[0] raised."""
+    _check(x, BF16, "fp8_gather_quant x")
+    _check_scales(scale, amax)
+    H = x.shape[1]
+    x8 = torch.empty(d.rows_cap, H, device=x.device, dtype=E4M3)
+    if d.num_tokens == 0:
+        return x8.zero_()
+    _launch("gather", 1, "b200moe_fp8_gather_quant", _p(x), _p(d.row_flat), _p(d.inv_pad),
+            _p(d.pad_offsets), d.num_tokens, d.num_experts, d.top_k, H, d.rows_cap, _p(scale),
+            _p(amax), _p(x8), _s(x))
+    return x8
+
+
+def fp8_quantize_rows(src: torch.Tensor, scale_slot: torch.Tensor, amax_slot: torch.Tensor,
+                      dtype=E5M2) -> torch.Tensor:
+    """fp8(src * scale_slot[0]) of a bf16 matrix, amax_slot[0] raised."""
+    _check(src, BF16, "fp8_quantize_rows src")
+    dst = torch.empty(src.shape, device=src.device, dtype=dtype)
+    rows, cols = src.shape
+    _launch("fp8_quantize_rows", 1, "b200moe_fp8_quantize_rows", _p(src), rows, cols,
+            _p(scale_slot), _p(amax_slot), _FP8_FMT[dtype], _p(dst), _s(src))
+    return dst
+
+
+def fp8_gate_up_fwd(x8, w8_gu, q_gu, d: Dispatch, scale, amax):
+    """gu8 (Rcap, 2I), h8 (Rcap, I) e4m3 (train.py:1317-1354)."""
+    _check_fp8(x8, "fp8_gate_up_fwd x8", (E4M3,))
+    _check_fp8(w8_gu, "fp8_gate_up_fwd w8", (E4M3,))
+    _check_scales(scale, amax)
+    E, two_i, H = w8_gu.shape
+    I = two_i // 2
+    gu8 = torch.empty(d.rows_cap, two_i, device=x8.device, dtype=E4M3)
+    h8 = torch.empty(d.rows_cap, I, device=x8.device, dtype=E4M3)
+    _launch("gate_up_fwd", 1, "b200moe_fp8_expert_gate_up_fwd", _p(x8), _p(w8_gu), _p(q_gu),
+            _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, I, _p(scale), _p(amax),
+            _p(gu8), _p(h8), _s(x8))
+    return gu8, h8
+
+
+def fp8_down_fwd(h8, wd8, q_d, d: Dispatch, scale):
+    """y (Rcap, H) bf16 = h8 . W8_d[e]^T / (scale[2] q_d[e]) (train.py:1357-1379)."""
+    _check_fp8(h8, "fp8_down_fwd h8", (E4M3,))
+    _check_fp8(wd8, "fp8_down_fwd w8", (E4M3,))
+    _check_scales(scale)
+    E, H, I = wd8.shape
+    y = torch.empty(d.rows_cap, H, device=h8.device, dtype=BF16)
+    _launch("down_fwd", 1, "b200moe_fp8_expert_down_fwd", _p(h8), _p(wd8), _p(q_d),
+            _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, I, _p(scale), _p(y), _s(h8))
+    return y
+
+
+def fp8_down_dgrad_swiglu(dy, w_d, gu8, d: Dispatch, scale, amax):
+    """d_gu8 (Rcap, 2I) e5m2 from bf16 dy and W_d (train.py:1382-1423)."""
+    _check(dy, BF16, "fp8_down_dgrad dy")
+    _check(w_d, BF16, "fp8_down_dgrad w")
+    _check_fp8(gu8, "fp8_down_dgrad gu8", (E4M3,))
+    _check_scales(scale, amax)
+    E, H, I = w_d.shape
+    d_gu8 = torch.empty(d.rows_cap, 2 * I, device=dy.device, dtype=E5M2)
+    _launch("down_dgrad", 1, "b200moe_fp8_expert_down_dgrad_swiglu", _p(dy), _p(w_d), _p(gu8),
+            _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, I, _p(scale), _p(amax),
+            _p(d_gu8), _s(dy))
+    return d_gu8
+
+
+def fp8_gate_up_dgrad(d_gu8, w8_gu, q_gu, d: Dispatch, scale):
+    """dxs (Rcap, H) bf16 = d_gu8 . W8_gu[e] / (scale[3] q_gu[e]) (train.py:1426-1448)."""
+    _check_fp8(d_gu8, "fp8_gate_up_dgrad d_gu8", (E5M2,))
+    _check_fp8(w8_gu, "fp8_gate_up_dgrad w8", (E4M3,))
+    _check_scales(scale)
+    E, two_i, H = w8_gu.shape
+    dxs = torch.empty(d.rows_cap, H, device=d_gu8.device, dtype=BF16)
+    _launch("gate_up_dgrad", 1, "b200moe_fp8_expert_gate_up_dgrad", _p(d_gu8), _p(w8_gu),
+            _p(q_gu), _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, two_i // 2,
+            _p(scale), _p(dxs), _s(d_gu8))
+    return dxs
+
+
+def fp8_wgrad(a8, b8, d: Dispatch, scale_a, scale_b, name="wgrad", out=None, accumulate=False):
+    """(E, M, N) fp32 (+)= a8_e^T b8_e / (scale_a[0] scale_b[0]) over the padded
+    rows of each expert (train.py:1451-1478, :1504-1530)."""
+    _check_fp8(a8, f"{name} a8")
+    _check_fp8(b8, f"{name} b8", (E4M3,))
+    M, N = a8.shape[1], b8.shape[1]
+    if out is None:
+        out = torch.empty(d.num_experts, M, N, device=a8.device, dtype=torch.float32)
+        accumulate = False
+    _launch(name, 1, "b200moe_fp8_expert_wgrad", _p(a8), _FP8_FMT[a8.dtype], M, _p(b8), N,
+            _p(d.pad_offsets), d.num_experts, d.rows_cap, _p(scale_a), _p(scale_b), _p(out),
+            int(accumulate), _s(a8))
+    return out
+
+
+# --------------------------------------------------------------------------- #
 # expert products with the row gather / combine backward fused in
 # --------------------------------------------------------------------------- #
 def gate_up_fwd_gather(x, w_gu, d: Dispatch):

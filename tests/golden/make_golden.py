@@ -14,7 +14,9 @@ It imports ``train.py`` from the reference checkout (not copied), runs its
 Newton-Schulz iteration (train.py:2877-2927) on its own, stored in
 ``tests/golden/muon_golden.pt`` (``--only muon`` writes just that file); and it runs
 the reference's ``RMSNorm`` (train.py:162-170) forward and backward into
-``tests/golden/norm_golden.pt`` (``--only norm``).  The large config-1 case stores its inputs as a
+``tests/golden/norm_golden.pt`` (``--only norm``), and the pure-torch pieces of
+its fp8 expert path (train.py:938-946, :1536-1540) into
+``tests/golden/fp8_golden.pt`` (``--only fp8``).  The large config-1 case stores its inputs as a
 seed plus checksums and keeps only slices and norms of the float outputs, so
 the fixture stays small.
 """
@@ -147,6 +149,40 @@ def make_norm_golden(train, out_path):
     print(f"wrote {out_path}: {', '.join(cases)}")
 
 
+def make_fp8_golden(train, out_path):
+    """The reference's pure-torch pieces of the fp8 expert path: the per-expert
+    e4m3 weight copies (train.py:1536-1540) and the delayed-scale update
+    (train.py:938-946) on seeded and edge-case inputs (an all-zero expert,
+    exact powers of two, amax slots that recorded nothing)."""
+    cases = {}
+    g = torch.Generator().manual_seed(21)
+    w = torch.randn(6, 64, 96, generator=g) * torch.tensor([0.02, 0.5, 3.0, 1e-4, 0.0, 7.0])[:, None, None]
+    w[5, 0, 0] = 448.0 / 8.0  # amax exactly 56: 448 / amax = 8 = 2^3
+    w8, q = train._fp8_quantize_experts(w)
+    cases["quantize_experts"] = {"w": w, "w8": w8.view(torch.uint8), "q": q}
+    amaxes = torch.tensor([
+        [4.5625, 3.4688, 5.1289, 0.0, 0.0],
+        [1.0, 448.0, 0.5, 57344.0, 3.0e-3],
+        [0.0, 0.0, 0.0, 0.0, 0.0],
+        [1e-35, 2.0 ** -20, 7.0, 1e10, 0.7],
+    ])
+    upd = []
+    for a in amaxes:
+        m = torch.nn.Module()
+        m.__class__ = type("M", (train.Experts,), {})  # fp8_update_scales matches Experts
+        torch.nn.Module.__init__(m)
+        m.register_buffer("fp8_scale", torch.tensor([2.0, 0.5, 1.0, 4.0, 1.0]))
+        m.register_buffer("fp8_amax", a.clone())
+        train.fp8_update_scales(m)
+        upd.append((a, m.fp8_scale.clone(), m.fp8_amax.clone()))
+    cases["update_scales"] = {"scale_in": torch.tensor([2.0, 0.5, 1.0, 4.0, 1.0]),
+                              "amax": torch.stack([u[0] for u in upd]),
+                              "scale_out": torch.stack([u[1] for u in upd]),
+                              "amax_out": torch.stack([u[2] for u in upd])}
+    torch.save(cases, out_path)
+    print(f"wrote {out_path}: {', '.join(cases)}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPARK_GPT_REFERENCE"),
@@ -154,7 +190,8 @@ def main():
     ap.add_argument("--out", default=str(HERE / "moe_golden.pt"))
     ap.add_argument("--muon-out", default=str(HERE / "muon_golden.pt"))
     ap.add_argument("--norm-out", default=str(HERE / "norm_golden.pt"))
-    ap.add_argument("--only", choices=["moe", "muon", "norm"], default=None)
+    ap.add_argument("--fp8-out", default=str(HERE / "fp8_golden.pt"))
+    ap.add_argument("--only", choices=["moe", "muon", "norm", "fp8"], default=None)
     args = ap.parse_args()
     if not args.reference:
         ap.error("name the reference checkout with --reference or SPARK_GPT_REFERENCE")
@@ -163,6 +200,10 @@ def main():
     import train  # the reference module, imported in place
     import torch.nn.functional as F
 
+    if args.only in (None, "fp8"):
+        make_fp8_golden(train, args.fp8_out)
+    if args.only == "fp8":
+        return
     if args.only in (None, "norm"):
         make_norm_golden(train, args.norm_out)
     if args.only == "norm":

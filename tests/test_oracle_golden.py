@@ -227,3 +227,25 @@ def test_rmsnorm_oracle_matches_reference(case):
     else:
         torch.testing.assert_close(dx, c["dx"], rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(dw, c["dw"], rtol=1e-5, atol=1e-6)
+
+
+def test_fp8_oracle_matches_reference_torch_pieces():
+    """The fp8 oracle's per-expert e4m3 weight copies and delayed-scale update
+    against the reference's own _fp8_quantize_experts and fp8_update_scales
+    (tests/golden/fp8_golden.pt, made by make_golden.py --only fp8): bit-exact,
+    including an all-zero expert, an amax that is an exact power of two, and
+    amax slots that recorded nothing (the scale is kept)."""
+    from oracle import fp8_oracle as F8
+    from tests.conftest import ROOT
+    c = torch.load(ROOT / "tests" / "golden" / "fp8_golden.pt", weights_only=True)
+    q = c["quantize_experts"]
+    w8, qe = F8.quantize_experts(q["w"])
+    assert torch.equal(qe, q["q"])
+    assert torch.equal(w8.view(torch.uint8), q["w8"])
+    u = c["update_scales"]
+    for a, s_out, a_out in zip(u["amax"], u["scale_out"], u["amax_out"]):
+        s = u["scale_in"].clone()
+        am = a.clone()
+        F8.update_scales(s, am)
+        assert torch.equal(s, s_out)
+        assert torch.equal(am, a_out)
