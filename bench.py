@@ -29,7 +29,13 @@ line also carries, measured in the same run:
   * ep: BASELINE configs[4] (cfg5) at this N -- the single-GPU layer at its
     per-GPU shape, and at N > 1 the expert-parallel layer with the
     peer-memory and the NCCL transports, with per-phase times and the
-    efficiency against the single-GPU layer.
+    efficiency against the single-GPU layer;
+  * torch_gpu_path (N = 1): the reference's own GPU path with FUSED_SWIGLU
+    off (F.grouped_mm) restated in stock torch ops, timed on the same GPU
+    with its agreement against this layer, plus cuBLAS on dense GEMMs of the
+    expert GEMMs' shapes (the library's rate for those M/N/K);
+  * fp8 (N = 1): the same step with the experts on the fp8 path
+    (spark-gpt --fp8-mlp), after a prewarm step and a scale update.
 
 --impl reference times the reference's CPU path (the oracle port of
 train.py's torch MoE path, fp32) on the host cores on a bounded token sample
@@ -704,6 +710,66 @@ def dense_gemm_block(c, T, pk, reps=10):
     return out
 
 
+def fp8_block(run, args, pk):
+    """The layer step on the fp8 expert path (spark-gpt --fp8-mlp on MoE
+    layers, train.py:1258-1604) at this config, N = 1: the same step as the
+    headline with spark_gpt_b200.fp8.FP8_MLP on, after a prewarm step and a
+    scale update as the reference's trainer does (train.py:4001-4002).  The
+    fp8 GEMMs' rates are against twice the measured bf16 burst peak (the dense
+    fp8 rate is twice the bf16 one on this part; no fp8 peak is measured
+    here), and the bf16 step is timed in the same run for the speed-up."""
+    from spark_gpt_b200 import fp8, fp8_update_scales
+    c = dict(CONFIGS[args.config])
+    T = c["T"]
+    layer = make_layer(c, run)
+    layer.train()
+    _, _, x, d_out = make_inputs(c, T, run)
+    valid = torch.ones(T, dtype=torch.bool, device=run.dev)
+    coef = torch.tensor(AUX_COEF, device=run.dev)
+    step = layer_step(layer, c, valid, coef)
+    names = list(gemm_flops(c, T)) + ROW_KERNELS + ["fp8_quantize", "fp8_quantize_rows"]
+    ms_bf16, _, _, _ = time_steps(run, lambda: step(x, d_out), args.sub_steps,
+                                  max(3, args.warmup), names)
+    saved = fp8.FP8_MLP
+    fp8.FP8_MLP = True
+    try:
+        if not fp8.use_fp8(layer.experts, x):
+            return {"unavailable": "shape outside the fp8 kernels' range"}
+        step(x, d_out)                    # prewarm: records the amax
+        fp8_update_scales(layer)
+        ms, per_op, _, launches = time_steps(run, lambda: step(x, d_out), args.sub_steps,
+                                             max(3, args.warmup), names)
+        scale = [float(v) for v in layer.experts.fp8_scale]
+    finally:
+        fp8.FP8_MLP = saved
+    flops = gemm_flops(c, T)
+    peak8 = 2 * pk["bf16"]
+    gemms = {}
+    for n in ("gate_up_fwd", "down_fwd", "gate_up_dgrad", "gate_up_wgrad", "down_wgrad"):
+        if n in per_op:
+            tf = flops[n] / (per_op[n] / 1e3) / 1e12
+            gemms[n] = {"ms": round(per_op[n], 5), "tflops": round(tf, 1),
+                        "frac_of_2x_bf16_burst": round(tf / peak8, 3)}
+    if "down_dgrad" in per_op:  # bf16 operands on this path too (train.py:1382-1423)
+        tf = flops["down_dgrad"] / (per_op["down_dgrad"] / 1e3) / 1e12
+        gemms["down_dgrad"] = {"ms": round(per_op["down_dgrad"], 5), "tflops": round(tf, 1),
+                               "frac_of_bf16_burst": round(tf / pk["bf16"], 3),
+                               "operands": "bf16"}
+    del layer, x, d_out, step
+    return {
+        "workload": f"{args.config}, {T} tokens: the layer step with the experts on the fp8 path "
+                    f"(e4m3 x/gu/h/weights, e5m2 d_gu/dy, delayed scales)",
+        "steps": args.sub_steps, "ms_per_step": ms, "tokens_per_s": T / (ms / 1e3),
+        "bf16_ms_per_step": ms_bf16, "speedup_vs_bf16": ms_bf16 / ms,
+        "scales_after_prewarm": scale,
+        "gemms": gemms,
+        "kernels_ms": {n: round(v, 5) for n, v in sorted(per_op.items())},
+        "gpu_launches_per_step": launches / args.sub_steps,
+        "peak_note": "fp8 GEMM fractions are of 2x the measured bf16 burst peak "
+                     f"({peak8:.0f} TFLOP/s; the nominal dense fp8 rate is 2x bf16)",
+    }
+
+
 def ep_block(run, args, pk):
     """BASELINE config 5 at this N: the single-GPU layer at cfg5's per-GPU
     shape on every rank (the baseline), then the expert-parallel layer over
@@ -843,6 +909,7 @@ def main():
 
     subs = {}
     torch_path = None
+    fp8_line = None
     if world == 1 and args.config == "cfg2" and not args.no_extra:
         for name in ("cfg3", "cfg4"):
             subs[name] = sub_block(name, run, args, pk)
@@ -850,6 +917,7 @@ def main():
             torch_path = torch_path_block(run, args, pk)
         except Exception as e:  # a comparator failure must not cost the product's line
             torch_path = {"unavailable": f"{type(e).__name__}: {str(e).splitlines()[0][:200]}"}
+        fp8_line = fp8_block(run, args, pk)
     ep = None
     if not args.no_ep and not c.get("ep"):
         ep = ep_block(run, args, pk)
@@ -882,6 +950,7 @@ def main():
         "muon_step": muon_line,
         "configs": subs or None,
         "torch_gpu_path": torch_path,
+        "fp8": fp8_line,
         "ep": ep,
         "gpu_launches": launches,
         "gpu_launches_per_step": launches / max(args.steps, 1),

@@ -279,11 +279,13 @@ int b200moe_fp8_gather_quant(const void* x, const int* row_flat, const int* inv_
                              void* stream);
 
 /* dst (rows,cols) fp8 = fp8(src * scale[0]) for a bf16 src, amax[0] raised;
- * fmt 0 = e4m3, 1 = e5m2.  The e5m2 copy of the rows' gradient that the down
- * weight gradient reads (the in-register quantization of
- * _fp8_moe_wgrad_rows_kernel, train.py:1504-1530). */
-int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const float* scale,
-                              float* amax, int fmt, void* dst, void* stream);
+ * fmt 0 = e4m3, 1 = e5m2.  total_rows (device int, or NULL for all rows)
+ * limits the rows read and written: the padded total pad_offsets[E] of a
+ * padded-row buffer, whose spare rows hold no data.  The e5m2 copy of the
+ * rows' gradient that the down weight gradient reads (the in-register
+ * quantization of _fp8_moe_wgrad_rows_kernel, train.py:1504-1530). */
+int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const int* total_rows,
+                              const float* scale, float* amax, int fmt, void* dst, void* stream);
 
 /* gu = x8 . W8_gu[e]^T / (scale[0] q_gu[e]) rounded to bf16, h = silu(g) u;
  * gu8 (Rcap,2I), h8 (Rcap,I) e4m3 with scale[1], scale[2]; amax[1], amax[2]

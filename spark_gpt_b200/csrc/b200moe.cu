@@ -246,6 +246,27 @@ int make_out_tmap_f32(CUtensorMap* m, const void* base, long long cols, long lon
   return B200MOE_OK;
 }
 
+// Output tensor maps of the fp8 TMA-store epilogues: a {32, 32} box of bytes,
+// unswizzled, over a (rows, cols) fp8 matrix.
+int make_out_tmap_u8(CUtensorMap* m, const void* base, long long cols, long long rows,
+                     const char* what) {
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0 || cols % 16 != 0)
+    return fail(B200MOE_ERR_INVALID_ARG, "%s: base or row stride not 16-byte aligned", what);
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI, int SCHED>
 int launch_expert_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
                        cudaStream_t st, const char* what, const CUtensorMap* to0 = nullptr,
@@ -1146,8 +1167,8 @@ int b200moe_fp8_gather_quant(const void* x, const int* row_flat, const int* inv_
   return check_launch("fp8_gather_quant");
 }
 
-int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const float* scale,
-                              float* amax, int fmt, void* dst, void* stream) {
+int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const int* total_rows,
+                              const float* scale, float* amax, int fmt, void* dst, void* stream) {
   REQUIRE(src && scale && amax && dst, "fp8_quantize_rows: null pointer");
   REQUIRE(rows >= 0 && cols > 0 && cols % 8 == 0, "fp8_quantize_rows: cols must be a multiple of 8");
   REQUIRE(fmt == 0 || fmt == 1, "fp8_quantize_rows: fmt 0 (e4m3) or 1 (e5m2)");
@@ -1157,11 +1178,13 @@ int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const f
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int grid = grid_for(n8, 256);
   if (fmt == 0)
-    fp8_quantize_rows_kernel<kE4M3><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), n8,
-                                                         scale, amax, static_cast<uint8_t*>(dst));
+    fp8_quantize_rows_kernel<kE4M3><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(src), n8, cols, total_rows, scale, amax,
+        static_cast<uint8_t*>(dst));
   else
-    fp8_quantize_rows_kernel<kE5M2><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), n8,
-                                                         scale, amax, static_cast<uint8_t*>(dst));
+    fp8_quantize_rows_kernel<kE5M2><<<grid, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(src), n8, cols, total_rows, scale, amax,
+        static_cast<uint8_t*>(dst));
   return check_launch("fp8_quantize_rows");
 }
 
@@ -1197,8 +1220,11 @@ int b200moe_fp8_expert_gate_up_fwd(const void* x8, const void* w8_gu, const floa
   p.fp8_amax = amax;
   p.deq_a = scale;  // x
   p.deq_g = q_gu;
+  CUtensorMap to0, to1;
+  if ((rc = make_out_tmap_u8(&to0, gu8, 2LL * I, rows_cap, "fp8_gate_up_fwd gu8"))) return rc;
+  if ((rc = make_out_tmap_u8(&to1, h8, I, rows_cap, "fp8_gate_up_fwd h8"))) return rc;
   return launch_gemm_pair<256, false, false, kEpiSwigluFwdF8, kRowsRagged, kOpE4m3>(
-      ta, tb, ta, ta, p, static_cast<cudaStream_t>(stream), "fp8_gate_up_fwd");
+      ta, tb, to0, to1, p, static_cast<cudaStream_t>(stream), "fp8_gate_up_fwd");
 }
 
 int b200moe_fp8_expert_down_fwd(const void* h8, const void* wd8, const float* q_d,
@@ -1260,11 +1286,13 @@ int b200moe_fp8_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const 
   p.inter = I;
   p.fp8_scale = scale;
   p.fp8_amax = amax;
+  CUtensorMap to0;
+  if ((rc = make_out_tmap_u8(&to0, d_gu8, 2LL * I, rows_cap, "fp8_down_dgrad d_gu8"))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (BN == 256)
-    return launch_gemm_pair<256, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, ta, ta, p, st,
-                                                                            "fp8_down_dgrad");
-  return launch_gemm_pair<128, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, ta, ta, p, st,
+    return launch_gemm_pair<256, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, to0, to0, p,
+                                                                            st, "fp8_down_dgrad");
+  return launch_gemm_pair<128, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, to0, to0, p, st,
                                                                           "fp8_down_dgrad");
 }
 

@@ -121,15 +121,19 @@ __global__ void fp8_weight_quant_kernel(const float* __restrict__ w, long long p
 }
 
 // ---------------------------------------------------------------------------
-// dst = fp8(src * scale) element-wise over a bf16 (rows, cols) matrix, amax of
-// |src| raised (the e5m2 copy of the expert rows' gradient that the down
-// projection's weight gradient reads, train.py:1504-1530).
+// dst = fp8(src * scale) element-wise over the first rows of a bf16 (rows,
+// cols) matrix (all rows, or *total_rows of them), amax of |src| raised (the
+// e5m2 copy of the expert rows' gradient that the down projection's weight
+// gradient reads, train.py:1504-1530).
 // ---------------------------------------------------------------------------
 template <int FMT>
 __global__ void fp8_quantize_rows_kernel(const __nv_bfloat16* __restrict__ src, long long n8,
+                                         int cols, const int* __restrict__ total_rows,
                                          const float* __restrict__ scale, float* __restrict__ amax,
                                          uint8_t* __restrict__ dst) {
   const float s = __ldg(scale);
+  // rows past the padded total (the buffer's spare capacity) hold no data
+  if (total_rows) n8 = min(n8, static_cast<long long>(*total_rows) * cols / 8);
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   float m = 0.f;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n8;

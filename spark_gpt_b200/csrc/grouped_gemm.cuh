@@ -362,113 +362,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams& p, const TileInf
         store_bf16x32(dgu + p.inter + col, du);
       }
     }
-  } else if (EPI == kEpiSwigluFwdF8) {
-    // gu = x8 . W8[e]^T / (s_x q_e) rounded to bf16; h = silu(g) u; gu and h
-    // leave as e4m3 with the gu / h scales; amax of the unquantized values
-    // (train.py:1317-1354)
-    constexpr int HALF = BN / 2;
-    const int lane = row_in & 31;
-    const long long row = static_cast<long long>(T.m) * BM + row_in;
-    const bool row_ok = row < p.m_valid;
-    uint8_t* gu = static_cast<uint8_t*>(p.out) + row * p.ld_out;
-    uint8_t* hh = static_cast<uint8_t*>(p.out2) + row * p.ld_out2;
-    const float deq = deq_factor(p, T.g);
-    const float s_gu = __ldg(p.fp8_scale + 1), s_h = __ldg(p.fp8_scale + 2);
-    float m_gu = 0.f, m_h = 0.f;
-#pragma unroll 1
-    for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
-      uint32_t rg[32], ru[32];
-      tmem_ld32(taddr + c * 32, rg);
-      tmem_ld32(taddr + HALF + c * 32, ru);
-      tmem_wait_ld();
-      if (row_ok) {
-        const int col = T.n * HALF + c * 32;
-        uint32_t wg[8], wu[8], wh[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float g[4], u[4], h[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            g[j] = bf16_round(__uint_as_float(rg[4 * q + j]) * deq);
-            u[j] = bf16_round(__uint_as_float(ru[4 * q + j]) * deq);
-            h[j] = g[j] * sigmoidf_(g[j]) * u[j];
-            m_gu = fmaxf(m_gu, fmaxf(fabsf(g[j]), fabsf(u[j])));
-            m_h = fmaxf(m_h, fabsf(h[j]));
-          }
-          wg[q] = pack_fp8x4<kE4M3>(g[0] * s_gu, g[1] * s_gu, g[2] * s_gu, g[3] * s_gu);
-          wu[q] = pack_fp8x4<kE4M3>(u[0] * s_gu, u[1] * s_gu, u[2] * s_gu, u[3] * s_gu);
-          wh[q] = pack_fp8x4<kE4M3>(h[0] * s_h, h[1] * s_h, h[2] * s_h, h[3] * s_h);
-        }
-        uint4* dg = reinterpret_cast<uint4*>(gu + col);
-        uint4* du = reinterpret_cast<uint4*>(gu + p.inter + col);
-        uint4* dh = reinterpret_cast<uint4*>(hh + col);
-        dg[0] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
-        dg[1] = make_uint4(wg[4], wg[5], wg[6], wg[7]);
-        du[0] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
-        du[1] = make_uint4(wu[4], wu[5], wu[6], wu[7]);
-        dh[0] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
-        dh[1] = make_uint4(wh[4], wh[5], wh[6], wh[7]);
-      }
-    }
-    m_gu = warp_max(m_gu);
-    m_h = warp_max(m_h);
-    if (lane == 0) {
-      atomic_max_nonneg(p.fp8_amax + 1, m_gu);
-      atomic_max_nonneg(p.fp8_amax + 2, m_h);
-    }
-  } else if (EPI == kEpiSwigluBwdF8) {
-    // dh = bf16(dy . W_d[e]); g, u from the e4m3 gu (x 1/s_gu); the SwiGLU
-    // backward; d_gu leaves as e5m2 with the d_gu scale; its amax recorded
-    // (train.py:1382-1423)
-    const int lane = row_in & 31;
-    const long long row = static_cast<long long>(T.m) * BM + row_in;
-    const bool row_ok = row < p.m_valid;
-    const uint8_t* gu = static_cast<const uint8_t*>(p.aux) + row * p.ld_aux;
-    uint8_t* dgu = static_cast<uint8_t*>(p.out) + row * p.ld_out;
-    const float inv_s_gu = 1.0f / __ldg(p.fp8_scale + 1);
-    const float s_dgu = __ldg(p.fp8_scale + 3);
-    float m_d = 0.f;
-#pragma unroll 1
-    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
-      uint32_t r[32];
-      tmem_ld32(taddr + c * 32, r);
-      tmem_wait_ld();
-      if (row_ok) {
-        const int col = T.n * BN + c * 32;
-        const uint4* gs = reinterpret_cast<const uint4*>(gu + col);
-        const uint4* us = reinterpret_cast<const uint4*>(gu + p.inter + col);
-        const uint4 g0 = gs[0], g1 = gs[1], u0 = us[0], u1 = us[1];
-        const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-        const uint32_t uw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-        uint32_t wg[8], wu[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float g[4], u[4], dg[4], du[4];
-          unpack_fp8x4<kE4M3>(gw[q], g);
-          unpack_fp8x4<kE4M3>(uw[q], u);
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            g[j] *= inv_s_gu;
-            u[j] *= inv_s_gu;
-            const float dh = bf16_round(__uint_as_float(r[4 * q + j]));
-            const float sig = sigmoidf_(g[j]);
-            dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
-            du[j] = dh * g[j] * sig;
-            m_d = fmaxf(m_d, fmaxf(fabsf(dg[j]), fabsf(du[j])));
-          }
-          wg[q] = pack_fp8x4<kE5M2>(dg[0] * s_dgu, dg[1] * s_dgu, dg[2] * s_dgu, dg[3] * s_dgu);
-          wu[q] = pack_fp8x4<kE5M2>(du[0] * s_dgu, du[1] * s_dgu, du[2] * s_dgu, du[3] * s_dgu);
-        }
-        uint4* og = reinterpret_cast<uint4*>(dgu + col);
-        uint4* ou = reinterpret_cast<uint4*>(dgu + p.inter + col);
-        og[0] = make_uint4(wg[0], wg[1], wg[2], wg[3]);
-        og[1] = make_uint4(wg[4], wg[5], wg[6], wg[7]);
-        ou[0] = make_uint4(wu[0], wu[1], wu[2], wu[3]);
-        ou[1] = make_uint4(wu[4], wu[5], wu[6], wu[7]);
-      }
-    }
-    m_d = warp_max(m_d);
-    if (lane == 0) atomic_max_nonneg(p.fp8_amax + 3, m_d);
+  } else if (EPI == kEpiSwigluFwdF8 || EPI == kEpiSwigluBwdF8) {
+    // the fp8 epilogues run only through the TMA-store ring (epilogue_tile_tma)
+    if (row_in == 0) raise_fault(kFaultBadShape);
   } else if (EPI == kEpiSwigluBwdCombine) {
     // acc = d_out[token] . W_d[e] (unscaled).  dh = bf16(w * acc); the routing
     // weight's gradient <d_out[token], y[row]> = <acc, h[row]> is summed here;
@@ -655,6 +551,24 @@ __device__ __forceinline__ void ring_flush(OutRing& ring, const CUtensorMap* con
   ring.next = (ring.next + G) % kOutRing;
 }
 
+// Chunk `slot` of the group: this lane's row of 32 fp8 bytes in the unswizzled
+// 32 x 32-byte box.
+__device__ __forceinline__ void ring_put_u8(const OutRing& ring, int slot, const uint32_t* w,
+                                            int lane) {
+  uint8_t* buf = ring.base + ((ring.next + slot) % kOutRing) * 2048;
+  uint4* rowp = reinterpret_cast<uint4*>(buf + lane * 32);
+  rowp[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  rowp[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+
+__device__ __forceinline__ void store_chunk_tma_u8(OutRing& ring, const CUtensorMap* tm,
+                                                   const uint32_t* w, int lane, int col,
+                                                   int row0) {
+  ring_acquire<1>(lane);
+  ring_put_u8(ring, 0, w, lane);
+  ring_flush<1>(ring, &tm, &col, row0, lane);
+}
+
 __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap* tm,
                                                 const float* v, int lane, int col, int row0) {
   ring_acquire<1>(lane);
@@ -739,6 +653,90 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
       ring_flush<G>(ring, tms, cols, row0, lane);
       B200_PROF(prof[2] += clock64() - q2;)
     }
+  } else if (EPI == kEpiSwigluFwdF8) {
+    // fp8 gate_up (train.py:1317-1354): g, u = bf16(acc / (s_x q_e)), h = silu(g) u;
+    // gu and h leave as e4m3 boxes with the gu / h scales; amax of g, u and h
+    constexpr int HALF = BN / 2;
+    const float deq = deq_factor(p, T.g);
+    const float s_gu = __ldg(p.fp8_scale + 1), s_h = __ldg(p.fp8_scale + 2);
+    float m_gu = 0.f, m_h = 0.f;
+#pragma unroll 1
+    for (int c = half * (HALF / 64); c < (half + 1) * (HALF / 64); ++c) {
+      uint32_t rg[32], ru[32];
+      tmem_ld32(taddr + c * 32, rg);
+      tmem_ld32(taddr + HALF + c * 32, ru);
+      tmem_wait_ld();
+      const int col = T.n * HALF + c * 32;
+      uint32_t wg[8], wu[8], wh[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float g[4], u[4], h[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          g[j] = bf16_round(__uint_as_float(rg[4 * q + j]) * deq);
+          u[j] = bf16_round(__uint_as_float(ru[4 * q + j]) * deq);
+          h[j] = g[j] * sigmoidf_(g[j]) * u[j];
+          m_gu = fmaxf(m_gu, fmaxf(fabsf(g[j]), fabsf(u[j])));
+          m_h = fmaxf(m_h, fabsf(h[j]));
+        }
+        wg[q] = pack_fp8x4<kE4M3>(g[0] * s_gu, g[1] * s_gu, g[2] * s_gu, g[3] * s_gu);
+        wu[q] = pack_fp8x4<kE4M3>(u[0] * s_gu, u[1] * s_gu, u[2] * s_gu, u[3] * s_gu);
+        wh[q] = pack_fp8x4<kE4M3>(h[0] * s_h, h[1] * s_h, h[2] * s_h, h[3] * s_h);
+      }
+      store_chunk_tma_u8(ring, tmO0, wg, lane, col, row0);
+      store_chunk_tma_u8(ring, tmO0, wu, lane, p.inter + col, row0);
+      store_chunk_tma_u8(ring, tmO1, wh, lane, col, row0);
+    }
+    m_gu = warp_max(m_gu);
+    m_h = warp_max(m_h);
+    if (lane == 0) {
+      atomic_max_nonneg(p.fp8_amax + 1, m_gu);
+      atomic_max_nonneg(p.fp8_amax + 2, m_h);
+    }
+  } else if (EPI == kEpiSwigluBwdF8) {
+    // down dgrad with the SwiGLU backward against the e4m3 gu (train.py:1382-1423):
+    // dh = bf16(acc); g, u = gu8 / s_gu; d_gu leaves as e5m2 boxes with the d_gu
+    // scale; amax of d_gate, d_up
+    const long long row = static_cast<long long>(row0) + lane;
+    const uint8_t* gu = static_cast<const uint8_t*>(p.aux) + row * p.ld_aux;
+    const float inv_s_gu = 1.0f / __ldg(p.fp8_scale + 1);
+    const float s_dgu = __ldg(p.fp8_scale + 3);
+    float m_d = 0.f;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      const int col = T.n * BN + c * 32;
+      const uint4* gs = reinterpret_cast<const uint4*>(gu + col);
+      const uint4* us = reinterpret_cast<const uint4*>(gu + p.inter + col);
+      const uint4 g0 = gs[0], g1 = gs[1], u0 = us[0], u1 = us[1];
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      const uint32_t gw[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const uint32_t uw[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+      uint32_t wg[8], wu[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float g[4], u[4], dg[4], du[4];
+        unpack_fp8x4<kE4M3>(gw[q], g);
+        unpack_fp8x4<kE4M3>(uw[q], u);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          g[j] *= inv_s_gu;
+          u[j] *= inv_s_gu;
+          const float dh = bf16_round(__uint_as_float(r[4 * q + j]));
+          const float sig = sigmoidf_(g[j]);
+          dg[j] = dh * u[j] * (sig * (1.0f + g[j] * (1.0f - sig)));
+          du[j] = dh * g[j] * sig;
+          m_d = fmaxf(m_d, fmaxf(fabsf(dg[j]), fabsf(du[j])));
+        }
+        wg[q] = pack_fp8x4<kE5M2>(dg[0] * s_dgu, dg[1] * s_dgu, dg[2] * s_dgu, dg[3] * s_dgu);
+        wu[q] = pack_fp8x4<kE5M2>(du[0] * s_dgu, du[1] * s_dgu, du[2] * s_dgu, du[3] * s_dgu);
+      }
+      store_chunk_tma_u8(ring, tmO0, wg, lane, col, row0);
+      store_chunk_tma_u8(ring, tmO0, wu, lane, p.inter + col, row0);
+    }
+    m_d = warp_max(m_d);
+    if (lane == 0) atomic_max_nonneg(p.fp8_amax + 3, m_d);
   } else if (EPI == kEpiSwigluFwd) {
     constexpr int HALF = BN / 2;
 #pragma unroll 1

@@ -121,7 +121,8 @@ constexpr int kMaxPairExperts = 256;  // the library takes E <= 256
 template <int EPI>
 struct TmaOut {
   static constexpr bool value = EPI == kEpiStoreBf16 || EPI == kEpiSwigluFwd ||
-                                EPI == kEpiSwigluBwd || EPI == kEpiStoreF32Tma;
+                                EPI == kEpiSwigluBwd || EPI == kEpiStoreF32Tma ||
+                                EPI == kEpiSwigluFwdF8 || EPI == kEpiSwigluBwdF8;
 };
 
 template <int BN, int STAGES, bool TMA_OUT>

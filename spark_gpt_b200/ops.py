@@ -424,12 +424,15 @@ def fp8_gather_quant(x: torch.Tensor, d: Dispatch, scale, amax) -> torch.Tensor:
 
 
 def fp8_quantize_rows(src: torch.Tensor, scale_slot: torch.Tensor, amax_slot: torch.Tensor,
-                      dtype=E5M2) -> torch.Tensor:
-    """fp8(src * scale_slot[0]) of a bf16 matrix, amax_slot[0] raised."""
+                      dtype=E5M2, d: Dispatch | None = None) -> torch.Tensor:
+    """fp8(src * scale_slot[0]) of a bf16 matrix, amax_slot[0] raised; with a
+    Dispatch, only the rows below its padded total (the rest of a padded-row
+    buffer holds no data and is left unwritten)."""
     _check(src, BF16, "fp8_quantize_rows src")
     dst = torch.empty(src.shape, device=src.device, dtype=dtype)
     rows, cols = src.shape
-    _launch("fp8_quantize_rows", 1, "b200moe_fp8_quantize_rows", _p(src), rows, cols,
+    total = None if d is None else d.pad_offsets[d.num_experts:]
+    _launch("fp8_quantize_rows", 1, "b200moe_fp8_quantize_rows", _p(src), rows, cols, _p(total),
             _p(scale_slot), _p(amax_slot), _FP8_FMT[dtype], _p(dst), _s(src))
     return dst
 

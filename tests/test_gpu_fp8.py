@@ -41,10 +41,12 @@ def _dispatch(sel, E):
 
 
 def _unpadded(d, t):
-    """Rows of a padded-row tensor in the reference's expert order (valid rows only)."""
-    rf = d.row_flat.cpu()
+    """Rows of a padded-row tensor in the reference's expert order (valid rows
+    only; rows past the padded total are spare capacity and hold nothing)."""
+    total = int(d.pad_offsets[-1])
+    rf = d.row_flat.cpu()[:total]
     keep = rf >= 0
-    return t.cpu()[keep], rf[keep]
+    return t.cpu()[:total][keep], rf[keep]
 
 
 def test_quantize_experts_bit_exact():
@@ -230,10 +232,11 @@ def test_fp8_gemms_match_oracle_arithmetic():
     # backward GEMMs on the device's own fp8 intermediates
     dy = (torch.randn(d.rows_cap, H) * 0.01).to(BF16).to(DEV)
     dy[d.row_flat < 0] = 0
+    dy[int(d.pad_offsets[-1]):] = float("nan")  # spare rows: never read
     wd = w_d.to(BF16).to(DEV)
     dgu8 = ops.fp8_down_dgrad_swiglu(dy, wd, gu8, d, scale, amax)
     dxs = ops.fp8_gate_up_dgrad(dgu8, w8, q_gu, d, scale)
-    dy8 = ops.fp8_quantize_rows(dy, scale[4:5], amax[4:5], ops.E5M2)
+    dy8 = ops.fp8_quantize_rows(dy, scale[4:5], amax[4:5], ops.E5M2, d)
     g_gu = ops.fp8_wgrad(dgu8, x8, d, scale[3:4], scale[0:1])
     g_d = ops.fp8_wgrad(dy8, h8, d, scale[4:5], scale[2:3])
     torch.cuda.synchronize()
