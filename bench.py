@@ -98,7 +98,7 @@ def parse_args():
                     help="skip the Muon optimizer-step measurement of the expert tensors")
     ap.add_argument("--ep-chunks", type=int, default=1,
                     help="expert parallel: token chunks pipelined against the exchanges")
-    ap.add_argument("--transport", default="p2p_pipe", choices=["nccl", "p2p", "p2p_pipe"],
+    ap.add_argument("--transport", default="p2p", choices=["nccl", "p2p", "p2p_pipe"],
                     help="expert parallel: NCCL all-to-all, peer-memory stores with group "
                          "barriers, or peer-memory stores pipelined per source rank")
     ap.add_argument("--comm-sms", type=int, default=16,
@@ -118,6 +118,10 @@ def parse_args():
                     help="expert-parallel block: uniform or Zipf-skewed routing")
     ap.add_argument("--ep-steps", type=int, default=20,
                     help="timed steps of each expert-parallel block measurement")
+    ap.add_argument("--fp8", action="store_true",
+                    help="N = 1: time the step with the experts on the fp8 path (spark-gpt "
+                         "--fp8-mlp), after a prewarm step and a scale update (profiling runs "
+                         "of the fp8 kernels; the default line is bf16)")
     return ap.parse_args()
 
 
@@ -872,6 +876,14 @@ def main():
     valid = torch.ones(T, dtype=torch.bool, device=dev)
     coef = torch.tensor(AUX_COEF, device=dev)
     step = layer_step(layer, c, valid, coef, sync)
+    if args.fp8:
+        if world > 1 or c.get("ep"):
+            raise SystemExit("bench.py --fp8: single-GPU, non-expert-parallel configs only")
+        from spark_gpt_b200 import fp8, fp8_update_scales
+        fp8.FP8_MLP = True
+        layer.train()
+        step(x, d_out)  # prewarm: the first amax
+        fp8_update_scales(layer)
 
     # ---------------- timed region: inputs resident in HBM
     names = list(gemm_flops(c, T)) + ROW_KERNELS + (EP_KERNELS if c.get("ep") else [])
@@ -930,7 +942,8 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp8 experts (e4m3/e5m2), bf16 elsewhere" if args.fp8 else "bf16",
         "data": "synthetic (seeded N(0,1) tokens, muP-init weights)",
         "config": config_block(args, c, world, sync is not None),
         "per_gpu_tokens_per_s": value / world,
