@@ -287,6 +287,18 @@ int b200moe_fp8_gather_quant(const void* x, const int* row_flat, const int* inv_
 int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const int* total_rows,
                               const float* scale, float* amax, int fmt, void* dst, void* stream);
 
+/* b200moe_combine_bwd (padded-row y) that also writes dy8 (Rcap,H) e5m2 =
+ * e5m2(dy * scale_dy[0]), padding rows zero, and raises amax_dy[0] with
+ * max|dy|: the combine backward of _CombineTopK (train.py:2235-2241) fused
+ * with the e5m2 quantization of its rows that _fp8_moe_wgrad_rows_kernel does
+ * in registers (train.py:1504-1530), so dy is not read a second time.  Pass
+ * scale + 4 and amax + 4 of the layer's five slots. */
+int b200moe_fp8_combine_bwd(const void* d_out, const void* y, const int* row_flat,
+                            const int* inv_pad, const int* pad_offsets, const void* weights,
+                            int E, long long T, int k, int H, long long rows_cap,
+                            const float* scale_dy, float* amax_dy, void* dy, float* d_weights,
+                            void* dy8, void* stream);
+
 /* gu = x8 . W8_gu[e]^T / (scale[0] q_gu[e]) rounded to bf16, h = silu(g) u;
  * gu8 (Rcap,2I), h8 (Rcap,I) e4m3 with scale[1], scale[2]; amax[1], amax[2]
  * raised.  Replaces _fp8_moe_swiglu_fwd_kernel (train.py:1317-1354). */

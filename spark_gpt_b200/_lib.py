@@ -55,6 +55,7 @@ PROTOTYPES = {
     "b200moe_fp8_quantize_experts": (I, [P, I, L, P, P, P, L, P]),
     "b200moe_fp8_gather_quant": (I, [P, P, P, P, L, I, I, I, L, P, P, P, P]),
     "b200moe_fp8_quantize_rows": (I, [P, L, I, P, P, P, I, P, P]),
+    "b200moe_fp8_combine_bwd": (I, [P, P, P, P, P, P, I, L, I, I, L, P, P, P, P, P, P]),
     "b200moe_fp8_expert_gate_up_fwd": (I, [P, P, P, P, P, L, I, I, I, P, P, P, P, P]),
     "b200moe_fp8_expert_down_fwd": (I, [P, P, P, P, P, L, I, I, I, P, P, P]),
     "b200moe_fp8_expert_down_dgrad_swiglu": (I, [P, P, P, P, P, L, I, I, I, P, P, P, P]),

@@ -1188,6 +1188,41 @@ int b200moe_fp8_quantize_rows(const void* src, long long rows, int cols, const i
   return check_launch("fp8_quantize_rows");
 }
 
+int b200moe_fp8_combine_bwd(const void* d_out, const void* y, const int* row_flat,
+                            const int* inv_pad, const int* pad_offsets, const void* weights,
+                            int E, long long T, int k, int H, long long rows_cap,
+                            const float* scale_dy, float* amax_dy, void* dy, float* d_weights,
+                            void* dy8, void* stream) {
+  REQUIRE(d_out && y && row_flat && inv_pad && pad_offsets && weights && dy && d_weights &&
+              scale_dy && amax_dy && dy8,
+          "fp8_combine_bwd: null pointer");
+  REQUIRE(H % 16 == 0 && H > 0 && k >= 1 && T >= 0, "fp8_combine_bwd: bad shape");
+  REQUIRE(aligned16(dy) && aligned16(dy8), "fp8_combine_bwd: pointers must be 16-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!(B200MOE_TOKEN_ORDER && k <= 32 && (H == 256 || H == 512 || H == 1024 || H == 2048))) {
+    // other shapes: the plain combine backward, then the e5m2 copy of its rows
+    int rc = b200moe_combine_bwd(d_out, y, row_flat, inv_pad, pad_offsets, weights, E, T, k, H,
+                                 rows_cap, 0, dy, d_weights, stream);
+    if (rc) return rc;
+    return b200moe_fp8_quantize_rows(dy, rows_cap, H, pad_offsets + E, scale_dy, amax_dy, 1, dy8,
+                                     stream);
+  }
+  auto* dop = static_cast<const __nv_bfloat16*>(d_out);
+  auto* yp = static_cast<const __nv_bfloat16*>(y);
+  auto* wp = static_cast<const __nv_bfloat16*>(weights);
+  auto* dyp = static_cast<__nv_bfloat16*>(dy);
+  auto* d8 = static_cast<uint8_t*>(dy8);
+  const int grid = grid_for(T > rows_cap / 32 ? T : rows_cap / 32, 8);
+  const int* tot = pad_offsets + E;
+  switch (H) {
+    case 256: combine_bwd_tokens_kernel<1, true><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights, scale_dy, amax_dy, d8); break;
+    case 512: combine_bwd_tokens_kernel<2, true><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights, scale_dy, amax_dy, d8); break;
+    case 1024: combine_bwd_tokens_kernel<4, true><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights, scale_dy, amax_dy, d8); break;
+    default: combine_bwd_tokens_kernel<8, true><<<grid, 256, 0, st>>>(dop, yp, inv_pad, row_flat, tot, wp, T, k, H, dyp, d_weights, scale_dy, amax_dy, d8); break;
+  }
+  return check_launch("fp8_combine_bwd");
+}
+
 int b200moe_fp8_expert_gate_up_fwd(const void* x8, const void* w8_gu, const float* q_gu,
                                    const int* tile_expert, const int* pad_offsets,
                                    long long rows_cap, int E, int H, int I, const float* scale,

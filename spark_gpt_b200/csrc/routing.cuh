@@ -343,8 +343,10 @@ __global__ void scatter_rows_kernel(const __nv_bfloat16* __restrict__ x,
 // is read once and the rows of its k slots are visited through inv_pad (the
 // next slot's y row is loaded while the current one is processed):
 //   dy[r] = bf16(d_out[t] * w[t,s]),  d_weights[t*k+s] = <d_out[t], y[r]>,
-// then the padding rows of dy are zeroed.
-template <int VPL>
+// then the padding rows of dy are zeroed.  F8: the same rows also leave as
+// dy8 = e5m2(dy * q_scale[0]) (the fp8 down weight gradient's operand), with
+// the amax of |dy| raised in q_amax[0].
+template <int VPL, bool F8 = false>
 __global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_out,
                                           const __nv_bfloat16* __restrict__ y,
                                           const int* __restrict__ inv_pad,
@@ -352,9 +354,14 @@ __global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_ou
                                           const int* __restrict__ total_rows,
                                           const __nv_bfloat16* __restrict__ weights, long long T,
                                           int k, int H, __nv_bfloat16* __restrict__ dy,
-                                          float* __restrict__ d_weights) {
+                                          float* __restrict__ d_weights,
+                                          const float* __restrict__ q_scale = nullptr,
+                                          float* __restrict__ q_amax = nullptr,
+                                          uint8_t* __restrict__ dy8 = nullptr) {
   static_assert(VPL > 0, "token-order combine backward needs H in {256, 512, 1024, 2048}");
   const int lane = threadIdx.x & 31;
+  const float qs = F8 ? __ldg(q_scale) : 0.f;
+  float qm = 0.f;
   const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
   const long long warp_id = blockIdx.x * static_cast<long long>(blockDim.x >> 5) + (threadIdx.x >> 5);
   for (long long t = warp_id; t < T; t += warps) {
@@ -409,6 +416,15 @@ __global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_ou
         o.z = pack_bf16x2(ga[j][4] * w, ga[j][5] * w);
         o.w = pack_bf16x2(ga[j][6] * w, ga[j][7] * w);
         dst[lane + 32 * j] = o;
+        if constexpr (F8) {
+          const float v[8] = {bf16_lo(o.x), bf16_hi(o.x), bf16_lo(o.y), bf16_hi(o.y),
+                              bf16_lo(o.z), bf16_hi(o.z), bf16_lo(o.w), bf16_hi(o.w)};
+#pragma unroll
+          for (int e = 0; e < 8; ++e) qm = fmaxf(qm, fabsf(v[e]));
+          reinterpret_cast<uint2*>(dy8 + r * H)[lane + 32 * j] =
+              make_uint2(pack_fp8x4<kE5M2>(v[0] * qs, v[1] * qs, v[2] * qs, v[3] * qs),
+                         pack_fp8x4<kE5M2>(v[4] * qs, v[5] * qs, v[6] * qs, v[7] * qs));
+        }
       }
       dot = warp_sum(dot);
       if (lane == s) my_dot = dot;
@@ -416,6 +432,22 @@ __global__ void combine_bwd_tokens_kernel(const __nv_bfloat16* __restrict__ d_ou
     if (lane < k) d_weights[t * k + lane] = my_dot;
   }
   zero_padding_rows<VPL>(row_flat, *total_rows, H, warp_id, warps, lane, dy);
+  if constexpr (F8) {
+    // the padding rows of dy8 (H bytes each)
+    const long long total = *total_rows;
+    for (long long base = warp_id * 32; base < total; base += warps * 32) {
+      const long long r = base + lane;
+      unsigned pad = __ballot_sync(0xffffffffu, r < total && row_flat[r] < 0);
+      while (pad) {
+        const int i = __ffs(pad) - 1;
+        pad &= pad - 1;
+        uint4* d8 = reinterpret_cast<uint4*>(dy8 + (base + i) * H);
+        for (int v = lane; v < H / 16; v += 32) d8[v] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    qm = warp_max(qm);
+    if (lane == 0 && qm > 0.f) atomic_max_nonneg(q_amax, qm);
+  }
 }
 
 // dx[t] = sum_s dxs[inv_pad[t*k+s]] (+ addend[t]); fp32 accumulation.  With

@@ -98,8 +98,7 @@ class FP8ExpertsFn(torch.autograd.Function):
         faults.raise_pending(y.device)
         d = ctx.dispatch
         xdtype, wdtype = ctx.cfg
-        dy, d_rw = ops.combine_bwd(_as_bf16(d_out), y, d, rw)
-        dy8 = ops.fp8_quantize_rows(dy, scale[4:5], amax[4:5], ops.E5M2, d)
+        dy, d_rw, dy8 = ops.fp8_combine_bwd(_as_bf16(d_out), y, d, rw, scale[4:5], amax[4:5])
         d_gu8 = ops.fp8_down_dgrad_swiglu(dy, wd, gu8, d, scale, amax)
         dxs = ops.fp8_gate_up_dgrad(d_gu8, w8, q_gu, d, scale)
         g_gu = (ops.fp8_wgrad(d_gu8, x8, d, scale[3:4], scale[0:1], name="gate_up_wgrad")

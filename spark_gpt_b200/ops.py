@@ -437,6 +437,26 @@ def fp8_quantize_rows(src: torch.Tensor, scale_slot: torch.Tensor, amax_slot: to
     return dst
 
 
+def fp8_combine_bwd(d_out, y, d: Dispatch, weights, scale_slot, amax_slot):
+    """combine_bwd that also returns dy8 = e5m2(dy * scale_slot[0]) (padding
+    rows zero) and raises amax_slot[0] with max|dy| (one pass over dy)."""
+    _check(d_out, BF16, "fp8_combine_bwd d_out")
+    _check(weights, BF16, "fp8_combine_bwd weights")
+    H = y.shape[1]
+    if d.num_tokens == 0:
+        return (torch.zeros(d.rows_cap, H, device=y.device, dtype=BF16),
+                torch.zeros(0, d.top_k, device=y.device, dtype=torch.float32),
+                torch.zeros(d.rows_cap, H, device=y.device, dtype=E5M2))
+    dy = torch.empty(d.rows_cap, H, device=y.device, dtype=BF16)
+    dy8 = torch.empty(d.rows_cap, H, device=y.device, dtype=E5M2)
+    dw = torch.empty(d.num_tokens, d.top_k, device=y.device, dtype=torch.float32)
+    _launch("combine_bwd", 1, "b200moe_fp8_combine_bwd", _p(d_out), _p(y), _p(d.row_flat),
+            _p(d.inv_pad), _p(d.pad_offsets), _p(weights), d.num_experts, d.num_tokens,
+            d.top_k, H, d.rows_cap, _p(scale_slot), _p(amax_slot), _p(dy), _p(dw), _p(dy8),
+            _s(y))
+    return dy, dw, dy8
+
+
 def fp8_gate_up_fwd(x8, w8_gu, q_gu, d: Dispatch, scale, amax):
     """gu8 (Rcap, 2I), h8 (Rcap, I) e4m3 (train.py:1317-1354)."""
     _check_fp8(x8, "fp8_gate_up_fwd x8", (E4M3,))

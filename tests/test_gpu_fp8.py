@@ -83,6 +83,30 @@ def test_gather_quant_and_row_quant_bit_exact(T, H, E, k):
     assert float(amax[4]) == float(src.float().abs().max())
 
 
+@pytest.mark.parametrize("T,H,E,k", [(777, 256, 8, 2), (2048, 1024, 64, 8), (512, 4096, 16, 4)])
+def test_fused_combine_bwd_e5m2_bit_exact(T, H, E, k):
+    """The combine backward with the e5m2 copy of its rows fused in equals the
+    plain combine backward followed by the separate quantization, bit for bit
+    (H = 4096 takes the unfused fallback inside the entry point)."""
+    from spark_gpt_b200 import ops
+    torch.manual_seed(T + H)
+    sel = torch.stack([torch.randperm(E)[:k] for _ in range(T)])
+    d = _dispatch(sel, E)
+    y = (torch.randn(d.rows_cap, H, device=DEV) * 0.5).to(BF16)
+    d_out = (torch.randn(T, H, device=DEV) * 30).to(BF16)
+    w = torch.softmax(torch.randn(T, k, device=DEV), -1).to(BF16)
+    scale = torch.tensor([1.0, 1, 1, 1, 512.0], device=DEV)
+    am1, am2 = torch.zeros(5, device=DEV), torch.zeros(5, device=DEV)
+    dy, dw, dy8 = ops.fp8_combine_bwd(d_out, y, d, w, scale[4:5], am1[4:5])
+    dy_r, dw_r = ops.combine_bwd(d_out, y, d, w)
+    dy8_r = ops.fp8_quantize_rows(dy_r, scale[4:5], am2[4:5], ops.E5M2, d)
+    total = int(d.pad_offsets[-1])
+    assert torch.equal(dy[:total], dy_r[:total])
+    assert torch.equal(dw, dw_r)
+    assert torch.equal(_bytes(dy8[:total]), _bytes(dy8_r[:total]))
+    assert float(am1[4]) == float(am2[4]) > 0
+
+
 def _layer_case(T, H, E, k, I, seed, unused=None):
     torch.manual_seed(seed)
     w_gu = torch.randn(E, 2 * I, H) * 0.05
