@@ -160,9 +160,9 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
 #endif
 constexpr uint32_t kMaxDynSmem = 227 * 1024;
 
-template <int BN, bool TMA_OUT>
+template <int BN, bool TMA_OUT, bool GU_IN = false>
 constexpr int pair_stages() {
-  using S1 = PairSmem<BN, 1, TMA_OUT>;
+  using S1 = PairSmem<BN, 1, TMA_OUT, GU_IN>;
   constexpr int fit = static_cast<int>((kMaxDynSmem - (S1::kTotal - S1::kStageBytes)) /
                                        S1::kStageBytes);
   return fit < B200MOE_PAIR_STAGES_MAX ? fit : B200MOE_PAIR_STAGES_MAX;
@@ -177,9 +177,10 @@ int launch_gemm_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
                      const CUtensorMap& to1, const GemmParams& p, cudaStream_t st,
                      const char* what) {
   constexpr bool kTmaOut = TmaOut<EPI>::value;
-  constexpr int STAGES = pair_stages<BN, kTmaOut>();
+  constexpr bool kGuIn = GuIn<EPI>::value;
+  constexpr int STAGES = pair_stages<BN, kTmaOut, kGuIn>();
   auto kern = grouped_gemm_pair_kernel<BN, A_MN, B_MN, EPI, SCHED, STAGES, OP>;
-  const int smem = static_cast<int>(PairSmem<BN, STAGES, kTmaOut>::kTotal);
+  const int smem = static_cast<int>(PairSmem<BN, STAGES, kTmaOut, kGuIn>::kTotal);
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return fail(B200MOE_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
@@ -1019,10 +1020,11 @@ int b200moe_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const void
   p.ld_aux = 2 * I;
   p.inter = I;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  CUtensorMap to0;
+  CUtensorMap to0, to1;  // d_gu out, gu in (the pair kernel's epilogue loads it by TMA)
   if ((rc = make_out_tmap(&to0, d_gu, 2LL * I, rows_cap, "down_dgrad d_gu"))) return rc;
-  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad", &to0);
-  if (BN == 128) return launch_expert_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad", &to0);
+  if ((rc = make_out_tmap(&to1, gu, 2LL * I, rows_cap, "down_dgrad gu"))) return rc;
+  if (BN == 256) return launch_expert_gemm<256, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad", &to0, &to1);
+  if (BN == 128) return launch_expert_gemm<128, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad", &to0, &to1);
   return launch_expert_gemm<64, false, true, kEpiSwigluBwd, kRowsRagged>(ta, tb, p, st, "down_dgrad");
 }
 

@@ -494,7 +494,30 @@ constexpr int kOutRing = B200MOE_OUT_RING;
 struct OutRing {
   uint8_t* base;  // kOutRing x 2048 bytes, 512-byte aligned
   int next;
+  // SwiGLU-backward epilogue of the pair kernel: two 2 KB buffers that a TMA
+  // load fills with the warp's 32 x 32 chunk of g and of u, completing on
+  // in_bar (one phase per chunk)
+  uint8_t* in = nullptr;
+  uint64_t* in_bar = nullptr;
+  uint32_t in_phase = 0;
+  volatile int* abort = nullptr;
 };
+
+// Issue the TMA loads of one 32-row x 32-column chunk of g (column col) and of
+// u (column inter + col) into the warp's input buffers (64-byte swizzle, the
+// layout ring_put writes).  Every lane's earlier reads of the buffers are
+// ordered before the asynchronous refill (proxy fence, then the warp
+// converges); lane 0 issues; completion on ring.in_bar.
+__device__ __forceinline__ void gu_chunk_load(const OutRing& ring, const CUtensorMap* tm,
+                                              int col, int inter, int row0, int lane) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    mbar_expect_tx(ring.in_bar, 2 * 2048);
+    tma_load_2d(ring.in, tm, ring.in_bar, col, row0);
+    tma_load_2d(ring.in + 2048, tm, ring.in_bar, inter + col, row0);
+  }
+}
 
 // Chunks of one warp are stored in groups of G: G chunks are written to
 // consecutive ring buffers, then one proxy fence and one bulk group of G TMA
@@ -759,37 +782,27 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
       store_chunk_tma(ring, tmO1, g, lane, col, row0);
     }
   } else {  // kEpiSwigluBwd
-    // g, u of the next 32-column chunk are loaded while this one is processed
-    const long long row = static_cast<long long>(row0) + lane;
-    const __nv_bfloat16* gu = static_cast<const __nv_bfloat16*>(p.aux) + row * p.ld_aux;
+    // g, u of each 32-column chunk arrive by TMA in the warp's input buffers
+    // (the first chunk's load was issued before the accumulator wait); the
+    // next chunk's load is issued as soon as this one's values are in registers
     const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
-    uint4 gn[4], un[4];
-    {
-      const uint4* gs = reinterpret_cast<const uint4*>(gu + T.n * BN + c0 * 32);
-      const uint4* us = reinterpret_cast<const uint4*>(gu + p.inter + T.n * BN + c0 * 32);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        gn[j] = gs[j];
-        un[j] = us[j];
-      }
-    }
+    const int sw = (lane >> 1) & 3;
 #pragma unroll 1
     for (int c = c0; c < c1; ++c) {
+      const bool got = __all_sync(0xffffffffu, mbar_wait(ring.in_bar, ring.in_phase, ring.abort));
+      if (!got) return;
+      ring.in_phase ^= 1u;
       uint4 gc[4], uc[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        gc[j] = gn[j];
-        uc[j] = un[j];
-      }
-      if (c + 1 < c1) {
-        const uint4* gs = reinterpret_cast<const uint4*>(gu + T.n * BN + (c + 1) * 32);
-        const uint4* us = reinterpret_cast<const uint4*>(gu + p.inter + T.n * BN + (c + 1) * 32);
+      {
+        const uint4* gs = reinterpret_cast<const uint4*>(ring.in + lane * 64);
+        const uint4* us = reinterpret_cast<const uint4*>(ring.in + 2048 + lane * 64);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-          gn[j] = gs[j];
-          un[j] = us[j];
+          gc[j] = gs[j ^ sw];
+          uc[j] = us[j ^ sw];
         }
       }
+      if (c + 1 < c1) gu_chunk_load(ring, tmO1, T.n * BN + (c + 1) * 32, p.inter, row0, lane);
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_wait_ld();

@@ -125,16 +125,24 @@ struct TmaOut {
                                 EPI == kEpiSwigluFwdF8 || EPI == kEpiSwigluBwdF8;
 };
 
-template <int BN, int STAGES, bool TMA_OUT>
+// Epilogues that read a second input tile (g and u of the SwiGLU backward)
+// through TMA into per-warp buffers.
+template <int EPI>
+struct GuIn {
+  static constexpr bool value = EPI == kEpiSwigluBwd;
+};
+
+template <int BN, int STAGES, bool TMA_OUT, bool GU_IN = false>
 struct PairSmem {
   static constexpr uint32_t kABytes = 128 * 64 * 2;
   static constexpr uint32_t kBBytes = (BN / 2) * 64 * 2;
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t kOutBytes = TMA_OUT ? kEpilogueWarps * kOutRing * 2048 : 0;
+  static constexpr uint32_t kInBytes = GU_IN ? kEpilogueWarps * 2 * 2048 : 0;
   static constexpr uint32_t kBarrierBytes = 256;
   static constexpr uint32_t kPairTableBytes = (kMaxPairExperts + 1) * 4;
   static constexpr uint32_t kTotal =
-      STAGES * kStageBytes + kOutBytes + kBarrierBytes + kPairTableBytes + 1024;
+      STAGES * kStageBytes + kOutBytes + kInBytes + kBarrierBytes + kPairTableBytes + 1024;
 };
 
 // This CTA's 128-row tile of pair tile t.  `half_ok` is false for the second
@@ -196,7 +204,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int BK = OpTraits<OP>::kBK;
   constexpr int kMmaK = OpTraits<OP>::kMmaK;
   constexpr bool kTmaOut = TmaOut<EPI>::value;
-  using S = PairSmem<BN, STAGES, kTmaOut>;
+  constexpr bool kGuIn = GuIn<EPI>::value;
+  static_assert(!kGuIn || kTmaOut, "the gu input buffers come with the TMA-store ring");
+  using S = PairSmem<BN, STAGES, kTmaOut, kGuIn>;
   constexpr uint32_t kTmemCols = TmemCols<BN>::value;
   constexpr uint32_t kIdesc = kF8 ? make_idesc_f8(2 * BM, BN, OpTraits<OP>::kAFmt, 0u, A_MN, B_MN)
                                   : make_idesc_bf16(2 * BM, BN, A_MN, B_MN);
@@ -207,13 +217,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kABytes;
   uint8_t* sOut = sB + STAGES * S::kBBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + S::kOutBytes);
+  uint8_t* sIn = sOut + S::kOutBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sIn + S::kInBytes);
   uint64_t* full = bars;
   uint64_t* empty = bars + STAGES;
   uint64_t* tfull = bars + 2 * STAGES;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* in_bars = tempty + 3;  // kGuIn: one per epilogue warp, after tmem_slot / abort_flag
+  static_assert(!kGuIn || (2 * STAGES + 5 + kEpilogueWarps) * 8 <= S::kBarrierBytes,
+                "barrier area");
   int* pair_start = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + S::kBarrierBytes);
 
   const int warp = threadIdx.x >> 5;
@@ -232,6 +246,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 2 * kEpilogueWarps);
     }
+    if (kGuIn)
+      for (int w = 0; w < kEpilogueWarps; ++w) mbar_init(&in_bars[w], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -410,6 +426,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int half = (warp - 2) >> 2;
     const int row_in = q * 32 + lane;
     OutRing ring{sOut + (warp - 2) * kOutRing * 2048, 0};
+    if (kGuIn) {
+      ring.in = sIn + (warp - 2) * 2 * 2048;
+      ring.in_bar = in_bars + (warp - 2);
+      ring.abort = abort_flag;
+    }
     const bool tma_out = kTmaOut && p.scatter_rows == nullptr;
     int local = 0;
     B200_PROF(unsigned long long ew = 0, eb = 0, ea = 0; const long long et0 = clock64();
@@ -424,7 +445,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
-      if (EPI == kEpiSwigluBwd && half_ok) prefetch_gu_row<BN>(p, T, row_in, half);
+      // the first g/u chunk of this warp's part of the tile, loaded while the MMA runs
+      if (kGuIn && half_ok && tma_out)
+        gu_chunk_load(ring, &tmO1, T.n * BN + half * (BN / 2), p.inter, T.m * 128 + q * 32, lane);
       B200_PROF(const long long w0 = clock64();)
       const bool got_acc = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag));
       B200_PROF(const long long w1 = clock64(); ew += w1 - w0;)
