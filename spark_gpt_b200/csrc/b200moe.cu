@@ -1323,13 +1323,14 @@ int b200moe_fp8_expert_down_dgrad_swiglu(const void* dy, const void* w_d, const 
   p.inter = I;
   p.fp8_scale = scale;
   p.fp8_amax = amax;
-  CUtensorMap to0;
+  CUtensorMap to0, to1;  // d_gu8 out, gu8 in (loaded by TMA in the epilogue)
   if ((rc = make_out_tmap_u8(&to0, d_gu8, 2LL * I, rows_cap, "fp8_down_dgrad d_gu8"))) return rc;
+  if ((rc = make_out_tmap_u8(&to1, gu8, 2LL * I, rows_cap, "fp8_down_dgrad gu8"))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (BN == 256)
-    return launch_gemm_pair<256, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, to0, to0, p,
+    return launch_gemm_pair<256, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, to0, to1, p,
                                                                             st, "fp8_down_dgrad");
-  return launch_gemm_pair<128, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, to0, to0, p, st,
+  return launch_gemm_pair<128, false, true, kEpiSwigluBwdF8, kRowsRagged>(ta, tb, to0, to1, p, st,
                                                                           "fp8_down_dgrad");
 }
 

@@ -508,12 +508,14 @@ struct OutRing {
 // layout ring_put writes).  Every lane's earlier reads of the buffers are
 // ordered before the asynchronous refill (proxy fence, then the warp
 // converges); lane 0 issues; completion on ring.in_bar.
+// BYTES: one chunk's size (2048 for bf16, 1024 for the unswizzled fp8 boxes).
+template <int BYTES = 2048>
 __device__ __forceinline__ void gu_chunk_load(const OutRing& ring, const CUtensorMap* tm,
                                               int col, int inter, int row0, int lane) {
   fence_proxy_async_smem();
   __syncwarp();
   if (lane == 0) {
-    mbar_expect_tx(ring.in_bar, 2 * 2048);
+    mbar_expect_tx(ring.in_bar, 2 * BYTES);
     tma_load_2d(ring.in, tm, ring.in_bar, col, row0);
     tma_load_2d(ring.in + 2048, tm, ring.in_bar, inter + col, row0);
   }
@@ -719,18 +721,22 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
   } else if (EPI == kEpiSwigluBwdF8) {
     // down dgrad with the SwiGLU backward against the e4m3 gu (train.py:1382-1423):
     // dh = bf16(acc); g, u = gu8 / s_gu; d_gu leaves as e5m2 boxes with the d_gu
-    // scale; amax of d_gate, d_up
-    const long long row = static_cast<long long>(row0) + lane;
-    const uint8_t* gu = static_cast<const uint8_t*>(p.aux) + row * p.ld_aux;
+    // scale; amax of d_gate, d_up.  The gu8 chunks arrive by TMA in the warp's
+    // input buffers (32 rows x 32 bytes, unswizzled), as in the bf16 version.
     const float inv_s_gu = 1.0f / __ldg(p.fp8_scale + 1);
     const float s_dgu = __ldg(p.fp8_scale + 3);
     float m_d = 0.f;
+    const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
 #pragma unroll 1
-    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+    for (int c = c0; c < c1; ++c) {
       const int col = T.n * BN + c * 32;
-      const uint4* gs = reinterpret_cast<const uint4*>(gu + col);
-      const uint4* us = reinterpret_cast<const uint4*>(gu + p.inter + col);
+      const bool got = __all_sync(0xffffffffu, mbar_wait(ring.in_bar, ring.in_phase, ring.abort));
+      if (!got) return;
+      ring.in_phase ^= 1u;
+      const uint4* gs = reinterpret_cast<const uint4*>(ring.in + lane * 32);
+      const uint4* us = reinterpret_cast<const uint4*>(ring.in + 2048 + lane * 32);
       const uint4 g0 = gs[0], g1 = gs[1], u0 = us[0], u1 = us[1];
+      if (c + 1 < c1) gu_chunk_load<1024>(ring, tmO1, col + 32, p.inter, row0, lane);
       uint32_t r[32];
       tmem_ld32(taddr + c * 32, r);
       tmem_wait_ld();
