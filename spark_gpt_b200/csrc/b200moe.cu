@@ -1848,17 +1848,39 @@ NsScratch ns_layout(void* base, int batch, int rows, int cols) {
 // Qwen3-30B-A3B expert shapes: measured faster) and as single-CTA tiles below
 // (cfg2-sized 256..512 matrices: the pair tiles' longer pipeline fill per short
 // K loop made them slower).
-bool ns_pair(int g) { return g >= 768; }
+// The Newton-Schulz products run as two-CTA pair tiles, whose epilogue stores
+// through the TMA ring and reads the C operand through TMA.
+bool ns_pair(int) { return true; }
+
+// Output and C-operand tensor maps of one Newton-Schulz product: bf16 out
+// (rows, cols), or the fp32 update when p.update is set; C = p.aux (rows, cols).
+int ns_out_maps(const GemmParams& p, long long rows, int cols, CUtensorMap* to0,
+                CUtensorMap* to1) {
+  int rc;
+  if (p.update != nullptr) {
+    if ((rc = make_out_tmap_f32(to0, p.update, cols, rows, "ns update fp32"))) return rc;
+  } else {
+    if ((rc = make_out_tmap(to0, p.out, cols, rows, "ns out"))) return rc;
+  }
+  *to1 = *to0;
+  if (p.aux != nullptr && (rc = make_out_tmap(to1, p.aux, cols, rows, "ns c"))) return rc;
+  return B200MOE_OK;
+}
 
 // One row-ragged product of the Newton-Schulz step: out = alpha * A.B + beta *
-// aux over `batch` groups.
+// aux over `batch` groups; `rows` x n is the output (and C) matrix.
 template <bool B_MN>
 int ns_rows_product(const CUtensorMap& ta, const CUtensorMap& tb, int n, bool pair, GemmParams p,
-                    cudaStream_t st, const char* what) {
+                    cudaStream_t st, const char* what, long long rows) {
   if (pair) {
+    CUtensorMap to0, to1;
+    const int rc = ns_out_maps(p, rows, n, &to0, &to1);
+    if (rc) return rc;
     if (n % 256 == 0)
-      return launch_expert_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
-    return launch_expert_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
+      return launch_expert_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what,
+                                                                           &to0, &to1);
+    return launch_expert_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what, &to0,
+                                                                         &to1);
   }
   if (n % 256 == 0) return launch_gemm<256, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
   return launch_gemm<128, false, B_MN, kEpiAxpby, kRowsRagged>(ta, tb, p, st, what);
@@ -1938,7 +1960,7 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       p.k_blocks = cols / 64;
       p.b_group_rows = rows;
       p.m_valid = R;
-      if ((rc = ns_rows_product<false>(ta, tb, g, pair, p, st, "ns gram"))) return rc;
+      if ((rc = ns_rows_product<false>(ta, tb, g, pair, p, st, "ns gram", G))) return rc;
     } else {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 64, "ns gram a"))) return rc;
       if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, 64, "ns gram b"))) return rc;
@@ -1946,11 +1968,14 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       p.m_tiles = g / 128;
       p.m_valid = g;
       p.out_group_stride = static_cast<long long>(g) * g;
-      if (pair)
-        rc = bn_g == 256
-                 ? launch_expert_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
-                 : launch_expert_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
-      else
+      if (pair) {
+        CUtensorMap to0, to1;  // the (batch x g, g) view of the Gram stack
+        if ((rc = ns_out_maps(p, G, g, &to0, &to1))) return rc;
+        rc = bn_g == 256 ? launch_expert_gemm<256, true, true, kEpiAxpby, kKRagged>(
+                               ta, tb, p, st, "ns gram", &to0, &to1)
+                         : launch_expert_gemm<128, true, true, kEpiAxpby, kKRagged>(
+                               ta, tb, p, st, "ns gram", &to0, &to1);
+      } else
         rc = bn_g == 256 ? launch_gemm<256, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram")
                          : launch_gemm<128, true, true, kEpiAxpby, kKRagged>(ta, tb, p, st, "ns gram");
       if (rc) return rc;
@@ -1973,7 +1998,7 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
     p.ld_aux = g;
     p.alpha = c;
     p.beta = b;
-    if ((rc = ns_rows_product<false>(ta, tb, g, pair, p, st, "ns poly"))) return rc;
+    if ((rc = ns_rows_product<false>(ta, tb, g, pair, p, st, "ns poly", G))) return rc;
     // 3. X' = P.X + a*X (wide) or X.P + a*X (tall), in X's layout
     p = blank_params();
     p.tile_expert = S.tile_r;
@@ -1999,13 +2024,13 @@ int b200moe_newton_schulz(void* x, int batch, int rows, int cols, int steps, flo
       if ((rc = make_tmap(&tb, cur, cols, R, cols, 64, 64, "ns update b"))) return rc;
       p.k_blocks = rows / 64;
       p.b_group_rows = rows;
-      if ((rc = ns_rows_product<true>(ta, tb, cols, pair, p, st, "ns update"))) return rc;
+      if ((rc = ns_rows_product<true>(ta, tb, cols, pair, p, st, "ns update", R))) return rc;
     } else {
       if ((rc = make_tmap(&ta, cur, cols, R, cols, 64, 128, "ns update a"))) return rc;
       if ((rc = make_tmap(&tb, S.poly, g, G, g, 64, ns_b_box(cols, batch, pair), "ns update b"))) return rc;
       p.k_blocks = cols / 64;
       p.b_group_rows = g;
-      if ((rc = ns_rows_product<false>(ta, tb, cols, pair, p, st, "ns update"))) return rc;
+      if ((rc = ns_rows_product<false>(ta, tb, cols, pair, p, st, "ns update", R))) return rc;
     }
     cur = nxt;
   }

@@ -594,6 +594,18 @@ __device__ __forceinline__ void store_chunk_tma_u8(OutRing& ring, const CUtensor
   ring_flush<1>(ring, &tm, &col, row0, lane);
 }
 
+// One 32 x 32 bf16 chunk of a single input tile (the C operand of kEpiAxpby)
+// into the warp's first input buffer; lane 0 issues; completion on ring.in_bar.
+__device__ __forceinline__ void aux_chunk_load(const OutRing& ring, const CUtensorMap* tm,
+                                               int col, int row0, int lane) {
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    mbar_expect_tx(ring.in_bar, 2048);
+    tma_load_2d(ring.in, tm, ring.in_bar, col, row0);
+  }
+}
+
 __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap* tm,
                                                 const float* v, int lane, int col, int row0) {
   ring_acquire<1>(lane);
@@ -648,6 +660,66 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
           bulk_commit_group();
         }
         ring.next = (ring.next + 1) % kOutRing;
+      }
+    }
+  } else if (EPI == kEpiAxpby) {
+    // Newton-Schulz products (Muon): v = alpha*acc + beta*C, C's chunks arriving
+    // by TMA in the warp's input buffer (the first one loaded before the
+    // accumulator wait); v leaves as bf16 through the ring, or, with `update`,
+    // update += neg_lr * bf16(v) as fp32 TMA reduce-adds.  Rows: the (groups x
+    // M, N) view for weight-gradient-shaped (K-ragged) products, the stacked
+    // rows otherwise (m_tiles is 0 there).
+    const int rowg = T.g * p.m_tiles * BM + row0;
+    const bool has_c = p.aux != nullptr;
+    const int c0 = half * (BN / 64), c1 = (half + 1) * (BN / 64);
+    const int sw = (lane >> 1) & 3;
+#pragma unroll 1
+    for (int c = c0; c < c1; ++c) {
+      const int col = T.n * BN + c * 32;
+      float v[32];
+      uint4 cc[4];
+      if (has_c) {
+        const bool got =
+            __all_sync(0xffffffffu, mbar_wait(ring.in_bar, ring.in_phase, ring.abort));
+        if (!got) return;
+        ring.in_phase ^= 1u;
+        const uint4* cs = reinterpret_cast<const uint4*>(ring.in + lane * 64);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cc[j] = cs[j ^ sw];
+        if (c + 1 < c1) aux_chunk_load(ring, tmO1, col + 32, rowg, lane);
+      }
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = p.alpha * __uint_as_float(r[j]);
+      if (has_c) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[8 * j + 0] += p.beta * bf16_lo(cc[j].x); v[8 * j + 1] += p.beta * bf16_hi(cc[j].x);
+          v[8 * j + 2] += p.beta * bf16_lo(cc[j].y); v[8 * j + 3] += p.beta * bf16_hi(cc[j].y);
+          v[8 * j + 4] += p.beta * bf16_lo(cc[j].z); v[8 * j + 5] += p.beta * bf16_hi(cc[j].z);
+          v[8 * j + 6] += p.beta * bf16_lo(cc[j].w); v[8 * j + 7] += p.beta * bf16_hi(cc[j].w);
+        }
+      }
+      if (p.update != nullptr) {
+#pragma unroll
+        for (int part = 0; part < 2; ++part) {
+          ring_acquire<1>(lane);
+          float w[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) w[j] = p.neg_lr * bf16_round(v[16 * part + j]);
+          ring_put_f32(ring, 0, w, lane);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_reduce_add_2d(tmO0, ring.base + ring.next * 2048, col + 16 * part, rowg);
+            bulk_commit_group();
+          }
+          ring.next = (ring.next + 1) % kOutRing;
+        }
+      } else {
+        store_chunk_tma(ring, tmO0, v, lane, col, rowg);
       }
     }
   } else if (EPI == kEpiStoreBf16) {

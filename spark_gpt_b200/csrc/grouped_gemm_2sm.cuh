@@ -122,14 +122,16 @@ template <int EPI>
 struct TmaOut {
   static constexpr bool value = EPI == kEpiStoreBf16 || EPI == kEpiSwigluFwd ||
                                 EPI == kEpiSwigluBwd || EPI == kEpiStoreF32Tma ||
-                                EPI == kEpiSwigluFwdF8 || EPI == kEpiSwigluBwdF8;
+                                EPI == kEpiSwigluFwdF8 || EPI == kEpiSwigluBwdF8 ||
+                                EPI == kEpiAxpby;
 };
 
 // Epilogues that read a second input tile (g and u of the SwiGLU backward)
 // through TMA into per-warp buffers.
 template <int EPI>
 struct GuIn {
-  static constexpr bool value = EPI == kEpiSwigluBwd || EPI == kEpiSwigluBwdF8;
+  static constexpr bool value = EPI == kEpiSwigluBwd || EPI == kEpiSwigluBwdF8 ||
+                                EPI == kEpiAxpby;
 };
 
 template <int BN, int STAGES, bool TMA_OUT, bool GU_IN = false>
@@ -446,9 +448,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       ++local;
       // the first g/u chunk of this warp's part of the tile, loaded while the MMA runs
-      if (kGuIn && half_ok && tma_out)
-        gu_chunk_load<EPI == kEpiSwigluBwdF8 ? 1024 : 2048>(
-            ring, &tmO1, T.n * BN + half * (BN / 2), p.inter, T.m * 128 + q * 32, lane);
+      if (kGuIn && half_ok && tma_out) {
+        if (EPI == kEpiAxpby) {
+          if (p.aux != nullptr)
+            aux_chunk_load(ring, &tmO1, T.n * BN + half * (BN / 2),
+                           T.g * p.m_tiles * 128 + T.m * 128 + q * 32, lane);
+        } else {
+          gu_chunk_load<EPI == kEpiSwigluBwdF8 ? 1024 : 2048>(
+              ring, &tmO1, T.n * BN + half * (BN / 2), p.inter, T.m * 128 + q * 32, lane);
+        }
+      }
       B200_PROF(const long long w0 = clock64();)
       const bool got_acc = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort_flag));
       B200_PROF(const long long w1 = clock64(); ew += w1 - w0;)
