@@ -969,6 +969,12 @@ def main():
         "gpu_launches_per_step": launches / max(args.steps, 1),
         "clocks": clocks,
     }
+    # the dominant kernel against cuBLAS on a dense GEMM of its own shape, measured
+    # in this run (the square-GEMM burst peak is out of reach for short-K shapes)
+    dense = (torch_path or {}).get("cublas_dense_same_shapes") or {}
+    if dominant in dense:
+        line["roofline"]["cublas_same_shape_tflops"] = dense[dominant]["tflops"]
+        line["roofline"]["frac_of_cublas_same_shape"] = ach / dense[dominant]["tflops"]
     print(json.dumps(line), flush=True)
 
 
