@@ -275,3 +275,56 @@ def test_fp8_gemms_match_oracle_arithmetic():
     assert_bf16_close(dxu, dx_o.float(), "fp8 gate_up dgrad", max_rel=6e-2, mean_rel=4e-3)
     assert _rel(g_gu, dwgu_o) < 1e-2
     assert _rel(g_d, dwd_o) < 1e-3
+
+
+def test_sparse_moe_takes_the_fp8_path_when_enabled():
+    """SparseMoE.forward (router in bf16, experts on the fp8 path) with
+    spark_gpt_b200.fp8.FP8_MLP set and the module training: the experts'
+    amax slots are raised, the output and gradients stay within the fp8 bar of
+    the same layer's bf16 path, and in eval mode (or with the flag off) the
+    bf16 path runs and leaves the amax untouched."""
+    from types import SimpleNamespace
+    from spark_gpt_b200 import SparseMoE, fp8, fp8_update_scales
+    torch.manual_seed(11)
+    T, H, E, k, I = 2048, 1024, 32, 4, 256
+    cfg = SimpleNamespace(hidden_size=H, num_experts=E, num_experts_per_tok=k,
+                          moe_intermediate_size=I, norm_topk_prob=True)
+    m = SparseMoE(cfg).to(DEV).train()
+    with torch.no_grad():
+        m.gate.weight.normal_(0.0, 0.02)
+        m.experts.gate_up_proj.normal_(0.0, 0.05)
+        m.experts.down_proj.normal_(0.0, 0.05)
+    x = torch.randn(T, H, device=DEV).to(BF16)
+    probe = torch.randn(T, H, device=DEV)
+
+    def run():
+        for p in m.parameters():
+            p.grad = None
+        xx = x.clone().requires_grad_(True)
+        out, logits, sel = m(xx)
+        (out.float() * probe).sum().backward()
+        torch.cuda.synchronize()
+        return out.detach(), sel, xx.grad, m.experts.gate_up_proj.grad.clone()
+
+    ref = run()                                   # bf16 path (flag off)
+    assert torch.count_nonzero(m.experts.fp8_amax) == 0
+    saved = fp8.FP8_MLP
+    fp8.FP8_MLP = True
+    try:
+        run()                                     # prewarm on the fp8 path
+        assert bool((m.experts.fp8_amax > 0).all()), m.experts.fp8_amax
+        fp8_update_scales(m)
+        res = run()
+        m.eval()
+        amax0 = m.experts.fp8_amax.clone()
+        with torch.no_grad():
+            m(x)                                  # eval: the bf16 path
+        assert torch.equal(m.experts.fp8_amax, amax0)
+    finally:
+        fp8.FP8_MLP = saved
+        m.train()
+    assert torch.equal(res[1], ref[1])            # the router stays bf16: same routing
+    for n, a, b in (("out", res[0], ref[0]), ("dx", res[2], ref[2]), ("dW_gate_up", res[3], ref[3])):
+        e = _rel(a, b)
+        print(f"\nSparseMoE fp8 vs bf16 {n}: {e:.3e}")
+        assert e < 0.12, f"{n}: {e:.3e}"
