@@ -175,8 +175,9 @@ __device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* 
   } else {
     const int mp = p.m_tiles / 2;
     const int per = mp * p.n_tiles;
-    T.g = t / per;
-    const int r = t - T.g * per;
+    const int gi = t / per;
+    T.g = pair_start[gi];  // the expert order table (most rows first)
+    const int r = t - gi * per;
     const int mpair = r / p.n_tiles;
     T.n = r - mpair * p.n_tiles;
     T.m = 2 * mpair + static_cast<int>(rank);
@@ -273,6 +274,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (e <= p.num_groups) pair_start[e] = carry + incl - v;
       carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+  }
+  if (SCHED == kKRagged) {
+    // Weight-gradient tiles run expert by expert, the experts with the most rows
+    // first (ties by index), so the persistent schedule's last tiles are its
+    // shortest ones: pair_start[i] = the expert of rank i.  The first A stage,
+    // unused until the producer starts, holds the row counts meanwhile.
+    static_assert(S::kABytes >= kMaxPairExperts * 4, "row counts fit one A stage");
+    int* cnt = reinterpret_cast<int*>(sA);
+    for (int e = threadIdx.x; e < p.num_groups; e += blockDim.x)
+      cnt[e] = __ldg(p.pad_offsets + e + 1) - __ldg(p.pad_offsets + e);
+    __syncthreads();
+    for (int e = threadIdx.x; e < p.num_groups; e += blockDim.x) {
+      const int ce = cnt[e];
+      int rank = 0;
+      for (int j = 0; j < p.num_groups; ++j) {
+        const int cj = cnt[j];
+        rank += (cj > ce) || (cj == ce && j < e);
+      }
+      pair_start[rank] = e;
     }
   }
   if (warp == 0 && lane == 0) {
