@@ -251,6 +251,21 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gate_up, const 
 int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* pad_offsets,
                          int E, long long rows_cap, float* dw, int accumulate, void* stream);
 
+/* The same weight gradient when each expert's rows lie in several row
+ * segments of one (rows_total, M) / (rows_total, N) allocation: seg_offsets
+ * is (segments, E+1) int32 of absolute row offsets, and expert e's K rows are
+ * the union over s of [seg_offsets[s][e], seg_offsets[s][e+1]) (each a
+ * multiple of 128 rows long), in segment order.  The expert-parallel layer's
+ * per-source chunks use it for one weight gradient over all of them (no
+ * accumulation pass per chunk); the reference computes the same product per
+ * expert over one contiguous block (_grouped_wgrad, train.py:1863).
+ * M % 128 == 0, N % 64 == 0, 1 <= segments <= 64.  Shapes the two-CTA tiles
+ * do not take (N < 128, an odd number of 128-row M tiles, E > 256) run one
+ * b200moe_expert_wgrad per segment, adding into dw after the first. */
+int b200moe_expert_wgrad_segments(const void* a, int M, const void* b, int N,
+                                  const int* seg_offsets, int segments, int E,
+                                  long long rows_total, float* dw, int accumulate, void* stream);
+
 /* ---- the fp8 expert path: _FP8Experts (train.py:1543-1604) --------------
  * spark-gpt's --fp8-mlp on MoE layers.  x, gu, h and the expert weights are
  * e4m3, d_gu and the rows' gradient dy e5m2.  `scale` points at the layer's

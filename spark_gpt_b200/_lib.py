@@ -51,6 +51,7 @@ PROTOTYPES = {
     "b200moe_expert_down_dgrad_swiglu": (I, [P, P, P, P, P, L, I, I, I, P, P]),
     "b200moe_expert_gate_up_dgrad": (I, [P, P, P, P, P, L, I, I, I, P, P]),
     "b200moe_expert_wgrad": (I, [P, I, P, I, P, I, L, P, I, P]),
+    "b200moe_expert_wgrad_segments": (I, [P, I, P, I, P, I, I, L, P, I, P]),
     "b200moe_fp8_quantize_experts_scratch_bytes": (L, [I]),
     "b200moe_fp8_quantize_experts": (I, [P, I, L, P, P, P, L, P]),
     "b200moe_fp8_gather_quant": (I, [P, P, P, P, L, I, I, I, L, P, P, P, P]),

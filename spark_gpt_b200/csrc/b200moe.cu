@@ -159,6 +159,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& 
 #define B200MOE_PAIR_STAGES_MAX 8
 #endif
 constexpr uint32_t kMaxDynSmem = 227 * 1024;
+constexpr int kMaxWgradSegments = 64;  // row segments of one segmented weight gradient
 
 template <int BN, bool TMA_OUT, bool GU_IN = false>
 constexpr int pair_stages() {
@@ -222,6 +223,27 @@ int make_out_tmap(CUtensorMap* m, const void* base, long long cols, long long ro
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
+// Output tensor maps of the plain bf16-store epilogue (kEpiStoreBf16): the
+// {32, 32} box above, or a {64, 32} box with the 128-byte swizzle when that
+// epilogue stores two TMEM chunks per box.
+int make_store_tmap(CUtensorMap* m, const void* base, long long cols, long long rows,
+                    const char* what) {
+  if (!kWideBf16Store) return make_out_tmap(m, base, cols, rows, what);
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 2)};
+  cuuint32_t box[2] = {64, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
@@ -536,7 +558,7 @@ int b200moe_router_dgrad(const void* d_logits, const void* w, long long T, int H
     // two-CTA kernel writes it through shared memory with TMA stores (rows >= T are
     // clipped by the tensor map; the rows of the tile past T load as zeros)
     CUtensorMap to;
-    if ((rc = make_out_tmap(&to, dx, H, T, "router_dgrad dx"))) return rc;
+    if ((rc = make_store_tmap(&to, dx, H, T, "router_dgrad dx"))) return rc;
     return launch_gemm_pair<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, to, to, p, st,
                                                                           "router_dgrad");
   }
@@ -985,7 +1007,7 @@ int b200moe_expert_down_fwd(const void* h, const void* w_d, const int* tile_expe
   CUtensorMap to0;
   const CUtensorMap* o0 = nullptr;
   if (row_flat_out == nullptr) {
-    if ((rc = make_out_tmap(&to0, y, H, rows_cap, "down_fwd y"))) return rc;
+    if ((rc = make_store_tmap(&to0, y, H, rows_cap, "down_fwd y"))) return rc;
     o0 = &to0;
   }
   if (BN == 256) return launch_expert_gemm<256, false, false, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "down_fwd", o0);
@@ -1057,7 +1079,7 @@ int b200moe_expert_gate_up_dgrad(const void* d_gu, const void* w_gu, const int* 
   CUtensorMap to0;
   const CUtensorMap* o0 = nullptr;
   if (row_flat_out == nullptr) {
-    if ((rc = make_out_tmap(&to0, dxs, H, rows_cap, "gate_up_dgrad dxs"))) return rc;
+    if ((rc = make_store_tmap(&to0, dxs, H, rows_cap, "gate_up_dgrad dxs"))) return rc;
     o0 = &to0;
   }
   if (BN == 256) return launch_expert_gemm<256, false, true, kEpiStoreBf16, kRowsRagged>(ta, tb, p, st, "gate_up_dgrad", o0);
@@ -1101,6 +1123,53 @@ int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* 
   if (BN == 256) return launch_expert_gemm<256, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   if (BN == 128) return launch_expert_gemm<128, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
   return launch_expert_gemm<64, true, true, kEpiStoreF32, kKRagged>(ta, tb, p, st, "expert_wgrad");
+}
+
+int b200moe_expert_wgrad_segments(const void* a, int M, const void* b, int N,
+                                  const int* seg_offsets, int segments, int E,
+                                  long long rows_total, float* dw, int accumulate, void* stream) {
+  REQUIRE(a && b && seg_offsets && dw, "expert_wgrad_segments: null pointer");
+  REQUIRE(M > 0 && M % 128 == 0, "expert_wgrad_segments: M must be a multiple of 128");
+  REQUIRE(N > 0 && N % 64 == 0, "expert_wgrad_segments: N must be a multiple of 64");
+  REQUIRE(E >= 1 && rows_total > 0 && rows_total % 128 == 0 && rows_total < 0x7fffffffLL,
+          "expert_wgrad_segments: bad rows/E");
+  REQUIRE(segments >= 1 && segments <= kMaxWgradSegments,
+          "expert_wgrad_segments: 1 <= segments <= %d", kMaxWgradSegments);
+  const int BN = N % 256 == 0 ? 256 : 128;
+  if (N < 128 || !use_pair(BN, kKRagged, E, M / 128)) {
+    // shapes the two-CTA tiles do not take: one weight gradient per segment,
+    // each after the first added into dw
+    for (int s = 0; s < segments; ++s) {
+      const int rc = b200moe_expert_wgrad(a, M, b, N, seg_offsets + static_cast<long long>(s) * (E + 1),
+                                          E, rows_total, dw, accumulate || s > 0, stream);
+      if (rc) return rc;
+    }
+    return B200MOE_OK;
+  }
+  CUtensorMap ta, tb, to;
+  int rc;
+  if ((rc = make_tmap(&ta, a, M, rows_total, M, 64, 64, "expert_wgrad_segments a"))) return rc;
+  if ((rc = make_tmap(&tb, b, N, rows_total, N, 64, 64, "expert_wgrad_segments b"))) return rc;
+  if ((rc = make_out_tmap_f32(&to, dw, N, static_cast<long long>(E) * M,
+                              "expert_wgrad_segments dw")))
+    return rc;
+  GemmParams p = blank_params();
+  p.pad_offsets = seg_offsets;
+  p.k_segments = segments;
+  p.num_groups = E;
+  p.m_tiles = M / 128;
+  p.n_tiles = (N + BN - 1) / BN;  // columns past N: zero-filled loads, not stored
+  p.n_valid = N;
+  p.out = dw;
+  p.ld_out = N;
+  p.accumulate = accumulate;
+  p.out_group_stride = static_cast<long long>(M) * N;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (BN == 256)
+    return launch_gemm_pair<256, true, true, kEpiStoreF32Tma, kKRagged>(ta, tb, to, to, p, st,
+                                                                        "expert_wgrad_segments");
+  return launch_gemm_pair<128, true, true, kEpiStoreF32Tma, kKRagged>(ta, tb, to, to, p, st,
+                                                                      "expert_wgrad_segments");
 }
 
 // ---------------------------------------------------------------- fp8 expert path
@@ -1274,7 +1343,7 @@ int b200moe_fp8_expert_down_fwd(const void* h8, const void* wd8, const float* q_
   if ((rc = make_tmap_u8(&ta, h8, I, rows_cap, I, 128, 128, "fp8_down_fwd h8"))) return rc;
   if ((rc = make_tmap_u8(&tb, wd8, I, static_cast<long long>(E) * H, I, 128, 128, "fp8_down_fwd w8")))
     return rc;
-  if ((rc = make_out_tmap(&to0, y, H, rows_cap, "fp8_down_fwd y"))) return rc;
+  if ((rc = make_store_tmap(&to0, y, H, rows_cap, "fp8_down_fwd y"))) return rc;
   GemmParams p = blank_params();
   p.tile_expert = tile_expert;
   p.pad_offsets = pad_offsets;
@@ -1349,7 +1418,7 @@ int b200moe_fp8_expert_gate_up_dgrad(const void* d_gu8, const void* w8_gu, const
   if ((rc = make_tmap_u8(&tb, w8_gu, H, static_cast<long long>(E) * 2 * I, H, 128, 128,
                          "fp8_gate_up_dgrad w8")))
     return rc;
-  if ((rc = make_out_tmap(&to0, dxs, H, rows_cap, "fp8_gate_up_dgrad dxs"))) return rc;
+  if ((rc = make_store_tmap(&to0, dxs, H, rows_cap, "fp8_gate_up_dgrad dxs"))) return rc;
   GemmParams p = blank_params();
   p.tile_expert = tile_expert;
   p.pad_offsets = pad_offsets;

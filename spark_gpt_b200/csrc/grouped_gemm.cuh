@@ -133,6 +133,12 @@ struct GemmParams {
   const float* deq_a;
   const float* deq_b;
   const float* deq_g;
+  // kKRagged pair tiles over several row segments (the weight gradient of an
+  // expert whose rows sit in several buffers of one allocation): with
+  // k_segments > 1, pad_offsets holds k_segments rows of num_groups + 1
+  // absolute row offsets, and group g's K rows are the union over segments s
+  // of [pad_offsets[s][g], pad_offsets[s][g + 1]), in segment order.
+  int k_segments;
 };
 
 __device__ __forceinline__ float deq_factor(const GemmParams& p, int g) {
@@ -616,6 +622,10 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
 #ifndef B200MOE_EPI_GROUP
 #define B200MOE_EPI_GROUP 1  // chunks per proxy fence in the plain bf16 epilogue
 #endif
+#ifndef B200MOE_WIDE_BF16
+#define B200MOE_WIDE_BF16 0  // plain bf16 stores as 32 x 64 boxes (128-byte swizzle)
+#endif
+constexpr bool kWideBf16Store = B200MOE_WIDE_BF16 != 0;
 
 // The bf16-output epilogues (plain store, SwiGLU forward, SwiGLU backward) with
 // TMA stores.  Outputs: O0 = out (or gu / d_gu), O1 = h (SwiGLU forward).
@@ -721,6 +731,37 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
       } else {
         store_chunk_tma(ring, tmO0, v, lane, col, rowg);
       }
+    }
+  } else if (EPI == kEpiStoreBf16 && kWideBf16Store) {
+    // two 32-column TMEM chunks leave as one 32 x 64 bf16 box (4 KB, 128-byte
+    // swizzle) in two consecutive ring buffers: half the TMA stores
+    static_assert(kOutRing % 2 == 0 && (BN / 64) % 2 == 0, "wide stores take buffer pairs");
+    const float sc = SCALED ? deq_factor(p, T.g) : 1.f;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c += 2) {
+      uint32_t r0[32], r1[32];
+      tmem_ld32(taddr + c * 32, r0);
+      tmem_ld32(taddr + (c + 1) * 32, r1);
+      tmem_wait_ld();
+      ring_acquire<2>(lane);
+      uint4* rowp = reinterpret_cast<uint4*>(ring.base + ring.next * 2048 + lane * 128);
+      const int sw = lane & 7;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t* r = j < 4 ? r0 + 8 * j : r1 + 8 * (j - 4);
+        float v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = SCALED ? __uint_as_float(r[q]) * sc : __uint_as_float(r[q]);
+        rowp[j ^ sw] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                  pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmO0, ring.base + ring.next * 2048, T.n * BN + c * 32, row0);
+        bulk_commit_group();
+      }
+      ring.next = (ring.next + 2) % kOutRing;
     }
   } else if (EPI == kEpiStoreBf16) {
     constexpr int G = B200MOE_EPI_GROUP < BN / 64 ? B200MOE_EPI_GROUP : BN / 64;

@@ -185,8 +185,29 @@ __device__ __forceinline__ TileInfo decode_pair(const GemmParams& p, const int* 
     const int e = __ldg(p.pad_offsets + T.g + 1);
     T.krow0 = s;
     T.kblocks = (e - s) / BK;
+    for (int seg = 1; seg < p.k_segments; ++seg) {
+      const int* po = p.pad_offsets + seg * (p.num_groups + 1) + T.g;
+      T.kblocks += (__ldg(po + 1) - __ldg(po)) / BK;
+    }
   }
   return T;
+}
+
+// The first row of a K-ragged tile's next k-block: rows advance by BK inside a
+// segment and continue at the start of the group's next non-empty segment.
+// `row` / `end` / `seg` carry the walk from one k-block to the next.
+template <int BK>
+__device__ __forceinline__ int kragged_next_row(const GemmParams& p, int g, int& row, int& end,
+                                                int& seg) {
+  while (row >= end && seg + 1 < p.k_segments) {
+    ++seg;
+    const int* po = p.pad_offsets + seg * (p.num_groups + 1) + g;
+    row = __ldg(po);
+    end = __ldg(po + 1);
+  }
+  const int r = row;
+  row += BK;
+  return r;
 }
 
 // OP: operand kind (OperandKind).  An fp8 stage carries 128 K elements in the
@@ -283,8 +304,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     // unused until the producer starts, holds the row counts meanwhile.
     static_assert(S::kABytes >= kMaxPairExperts * 4, "row counts fit one A stage");
     int* cnt = reinterpret_cast<int*>(sA);
-    for (int e = threadIdx.x; e < p.num_groups; e += blockDim.x)
-      cnt[e] = __ldg(p.pad_offsets + e + 1) - __ldg(p.pad_offsets + e);
+    for (int e = threadIdx.x; e < p.num_groups; e += blockDim.x) {
+      int c = 0;
+      for (int seg = 0; seg < max(p.k_segments, 1); ++seg) {
+        const int* po = p.pad_offsets + seg * (p.num_groups + 1) + e;
+        c += __ldg(po + 1) - __ldg(po);
+      }
+      cnt[e] = c;
+    }
     __syncthreads();
     for (int e = threadIdx.x; e < p.num_groups; e += blockDim.x) {
       const int ce = cnt[e];
@@ -331,7 +358,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int t = cluster_id; ok && t < num_tiles; t += num_clusters) {
         bool half_ok;
         const TileInfo T = decode_pair<SCHED, BK>(p, pair_start, t, rank, half_ok);
+        // K-ragged: the walk over the group's row segments
+        int k_row = T.krow0, k_seg = 0;
+        int k_end = SCHED == kKRagged ? __ldg(p.pad_offsets + T.g + 1) : 0;
         for (int kb = 0; kb < T.kblocks; ++kb) {
+          const int krow_k = SCHED == kKRagged ? kragged_next_row<BK>(p, T.g, k_row, k_end, k_seg)
+                                               : 0;
           B200_PROF(const long long w0 = clock64();)
           const bool got = mbar_wait(&empty[stage], phase ^ 1u, abort_flag);
           B200_PROF(pw += clock64() - w0;)
@@ -346,7 +378,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (!A_MN) {
             tma_load_2d_pair(a, &tmA, full_leader, kb * BK, T.m * BM);
           } else {
-            const int krow = T.krow0 + kb * BK;
+            const int krow = SCHED == kKRagged ? krow_k : T.krow0 + kb * BK;
             tma_load_2d_pair(a, &tmA, full_leader, T.m * BM, krow);
             if (!kF8) tma_load_2d_pair(a + 8192, &tmA, full_leader, T.m * BM + 64, krow);
           }
@@ -359,8 +391,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 : T.g * p.b_group_rows + T.n * BN + static_cast<int>(rank) * (BN / 2);
             tma_load_2d_pair(b, &tmB, full_leader, kb * BK, row);
           } else {
-            const int krow =
-                (SCHED == kKRagged) ? (T.krow0 + kb * BK) : (T.g * p.b_group_rows + kb * BK);
+            const int krow = (SCHED == kKRagged) ? krow_k : (T.g * p.b_group_rows + kb * BK);
             if (kF8) {
               tma_load_2d_pair(b, &tmB, full_leader, T.n * BN + static_cast<int>(rank) * (BN / 2),
                                krow);

@@ -107,30 +107,34 @@ class CudaExpertOps:
         return ops.ep_unpack(meta)
 
     @staticmethod
-    def experts_fwd(rows, sel_loc, w_loc, w_gu, w_d, slots, combine=True):
+    def experts_fwd(rows, sel_loc, w_loc, w_gu, w_d, slots, combine=True, arena=None, src=0):
         """partial[i] = sum over row i's local slots of bf16(expert(rows[i]) * w);
-        combine=False returns the expert outputs y (padded rows) instead."""
+        combine=False returns the expert outputs y (padded rows) instead.
+        arena: a RowArena whose chunk `src` receives the gathered rows xs and h."""
         E = w_gu.shape[0]
         if rows.shape[0] == 0 or slots == 0:
             return rows.new_zeros(rows.shape), None
         d = ops.dispatch(sel_loc, E, routed_slots=slots)
-        xs = ops.gather_rows(rows, d)
-        gu, h = ops.gate_up_fwd(xs, w_gu, d)
+        xs = ops.gather_rows(rows, d, out=arena.rows("xs", src) if arena else None)
+        gu, h = ops.gate_up_fwd(xs, w_gu, d, out_h=arena.rows("h", src) if arena else None)
         y = ops.down_fwd(h, w_d, d)
         ctx = (d, w_loc, xs, gu, h, y, w_gu, w_d)
         return (ops.combine(y, d, w_loc) if combine else y), ctx
 
     @staticmethod
-    def experts_dgrad(ctx, d_rows, k, device, reduce=True):
+    def experts_dgrad(ctx, d_rows, k, device, reduce=True, arena=None, src=0):
         """-> (dx rows, d_weights (rows, k) fp32, state for experts_wgrad);
         reduce=False returns the slot input-gradients dxs (padded rows) instead
-        of their per-row sums."""
+        of their per-row sums.  arena: a RowArena whose chunk `src` receives
+        the rows' gradient dy and d_gu."""
         n, H = d_rows.shape
         if ctx is None:
             return d_rows.new_zeros(n, H), torch.zeros(n, k, device=device), None
         d, w_loc, xs, gu, h, y, w_gu, w_d = ctx
-        dy, dw = ops.combine_bwd(_as_bf16(d_rows), y, d, w_loc)
-        d_gu = ops.down_dgrad_swiglu(dy, w_d, gu, d)
+        dy, dw = ops.combine_bwd(_as_bf16(d_rows), y, d, w_loc,
+                                 out=arena.rows("dy", src) if arena else None)
+        d_gu = ops.down_dgrad_swiglu(dy, w_d, gu, d,
+                                     out=arena.rows("d_gu", src) if arena else None)
         dxs = ops.gate_up_dgrad(d_gu, w_gu, d)
         return (ops.gather_rows_bwd(dxs, d) if reduce else dxs), dw, (d, dy, h, d_gu, xs)
 
@@ -146,6 +150,21 @@ class CudaExpertOps:
         acc = g_gu is not None
         g_d = ops.wgrad(dy, h, d, name="down_wgrad", out=g_d, accumulate=acc)
         g_gu = ops.wgrad(d_gu, xs, d, name="gate_up_wgrad", out=g_gu, accumulate=acc)
+        return g_gu, g_d
+
+    @staticmethod
+    def experts_wgrad_segments(states, arena, E, H, I, device):
+        """Both expert weight gradients over every chunk of `arena` at once
+        (one launch each, no accumulation pass per chunk); states[s] is chunk
+        s's experts_dgrad state or None."""
+        ds = [None if st is None else st[0] for st in states]
+        if all(d is None for d in ds):
+            return (torch.zeros(E, 2 * I, H, device=device),
+                    torch.zeros(E, H, I, device=device))
+        segs = arena.segments(ds, E)
+        g_d = ops.wgrad_segments(arena.bufs["dy"], arena.bufs["h"], segs, E, name="down_wgrad")
+        g_gu = ops.wgrad_segments(arena.bufs["d_gu"], arena.bufs["xs"], segs, E,
+                                  name="gate_up_wgrad")
         return g_gu, g_d
 
     @staticmethod
@@ -176,6 +195,43 @@ class CudaExpertOps:
         """Persistent kernels leave `comm_sms` SMs to the all-to-all beside them."""
         return ops.persistent_sm_limit(max(2, torch.cuda.get_device_properties(
             torch.cuda.current_device()).multi_processor_count - comm_sms))
+
+
+class RowArena:
+    """Row buffers shared by the per-source chunks of the pipelined layer: one
+    allocation per activation the expert weight gradients read (xs and h in
+    the forward, dy and d_gu in the backward), chunk s owning rows
+    [base[s], base[s] + caps[s]) of each in source order, so that one
+    weight-gradient launch per weight covers every chunk
+    (b200moe_expert_wgrad_segments)."""
+
+    def __init__(self, caps, device):
+        self.caps = [int(c) for c in caps]
+        self.base = [sum(self.caps[:s]) for s in range(len(self.caps))]
+        self.total = max(sum(self.caps), 128)
+        self.device = device
+        self.bufs = {}
+
+    @classmethod
+    def for_chunks(cls, rows_from, slots_from, num_experts, device):
+        """Capacities of the chunks' dispatches (routed_slots = the chunk's
+        slots): none for a chunk without rows or slots (no experts run)."""
+        return cls([ops.padded_rows(sl, num_experts) if (n and sl) else 0
+                    for n, sl in zip(rows_from, slots_from)], device)
+
+    def alloc(self, name, cols):
+        self.bufs[name] = torch.empty(self.total, cols, device=self.device,
+                                      dtype=torch.bfloat16)
+
+    def rows(self, name, s):
+        return self.bufs[name][self.base[s]:self.base[s] + self.caps[s]]
+
+    def segments(self, dispatches, num_experts):
+        """(chunks, E+1) int32 absolute row offsets: each chunk's padded
+        expert offsets moved to its base (a chunk without experts: empty)."""
+        i32 = dict(device=self.device, dtype=torch.int32)
+        return torch.stack([torch.full((num_experts + 1,), self.base[s], **i32) if d is None
+                            else d.pad_offsets + self.base[s] for s, d in enumerate(dispatches)])
 
 
 def _backend_call(backend, name, device):
@@ -640,8 +696,9 @@ class _EPMoEPipeFn(torch.autograd.Function):
     owner when all its rows are stored, an owner sets one at a source when
     that source's results are stored (b200moe_ep_signal / _wait, bounded
     waits).  The backward mirrors it with the upstream gradient rows; the
-    expert weight gradients accumulate over the chunks and run beside the
-    last returns.  Every buffer is reused only after the flag that orders it:
+    chunks' activations sit in shared row buffers (RowArena), so each expert
+    weight gradient is one launch over every source's rows, beside the last
+    returns.  Every buffer is reused only after the flag that orders it:
     a source stores the backward's rows only after its forward has received
     every owner's results, which each owner signals after it consumed that
     source's forward rows (and likewise from one step to the next)."""
@@ -688,6 +745,9 @@ class _EPMoEPipeFn(torch.autograd.Function):
             ops.ep_signal(tr.peer_flags, PH_FWD_SEND, me, P, step)
         order = [(me - j) % P for j in range(P)]
         ectxs, keep = [None] * P, []
+        arena = RowArena.for_chunks(rows_from, slots_from, E_loc, dev)
+        arena.alloc("xs", H)
+        arena.alloc("h", w_gu.shape[1] // 2)
         with backend_overlap(comm_sms) if (comm_sms and P > 1) else nullcontext():
             for s in order:
                 if s != me:
@@ -696,7 +756,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
                 rows = tr.recv_rows[base[s]:base[s] + n]
                 sel_loc, w_loc = B.unpack(tr.recv_meta[base[s]:base[s] + n])
                 y, ectxs[s] = B.experts_fwd(rows, sel_loc, w_loc, wgu_b, wd_b, slots_from[s],
-                                            combine=False)
+                                            combine=False, arena=arena, src=s)
                 done = s0.record_event()
                 with torch.cuda.stream(s1):
                     s1.wait_event(done)
@@ -713,7 +773,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
         faults.snapshot(dev)
         ctx.save_for_backward(xb, logits_buf, wr, sel)
         ctx.meta = (send, back, plan, ectxs, rows_from, base, n_back, tr, step, top_k, norm,
-                    num_experts, E_loc, H, w_gu.shape[1] // 2, x.dtype, comm_sms)
+                    num_experts, E_loc, H, w_gu.shape[1] // 2, x.dtype, comm_sms, arena)
         ctx.mark_non_differentiable(sel)
         E = num_experts
         logits = logits_buf if logits_buf.shape[1] == E else logits_buf[:, :E]
@@ -723,7 +783,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
     def backward(ctx, d_out, d_logits, _d_sel):
         xb, logits_buf, wr, sel = ctx.saved_tensors
         (send, back, plan, ectxs, rows_from, base, n_back, tr, step, top_k, norm, num_experts,
-         E_loc, H, I, xdtype, comm_sms) = ctx.meta
+         E_loc, H, I, xdtype, comm_sms, arena) = ctx.meta
         faults.raise_pending(xb.device)
         B = CudaExpertOps
         P, me = tr.P, tr.me
@@ -741,13 +801,15 @@ class _EPMoEPipeFn(torch.autograd.Function):
             ops.ep_signal(tr.peer_flags, PH_BWD_SEND, me, P, step)
         order = [(me - j) % P for j in range(P)]
         states, keep = [None] * P, []
+        arena.alloc("dy", H)
+        arena.alloc("d_gu", 2 * I)
         with backend_overlap(comm_sms) if (comm_sms and P > 1) else nullcontext():
             for s in order:
                 if s != me:
                     ops.ep_wait(tr.flags, PH_BWD_SEND, P, step, src=s)
                 d_rows = tr.recv_rows[base[s]:base[s] + rows_from[s]]
                 dxs, dw_rows, states[s] = B.experts_dgrad(ectxs[s], d_rows, top_k, dev,
-                                                          reduce=False)
+                                                          reduce=False, arena=arena, src=s)
                 done = s0.record_event()
                 with torch.cuda.stream(s1):
                     s1.wait_event(done)
@@ -757,10 +819,9 @@ class _EPMoEPipeFn(torch.autograd.Function):
                                                      peer_dw=tr.peer_back_dw)
                     ops.ep_signal(tr.peer_flags, PH_BWD_RETURN, me, P, step, dest=s)
                 keep.append((dxs, dw_rows))
-            # the expert weight gradients run beside the last returns
-            g_gu = g_d = None
-            for s in order:
-                g_gu, g_d = B.experts_wgrad(states[s], g_gu, g_d, E_loc, H, I, dev)
+            # the expert weight gradients, one launch each over every source's
+            # rows, run beside the last returns
+            g_gu, g_d = B.experts_wgrad_segments(states, arena, E_loc, H, I, dev)
         s0.wait_stream(s1)
         del keep
         ops.ep_wait(tr.flags, PH_BWD_RETURN, P, step)

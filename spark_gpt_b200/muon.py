@@ -66,39 +66,62 @@ def newton_schulz(x: torch.Tensor, steps: int = 5, update: torch.Tensor | None =
     return out
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def _side_stream(dev: torch.device, i: int) -> torch.cuda.Stream:
+    key = (dev.index, i)
+    if key not in _SIDE_STREAMS:
+        _SIDE_STREAMS[key] = torch.cuda.Stream(dev)
+    return _SIDE_STREAMS[key]
+
+
 @torch.no_grad()
 def muon_step_packed(params, momentum_buffers, lr: float, momentum: float = 0.95,
-                     nesterov: bool = True, ns_steps: int = 5) -> None:
+                     nesterov: bool = True, ns_steps: int = 5, streams: int = 2) -> None:
     """One Muon step of packed 3-D fp32 parameters with .grad set
     (MuonAdamWHybrid._muon_group, train.py:2972-3024, for 3-D tensors).
 
     momentum_buffers: one fp32 tensor per parameter (zeros at the first step),
-    updated in place."""
-    dev = None
-    for p, v in zip(params, momentum_buffers):
-        if p.grad is None:
-            continue
-        if p.dim() != 3 or p.dtype != torch.float32 or not p.is_contiguous():
-            raise RuntimeError("muon_step_packed: parameters must be contiguous fp32 (E, rows, cols)")
-        if dev is None:
-            dev = p.device
-            faults.raise_pending(dev)
-        g = p.grad.float().contiguous()
-        staged = momentum_stage(g, v, momentum, nesterov)
-        rows, cols = p.shape[-2], p.shape[-1]
-        lr_eff = lr * max(1, rows / cols) ** 0.5
-        newton_schulz(staged, ns_steps, update=p.data, neg_lr=-lr_eff)
-    if dev is not None:
-        faults.snapshot(dev)
+    updated in place.  The parameters' updates are independent, so they run on
+    `streams` CUDA streams in turn (the caller's and side streams that start
+    after the caller's pending work and that the caller's stream waits for on
+    return): one tensor's short Newton-Schulz products fill the SMs that
+    another's leave idle at the end of each launch."""
+    todo = [(p, v) for p, v in zip(params, momentum_buffers) if p.grad is not None]
+    if not todo:
+        return
+    for p, _ in todo:
+        if (not p.is_cuda or p.dim() != 3 or p.dtype != torch.float32
+                or not p.is_contiguous()):
+            raise RuntimeError("muon_step_packed: parameters must be contiguous fp32 "
+                               "(E, rows, cols) CUDA tensors")
+    dev = todo[0][0].device
+    faults.raise_pending(dev)
+    main = torch.cuda.current_stream(dev)
+    lanes = [main] + [_side_stream(dev, i) for i in range(max(1, min(streams, len(todo))) - 1)]
+    for s in lanes[1:]:
+        s.wait_stream(main)  # the gradients and parameters are ready
+    for i, (p, v) in enumerate(todo):
+        with torch.cuda.stream(lanes[i % len(lanes)]):
+            g = p.grad.float().contiguous()
+            staged = momentum_stage(g, v, momentum, nesterov)
+            rows, cols = p.shape[-2], p.shape[-1]
+            lr_eff = lr * max(1, rows / cols) ** 0.5
+            newton_schulz(staged, ns_steps, update=p.data, neg_lr=-lr_eff)
+    for s in lanes[1:]:
+        main.wait_stream(s)
+    faults.snapshot(dev)
 
 
 class PackedExpertMuon(torch.optim.Optimizer):
     """Muon over packed expert tensors only (a Muon param group of
     build_optimizer, train.py:3066-3070, whose members are all 3-D)."""
 
-    def __init__(self, params, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5):
+    def __init__(self, params, lr=0.02, momentum=0.95, nesterov=True, ns_steps=5, streams=2):
         super().__init__(params, dict(lr=lr, momentum=momentum, nesterov=nesterov,
                                       ns_steps=ns_steps))
+        self.streams = streams
 
     @torch.no_grad()
     def step(self, closure=None):
@@ -115,5 +138,5 @@ class PackedExpertMuon(torch.optim.Optimizer):
                     st["v"] = torch.zeros_like(p, dtype=torch.float32)
                 bufs.append(st["v"])
             muon_step_packed(params, bufs, group["lr"], group["momentum"], group["nesterov"],
-                             group["ns_steps"])
+                             group["ns_steps"], self.streams)
         return loss

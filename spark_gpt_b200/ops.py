@@ -230,12 +230,23 @@ def dispatch(selected: torch.Tensor, num_experts: int, routed_slots: int | None 
 # --------------------------------------------------------------------------- #
 # gather / combine (train.py:2195-2241)
 # --------------------------------------------------------------------------- #
-def gather_rows(x: torch.Tensor, d: Dispatch) -> torch.Tensor:
+def _rows_out(out, rows: int, cols: int, like: torch.Tensor, name: str) -> torch.Tensor:
+    """A caller's (rows, cols) bf16 destination (checked), or a new one."""
+    if out is None:
+        return torch.empty(rows, cols, device=like.device, dtype=BF16)
+    _check(out, BF16, name)
+    if tuple(out.shape) != (rows, cols):
+        raise RuntimeError(f"{name}: expected shape {(rows, cols)}, got {tuple(out.shape)}")
+    return out
+
+
+def gather_rows(x: torch.Tensor, d: Dispatch, out=None) -> torch.Tensor:
+    """out: an optional contiguous (rows_cap, H) bf16 destination."""
     _check(x, BF16, "gather_rows x")
     H = x.shape[1]
+    xs = _rows_out(out, d.rows_cap, H, x, "gather_rows out")
     if d.num_tokens == 0:  # only padding rows
-        return torch.zeros(d.rows_cap, H, device=x.device, dtype=BF16)
-    xs = torch.empty(d.rows_cap, H, device=x.device, dtype=BF16)
+        return xs.zero_()
     _launch("gather", 1, "b200moe_gather_rows", _p(x), _p(d.row_flat),
             _p(d.inv_pad) if d.inv_pad.numel() else None, _p(d.pad_offsets), d.num_tokens,
             d.num_experts, d.top_k, H, d.rows_cap, _p(xs), _s(x))
@@ -298,13 +309,14 @@ def combine(y, d: Dispatch, weights, token_major=False) -> torch.Tensor:
     return out
 
 
-def combine_bwd(d_out, y, d: Dispatch, weights, token_major=False):
+def combine_bwd(d_out, y, d: Dispatch, weights, token_major=False, out=None):
+    """-> (dy (rows_cap, H) bf16, d_weights (T, k) fp32); out: an optional
+    contiguous destination for dy."""
     _check(d_out, BF16, "combine_bwd d_out")
     H = y.shape[1]
+    dy = _rows_out(out, d.rows_cap, H, y, "combine_bwd out")
     if d.num_tokens == 0:  # only padding rows, no routing weights
-        return (torch.zeros(d.rows_cap, H, device=y.device, dtype=BF16),
-                torch.zeros(0, d.top_k, device=y.device, dtype=torch.float32))
-    dy = torch.empty(d.rows_cap, H, device=y.device, dtype=BF16)
+        return dy.zero_(), torch.zeros(0, d.top_k, device=y.device, dtype=torch.float32)
     dw = torch.empty(d.num_tokens, d.top_k, device=y.device, dtype=torch.float32)
     _launch("combine_bwd", 2 if token_major else 1, "b200moe_combine_bwd", _p(d_out), _p(y),
             _p(d.row_flat), _p(d.inv_pad), _p(d.pad_offsets), _p(weights), d.num_experts,
@@ -315,11 +327,12 @@ def combine_bwd(d_out, y, d: Dispatch, weights, token_major=False):
 # --------------------------------------------------------------------------- #
 # expert products (train.py:1625-2090)
 # --------------------------------------------------------------------------- #
-def gate_up_fwd(xs, w_gu, d: Dispatch):
+def gate_up_fwd(xs, w_gu, d: Dispatch, out_h=None):
+    """-> (gu, h); out_h: an optional contiguous (rows_cap, I) bf16 destination."""
     E, two_i, H = w_gu.shape
     I = two_i // 2
     gu = torch.empty(d.rows_cap, two_i, device=xs.device, dtype=BF16)
-    h = torch.empty(d.rows_cap, I, device=xs.device, dtype=BF16)
+    h = _rows_out(out_h, d.rows_cap, I, xs, "gate_up_fwd out_h")
     _launch("gate_up_fwd", 1, "b200moe_expert_gate_up_fwd", _p(xs), _p(w_gu), _p(d.tile_expert),
             _p(d.pad_offsets), d.rows_cap, E, H, I, _p(gu), _p(h), _s(xs))
     return gu, h
@@ -336,9 +349,10 @@ def down_fwd(h, w_d, d: Dispatch, token_major=False):
     return y
 
 
-def down_dgrad_swiglu(dy, w_d, gu, d: Dispatch):
+def down_dgrad_swiglu(dy, w_d, gu, d: Dispatch, out=None):
+    """d_gu (rows_cap, 2I) bf16; out: an optional contiguous destination."""
     E, H, I = w_d.shape
-    d_gu = torch.empty(d.rows_cap, 2 * I, device=dy.device, dtype=BF16)
+    d_gu = _rows_out(out, d.rows_cap, 2 * I, dy, "down_dgrad_swiglu out")
     _launch("down_dgrad", 1, "b200moe_expert_down_dgrad_swiglu", _p(dy), _p(w_d), _p(gu),
             _p(d.tile_expert), _p(d.pad_offsets), d.rows_cap, E, H, I, _p(d_gu), _s(dy))
     return d_gu
@@ -363,6 +377,26 @@ def wgrad(a, b, d: Dispatch, name="wgrad", out=None, accumulate=False):
         accumulate = False
     _launch(name, 1, "b200moe_expert_wgrad", _p(a), M, _p(b), N, _p(d.pad_offsets),
             d.num_experts, d.rows_cap, _p(out), int(accumulate), _s(a))
+    return out
+
+
+def wgrad_segments(a, b, seg_offsets, num_experts, name="wgrad", out=None, accumulate=False):
+    """(E, M, N) fp32: a_e^T b_e where expert e's rows are the union over
+    segments s of [seg_offsets[s, e], seg_offsets[s, e+1]) of a and b
+    (rows_total, M) / (rows_total, N) bf16; seg_offsets (S, E+1) int32."""
+    M, N = a.shape[1], b.shape[1]
+    _check(a, BF16, f"{name} a")
+    _check(b, BF16, f"{name} b")
+    if a.shape[0] != b.shape[0]:
+        raise RuntimeError(f"{name}: a and b must have the same rows")
+    _check(seg_offsets, torch.int32, f"{name} seg_offsets")
+    if seg_offsets.dim() != 2 or seg_offsets.shape[1] != num_experts + 1:
+        raise RuntimeError(f"{name}: seg_offsets must be (segments, E+1)")
+    if out is None:
+        out = torch.empty(num_experts, M, N, device=a.device, dtype=torch.float32)
+        accumulate = False
+    _launch(name, 1, "b200moe_expert_wgrad_segments", _p(a), M, _p(b), N, _p(seg_offsets),
+            seg_offsets.shape[0], num_experts, a.shape[0], _p(out), int(accumulate), _s(a))
     return out
 
 

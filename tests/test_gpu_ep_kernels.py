@@ -367,7 +367,7 @@ def _emulated_pipe(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
     the backward.  The point-to-point flags live in per-rank device tensors
     reached through a peer table, as over NVLink."""
     from spark_gpt_b200.ep import (CudaExpertOps as B, FLAG_WORDS, PH_BWD_RETURN,
-                                   PH_BWD_SEND, PH_FWD_RETURN, PH_FWD_SEND)
+                                   PH_BWD_SEND, PH_FWD_RETURN, PH_FWD_SEND, RowArena)
     E = w_gu.shape[0]
     E_loc = E // P
     I, H = w_d.shape[2], w_d.shape[1]
@@ -406,18 +406,22 @@ def _emulated_pipe(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
         wgu_b = ops.cast_bf16(w_gu[o * E_loc:(o + 1) * E_loc].contiguous())
         wd_b = ops.cast_bf16(w_d[o * E_loc:(o + 1) * E_loc].contiguous())
         ectxs = [None] * P
+        arena = RowArena.for_chunks(rows_from, slots_from, E_loc, DEV)
+        arena.alloc("xs", H)
+        arena.alloc("h", I)
         for s in [(o - j) % P for j in range(P)]:
             if s != o:
                 ops.ep_wait(bufs[o].flags, PH_FWD_SEND, P, step, src=s)
             n = rows_from[s]
             sel_loc, w_loc = B.unpack(bufs[o].recv_meta[base[s]:base[s] + n])
             y, ectxs[s] = B.experts_fwd(bufs[o].recv_rows[base[s]:base[s] + n], sel_loc, w_loc,
-                                        wgu_b, wd_b, slots_from[s], combine=False)
+                                        wgu_b, wd_b, slots_from[s], combine=False,
+                                        arena=arena, src=s)
             if ectxs[s] is not None:
                 ops.ep_p2p_reduce_return_src(y, ectxs[s][0], st[o].plan, peers["back_rows"], P,
                                              s, weights=w_loc)
             ops.ep_signal(peers["flags"], PH_FWD_RETURN, o, P, step, dest=s)
-        own.append(SimpleNamespace(ectxs=ectxs, rows_from=rows_from, base=base))
+        own.append(SimpleNamespace(ectxs=ectxs, rows_from=rows_from, base=base, arena=arena))
     outs = []
     for r in range(P):
         ops.ep_wait(bufs[r].flags, PH_FWD_RETURN, P, step)
@@ -433,18 +437,22 @@ def _emulated_pipe(ops, x_list, d_out_list, w_r, w_gu, w_d, k, P):
         ops.ep_signal(peers["flags"], PH_BWD_SEND, r, P, step)
     ggu, gd = [], []
     for o in range(P):
-        g_gu = g_d = None
+        arena = own[o].arena
+        arena.alloc("dy", H)
+        arena.alloc("d_gu", 2 * I)
+        states = [None] * P
         for s in [(o - j) % P for j in range(P)]:
             if s != o:
                 ops.ep_wait(bufs[o].flags, PH_BWD_SEND, P, step, src=s)
             e = own[o].ectxs[s]
             d_rows = bufs[o].recv_rows[own[o].base[s]:own[o].base[s] + own[o].rows_from[s]]
-            dxs, dw_rows, state = B.experts_dgrad(e, d_rows, k, DEV, reduce=False)
+            dxs, dw_rows, states[s] = B.experts_dgrad(e, d_rows, k, DEV, reduce=False,
+                                                      arena=arena, src=s)
             if e is not None:
                 ops.ep_p2p_reduce_return_src(dxs, e[0], st[o].plan, peers["back_rows"], P, s,
                                              dw_rows=dw_rows, peer_dw=peers["back_dw"])
             ops.ep_signal(peers["flags"], PH_BWD_RETURN, o, P, step, dest=s)
-            g_gu, g_d = B.experts_wgrad(state, g_gu, g_d, E_loc, H, I, DEV)
+        g_gu, g_d = B.experts_wgrad_segments(states, arena, E_loc, H, I, DEV)
         ggu.append(g_gu)
         gd.append(g_d)
     dxs, g_routers = [], []

@@ -268,3 +268,58 @@ def test_pair_tiles_equal_single_cta_tiles(ops, T, k, E, H, I):
     names = ["gu", "h", "y", "d_gu", "dxs", "dW_gate_up", "dW_down"]
     for name, a, b in zip(names, single, pair):
         assert torch.equal(a, b), name
+
+
+@pytest.mark.parametrize("E,M,N,chunks", [(16, 1536, 2048, 4), (8, 512, 192, 3), (8, 384, 256, 2),
+                                          (32, 512, 1024, 8), (4, 256, 128, 1)])
+def test_wgrad_over_row_segments(ops, E, M, N, chunks):
+    """One weight gradient over several chunks' padded rows in one allocation
+    (the pipelined expert-parallel layer's arena) equals the fp32 product over
+    every chunk's rows of each expert: two-CTA tiles with segmented K (and a
+    partial last N tile at N = 192), per-segment launches where the pair tiles
+    do not apply (M = 384); an empty chunk and an expert without rows in any
+    chunk included; accumulation into an existing gradient."""
+    from spark_gpt_b200.ep import RowArena
+    g = torch.Generator().manual_seed(E + M + N + chunks)
+    sels, slots = [], []
+    for c in range(chunks):
+        T = 0 if (c == 1 and chunks > 2) else int(torch.randint(200, 1500, (1,), generator=g))
+        p = torch.ones(E)
+        p[0] = 0.0          # expert 0 gets no rows in any chunk
+        p[-1] = 6.0
+        sel = (torch.stack([torch.multinomial(p, 2, generator=g) for _ in range(T)])
+               if T else torch.zeros(0, 2, dtype=torch.int64))
+        sels.append(sel)
+        slots.append(sel.numel())
+    arena = RowArena.for_chunks([s.shape[0] for s in sels], slots, E, DEV)
+    arena.alloc("a", M)
+    arena.alloc("b", N)
+    ds = []
+    ref = torch.zeros(E, M, N, device=DEV)
+    for c, sel in enumerate(sels):
+        if sel.shape[0] == 0:
+            ds.append(None)
+            continue
+        d = ops.dispatch(sel.to(DEV), E, routed_slots=sel.numel())
+        a = arena.rows("a", c)
+        b = arena.rows("b", c)
+        a.copy_(torch.randn(a.shape, generator=g).to(torch.bfloat16))
+        b.copy_(torch.randn(b.shape, generator=g).to(torch.bfloat16))
+        rows = d.row_flat[: d.rows_cap].clone()
+        rows[int(d.pad_offsets[-1]):] = -1
+        a[rows < 0] = 0     # padding rows carry zeros in the layer
+        b[rows < 0] = 0
+        for e, s, t in _segments(d):
+            if t > s:
+                ref[e] += a[s:t].float().t() @ b[s:t].float()
+        ds.append(d)
+    segs = arena.segments(ds, E)
+    dw = ops.wgrad_segments(arena.bufs["a"], arena.bufs["b"], segs, E)
+    torch.testing.assert_close(dw, ref, rtol=1e-3, atol=1e-3 * ref.abs().max().item())
+    assert torch.all(dw[0] == 0)
+    dw2 = ops.wgrad_segments(arena.bufs["a"], arena.bufs["b"], segs, E, out=dw.clone(),
+                             accumulate=True)
+    torch.testing.assert_close(dw2, 2 * ref, rtol=1e-3, atol=2e-3 * ref.abs().max().item())
+    torch.cuda.synchronize()
+    from spark_gpt_b200 import _lib
+    assert _lib.read_fault() == 0

@@ -120,3 +120,25 @@ def test_newton_schulz_orthogonalises_full_size(muon):
     out = muon.newton_schulz(x, 5)
     s = torch.linalg.svdvals(out.float())
     assert float(s.min()) > 0.5 and float(s.max()) < 1.3
+
+
+def test_muon_streams_match_single_stream(muon):
+    """The parameters' updates on two streams equal the one-stream step bit for
+    bit (the same kernels, only overlapped), over three steps at the cfg2
+    expert shapes, and the caller's stream sees the finished parameters."""
+    g = torch.Generator(device=DEV).manual_seed(11)
+    shapes = [(64, 512, 1024), (64, 1024, 256)]
+    init = [torch.randn(*s, device=DEV, generator=g) * 0.01 for s in shapes]
+    grads = [[torch.randn(*s, device=DEV, generator=g) * 1e-3 for s in shapes] for _ in range(3)]
+    results = []
+    for streams in (1, 2):
+        params = [torch.nn.Parameter(t.clone()) for t in init]
+        opt = muon.PackedExpertMuon(params, lr=0.02, streams=streams)
+        for step_grads in grads:
+            for p, gr in zip(params, step_grads):
+                p.grad = gr.clone()
+            opt.step()
+        results.append([p.detach().clone() for p in params])  # on the caller's stream
+    torch.cuda.synchronize()
+    for a, b in zip(*results):
+        assert torch.equal(a, b)
