@@ -623,7 +623,7 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
 #define B200MOE_EPI_GROUP 1  // chunks per proxy fence in the plain bf16 epilogue
 #endif
 #ifndef B200MOE_WIDE_BF16
-#define B200MOE_WIDE_BF16 0  // plain bf16 stores as 32 x 64 boxes (128-byte swizzle)
+#define B200MOE_WIDE_BF16 1  // plain bf16 stores as 32 x 64 boxes (128-byte swizzle)
 #endif
 constexpr bool kWideBf16Store = B200MOE_WIDE_BF16 != 0;
 
