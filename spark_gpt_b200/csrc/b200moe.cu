@@ -269,6 +269,27 @@ int make_out_tmap_f32(CUtensorMap* m, const void* base, long long cols, long lon
   return B200MOE_OK;
 }
 
+// Output tensor maps of the weight-gradient epilogue (kEpiStoreF32Tma): the
+// {16, 32} box above, or a {32, 32} box with the 128-byte swizzle when that
+// epilogue stores a whole TMEM chunk per box.
+int make_wgrad_tmap(CUtensorMap* m, const void* base, long long cols, long long rows,
+                    const char* what) {
+  if (!kWideF32Store) return make_out_tmap_f32(m, base, cols, rows, what);
+  auto fn = encode_fn();
+  if (!fn) return fail(B200MOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols * 4)};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(B200MOE_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed (%d)", what, static_cast<int>(r));
+  return B200MOE_OK;
+}
+
 // Output tensor maps of the fp8 TMA-store epilogues: a {32, 32} box of bytes,
 // unswizzled, over a (rows, cols) fp8 matrix.
 int make_out_tmap_u8(CUtensorMap* m, const void* base, long long cols, long long rows,
@@ -1112,7 +1133,7 @@ int b200moe_expert_wgrad(const void* a, int M, const void* b, int N, const int* 
     // two-CTA tiles whose fp32 output leaves through shared memory with TMA
     // stores (reduce-adds when accumulating): coalesced and asynchronous
     CUtensorMap to;
-    if ((rc = make_out_tmap_f32(&to, dw, N, static_cast<long long>(E) * M, "expert_wgrad dw")))
+    if ((rc = make_wgrad_tmap(&to, dw, N, static_cast<long long>(E) * M, "expert_wgrad dw")))
       return rc;
     if (BN == 256)
       return launch_gemm_pair<256, true, true, kEpiStoreF32Tma, kKRagged>(ta, tb, to, to, p, st,
@@ -1150,7 +1171,7 @@ int b200moe_expert_wgrad_segments(const void* a, int M, const void* b, int N,
   int rc;
   if ((rc = make_tmap(&ta, a, M, rows_total, M, 64, 64, "expert_wgrad_segments a"))) return rc;
   if ((rc = make_tmap(&tb, b, N, rows_total, N, 64, 64, "expert_wgrad_segments b"))) return rc;
-  if ((rc = make_out_tmap_f32(&to, dw, N, static_cast<long long>(E) * M,
+  if ((rc = make_wgrad_tmap(&to, dw, N, static_cast<long long>(E) * M,
                               "expert_wgrad_segments dw")))
     return rc;
   GemmParams p = blank_params();
@@ -1451,7 +1472,7 @@ int b200moe_fp8_expert_wgrad(const void* a8, int a_fmt, int M, const void* b8, i
   int rc;
   if ((rc = make_tmap_u8(&ta, a8, M, rows_cap, M, 128, 128, "fp8_wgrad a"))) return rc;
   if ((rc = make_tmap_u8(&tb, b8, N, rows_cap, N, 128, 128, "fp8_wgrad b"))) return rc;
-  if ((rc = make_out_tmap_f32(&to, dw, N, static_cast<long long>(E) * M, "fp8_wgrad dw"))) return rc;
+  if ((rc = make_wgrad_tmap(&to, dw, N, static_cast<long long>(E) * M, "fp8_wgrad dw"))) return rc;
   GemmParams p = blank_params();
   p.pad_offsets = pad_offsets;
   p.num_groups = E;

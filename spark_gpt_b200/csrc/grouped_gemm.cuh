@@ -626,6 +626,10 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
 #define B200MOE_WIDE_BF16 1  // plain bf16 stores as 32 x 64 boxes (128-byte swizzle)
 #endif
 constexpr bool kWideBf16Store = B200MOE_WIDE_BF16 != 0;
+#ifndef B200MOE_WIDE_F32
+#define B200MOE_WIDE_F32 0  // fp32 weight-gradient stores as 32 x 32 boxes (128-byte swizzle)
+#endif
+constexpr bool kWideF32Store = B200MOE_WIDE_F32 != 0;
 
 // The bf16-output epilogues (plain store, SwiGLU forward, SwiGLU backward) with
 // TMA stores.  Outputs: O0 = out (or gu / d_gu), O1 = h (SwiGLU forward).
@@ -638,7 +642,45 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
                                                   unsigned long long* prof = nullptr) {
   constexpr int BM = 128;
   const int row0 = T.m * BM + quarter * 32;
-  if (EPI == kEpiStoreF32Tma) {
+  if (EPI == kEpiStoreF32Tma && kWideF32Store) {
+    // fp32 weight-gradient tile: each 32-column TMEM chunk leaves as one 32 x 32
+    // box (4 KB, 128-byte swizzle) in the ring's two buffers, stored (or
+    // reduce-added into the gradient when accumulating)
+    static_assert(kOutRing % 2 == 0, "wide stores take buffer pairs");
+    const int rowg = T.g * p.m_tiles * BM + row0;  // (E*M, N) view of the output
+    const float sc = SCALED ? deq_factor(p, T.g) : 1.f;
+#pragma unroll 1
+    for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); ++c) {
+      if (T.n * BN + c * 32 >= p.n_valid) break;
+      uint32_t r[32];
+      tmem_ld32(taddr + c * 32, r);
+      tmem_wait_ld();
+      ring_acquire<2>(lane);
+      uint4* rowp = reinterpret_cast<uint4*>(ring.base + ring.next * 2048 + lane * 128);
+      const int sw = lane & 7;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          v[q] = SCALED ? __uint_as_float(r[4 * j + q]) * sc : __uint_as_float(r[4 * j + q]);
+        rowp[j ^ sw] = make_uint4(__float_as_uint(v[0]), __float_as_uint(v[1]),
+                                  __float_as_uint(v[2]), __float_as_uint(v[3]));
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const uint8_t* buf = ring.base + ring.next * 2048;
+        const int col = T.n * BN + c * 32;
+        if (p.accumulate)
+          tma_reduce_add_2d(tmO0, buf, col, rowg);
+        else
+          tma_store_2d(tmO0, buf, col, rowg);
+        bulk_commit_group();
+      }
+      ring.next = (ring.next + 2) % kOutRing;
+    }
+  } else if (EPI == kEpiStoreF32Tma) {
     // fp32 weight-gradient tile: each 32-column TMEM chunk leaves as two 32 x 16
     // boxes, stored (or reduce-added into the gradient when accumulating)
     const int rowg = T.g * p.m_tiles * BM + row0;  // (E*M, N) view of the output
