@@ -627,7 +627,7 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
 #endif
 constexpr bool kWideBf16Store = B200MOE_WIDE_BF16 != 0;
 #ifndef B200MOE_WIDE_F32
-#define B200MOE_WIDE_F32 0  // fp32 weight-gradient stores as 32 x 32 boxes (128-byte swizzle)
+#define B200MOE_WIDE_F32 1  // fp32 weight-gradient stores as 32 x 32 boxes (128-byte swizzle)
 #endif
 constexpr bool kWideF32Store = B200MOE_WIDE_F32 != 0;
 
