@@ -43,11 +43,8 @@ int b200moe_set_pair_gemm(int enable);
  * the default), leaving the rest to kernels that run beside them on other
  * streams, such as the NCCL all-to-all of the expert-parallel layer: every
  * CTA of a persistent grid is then resident at once and no statically
- * scheduled tile waits for the collective to finish.  While it is set, the
- * peer-memory transfer kernels (b200moe_ep_p2p_send_part,
- * b200moe_ep_p2p_reduce_return(_src)) launch at most 8 blocks per SM left
- * outside it, so a transfer on a copy stream keeps to those SMs.  Results do
- * not depend on it.  Returns the previous setting; process-wide. */
+ * scheduled tile waits for the collective to finish.  Results do not depend
+ * on it.  Returns the previous setting; process-wide. */
 int b200moe_set_persistent_sm_limit(int sms);
 
 /* Message of this thread's last failed call ("" if none). */

@@ -344,19 +344,6 @@ int grid_for(long long items, int per_block) {
   return static_cast<int>(g);
 }
 
-// Grid of a transfer kernel (grid-stride warps over rows): while a persistent
-// SM limit is set (b200moe_set_persistent_sm_limit: the transfers run on a
-// copy stream beside the compute stream's kernels), at most 8 blocks of 256
-// threads per SM left outside that limit, so the copy kernels fill the SMs
-// the persistent GEMMs leave free instead of every SM the compute stream's
-// next kernels want.
-int transfer_grid(long long items, int per_block) {
-  const int g = grid_for(items, per_block);
-  const int n = num_sms();
-  if (g_sm_limit <= 0 || g_sm_limit >= n) return g;
-  return std::min(g, (n - g_sm_limit) * 8);
-}
-
 // lanes per token of the router kernels: 8 logits per lane, so 8*L >= width
 int lanes_for(long long width) {
   int l = 2;
@@ -1782,7 +1769,7 @@ int b200moe_ep_p2p_send_part(const void* src, const int* inv_send, const int* se
   auto* sp = static_cast<const __nv_bfloat16*>(src);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   auto* wp = static_cast<const unsigned short*>(weights);
-  const int grid = transfer_grid(T, 8);
+  const int grid = grid_for(T, 8);
   switch (H) {
     case 1024: ep_p2p_send_kernel<4><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
     case 2048: ep_p2p_send_kernel<8><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
@@ -1808,10 +1795,10 @@ int b200moe_ep_p2p_reduce_return_src(const void* rows, const int* inv_pad, const
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   switch (H) {
-    case 256: ep_p2p_reduce_return_kernel<1, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    case 512: ep_p2p_reduce_return_kernel<2, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    default: ep_p2p_reduce_return_kernel<4, 2><<<transfer_grid(2 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 256: ep_p2p_reduce_return_kernel<1, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 512: ep_p2p_reduce_return_kernel<2, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    default: ep_p2p_reduce_return_kernel<4, 2><<<grid_for(2 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
   }
   return check_launch("ep_p2p_reduce_return_src");
 }
@@ -1874,10 +1861,10 @@ int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const voi
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   switch (H) {  // a warp handles at most 1024 columns (4 vectors per lane)
-    case 256: ep_p2p_reduce_return_kernel<1, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    case 512: ep_p2p_reduce_return_kernel<2, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    default: ep_p2p_reduce_return_kernel<4, 2><<<transfer_grid(2 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 256: ep_p2p_reduce_return_kernel<1, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 512: ep_p2p_reduce_return_kernel<2, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    default: ep_p2p_reduce_return_kernel<4, 2><<<grid_for(2 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
   }
   return check_launch("ep_p2p_reduce_return");
 }

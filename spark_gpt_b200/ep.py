@@ -738,18 +738,17 @@ class _EPMoEPipeFn(torch.autograd.Function):
         ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 1, sel, rw, E_loc,
                              tr.peer_recv_meta)
         ready = s0.record_event()
+        with torch.cuda.stream(s1):
+            s1.wait_event(ready)
+            ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 2, sel, rw, E_loc,
+                                 tr.peer_recv_meta)
+            ops.ep_signal(tr.peer_flags, PH_FWD_SEND, me, P, step)
         order = [(me - j) % P for j in range(P)]
         ectxs, keep = [None] * P, []
         arena = RowArena.for_chunks(rows_from, slots_from, E_loc, dev)
         arena.alloc("xs", H)
         arena.alloc("h", w_gu.shape[1] // 2)
-        # the copy stream's kernels keep to the SMs the persistent GEMMs leave
         with backend_overlap(comm_sms) if (comm_sms and P > 1) else nullcontext():
-            with torch.cuda.stream(s1):
-                s1.wait_event(ready)
-                ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 2, sel, rw, E_loc,
-                                     tr.peer_recv_meta)
-                ops.ep_signal(tr.peer_flags, PH_FWD_SEND, me, P, step)
             for s in order:
                 if s != me:
                     ops.ep_wait(tr.flags, PH_FWD_SEND, P, step, src=s)
@@ -796,15 +795,15 @@ class _EPMoEPipeFn(torch.autograd.Function):
         d_out = _as_bf16(d_out)
         ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 1)
         ready = s0.record_event()
+        with torch.cuda.stream(s1):
+            s1.wait_event(ready)
+            ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 2)
+            ops.ep_signal(tr.peer_flags, PH_BWD_SEND, me, P, step)
         order = [(me - j) % P for j in range(P)]
         states, keep = [None] * P, []
         arena.alloc("dy", H)
         arena.alloc("d_gu", 2 * I)
         with backend_overlap(comm_sms) if (comm_sms and P > 1) else nullcontext():
-            with torch.cuda.stream(s1):
-                s1.wait_event(ready)
-                ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 2)
-                ops.ep_signal(tr.peer_flags, PH_BWD_SEND, me, P, step)
             for s in order:
                 if s != me:
                     ops.ep_wait(tr.flags, PH_BWD_SEND, P, step, src=s)
