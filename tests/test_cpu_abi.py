@@ -63,6 +63,10 @@ def test_entry_points_reject_bad_arguments_without_touching_the_gpu(lib):
         _lib.call("b200moe_expert_gate_up_fwd", 16, 16, 16, 16, 1024, 8, 256, 100, 16, 16, None)
     with pytest.raises(RuntimeError, match="scratch too small"):
         _lib.call("b200moe_dispatch", 16, 1000, 8, 64, 16, 16, 16, 16, 16, 16, 16, 4, None)
+    with pytest.raises(RuntimeError, match="segments"):
+        _lib.call("b200moe_expert_wgrad_segments", 16, 512, 16, 256, 16, 0, 8, 1024, 16, 0, None)
+    with pytest.raises(RuntimeError, match="N must be"):
+        _lib.call("b200moe_expert_wgrad_segments", 16, 512, 16, 100, 16, 2, 8, 1024, 16, 0, None)
 
 
 def _cfg():
@@ -89,3 +93,38 @@ def test_no_cpu_fallback():
     m = SparseMoE(_cfg())
     with pytest.raises(RuntimeError, match="no CPU path"):
         m(torch.randn(4, 256))
+
+
+def test_row_arena_layout(lib):
+    """The pipelined expert-parallel layer's shared row buffers: chunk s owns
+    rows [base_s, base_s + cap_s) in source order, capacities are the chunks'
+    dispatch capacities (none for a chunk without rows or slots), and the
+    segment table moves each chunk's padded expert offsets to its base."""
+    from spark_gpt_b200 import ops
+    from spark_gpt_b200.ep import RowArena
+    E = 4
+    arena = RowArena.for_chunks([10, 0, 7, 3], [25, 0, 9, 0], E, "cpu")
+    caps = [ops.padded_rows(25, E), 0, ops.padded_rows(9, E), 0]
+    assert arena.caps == caps and all(c % 128 == 0 for c in caps)
+    assert arena.base == [0, caps[0], caps[0], caps[0] + caps[2]]
+    assert arena.total == sum(caps)
+    arena.alloc("xs", 16)
+    assert arena.bufs["xs"].shape == (sum(caps), 16)
+    assert arena.rows("xs", 1).shape == (0, 16)
+    v = arena.rows("xs", 2)
+    assert v.shape == (caps[2], 16) and v.is_contiguous()
+    assert v.data_ptr() == arena.bufs["xs"].data_ptr() + caps[0] * 16 * 2
+    i32 = torch.int32
+    d0 = SimpleNamespace(pad_offsets=torch.tensor([0, 128, 128, 256, 384], dtype=i32))
+    d2 = SimpleNamespace(pad_offsets=torch.tensor([0, 0, 128, 128, 128], dtype=i32))
+    segs = arena.segments([d0, None, d2, None], E)
+    assert segs.dtype == i32 and segs.shape == (4, E + 1)
+    assert segs[0].tolist() == [0, 128, 128, 256, 384]
+    assert segs[1].tolist() == [caps[0]] * (E + 1)
+    assert segs[2].tolist() == [caps[0] + x for x in (0, 0, 128, 128, 128)]
+    assert segs[3].tolist() == [caps[0] + caps[2]] * (E + 1)
+    # per expert: the union of its segments holds every chunk's padded rows
+    lens = (segs[:, 1:] - segs[:, :-1]).sum(0).tolist()
+    assert lens == [128, 128, 128, 128]
+    # an arena without rows still has one 128-row block to hand out
+    assert RowArena.for_chunks([0, 0], [0, 0], E, "cpu").total == 128
