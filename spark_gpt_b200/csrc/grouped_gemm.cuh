@@ -626,9 +626,6 @@ __device__ __forceinline__ void store_chunk_tma(OutRing& ring, const CUtensorMap
 #define B200MOE_WIDE_BF16 1  // plain bf16 stores as 32 x 64 boxes (128-byte swizzle)
 #endif
 constexpr bool kWideBf16Store = B200MOE_WIDE_BF16 != 0;
-#ifndef B200MOE_EPI_PIPE
-#define B200MOE_EPI_PIPE 0  // wide bf16 stores: next chunk pair's TMEM loads ahead
-#endif
 #ifndef B200MOE_WIDE_F32
 #define B200MOE_WIDE_F32 1  // fp32 weight-gradient stores as 32 x 32 boxes (128-byte swizzle)
 #endif
@@ -782,31 +779,12 @@ __device__ __forceinline__ void epilogue_tile_tma(const GemmParams& p, const Til
     // swizzle) in two consecutive ring buffers: half the TMA stores
     static_assert(kOutRing % 2 == 0 && (BN / 64) % 2 == 0, "wide stores take buffer pairs");
     const float sc = SCALED ? deq_factor(p, T.g) : 1.f;
-#if B200MOE_EPI_PIPE
-    // the next chunk pair's TMEM loads are in flight while this pair is written
-    constexpr int NP = BN / 128;  // chunk pairs of this warp
-    uint32_t rr[2][2][32];
-    const int cb = half * (BN / 64);
-    tmem_ld32(taddr + cb * 32, rr[0][0]);
-    tmem_ld32(taddr + (cb + 1) * 32, rr[0][1]);
-#pragma unroll
-    for (int q = 0; q < NP; ++q) {
-      const int c = cb + 2 * q;
-      tmem_wait_ld();
-      if (q + 1 < NP) {
-        tmem_ld32(taddr + (c + 2) * 32, rr[(q + 1) & 1][0]);
-        tmem_ld32(taddr + (c + 3) * 32, rr[(q + 1) & 1][1]);
-      }
-      const uint32_t* r0 = rr[q & 1][0];
-      const uint32_t* r1 = rr[q & 1][1];
-#else
 #pragma unroll 1
     for (int c = half * (BN / 64); c < (half + 1) * (BN / 64); c += 2) {
       uint32_t r0[32], r1[32];
       tmem_ld32(taddr + c * 32, r0);
       tmem_ld32(taddr + (c + 1) * 32, r1);
       tmem_wait_ld();
-#endif
       ring_acquire<2>(lane);
       uint4* rowp = reinterpret_cast<uint4*>(ring.base + ring.next * 2048 + lane * 128);
       const int sw = lane & 7;
