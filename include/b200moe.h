@@ -47,6 +47,14 @@ int b200moe_set_pair_gemm(int enable);
  * on it.  Returns the previous setting; process-wide. */
 int b200moe_set_persistent_sm_limit(int sms);
 
+/* The peer-memory transfer kernels (b200moe_ep_p2p_send / _send_part,
+ * b200moe_ep_p2p_reduce_return / _src) launch at most 8 blocks per SM of
+ * `sms` SMs (0 = a grid over every SM, the default): for a transfer on a copy
+ * stream beside the compute stream, whose kernels then keep the other SMs
+ * instead of waiting for the transfer's blocks.  Results do not depend on
+ * it.  Returns the previous setting; process-wide. */
+int b200moe_set_transfer_sm_limit(int sms);
+
 /* Message of this thread's last failed call ("" if none). */
 const char* b200moe_last_error(void);
 

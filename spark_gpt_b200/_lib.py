@@ -25,6 +25,7 @@ PROTOTYPES = {
     "b200moe_last_error": (c_char_p, []),
     "b200moe_set_pair_gemm": (I, [I]),
     "b200moe_set_persistent_sm_limit": (I, [I]),
+    "b200moe_set_transfer_sm_limit": (I, [I]),
     "b200moe_fault_read_and_clear": (I, [POINTER(c_uint)]),
     "b200moe_fault_snapshot": (I, [P, P]),
     "b200moe_padded_rows": (L, [L, I]),

@@ -62,6 +62,11 @@ int num_sms() {
 // resident at once and no statically scheduled tile waits for the collective.
 int g_sm_limit = 0;
 
+// SMs' worth of blocks the peer-memory transfer kernels launch (0 = a grid
+// over every SM): set while a transfer runs on a copy stream beside the
+// compute stream, so that the compute stream's kernels keep their SMs.
+int g_transfer_sm_limit = 0;
+
 int persistent_sms() {
   const int n = num_sms();
   return (g_sm_limit > 0 && g_sm_limit < n) ? g_sm_limit : n;
@@ -344,6 +349,13 @@ int grid_for(long long items, int per_block) {
   return static_cast<int>(g);
 }
 
+// Grid of a transfer kernel (grid-stride warps over rows): at most 8 blocks of
+// 256 threads per SM of the transfer SM limit, when one is set.
+int transfer_grid(long long items, int per_block) {
+  const int g = grid_for(items, per_block);
+  return g_transfer_sm_limit > 0 ? std::min(g, g_transfer_sm_limit * 8) : g;
+}
+
 // lanes per token of the router kernels: 8 logits per lane, so 8*L >= width
 int lanes_for(long long width) {
   int l = 2;
@@ -419,6 +431,12 @@ int b200moe_version(void) { return 100; }
 int b200moe_set_persistent_sm_limit(int sms) {
   const int prev = g_sm_limit;
   g_sm_limit = sms > 0 ? (sms < 2 ? 2 : sms) : 0;
+  return prev;
+}
+
+int b200moe_set_transfer_sm_limit(int sms) {
+  const int prev = g_transfer_sm_limit;
+  g_transfer_sm_limit = sms > 0 ? sms : 0;
   return prev;
 }
 
@@ -1743,7 +1761,7 @@ int b200moe_ep_p2p_send(const void* src, const int* inv_send, const int* send_pa
   auto* sp = static_cast<const __nv_bfloat16*>(src);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   auto* wp = static_cast<const unsigned short*>(weights);
-  const int grid = grid_for(T, 8);
+  const int grid = transfer_grid(T, 8);
   switch (H) {
     case 1024: ep_p2p_send_kernel<4><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta); break;
     case 2048: ep_p2p_send_kernel<8><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta); break;
@@ -1769,7 +1787,7 @@ int b200moe_ep_p2p_send_part(const void* src, const int* inv_send, const int* se
   auto* sp = static_cast<const __nv_bfloat16*>(src);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   auto* wp = static_cast<const unsigned short*>(weights);
-  const int grid = grid_for(T, 8);
+  const int grid = transfer_grid(T, 8);
   switch (H) {
     case 1024: ep_p2p_send_kernel<4><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
     case 2048: ep_p2p_send_kernel<8><<<grid, 256, 0, st>>>(sp, inv_send, send_pad_offsets, plan, pr, T, H, ranks, selected, wp, k, experts_per_rank, peer_meta, me, dest_mode); break;
@@ -1795,10 +1813,10 @@ int b200moe_ep_p2p_reduce_return_src(const void* rows, const int* inv_pad, const
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   switch (H) {
-    case 256: ep_p2p_reduce_return_kernel<1, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    case 512: ep_p2p_reduce_return_kernel<2, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<grid_for(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    default: ep_p2p_reduce_return_kernel<4, 2><<<grid_for(2 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 256: ep_p2p_reduce_return_kernel<1, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 512: ep_p2p_reduce_return_kernel<2, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    default: ep_p2p_reduce_return_kernel<4, 2><<<transfer_grid(2 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
   }
   return check_launch("ep_p2p_reduce_return_src");
 }
@@ -1861,10 +1879,10 @@ int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const voi
   auto* wp = static_cast<const __nv_bfloat16*>(weights);
   auto* pr = reinterpret_cast<__nv_bfloat16* const*>(peer_rows);
   switch (H) {  // a warp handles at most 1024 columns (4 vectors per lane)
-    case 256: ep_p2p_reduce_return_kernel<1, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    case 512: ep_p2p_reduce_return_kernel<2, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<grid_for(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    default: ep_p2p_reduce_return_kernel<4, 2><<<grid_for(2 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 256: ep_p2p_reduce_return_kernel<1, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 512: ep_p2p_reduce_return_kernel<2, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    case 1024: ep_p2p_reduce_return_kernel<4, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    default: ep_p2p_reduce_return_kernel<4, 2><<<transfer_grid(2 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
   }
   return check_launch("ep_p2p_reduce_return");
 }

@@ -738,7 +738,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
         ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 1, sel, rw, E_loc,
                              tr.peer_recv_meta)
         ready = s0.record_event()
-        with torch.cuda.stream(s1):
+        with torch.cuda.stream(s1), _transfer_limit(comm_sms, P):
             s1.wait_event(ready)
             ops.ep_p2p_send_part(xb, send, plan, tr.peer_recv_rows, me, 2, sel, rw, E_loc,
                                  tr.peer_recv_meta)
@@ -758,7 +758,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
                 y, ectxs[s] = B.experts_fwd(rows, sel_loc, w_loc, wgu_b, wd_b, slots_from[s],
                                             combine=False, arena=arena, src=s)
                 done = s0.record_event()
-                with torch.cuda.stream(s1):
+                with torch.cuda.stream(s1), _transfer_limit(comm_sms, P):
                     s1.wait_event(done)
                     if ectxs[s] is not None:
                         ops.ep_p2p_reduce_return_src(y, ectxs[s][0], plan, tr.peer_back_rows, P,
@@ -795,7 +795,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
         d_out = _as_bf16(d_out)
         ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 1)
         ready = s0.record_event()
-        with torch.cuda.stream(s1):
+        with torch.cuda.stream(s1), _transfer_limit(comm_sms, P):
             s1.wait_event(ready)
             ops.ep_p2p_send_part(d_out, send, plan, tr.peer_recv_rows, me, 2)
             ops.ep_signal(tr.peer_flags, PH_BWD_SEND, me, P, step)
@@ -811,7 +811,7 @@ class _EPMoEPipeFn(torch.autograd.Function):
                 dxs, dw_rows, states[s] = B.experts_dgrad(ectxs[s], d_rows, top_k, dev,
                                                           reduce=False, arena=arena, src=s)
                 done = s0.record_event()
-                with torch.cuda.stream(s1):
+                with torch.cuda.stream(s1), _transfer_limit(comm_sms, P):
                     s1.wait_event(done)
                     if ectxs[s] is not None:
                         ops.ep_p2p_reduce_return_src(dxs, ectxs[s][0], plan, tr.peer_back_rows,
@@ -831,6 +831,13 @@ class _EPMoEPipeFn(torch.autograd.Function):
         dx = ops.gather_rows_bwd(tr.back_rows[:n_back], back, addend=dx_router)
         faults.snapshot(dev)
         return (dx.to(xdtype), g_router, g_gu, g_d, None, None, None, None, None, None)
+
+
+def _transfer_limit(comm_sms, P):
+    """The pipelined layer's copy-stream transfers keep to `comm_sms` SMs'
+    worth of blocks, so the compute stream's kernels do not wait for SMs the
+    transfers hold (at 8 ranks the transfers run for most of the step)."""
+    return ops.transfer_sm_limit(comm_sms) if (comm_sms and P > 1) else nullcontext()
 
 
 def backend_overlap(comm_sms):

@@ -54,6 +54,18 @@ def persistent_sm_limit(sms: int):
         _lib.value("b200moe_set_persistent_sm_limit", prev)
 
 
+@contextmanager
+def transfer_sm_limit(sms: int):
+    """Peer-memory transfer kernels enqueued inside the block launch at most 8
+    blocks per SM of `sms` SMs (0 = all), leaving the other SMs to the
+    kernels of the stream they run beside."""
+    prev = int(_lib.value("b200moe_set_transfer_sm_limit", int(sms)))
+    try:
+        yield
+    finally:
+        _lib.value("b200moe_set_transfer_sm_limit", prev)
+
+
 def _launch(name: str, kernels: int, fn, *args):
     LAUNCHES["count"] += kernels
     if _timing is not None and name in _timing:
