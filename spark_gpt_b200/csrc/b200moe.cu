@@ -1816,7 +1816,7 @@ int b200moe_ep_p2p_reduce_return_src(const void* rows, const int* inv_pad, const
     case 256: ep_p2p_reduce_return_kernel<1, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
     case 512: ep_p2p_reduce_return_kernel<2, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
     case 1024: ep_p2p_reduce_return_kernel<4, 1><<<transfer_grid(n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
-    default: ep_p2p_reduce_return_kernel<4, 2><<<transfer_grid(2 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
+    default: ep_p2p_reduce_return_kernel<2, 4><<<transfer_grid(4 * n_rows, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks, n_rows, src); break;
   }
   return check_launch("ep_p2p_reduce_return_src");
 }
@@ -1882,7 +1882,7 @@ int b200moe_ep_p2p_reduce_return(const void* rows, const int* inv_pad, const voi
     case 256: ep_p2p_reduce_return_kernel<1, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
     case 512: ep_p2p_reduce_return_kernel<2, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
     case 1024: ep_p2p_reduce_return_kernel<4, 1><<<transfer_grid(rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
-    default: ep_p2p_reduce_return_kernel<4, 2><<<transfer_grid(2 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
+    default: ep_p2p_reduce_return_kernel<2, 4><<<transfer_grid(4 * rows_cap, 8), 256, 0, st>>>(yp, inv_pad, wp, k, dw_rows, plan, pr, peer_dw, H, ranks); break;
   }
   return check_launch("ep_p2p_reduce_return");
 }

@@ -357,8 +357,8 @@ namespace b200moe {
 // rows; with dw (rows, k) fp32 its k routing-weight gradients go to the same
 // row of the source's back dw.  A warp takes one of SPLIT column parts of a
 // received row (VPL 16-byte vectors per lane), so the fp32 accumulators stay
-// few enough for three 256-thread blocks per SM; the rows of the valid slots
-// are loaded two at a time.
+// few enough for four 256-thread blocks per SM at H = 2048 (four 512-column
+// parts); the rows of the valid slots are loaded two at a time.
 template <int VPL, int SPLIT>
 __global__ void ep_p2p_reduce_return_kernel(const __nv_bfloat16* __restrict__ y,
                                             const int* __restrict__ inv_pad,
